@@ -1,0 +1,383 @@
+// Row-wise kernels of the decoder step: embedding gather, RMSNorm, RoPE + KV write (f16 or fp8 with per-page
+// scales), split-K reduction with the GEMM epilogues, argmax, and the KV block operations behind gc_copy_blocks and
+// gc_commit. Each is HBM- or latency-bound and touches every byte once.
+//
+// Reference math (goethe_engine/ref.py): rms ref.py:14-15, RoPE ref.py:31-37 (interleaved pairs), KV write ref.py:54,
+// SwiGLU ref.py:59, commit ref.py:114-120, copy_blocks ref.py:122-126.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace gck {
+
+// ----------------------------------------------------------------------------------------------------------------
+// embedding: x[t, :] = dequant(token_embd[tok[t], :])
+__device__ float dequant_elem(const uint8_t *row, int type, int e) {
+  switch (type) {
+    case kF32: return reinterpret_cast<const float *>(row)[e];
+    case kF16: return __half2float(reinterpret_cast<const __half *>(row)[e]);
+    case kQ8_0: {
+      const uint8_t *b = row + (e / 32) * 34;
+      return __half2float(*reinterpret_cast<const __half *>(b)) * static_cast<float>(static_cast<int8_t>(b[2 + e % 32]));
+    }
+    default: {  // Q4_K
+      const uint8_t *b = row + (e / 256) * 144;
+      int w = e % 256, sub = w / 32, l = w % 32, c = sub / 2;
+      const uint8_t *s = b + 4;
+      int sc, m;
+      if (sub < 4) { sc = s[sub] & 63; m = s[sub + 4] & 63; }
+      else { sc = (s[sub + 4] & 15) | ((s[sub - 4] >> 6) << 4); m = (s[sub + 4] >> 4) | ((s[sub] >> 6) << 4); }
+      int q = (sub & 1) ? (b[16 + 32 * c + l] >> 4) : (b[16 + 32 * c + l] & 15);
+      float d = __half2float(*reinterpret_cast<const __half *>(b));
+      float dm = __half2float(*reinterpret_cast<const __half *>(b + 2));
+      return d * static_cast<float>(sc) * static_cast<float>(q) - dm * static_cast<float>(m);
+    }
+  }
+}
+
+__global__ void embed_kernel(PlanView pv, const uint8_t *emb, int type, size_t row_bytes, int d, float *x) {
+  int t = blockIdx.x;
+  const uint8_t *row = emb + static_cast<size_t>(pv.tok_id[t]) * row_bytes;
+  for (int e = threadIdx.x; e < d; e += blockDim.x) x[static_cast<size_t>(t) * d + e] = dequant_elem(row, type, e);
+}
+
+void launch_embed(const PlanView &pv, const uint8_t *emb, int type, size_t row_bytes, int d, float *x,
+                  cudaStream_t s) {
+  embed_kernel<<<pv.T, 256, 0, s>>>(pv, emb, type, row_bytes, d, x);
+}
+
+// ----------------------------------------------------------------------------------------------------------------
+// RMSNorm: out[r, :] = f16(x[src(r), :] * rsqrt(mean(x^2) + eps) * gain); columns d .. ld-1 are zeroed.
+// The sum of squares has a fixed order (per-thread strided partials, then a fixed tree), independent of the batch.
+__global__ void rmsnorm_kernel(const float *x, const int *rows, const float *gain, float eps, int d, int ld,
+                               __half *out) {
+  int r = blockIdx.x;
+  int src = rows ? rows[r] : r;
+  const float *xr = x + static_cast<size_t>(src) * d;
+  float ss = 0.f;
+  for (int e = threadIdx.x; e < d; e += blockDim.x) ss = fmaf(xr[e], xr[e], ss);
+  ss = warp_sum(ss);
+  __shared__ float part[32];
+  int w = threadIdx.x / 32, l = threadIdx.x % 32;
+  if (l == 0) part[w] = ss;
+  __syncthreads();
+  if (w == 0) {
+    float v = l < blockDim.x / 32 ? part[l] : 0.f;
+    v = warp_sum(v);
+    if (l == 0) part[0] = v;
+  }
+  __syncthreads();
+  float inv = rsqrtf(part[0] / static_cast<float>(d) + eps);
+  __half *o = out + static_cast<size_t>(r) * ld;
+  for (int e = threadIdx.x; e < ld; e += blockDim.x) o[e] = __float2half_rn(e < d ? xr[e] * inv * gain[e] : 0.f);
+}
+
+void launch_rmsnorm(const float *x, const int *rows, int n, const float *gain, float eps, int d, int ld, __half *out,
+                    cudaStream_t s) {
+  if (n > 0) rmsnorm_kernel<<<n, 256, 0, s>>>(x, rows, gain, eps, d, ld, out);
+}
+
+// ----------------------------------------------------------------------------------------------------------------
+// RoPE and KV write. qkv [T, (H + 2 KVH) * dh] f32 -> q [T, H, dh] f16 (rotated); K (rotated) and V -> the layer's
+// pages. fp8 page mode: a page's exponent e (scale 2^e) is set by the row that is its first (row % 16 == 0) from that
+// row's amax (the largest e with amax * 2^e <= 64, clamped to [-8, 15]); later rows of the page use it, also within
+// the same step (a token recomputes its page's first row from this step's qkv).
+__device__ int page_exp(float amax) {
+  if (!(amax > 0.f) || !isfinite(amax)) return 0;
+  int k;
+  float m = frexpf(amax, &k);
+  int e = 6 - k + (m == 0.5f ? 1 : 0);
+  return min(max(e, -8), 15);
+}
+
+__device__ void rope_pair(const float *src, const float2 *cs, int i, float &a, float &b) {
+  float x0 = src[2 * i], x1 = src[2 * i + 1];
+  float2 c = cs[i];
+  a = x0 * c.x - x1 * c.y;
+  b = x0 * c.y + x1 * c.x;
+}
+
+template <int DH>
+__device__ float head_amax(const float *src, const float2 *cs, bool rot) {
+  float m = 0.f;
+  for (int i = threadIdx.x % 32; i < DH / 2; i += 32) {
+    float a, b;
+    if (rot) rope_pair(src, cs, i, a, b);
+    else { a = src[2 * i]; b = src[2 * i + 1]; }
+    m = fmaxf(m, fmaxf(fabsf(a), fabsf(b)));
+  }
+  return warp_max(m);
+}
+
+template <int DH>
+__global__ void rope_kv_kernel(PlanView pv, const float *qkv, int H, int KVH, const float2 *rope_tab, __half *q,
+                               void *kc, void *vc, int8_t *exps, int kv_fp8, int page_scale) {
+  int t = blockIdx.x;
+  int hh = threadIdx.x / 32 + blockIdx.y * (blockDim.x / 32);  // head slot: [0, H) q heads, [H, H + KVH) kv heads
+  if (hh >= H + KVH) return;
+  int lane = threadIdx.x % 32;
+  const int W = (H + 2 * KVH) * DH;
+  const float *row = qkv + static_cast<size_t>(t) * W;
+  const float2 *cs = rope_tab + static_cast<size_t>(pv.rope_pos[t]) * (DH / 2);
+  if (hh < H) {
+    const float *src = row + hh * DH;
+    __half2 *dst = reinterpret_cast<__half2 *>(q + (static_cast<size_t>(t) * H + hh) * DH);
+    for (int i = lane; i < DH / 2; i += 32) {
+      float a, b;
+      rope_pair(src, cs, i, a, b);
+      dst[i] = __floats2half2_rn(a, b);
+    }
+    return;
+  }
+  int h = hh - H;
+  const float *ks = row + H * DH + h * DH;
+  const float *vs = row + (H + KVH) * DH + h * DH;
+  int r = pv.kv_row[t];
+  int blk = r / kBlock, rip = r % kBlock;
+  size_t off = ((static_cast<size_t>(blk) * KVH + h) * kBlock + rip) * DH;
+  if (!kv_fp8) {
+    __half2 *kd = reinterpret_cast<__half2 *>(static_cast<__half *>(kc) + off);
+    __half2 *vd = reinterpret_cast<__half2 *>(static_cast<__half *>(vc) + off);
+    for (int i = lane; i < DH / 2; i += 32) {
+      float a, b;
+      rope_pair(ks, cs, i, a, b);
+      kd[i] = __floats2half2_rn(a, b);
+      vd[i] = __floats2half2_rn(vs[2 * i], vs[2 * i + 1]);
+    }
+    return;
+  }
+  int ek = 0, ev = 0;
+  if (page_scale) {
+    int ft = pv.first_tok[t];
+    int8_t *pe = exps + (static_cast<size_t>(blk) * KVH + h) * 2;
+    if (ft >= 0) {
+      // the page's first row is written in this step (possibly by this token): derive its exponents
+      const float *frow = qkv + static_cast<size_t>(ft) * W;
+      const float2 *fcs = rope_tab + static_cast<size_t>(pv.rope_pos[ft]) * (DH / 2);
+      ek = page_exp(head_amax<DH>(frow + H * DH + h * DH, fcs, true));
+      ev = page_exp(head_amax<DH>(frow + (H + KVH) * DH + h * DH, fcs, false));
+      if (ft == t && lane == 0) { pe[0] = static_cast<int8_t>(ek); pe[1] = static_cast<int8_t>(ev); }
+    } else {
+      ek = pe[0];
+      ev = pe[1];
+    }
+  }
+  float sk = exp2f(static_cast<float>(ek)), sv = exp2f(static_cast<float>(ev));
+  uint8_t *kd = static_cast<uint8_t *>(kc) + off;
+  uint8_t *vd = static_cast<uint8_t *>(vc) + off;
+  for (int i = lane; i < DH / 2; i += 32) {
+    float a, b;
+    rope_pair(ks, cs, i, a, b);
+    kd[2 * i] = f32_to_e4m3(a * sk);
+    kd[2 * i + 1] = f32_to_e4m3(b * sk);
+    vd[2 * i] = f32_to_e4m3(vs[2 * i] * sv);
+    vd[2 * i + 1] = f32_to_e4m3(vs[2 * i + 1] * sv);
+  }
+}
+
+void launch_rope_kv(const PlanView &pv, const float *qkv, int H, int KVH, int dh, const float2 *rope_tab, __half *q,
+                    void *kc, void *vc, int8_t *exps, int kv_fp8, int page_scale, cudaStream_t s) {
+  int heads = H + KVH, per = 8;
+  dim3 grid(pv.T, (heads + per - 1) / per);
+  if (dh == 128)
+    rope_kv_kernel<128><<<grid, per * 32, 0, s>>>(pv, qkv, H, KVH, rope_tab, q, kc, vc, exps, kv_fp8, page_scale);
+  else
+    rope_kv_kernel<64><<<grid, per * 32, 0, s>>>(pv, qkv, H, KVH, rope_tab, q, kc, vc, exps, kv_fp8, page_scale);
+}
+
+// ----------------------------------------------------------------------------------------------------------------
+// Split-K reduction: v = sum_{s=0..S-1} part[s, t, n] in that order, then the epilogue.
+__device__ __forceinline__ float silu(float g) { return g / (1.f + expf(-g)); }
+
+__global__ void splitk_reduce_kernel(const float *part, int S, int T, int Npad, Epi epi) {
+  size_t total = static_cast<size_t>(T) * (epi.kind == kEpiSwiGLU ? Npad / 2 : Npad);
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    if (epi.kind == kEpiSwiGLU) {
+      int half = Npad / 2;
+      int t = static_cast<int>(i / half), f = static_cast<int>(i % half);
+      int tile = f / 64, w = f % 64;
+      int ng = tile * 128 + w, nu = ng + 64;
+      float g = 0.f, u = 0.f;
+      for (int s = 0; s < S; s++) {
+        g += part[(static_cast<size_t>(s) * T + t) * Npad + ng];
+        u += part[(static_cast<size_t>(s) * T + t) * Npad + nu];
+      }
+      if (f < epi.n) epi.out_h[static_cast<size_t>(t) * epi.ld + f] = __float2half_rn(silu(g) * u);
+    } else {
+      int t = static_cast<int>(i / Npad), n = static_cast<int>(i % Npad);
+      if (n >= epi.n) continue;
+      float v = 0.f;
+      for (int s = 0; s < S; s++) v += part[(static_cast<size_t>(s) * T + t) * Npad + n];
+      float *o = epi.out_f + static_cast<size_t>(t) * epi.ld + n;
+      if (epi.kind == kEpiAdd) *o += v;
+      else *o = v;
+    }
+  }
+}
+
+void launch_splitk_reduce(const float *part, int S, int T, int Npad, const Epi &epi, cudaStream_t s) {
+  size_t total = static_cast<size_t>(T) * Npad;
+  int blocks = static_cast<int>((total + 255) / 256);
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  splitk_reduce_kernel<<<blocks, 256, 0, s>>>(part, S, T, Npad, epi);
+}
+
+// ----------------------------------------------------------------------------------------------------------------
+// argmax per row, first index of the maximum (torch.argmax); NaN never wins.
+__global__ void argmax_kernel(const float *logits, int V, int *out) {
+  int r = blockIdx.x;
+  const float *row = logits + static_cast<size_t>(r) * V;
+  float best = -INFINITY;
+  int idx = 0x7fffffff;
+  for (int v = threadIdx.x; v < V; v += blockDim.x) {
+    float x = row[v];
+    if (x > best) { best = x; idx = v; }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    float b2 = __shfl_xor_sync(0xffffffffu, best, o);
+    int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (b2 > best || (b2 == best && i2 < idx)) { best = b2; idx = i2; }
+  }
+  __shared__ float sb[32];
+  __shared__ int si[32];
+  int w = threadIdx.x / 32, l = threadIdx.x % 32;
+  if (l == 0) { sb[w] = best; si[w] = idx; }
+  __syncthreads();
+  if (w == 0) {
+    best = l < blockDim.x / 32 ? sb[l] : -INFINITY;
+    idx = l < blockDim.x / 32 ? si[l] : 0x7fffffff;
+    for (int o = 16; o > 0; o >>= 1) {
+      float b2 = __shfl_xor_sync(0xffffffffu, best, o);
+      int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
+      if (b2 > best || (b2 == best && i2 < idx)) { best = b2; idx = i2; }
+    }
+    if (l == 0) out[r] = idx == 0x7fffffff ? 0 : idx;
+  }
+}
+
+void launch_argmax(const float *logits, int R, int V, int *out, cudaStream_t s) {
+  if (R > 0) argmax_kernel<<<R, 1024, 0, s>>>(logits, V, out);
+}
+
+// ----------------------------------------------------------------------------------------------------------------
+// gc_copy_blocks: page src -> dst for every layer, K and V, and the fp8 page exponents. pairs: [n][2] (src, dst).
+__global__ void copy_blocks_kernel(const int *pairs, size_t page_bytes, size_t layer_bytes, uint8_t *kc, uint8_t *vc,
+                                   int8_t *exps, size_t exps_layer, int exps_per_block) {
+  int p = blockIdx.x, l = blockIdx.y;
+  int src = pairs[2 * p], dst = pairs[2 * p + 1];
+  const uint4 *ks = reinterpret_cast<const uint4 *>(kc + l * layer_bytes + src * page_bytes);
+  uint4 *kd = reinterpret_cast<uint4 *>(kc + l * layer_bytes + dst * page_bytes);
+  const uint4 *vs = reinterpret_cast<const uint4 *>(vc + l * layer_bytes + src * page_bytes);
+  uint4 *vd = reinterpret_cast<uint4 *>(vc + l * layer_bytes + dst * page_bytes);
+  for (size_t i = threadIdx.x; i < page_bytes / 16; i += blockDim.x) { kd[i] = ks[i]; vd[i] = vs[i]; }
+  if (exps && threadIdx.x < exps_per_block)
+    exps[l * exps_layer + static_cast<size_t>(dst) * exps_per_block + threadIdx.x] =
+        exps[l * exps_layer + static_cast<size_t>(src) * exps_per_block + threadIdx.x];
+}
+
+void launch_copy_blocks(const int *pairs, int n, int L, size_t page_bytes, size_t layer_bytes, uint8_t *kc,
+                        uint8_t *vc, int8_t *exps, size_t exps_layer, int exps_per_block, cudaStream_t s) {
+  if (n > 0) copy_blocks_kernel<<<dim3(n, L), 256, 0, s>>>(pairs, page_bytes, layer_bytes, kc, vc, exps, exps_layer,
+                                                            exps_per_block);
+}
+
+// ----------------------------------------------------------------------------------------------------------------
+// gc_commit: moves[m] = (src row, dst row). Phase 1 copies every source row (all layers, heads, K and V) to tmp as
+// decoded f32; phase 2 sets the exponents of pages whose first row is a destination (fp8 page mode); phase 3 writes
+// every destination. Reading all sources first makes overlapping moves (a destination that is another move's source)
+// behave like the reference's in-order loop, since destinations never lie after their own source.
+template <typename KV>
+__device__ float kv_load(const KV *p, size_t i, float inv);
+template <>
+__device__ float kv_load<__half>(const __half *p, size_t i, float) { return __half2float(p[i]); }
+template <>
+__device__ float kv_load<uint8_t>(const uint8_t *p, size_t i, float inv) { return e4m3_to_f32(p[i]) * inv; }
+
+__global__ void commit_gather_kernel(const int *moves, int L, int KVH, int dh, const uint8_t *kc, const uint8_t *vc,
+                                     const int8_t *exps, int kv_fp8, size_t layer_bytes, size_t exps_layer,
+                                     float *tmp) {
+  int m = blockIdx.x, l = blockIdx.y;
+  int src = moves[2 * m];
+  int blk = src / kBlock, rip = src % kBlock;
+  for (int i = threadIdx.x; i < KVH * dh; i += blockDim.x) {
+    int h = i / dh, e = i % dh;
+    size_t off = ((static_cast<size_t>(blk) * KVH + h) * kBlock + rip) * dh + e;
+    float kv, vv;
+    if (kv_fp8) {
+      float ik = 1.f, iv = 1.f;
+      if (exps) {
+        const int8_t *pe = exps + l * exps_layer + (static_cast<size_t>(blk) * KVH + h) * 2;
+        ik = exp2f(-static_cast<float>(pe[0]));
+        iv = exp2f(-static_cast<float>(pe[1]));
+      }
+      kv = kv_load<uint8_t>(kc + l * layer_bytes, off, ik);
+      vv = kv_load<uint8_t>(vc + l * layer_bytes, off, iv);
+    } else {
+      kv = kv_load<__half>(reinterpret_cast<const __half *>(kc + l * layer_bytes), off, 1.f);
+      vv = kv_load<__half>(reinterpret_cast<const __half *>(vc + l * layer_bytes), off, 1.f);
+    }
+    float *o = tmp + ((static_cast<size_t>(m) * L + l) * 2) * KVH * dh;
+    o[i] = kv;
+    o[KVH * dh + i] = vv;
+  }
+}
+
+__global__ void commit_exps_kernel(const int *moves, int L, int KVH, int dh, int8_t *exps, size_t exps_layer,
+                                   const float *tmp) {
+  int m = blockIdx.x, l = blockIdx.y;
+  int dst = moves[2 * m + 1];
+  if (dst % kBlock) return;
+  int blk = dst / kBlock;
+  int h = threadIdx.x / 32;
+  if (h >= KVH) return;
+  const float *o = tmp + ((static_cast<size_t>(m) * L + l) * 2) * KVH * dh;
+  float ak = 0.f, av = 0.f;
+  for (int e = threadIdx.x % 32; e < dh; e += 32) {
+    ak = fmaxf(ak, fabsf(o[h * dh + e]));
+    av = fmaxf(av, fabsf(o[KVH * dh + h * dh + e]));
+  }
+  ak = warp_max(ak);
+  av = warp_max(av);
+  if (threadIdx.x % 32 == 0) {
+    int8_t *pe = exps + l * exps_layer + (static_cast<size_t>(blk) * KVH + h) * 2;
+    pe[0] = static_cast<int8_t>(page_exp(ak));
+    pe[1] = static_cast<int8_t>(page_exp(av));
+  }
+}
+
+__global__ void commit_scatter_kernel(const int *moves, int L, int KVH, int dh, uint8_t *kc, uint8_t *vc,
+                                      const int8_t *exps, int kv_fp8, size_t layer_bytes, size_t exps_layer,
+                                      const float *tmp) {
+  int m = blockIdx.x, l = blockIdx.y;
+  int dst = moves[2 * m + 1];
+  int blk = dst / kBlock, rip = dst % kBlock;
+  const float *o = tmp + ((static_cast<size_t>(m) * L + l) * 2) * KVH * dh;
+  for (int i = threadIdx.x; i < KVH * dh; i += blockDim.x) {
+    int h = i / dh, e = i % dh;
+    size_t off = ((static_cast<size_t>(blk) * KVH + h) * kBlock + rip) * dh + e;
+    if (kv_fp8) {
+      float sk = 1.f, sv = 1.f;
+      if (exps) {
+        const int8_t *pe = exps + l * exps_layer + (static_cast<size_t>(blk) * KVH + h) * 2;
+        sk = exp2f(static_cast<float>(pe[0]));
+        sv = exp2f(static_cast<float>(pe[1]));
+      }
+      kc[l * layer_bytes + off] = f32_to_e4m3(o[i] * sk);
+      vc[l * layer_bytes + off] = f32_to_e4m3(o[KVH * dh + i] * sv);
+    } else {
+      reinterpret_cast<__half *>(kc + l * layer_bytes)[off] = __float2half_rn(o[i]);
+      reinterpret_cast<__half *>(vc + l * layer_bytes)[off] = __float2half_rn(o[KVH * dh + i]);
+    }
+  }
+}
+
+void launch_commit(const int *moves, int n, int L, int KVH, int dh, uint8_t *kc, uint8_t *vc, int8_t *exps,
+                   int kv_fp8, size_t layer_bytes, size_t exps_layer, float *tmp, cudaStream_t s) {
+  if (n <= 0) return;
+  dim3 g(n, L);
+  commit_gather_kernel<<<g, 256, 0, s>>>(moves, L, KVH, dh, kc, vc, exps, kv_fp8, layer_bytes, exps_layer, tmp);
+  if (kv_fp8 && exps) commit_exps_kernel<<<g, 32 * KVH, 0, s>>>(moves, L, KVH, dh, exps, exps_layer, tmp);
+  commit_scatter_kernel<<<g, 256, 0, s>>>(moves, L, KVH, dh, kc, vc, exps, kv_fp8, layer_bytes, exps_layer, tmp);
+}
+
+}  // namespace gck

@@ -1,0 +1,75 @@
+// Launch wrappers of the decoder-step kernels (host-callable; all run on the caller's stream).
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "plan.h"
+
+namespace gck {
+
+enum WType { kF32 = 0, kF16 = 1, kQ8_0 = 8, kQ4_K = 12 };  // GGUF type ids
+
+// GEMM tiles: a weight matrix [N, K] is stored as tiles of kBM rows x kBK columns, tile (nt, kt) at
+// (nt * KT + kt) * tile_bytes. Inside a tile, scales/headers come first, then the quants (see weights.cpp).
+constexpr int kBM = 128;
+constexpr int kBK = 256;
+constexpr int kBN = 64;   // tokens per CTA tile
+
+__host__ __device__ inline size_t tile_bytes(int type) {
+  switch (type) {
+    case kQ4_K: return static_cast<size_t>(kBM) * 144;               // 128 x (16 B header + 128 B quants)
+    case kQ8_0: return static_cast<size_t>(kBM) * (8 * 2 + 256);     // 128 x (8 fp16 scales + 256 int8)
+    default: return static_cast<size_t>(kBM) * kBK * 2;              // f16
+  }
+}
+
+enum EpiKind { kEpiStore = 0, kEpiAdd = 1, kEpiSwiGLU = 2 };
+struct Epi {
+  int kind;
+  int n;          // real output columns (features); SwiGLU: real FFN width
+  int ld;         // leading dimension of the output
+  float *out_f;   // Store / Add: f32 [T, ld]
+  __half *out_h;  // SwiGLU: f16 [T, ld]
+};
+
+struct QWeight {            // a relaid-out weight on the device
+  const uint8_t *data = nullptr;
+  int type = 0;
+  int N = 0, K = 0;         // logical rows (outputs) and columns (inputs)
+  int NT = 0, KT = 0;       // tiles
+  int splits = 1;           // split-K factor (fixed per weight: batch invariant)
+};
+
+void launch_embed(const PlanView &pv, const uint8_t *emb, int type, size_t row_bytes, int d, float *x, cudaStream_t s);
+void launch_rmsnorm(const float *x, const int *rows, int n, const float *gain, float eps, int d, int ld, __half *out,
+                    cudaStream_t s);
+void launch_rope_kv(const PlanView &pv, const float *qkv, int H, int KVH, int dh, const float2 *rope_tab, __half *q,
+                    void *kc, void *vc, int8_t *exps, int kv_fp8, int page_scale, cudaStream_t s);
+void launch_splitk_reduce(const float *part, int S, int T, int Npad, const Epi &epi, cudaStream_t s);
+void launch_argmax(const float *logits, int R, int V, int *out, cudaStream_t s);
+void launch_copy_blocks(const int *pairs, int n, int L, size_t page_bytes, size_t layer_bytes, uint8_t *kc,
+                        uint8_t *vc, int8_t *exps, size_t exps_layer, int exps_per_block, cudaStream_t s);
+void launch_commit(const int *moves, int n, int L, int KVH, int dh, uint8_t *kc, uint8_t *vc, int8_t *exps,
+                   int kv_fp8, size_t layer_bytes, size_t exps_layer, float *tmp, cudaStream_t s);
+
+// y = act[T, Kpad] (f16, row-major, Kpad = KT * kBK) times W^T, with the epilogue; part: split-K scratch
+// [splits, T, NT * kBM] f32 (unused when splits == 1).
+void gemm_init();   // once per device, before the first launch_gemm
+void launch_gemm(const QWeight &w, const __half *act, int T, const Epi &epi, float *part, cudaStream_t s);
+
+// Paged attention over the plan's work list: q [T, H, dh] f16 -> out [T, H, dh] f16. part_o / part_ml: split partials.
+struct AttnArgs {
+  const __half *q;
+  const void *kc, *vc;       // this layer's pages [nblk][KVH][16][dh]
+  const int8_t *exps;        // this layer's page exponents [nblk][KVH][2] (fp8 page mode) or null
+  __half *out;
+  float *part_o;             // [n_parts, 16, dh]
+  float2 *part_ml;           // [n_parts, 16] (running max in log2 units, sum)
+  int H, KVH, dh, kv_fp8;
+  float scale_log2;          // log2(e) / sqrt(dh)
+};
+void launch_attention(const PlanView &pv, const AttnArgs &a, int nw, cudaStream_t s);
+
+}  // namespace gck

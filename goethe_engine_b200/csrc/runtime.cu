@@ -1,0 +1,963 @@
+// libgck: the gc.h C ABI (runtime kind gc-c) over the sm_100a decoder-step kernels.
+//
+// The boundary follows the reference's abi/gc.h and its mock runtime (tests/mock/gck_mock.c:28-194): size-prefixed
+// structs read and written up to min(caller size, own size); negative GC_E_* codes with a per-handle error text; a
+// thread-local gc_open error; block ids checked against the pool (GC_E_ARG); an unknown sid in gc_release accepted.
+// What happens inside a step follows goethe_engine/ref.py (RefModel.token, TorchBackend.step/commit/copy_blocks).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <fstream>
+#include <memory>
+#include <sstream>
+#include <string>
+#include <thread>
+#include <unordered_map>
+#include <vector>
+
+#include "gc.h"
+#include "hostio.h"
+#include "kernels.h"
+
+using namespace gck;
+
+namespace {
+
+thread_local std::string g_open_err;
+
+struct GcError {
+  int code;
+  std::string msg;
+};
+
+[[noreturn]] void fail(int code, const char *fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  throw GcError{code, buf};
+}
+
+void ck(cudaError_t e, const char *what) {
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    if (e == cudaErrorMemoryAllocation) fail(GC_E_DEVICE, "%s: out of memory", what);
+    fail(GC_E_DEVICE, "%s: CUDA error %s", what, cudaGetErrorString(e));
+  }
+}
+
+struct Layer {
+  QWeight qkv, o, gu, dn;
+  const float *attn_norm = nullptr, *ffn_norm = nullptr;
+};
+
+struct Slot {
+  uint64_t sid = 0;
+  bool used = false;
+  std::vector<uint32_t> blocks;   // the table of the sequence's last step (gc_commit addresses rows through it)
+  uint32_t last_pos = 0, last_n = 0;
+};
+
+template <typename T>
+size_t vbytes(const std::vector<T> &v) { return v.size() * sizeof(T); }
+
+}  // namespace
+
+struct gc_handle {
+  int dev = 0;
+  cudaStream_t st = nullptr;
+  std::string err;
+  // model
+  int vocab = 0, d = 0, L = 0, H = 0, KVH = 0, dh = 0, F = 0;
+  float eps = 1e-5f, theta = 1e4f;
+  std::vector<Layer> layers;
+  const uint8_t *emb = nullptr;
+  int emb_type = 0;
+  size_t emb_row_bytes = 0;
+  QWeight head;
+  const float *out_norm = nullptr;
+  float2 *rope = nullptr;
+  // KV
+  int kv_fp8 = 0, page_scale = 0, nblk = 0;
+  uint8_t *kc = nullptr, *vc = nullptr;
+  int8_t *exps = nullptr;
+  size_t page_bytes = 0, layer_bytes = 0, exps_layer = 0;
+  // limits
+  int max_seqs = 0, max_cols = 0, max_ctx = 0, qg_tokens = 1;
+  // scratch
+  float *x = nullptr, *qkv = nullptr, *logits = nullptr, *part = nullptr, *attn_o = nullptr, *commit_tmp = nullptr;
+  __half *h = nullptr, *q = nullptr, *att = nullptr, *act = nullptr;
+  float2 *attn_ml = nullptr;
+  int *argmax = nullptr, *pairs = nullptr;
+  size_t part_cap = 0, attn_parts_cap = 0, commit_cap = 0, pairs_cap = 0;
+  uint8_t *plan_dev = nullptr, *plan_host = nullptr;
+  size_t plan_cap = 0;
+  int *tok_host = nullptr;
+  std::vector<Slot> slots;
+  std::vector<void *> allocs;
+  size_t device_bytes = 0;
+
+  void *dalloc(size_t n, const char *what) {
+    void *p = nullptr;
+    ck(cudaMalloc(&p, n ? n : 16), what);
+    allocs.push_back(p);
+    device_bytes += n;
+    return p;
+  }
+  void dfree(void *p, size_t n) {
+    if (!p) return;
+    cudaFree(p);
+    allocs.erase(std::remove(allocs.begin(), allocs.end(), p), allocs.end());
+    device_bytes -= n;
+  }
+  ~gc_handle() {
+    if (st) cudaStreamSynchronize(st);
+    for (void *p : allocs) cudaFree(p);
+    if (plan_host) cudaFreeHost(plan_host);
+    if (tok_host) cudaFreeHost(tok_host);
+    if (st) cudaStreamDestroy(st);
+  }
+};
+
+namespace {
+
+// -------------------------------------------------------------------------------------------- weights and relayout
+const GgufTensor &tensor(const std::vector<std::unique_ptr<GgufFile>> &files, const std::string &name) {
+  for (auto &f : files) {
+    auto it = f->tensors.find(name);
+    if (it != f->tensors.end()) return it->second;
+  }
+  fail(GC_E_WEIGHTS, "tensor %s not found in the weight files", name.c_str());
+}
+
+long long meta_int(const std::vector<std::unique_ptr<GgufFile>> &files, const std::string &k, long long dflt) {
+  for (auto &f : files) {
+    auto it = f->meta.find(k);
+    if (it != f->meta.end()) return it->second.i;
+  }
+  return dflt;
+}
+double meta_f(const std::vector<std::unique_ptr<GgufFile>> &files, const std::string &k, double dflt) {
+  for (auto &f : files) {
+    auto it = f->meta.find(k);
+    if (it != f->meta.end()) return it->second.f;
+  }
+  return dflt;
+}
+
+struct RowSrc {               // one source matrix of a (possibly concatenated / interleaved) weight
+  const GgufTensor *t;
+  int rows, cols;
+};
+
+// f32 -> f16 on the host (round to nearest even), for F32 checkpoints relaid to the F16 tile format
+uint16_t h_f32_to_f16(float f) {
+  __half h = __float2half_rn(f);
+  return *reinterpret_cast<uint16_t *>(&h);
+}
+
+// Build the tiled layout of a weight whose logical row n maps to (source, source row) by `rowmap`, on the host, and
+// upload it. Tile (nt, kt) of kBM x kBK: Q4_K = 128 x 16 B headers then 128 x 128 B quants; Q8_0 = 128 x 8 fp16
+// scales then 128 x 256 int8; F16 = 128 x 256 halves. Rows past N and columns past K are zero (weights of 0).
+template <typename RowMap>
+QWeight relayout(gc_handle *h, int type, int N, int K, RowMap rowmap, const char *what) {
+  QWeight w;
+  w.type = type == kF32 ? kF16 : type;
+  w.N = N;
+  w.K = K;
+  w.NT = (N + kBM - 1) / kBM;
+  w.KT = (K + kBK - 1) / kBK;
+  size_t tb = tile_bytes(w.type);
+  size_t total = tb * w.NT * w.KT;
+  std::vector<uint8_t> host(total, 0);
+  auto work = [&](int nt0, int nt1) {
+    for (int nt = nt0; nt < nt1; nt++)
+      for (int r = 0; r < kBM; r++) {
+        int n = nt * kBM + r;
+        if (n >= N) break;
+        const GgufTensor *t = nullptr;
+        int sr = 0;
+        rowmap(n, t, sr);
+        if (!t) continue;   // a padding row: zeros
+        const uint8_t *row = t->data;
+        for (int kt = 0; kt < w.KT; kt++) {
+          uint8_t *tile = host.data() + (static_cast<size_t>(nt) * w.KT + kt) * tb;
+          if (type == kQ4_K) {
+            int nsb = K / 256;
+            if (kt >= nsb) continue;
+            const uint8_t *src = row + (static_cast<size_t>(sr) * nsb + kt) * 144;
+            std::memcpy(tile + r * 16, src, 16);
+            std::memcpy(tile + kBM * 16 + r * 128, src + 16, 128);
+          } else if (type == kQ8_0) {
+            int nb = K / 32;
+            for (int i = 0; i < 8; i++) {
+              int b = kt * 8 + i;
+              if (b >= nb) break;
+              const uint8_t *src = row + (static_cast<size_t>(sr) * nb + b) * 34;
+              std::memcpy(tile + (r * 8 + i) * 2, src, 2);
+              std::memcpy(tile + kBM * 16 + r * 256 + i * 32, src + 2, 32);
+            }
+          } else {
+            uint16_t *dst = reinterpret_cast<uint16_t *>(tile) + r * kBK;
+            for (int c = 0; c < kBK; c++) {
+              int k = kt * kBK + c;
+              if (k >= K) break;
+              if (type == kF16) dst[c] = reinterpret_cast<const uint16_t *>(row)[static_cast<size_t>(sr) * K + k];
+              else dst[c] = h_f32_to_f16(reinterpret_cast<const float *>(row)[static_cast<size_t>(sr) * K + k]);
+            }
+          }
+        }
+      }
+  };
+  int nth = std::max(1, std::min(32, static_cast<int>(std::thread::hardware_concurrency())));
+  std::vector<std::thread> th;
+  int per = (w.NT + nth - 1) / nth;
+  for (int i = 0; i < nth; i++) {
+    int a = i * per, b = std::min(w.NT, a + per);
+    if (a < b) th.emplace_back(work, a, b);
+  }
+  for (auto &x : th) x.join();
+  uint8_t *dev = static_cast<uint8_t *>(h->dalloc(total, what));
+  ck(cudaMemcpy(dev, host.data(), total, cudaMemcpyHostToDevice), what);
+  w.data = dev;
+  // split-K: the fewest K slices (a divisor of KT, at most 8) that give at least one CTA per SM
+  w.splits = 1;
+  for (int s = 1; s <= std::min(8, w.KT); s++) {
+    if (w.KT % s) continue;
+    w.splits = s;
+    if (w.NT * s >= 148) break;
+  }
+  return w;
+}
+
+void check_type(const GgufTensor &t, int K) {
+  if (t.type != kF32 && t.type != kF16 && t.type != kQ8_0 && t.type != kQ4_K)
+    fail(GC_E_WEIGHTS, "tensor %s: ggml type %u is not supported (F32, F16, Q8_0, Q4_K)", t.name.c_str(), t.type);
+  if ((t.type == kQ4_K && K % 256) || (t.type == kQ8_0 && K % 32))
+    fail(GC_E_WEIGHTS, "tensor %s: row length %d does not fit its blocks", t.name.c_str(), K);
+  if (t.dims.size() < 2 || static_cast<int>(t.dims[0]) != K)
+    fail(GC_E_WEIGHTS, "tensor %s: row length %llu, expected %d", t.name.c_str(),
+         static_cast<unsigned long long>(t.dims.empty() ? 0 : t.dims[0]), K);
+}
+
+const float *upload_f32(gc_handle *h, const GgufTensor &t, int n, const char *what) {
+  std::vector<float> v(n);
+  for (int i = 0; i < n; i++) {
+    if (t.type == kF32) v[i] = reinterpret_cast<const float *>(t.data)[i];
+    else if (t.type == kF16) v[i] = __half2float(reinterpret_cast<const __half *>(t.data)[i]);
+    else fail(GC_E_WEIGHTS, "tensor %s: norm weights must be F32 or F16", t.name.c_str());
+  }
+  float *p = static_cast<float *>(h->dalloc(n * 4, what));
+  ck(cudaMemcpy(p, v.data(), n * 4, cudaMemcpyHostToDevice), what);
+  return p;
+}
+
+void load_model(gc_handle *h, const std::vector<std::unique_ptr<GgufFile>> &files) {
+  std::string arch;
+  for (auto &f : files) {
+    auto it = f->meta.find("general.architecture");
+    if (it != f->meta.end()) arch = it->second.s;
+  }
+  if (arch != "llama") fail(GC_E_WEIGHTS, "architecture '%s': this library runs llama-architecture GGUF", arch.c_str());
+  h->L = static_cast<int>(meta_int(files, "llama.block_count", 0));
+  h->d = static_cast<int>(meta_int(files, "llama.embedding_length", 0));
+  h->F = static_cast<int>(meta_int(files, "llama.feed_forward_length", 0));
+  h->H = static_cast<int>(meta_int(files, "llama.attention.head_count", 0));
+  h->KVH = static_cast<int>(meta_int(files, "llama.attention.head_count_kv", h->H));
+  h->eps = static_cast<float>(meta_f(files, "llama.attention.layer_norm_rms_epsilon", 1e-5));
+  h->theta = static_cast<float>(meta_f(files, "llama.rope.freq_base", 1e4));
+  if (h->L <= 0 || h->d <= 0 || h->H <= 0 || h->KVH <= 0 || h->F <= 0 || h->H % h->KVH)
+    fail(GC_E_WEIGHTS, "llama metadata incomplete or inconsistent");
+  h->dh = h->d / h->H;
+  int G = h->H / h->KVH;
+  if (h->dh != 64 && h->dh != 128) fail(GC_E_UNSUPPORTED, "head dim %d: this library runs 64 and 128", h->dh);
+  if (16 % G) fail(GC_E_UNSUPPORTED, "GQA group %d: must divide 16", G);
+  if (h->d % kBK || (h->H * h->dh) % kBK)
+    fail(GC_E_UNSUPPORTED, "model width %d: must be a multiple of %d", h->d, kBK);
+  h->qg_tokens = 16 / G;
+  const GgufTensor &emb = tensor(files, "token_embd.weight");
+  if (emb.dims.size() < 2 || static_cast<int>(emb.dims[0]) != h->d) fail(GC_E_WEIGHTS, "token_embd.weight shape");
+  h->vocab = static_cast<int>(emb.dims[1]);
+  check_type(emb, h->d);
+  h->emb_type = static_cast<int>(emb.type);
+  h->emb_row_bytes = emb.bytes / h->vocab;
+  uint8_t *e = static_cast<uint8_t *>(h->dalloc(emb.bytes, "token_embd"));
+  ck(cudaMemcpy(e, emb.data, emb.bytes, cudaMemcpyHostToDevice), "token_embd");
+  h->emb = e;
+  const int dq = h->H * h->dh, dkv = h->KVH * h->dh;
+  for (int l = 0; l < h->L; l++) {
+    std::string b = "blk." + std::to_string(l) + ".";
+    Layer ly;
+    const GgufTensor &tq = tensor(files, b + "attn_q.weight"), &tk = tensor(files, b + "attn_k.weight"),
+                     &tv = tensor(files, b + "attn_v.weight"), &to = tensor(files, b + "attn_output.weight"),
+                     &tg = tensor(files, b + "ffn_gate.weight"), &tu = tensor(files, b + "ffn_up.weight"),
+                     &td = tensor(files, b + "ffn_down.weight");
+    for (auto *t : {&tq, &tk, &tv, &tg, &tu}) check_type(*t, h->d);
+    check_type(to, dq);
+    check_type(td, h->F);
+    if (tq.type != tk.type || tq.type != tv.type || tg.type != tu.type)
+      fail(GC_E_WEIGHTS, "layer %d: q/k/v (and gate/up) must share one type", l);
+    ly.qkv = relayout(h, static_cast<int>(tq.type), dq + 2 * dkv, h->d, [&](int n, const GgufTensor *&t, int &r) {
+      if (n < dq) { t = &tq; r = n; }
+      else if (n < dq + dkv) { t = &tk; r = n - dq; }
+      else { t = &tv; r = n - dq - dkv; }
+    }, "attn_qkv");
+    ly.o = relayout(h, static_cast<int>(to.type), h->d, dq, [&](int n, const GgufTensor *&t, int &r) { t = &to; r = n; },
+                    "attn_output");
+    // gate/up interleaved in 64-row halves of each 128-row tile: the SwiGLU epilogue finds g and u in one tile
+    int Fp = (h->F + 63) / 64 * 64;
+    ly.gu = relayout(h, static_cast<int>(tg.type), 2 * Fp, h->d, [&](int n, const GgufTensor *&t, int &r) {
+      int tile = n / 128, w = n % 128;
+      int f = tile * 64 + (w % 64);
+      t = w < 64 ? &tg : &tu;
+      r = std::min(f, h->F - 1);
+      if (f >= h->F) t = nullptr;
+    }, "ffn_gate_up");
+    ly.gu.N = 2 * Fp;
+    ly.dn = relayout(h, static_cast<int>(td.type), h->d, h->F, [&](int n, const GgufTensor *&t, int &r) { t = &td; r = n; },
+                     "ffn_down");
+    ly.attn_norm = upload_f32(h, tensor(files, b + "attn_norm.weight"), h->d, "attn_norm");
+    ly.ffn_norm = upload_f32(h, tensor(files, b + "ffn_norm.weight"), h->d, "ffn_norm");
+    h->layers.push_back(ly);
+  }
+  h->out_norm = upload_f32(h, tensor(files, "output_norm.weight"), h->d, "output_norm");
+  const GgufTensor &th = tensor(files, "output.weight");
+  check_type(th, h->d);
+  h->head = relayout(h, static_cast<int>(th.type), h->vocab, h->d,
+                     [&](int n, const GgufTensor *&t, int &r) { t = &th; r = n; }, "output");
+}
+
+}  // namespace
+
+namespace {
+
+void build_rope(gc_handle *h) {
+  // ref.py:31: inv = theta ** (-arange(0, dh, 2) / dh) in float32; angle = inv * p in float32
+  int half = h->dh / 2;
+  std::vector<float2> tab(static_cast<size_t>(h->max_ctx) * half);
+  std::vector<float> inv(half);
+  for (int i = 0; i < half; i++)
+    inv[i] = std::pow(h->theta, -(static_cast<float>(2 * i) / static_cast<float>(h->dh)));
+  for (int p = 0; p < h->max_ctx; p++)
+    for (int i = 0; i < half; i++) {
+      float a = inv[i] * static_cast<float>(p);
+      tab[static_cast<size_t>(p) * half + i] = make_float2(static_cast<float>(std::cos(static_cast<double>(a))),
+                                                           static_cast<float>(std::sin(static_cast<double>(a))));
+    }
+  h->rope = static_cast<float2 *>(h->dalloc(vbytes(tab), "rope table"));
+  ck(cudaMemcpy(h->rope, tab.data(), vbytes(tab), cudaMemcpyHostToDevice), "rope table");
+}
+
+template <typename T>
+T *grow(gc_handle *h, T *p, size_t &cap, size_t need, const char *what) {
+  if (need <= cap) return p;
+  if (p) {
+    cudaStreamSynchronize(h->st);
+    h->dfree(p, cap);
+  }
+  size_t n = std::max(need, cap * 3 / 2);
+  p = static_cast<T *>(h->dalloc(n, what));
+  cap = n;
+  return p;
+}
+
+std::string read_file(const std::string &path) {
+  std::ifstream f(path, std::ios::binary);
+  if (!f) fail(GC_E_MANIFEST, "%s: cannot read", path.c_str());
+  std::stringstream ss;
+  ss << f.rdbuf();
+  return ss.str();
+}
+
+}  // namespace
+
+// ============================================================================================== exported ABI
+extern "C" {
+
+GC_API uint32_t gc_abi_version(void) { return GC_ABI_VERSION; }
+
+GC_API const char *gc_last_error(gc_handle *h) { return h ? h->err.c_str() : g_open_err.c_str(); }
+
+GC_API int gc_open(const gc_open_params *p, gc_handle **out) {
+  if (out) *out = nullptr;
+  gc_handle *h = nullptr;
+  try {
+    if (!p || !out) fail(GC_E_ARG, "gc_open: null argument");
+    // fields read: up to n_buckets and pool_blocks; anything the caller's struct does not have reads as zero
+    gc_open_params P{};
+    std::memcpy(&P, p, std::min<size_t>(p->size, sizeof P));
+    if (p->size < offsetof(gc_open_params, pool_blocks) + sizeof(uint32_t)) fail(GC_E_ARG, "gc_open: struct size %u", p->size);
+    if (P.flags & GC_OPEN_SPEC) fail(GC_E_UNSUPPORTED, "speculative pairs (GC_OPEN_SPEC) are not supported by this library");
+    if (!P.pack_dir) fail(GC_E_ARG, "gc_open: no pack_dir");
+    if (!P.n_buckets || !P.buckets) fail(GC_E_ARG, "gc_open: no bucket ids");
+    // manifest: the requested buckets
+    Json m;
+    try {
+      std::string txt = read_file(std::string(P.pack_dir) + "/manifest.json");
+      m = JsonParser(txt).parse();
+    } catch (const std::runtime_error &e) {
+      fail(GC_E_MANIFEST, "manifest.json: %s", e.what());
+    }
+    const Json *bl = m.get("buckets");
+    if (!bl || bl->kind != Json::Arr) fail(GC_E_MANIFEST, "manifest.json has no buckets");
+    int ncol = 0, maxctx = 0, max_cols = 0, pool_tune = 0;
+    std::string kv, kv_scale;
+    for (uint32_t i = 0; i < P.n_buckets; i++) {
+      if (!P.buckets[i]) fail(GC_E_ARG, "gc_open: null bucket id");
+      const Json *b = nullptr;
+      for (auto &x : bl->arr)
+        if (x.str_or("id", "") == P.buckets[i]) b = &x;
+      if (!b) fail(GC_E_MANIFEST, "bucket %s is not in the manifest", P.buckets[i]);
+      ncol = std::max(ncol, static_cast<int>(b->num_or("ncol", 1)));
+      maxctx = std::max(maxctx, static_cast<int>(b->num_or("maxctx", 4096)));
+      std::string bkv = b->str_or("kv", "f16");
+      if (!kv.empty() && bkv != kv) fail(GC_E_MANIFEST, "buckets disagree on the KV dtype");
+      kv = bkv;
+      if (const Json *t = b->get("tune")) {
+        max_cols = std::max(max_cols, static_cast<int>(t->num_or("max_cols", 0)));
+        pool_tune = std::max(pool_tune, static_cast<int>(t->num_or("pool_blocks", 0)));
+        kv_scale = t->str_or("kv_scale", kv_scale);
+      }
+    }
+    if (kv != "f16" && kv != "fp8") fail(GC_E_MANIFEST, "kv dtype %s: f16 or fp8", kv.c_str());
+    // weights: the target's files (a NULL entry separates a drafter's, which a non-spec open has none of)
+    std::vector<std::unique_ptr<GgufFile>> files;
+    if (!P.weights || !P.n_weights) fail(GC_E_WEIGHTS, "no weight files");
+    for (uint32_t i = 0; i < P.n_weights; i++) {
+      if (!P.weights[i]) break;
+      try {
+        files.emplace_back(new GgufFile(P.weights[i]));
+      } catch (const std::runtime_error &e) {
+        fail(GC_E_WEIGHTS, "%s", e.what());
+      }
+    }
+    if (files.empty()) fail(GC_E_WEIGHTS, "no weight files");
+    // device
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+      cudaGetLastError();
+      fail(GC_E_DEVICE, "no CUDA device");
+    }
+    int dev = P.device;
+    if (dev < 0) ck(cudaGetDevice(&dev), "cudaGetDevice");
+    if (dev >= ndev) fail(GC_E_DEVICE, "device %d: no such device (%d present)", dev, ndev);
+    cudaDeviceProp prop;
+    ck(cudaGetDeviceProperties(&prop, dev), "cudaGetDeviceProperties");
+    if (prop.major != 10 || prop.minor != 0)
+      fail(GC_E_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a (B200)", dev, prop.major, prop.minor);
+    ck(cudaSetDevice(dev), "cudaSetDevice");
+    h = new gc_handle();
+    h->dev = dev;
+    ck(cudaStreamCreateWithFlags(&h->st, cudaStreamNonBlocking), "stream");
+    gemm_init();
+    load_model(h, files);
+    files.clear();
+    h->max_seqs = std::max(1, ncol);
+    h->max_ctx = std::max(kBlock, maxctx);
+    h->max_cols = max_cols > 0 ? max_cols : 2048;
+    h->kv_fp8 = kv == "fp8";
+    h->page_scale = h->kv_fp8 && kv_scale != "unit";
+    build_rope(h);
+    // KV pool: [L][nblk][KVH][16][dh] for K and for V, plus fp8 page exponents [L][nblk][KVH][2]
+    const size_t esz = h->kv_fp8 ? 1 : 2;
+    h->page_bytes = static_cast<size_t>(h->KVH) * kBlock * h->dh * esz;
+    size_t per_block = 2 * h->page_bytes * h->L + (h->kv_fp8 ? static_cast<size_t>(h->L) * h->KVH * 2 : 0);
+    size_t nblk = P.pool_blocks ? P.pool_blocks : pool_tune;
+    // scratch first, so that "what fits" is measured after it
+    const int T = h->max_cols, d = h->d;
+    const int wq = (h->H + 2 * h->KVH) * h->dh;
+    int Fpad = h->layers[0].dn.KT * kBK;
+    h->x = static_cast<float *>(h->dalloc(static_cast<size_t>(T) * d * 4, "x"));
+    h->h = static_cast<__half *>(h->dalloc(static_cast<size_t>(T) * d * 2, "h"));
+    h->qkv = static_cast<float *>(h->dalloc(static_cast<size_t>(T) * wq * 4, "qkv"));
+    h->q = static_cast<__half *>(h->dalloc(static_cast<size_t>(T) * h->H * h->dh * 2, "q"));
+    h->att = static_cast<__half *>(h->dalloc(static_cast<size_t>(T) * h->H * h->dh * 2, "att"));
+    h->act = static_cast<__half *>(h->dalloc(static_cast<size_t>(T) * Fpad * 2, "act"));
+    ck(cudaMemset(h->act, 0, static_cast<size_t>(T) * Fpad * 2), "act");
+    h->logits = static_cast<float *>(h->dalloc(static_cast<size_t>(T) * h->vocab * 4, "logits"));
+    h->argmax = static_cast<int *>(h->dalloc(static_cast<size_t>(T) * 4, "argmax"));
+    ck(cudaMallocHost(&h->tok_host, static_cast<size_t>(T) * 4), "pinned tokens");
+    if (!nblk) {
+      size_t fr = 0, tot = 0;
+      ck(cudaMemGetInfo(&fr, &tot), "cudaMemGetInfo");
+      size_t reserve = static_cast<size_t>(4) << 30;
+      nblk = fr > reserve ? (fr - reserve) / per_block : 0;
+      nblk = std::min<size_t>(nblk, static_cast<size_t>(h->max_seqs) * ((h->max_ctx + kBlock - 1) / kBlock) + 64);
+    }
+    if (nblk < 1 || nblk > (1u << 26)) fail(GC_E_DEVICE, "KV pool of %zu blocks: out of memory", nblk);
+    h->nblk = static_cast<int>(nblk);
+    h->layer_bytes = h->page_bytes * nblk;
+    h->kc = static_cast<uint8_t *>(h->dalloc(h->layer_bytes * h->L, "KV pool K"));
+    h->vc = static_cast<uint8_t *>(h->dalloc(h->layer_bytes * h->L, "KV pool V"));
+    ck(cudaMemset(h->kc, 0, h->layer_bytes * h->L), "KV pool");
+    ck(cudaMemset(h->vc, 0, h->layer_bytes * h->L), "KV pool");
+    if (h->kv_fp8) {
+      h->exps_layer = nblk * h->KVH * 2;
+      h->exps = static_cast<int8_t *>(h->dalloc(h->exps_layer * h->L, "KV page exponents"));
+      ck(cudaMemset(h->exps, 0, h->exps_layer * h->L), "KV page exponents");
+    }
+    h->slots.resize(h->max_seqs);
+    ck(cudaStreamSynchronize(h->st), "open");
+    *out = h;
+    return GC_OK;
+  } catch (const GcError &e) {
+    g_open_err = e.msg;
+    delete h;
+    return e.code;
+  } catch (const std::exception &e) {
+    g_open_err = e.what();
+    delete h;
+    return GC_E_DEVICE;
+  }
+}
+
+GC_API int gc_layout_get(gc_handle *h, gc_layout *o) {
+  if (!h || !o || o->size < 8) return GC_E_ARG;
+  gc_layout l{};
+  l.size = sizeof l;
+  l.flags = GC_L_PAGED | GC_L_DEVICE_ARGMAX;
+  l.vocab = h->vocab;
+  l.max_cols = h->max_cols;
+  l.max_seqs = h->max_seqs;
+  l.max_ctx = h->max_ctx;
+  l.block_size = kBlock;
+  l.num_blocks = h->nblk;
+  l.layers = h->L;
+  l.kv_heads = h->KVH;
+  l.head_dim = h->dh;
+  l.kv_dtype = h->kv_fp8 ? GC_KV_FP8 : GC_KV_F16;
+  l.kv_bytes = 2 * h->layer_bytes * h->L + h->exps_layer * h->L;
+  l.device_bytes = h->device_bytes;
+  uint32_t n = std::min<uint32_t>(o->size, sizeof l);
+  std::memcpy(o, &l, n);
+  o->size = n;
+  return GC_OK;
+}
+
+}  // extern "C"
+
+// ============================================================================================== the step
+namespace {
+
+struct HostPlan {
+  std::vector<int> tok_id, rope_pos, kv_row, first_tok, want_tok, paths;
+  std::vector<Item> items;
+  std::vector<QGroup> qgroups;
+  std::vector<AttnWork> work;
+  std::vector<unsigned> blocks;
+  int n_parts = 0, nw = 1;
+};
+
+struct WorkIn {
+  uint32_t flags;
+  uint64_t sid;
+  uint32_t pos, n;
+  const int32_t *tokens, *parents;
+  const uint32_t *blocks;
+  uint32_t nblocks, want;
+};
+
+void build_plan(gc_handle *h, const std::vector<WorkIn> &ws, HostPlan &pl) {
+  const int G = h->H / h->KVH, QG = h->qg_tokens;
+  int T = 0;
+  bool multi = false;
+  for (auto &w : ws) {
+    Item it{};
+    it.pos = static_cast<int>(w.pos);
+    it.ntok = static_cast<int>(w.n);
+    it.tok0 = T;
+    it.blk_off = static_cast<int>(pl.blocks.size());
+    it.nblk = static_cast<int>(w.nblocks);
+    it.tree = w.parents != nullptr;
+    it.path_off = static_cast<int>(pl.paths.size());
+    pl.blocks.insert(pl.blocks.end(), w.blocks, w.blocks + w.nblocks);
+    std::vector<int> depth(w.n), poff(w.n), plen(w.n);
+    for (uint32_t j = 0; j < w.n; j++) {
+      int par = w.parents ? w.parents[j] : static_cast<int>(j) - 1;
+      depth[j] = w.parents ? (par < 0 ? 0 : depth[par] + 1) : static_cast<int>(j);
+      if (w.parents) {
+        std::vector<int> p;
+        for (int a = static_cast<int>(j); a >= 0; a = w.parents[a]) p.push_back(a);
+        std::reverse(p.begin(), p.end());
+        poff[j] = static_cast<int>(pl.paths.size());
+        plen[j] = static_cast<int>(p.size());
+        pl.paths.insert(pl.paths.end(), p.begin(), p.end());
+      }
+      int row = static_cast<int>(w.pos + j);
+      pl.tok_id.push_back(w.tokens[j]);
+      pl.rope_pos.push_back(static_cast<int>(w.pos) + depth[j]);
+      pl.kv_row.push_back(static_cast<int>(w.blocks[row / kBlock]) * kBlock + row % kBlock);
+      int p0 = row - row % kBlock;
+      pl.first_tok.push_back(p0 >= static_cast<int>(w.pos) ? T + (p0 - static_cast<int>(w.pos)) : -1);
+      if (j + w.want >= w.n) pl.want_tok.push_back(T + static_cast<int>(j));
+    }
+    int item = static_cast<int>(pl.items.size());
+    pl.items.push_back(it);
+    // query groups, then the attention work over kv heads and splits
+    int qfirst = static_cast<int>(pl.qgroups.size());
+    if (w.parents) {
+      for (uint32_t j = 0; j < w.n; j++) {
+        QGroup q{};
+        q.item = item; q.j0 = static_cast<int>(j); q.ntok = 1;
+        q.nvis = static_cast<int>(w.pos) + plen[j];
+        q.path_off = poff[j]; q.path_len = plen[j];
+        pl.qgroups.push_back(q);
+      }
+    } else {
+      for (uint32_t j = 0; j < w.n; j += QG) {
+        QGroup q{};
+        q.item = item; q.j0 = static_cast<int>(j); q.ntok = static_cast<int>(std::min<uint32_t>(QG, w.n - j));
+        q.nvis = static_cast<int>(w.pos + j) + q.ntok;
+        pl.qgroups.push_back(q);
+      }
+      if (pl.qgroups.size() - qfirst > 1) multi = true;
+    }
+    for (size_t k = qfirst; k < pl.qgroups.size(); k++) {
+      QGroup &q = pl.qgroups[k];
+      q.nsplit = (q.nvis + kSplit - 1) / kSplit;
+      q.part_base = pl.n_parts;
+      pl.n_parts += h->KVH * q.nsplit;
+    }
+    T += static_cast<int>(w.n);
+  }
+  (void)G;
+  pl.nw = multi ? 4 : 1;
+  // work: per item, kv head, split: chain groups of the item packed nw to a CTA, tree groups one to a CTA
+  for (size_t i = 0; i < pl.items.size(); i++) {
+    int q0 = -1, q1 = -1;
+    for (size_t k = 0; k < pl.qgroups.size(); k++)
+      if (pl.qgroups[k].item == static_cast<int>(i)) {
+        if (q0 < 0) q0 = static_cast<int>(k);
+        q1 = static_cast<int>(k) + 1;
+      }
+    int maxs = 0;
+    for (int k = q0; k < q1; k++) maxs = std::max(maxs, pl.qgroups[k].nsplit);
+    for (int head = 0; head < h->KVH; head++)
+      for (int s = 0; s < maxs; s++) {
+        if (pl.items[i].tree) {
+          for (int k = q0; k < q1; k++)
+            if (s < pl.qgroups[k].nsplit) pl.work.push_back(AttnWork{k, 1, head, s});
+        } else {
+          int k = q0;
+          while (k < q1 && pl.qgroups[k].nsplit <= s) k++;
+          while (k < q1) {
+            int n = std::min(pl.nw, q1 - k);
+            pl.work.push_back(AttnWork{k, n, head, s});
+            k += n;
+          }
+        }
+      }
+  }
+}
+
+// pack the plan into the pinned buffer and upload it; returns the device view
+PlanView upload_plan(gc_handle *h, HostPlan &pl) {
+  std::vector<std::pair<const void *, size_t>> parts = {
+      {pl.tok_id.data(), vbytes(pl.tok_id)},   {pl.rope_pos.data(), vbytes(pl.rope_pos)},
+      {pl.kv_row.data(), vbytes(pl.kv_row)},   {pl.first_tok.data(), vbytes(pl.first_tok)},
+      {pl.items.data(), vbytes(pl.items)},     {pl.qgroups.data(), vbytes(pl.qgroups)},
+      {pl.work.data(), vbytes(pl.work)},       {pl.blocks.data(), vbytes(pl.blocks)},
+      {pl.paths.data(), vbytes(pl.paths)},     {pl.want_tok.data(), vbytes(pl.want_tok)}};
+  size_t total = 0;
+  std::vector<size_t> off;
+  for (auto &p : parts) {
+    off.push_back(total);
+    total += (p.second + 255) / 256 * 256;
+  }
+  if (total > h->plan_cap) {
+    cudaStreamSynchronize(h->st);
+    if (h->plan_host) cudaFreeHost(h->plan_host);
+    h->plan_host = nullptr;
+    size_t cap = std::max<size_t>(total * 2, 1 << 20);
+    if (h->plan_dev) h->dfree(h->plan_dev, h->plan_cap);
+    h->plan_dev = static_cast<uint8_t *>(h->dalloc(cap, "plan"));
+    ck(cudaMallocHost(&h->plan_host, cap), "pinned plan");
+    h->plan_cap = cap;
+  }
+  // the previous step's upload has finished: every step ends with a stream synchronize
+  for (size_t i = 0; i < parts.size(); i++)
+    if (parts[i].second) std::memcpy(h->plan_host + off[i], parts[i].first, parts[i].second);
+  ck(cudaMemcpyAsync(h->plan_dev, h->plan_host, total, cudaMemcpyHostToDevice, h->st), "plan upload");
+  PlanView pv;
+  uint8_t *b = h->plan_dev;
+  pv.tok_id = reinterpret_cast<const int *>(b + off[0]);
+  pv.rope_pos = reinterpret_cast<const int *>(b + off[1]);
+  pv.kv_row = reinterpret_cast<const int *>(b + off[2]);
+  pv.first_tok = reinterpret_cast<const int *>(b + off[3]);
+  pv.items = reinterpret_cast<const Item *>(b + off[4]);
+  pv.qgroups = reinterpret_cast<const QGroup *>(b + off[5]);
+  pv.work = reinterpret_cast<const AttnWork *>(b + off[6]);
+  pv.blocks = reinterpret_cast<const unsigned *>(b + off[7]);
+  pv.paths = reinterpret_cast<const int *>(b + off[8]);
+  pv.want_tok = reinterpret_cast<const int *>(b + off[9]);
+  pv.T = static_cast<int>(pl.tok_id.size());
+  pv.n_items = static_cast<int>(pl.items.size());
+  pv.n_qg = static_cast<int>(pl.qgroups.size());
+  pv.n_work = static_cast<int>(pl.work.size());
+  pv.R = static_cast<int>(pl.want_tok.size());
+  pv.n_parts = pl.n_parts;
+  return pv;
+}
+
+void forward(gc_handle *h, const PlanView &pv, int nw) {
+  const int T = pv.T;
+  cudaStream_t s = h->st;
+  // split-K and attention scratch for this step's sizes
+  size_t need = 0;
+  for (auto &ly : h->layers)
+    for (const QWeight *w : {&ly.qkv, &ly.o, &ly.gu, &ly.dn})
+      if (w->splits > 1) need = std::max(need, static_cast<size_t>(w->splits) * T * w->NT * kBM * 4);
+  if (h->head.splits > 1) need = std::max(need, static_cast<size_t>(h->head.splits) * pv.R * h->head.NT * kBM * 4);
+  h->part = grow(h, h->part, h->part_cap, need, "split-K scratch");
+  if (static_cast<size_t>(pv.n_parts) > h->attn_parts_cap) {
+    cudaStreamSynchronize(s);
+    if (h->attn_o) h->dfree(h->attn_o, h->attn_parts_cap * 16 * h->dh * 4);
+    if (h->attn_ml) h->dfree(h->attn_ml, h->attn_parts_cap * 16 * 8);
+    size_t cap = std::max<size_t>(pv.n_parts, h->attn_parts_cap * 3 / 2);
+    h->attn_o = static_cast<float *>(h->dalloc(cap * 16 * h->dh * 4, "attention partials"));
+    h->attn_ml = static_cast<float2 *>(h->dalloc(cap * 16 * 8, "attention partials"));
+    h->attn_parts_cap = cap;
+  }
+
+  launch_embed(pv, h->emb, h->emb_type, h->emb_row_bytes, h->d, h->x, s);
+  const int wq = (h->H + 2 * h->KVH) * h->dh;
+  AttnArgs aa{};
+  aa.q = h->q;
+  aa.out = h->att;
+  aa.part_o = h->attn_o;
+  aa.part_ml = h->attn_ml;
+  aa.H = h->H;
+  aa.KVH = h->KVH;
+  aa.dh = h->dh;
+  aa.kv_fp8 = h->kv_fp8;
+  aa.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(h->dh)));
+  for (int l = 0; l < h->L; l++) {
+    const Layer &ly = h->layers[l];
+    launch_rmsnorm(h->x, nullptr, T, ly.attn_norm, h->eps, h->d, h->d, h->h, s);
+    launch_gemm(ly.qkv, h->h, T, Epi{kEpiStore, wq, wq, h->qkv, nullptr}, h->part, s);
+    uint8_t *kc = h->kc + l * h->layer_bytes, *vc = h->vc + l * h->layer_bytes;
+    int8_t *ex = h->exps ? h->exps + l * h->exps_layer : nullptr;
+    launch_rope_kv(pv, h->qkv, h->H, h->KVH, h->dh, h->rope, h->q, kc, vc, ex, h->kv_fp8, h->page_scale, s);
+    aa.kc = kc;
+    aa.vc = vc;
+    aa.exps = h->page_scale ? ex : nullptr;
+    launch_attention(pv, aa, nw, s);
+    launch_gemm(ly.o, h->att, T, Epi{kEpiAdd, h->d, h->d, h->x, nullptr}, h->part, s);
+    launch_rmsnorm(h->x, nullptr, T, ly.ffn_norm, h->eps, h->d, h->d, h->h, s);
+    launch_gemm(ly.gu, h->h, T, Epi{kEpiSwiGLU, h->F, ly.dn.KT * kBK, nullptr, h->act}, h->part, s);
+    launch_gemm(ly.dn, h->act, T, Epi{kEpiAdd, h->d, h->d, h->x, nullptr}, h->part, s);
+  }
+  if (pv.R > 0) {
+    launch_rmsnorm(h->x, pv.want_tok, pv.R, h->out_norm, h->eps, h->d, h->d, h->h, s);
+    launch_gemm(h->head, h->h, pv.R, Epi{kEpiStore, h->vocab, h->vocab, h->logits, nullptr}, h->part, s);
+  }
+}
+
+Slot *find_slot(gc_handle *h, uint64_t sid, bool make) {
+  Slot *fr = nullptr;
+  for (auto &s : h->slots) {
+    if (s.used && s.sid == sid) return &s;
+    if (!s.used && !fr) fr = &s;
+  }
+  if (make && fr) {
+    fr->used = true;
+    fr->sid = sid;
+    return fr;
+  }
+  return nullptr;
+}
+
+}  // namespace
+
+extern "C" {
+
+GC_API int gc_step(gc_handle *h, const gc_step_in *in, gc_step_out *o) {
+  if (!h) return GC_E_ARG;
+  try {
+    if (!in || !o || in->size < offsetof(gc_step_in, n_work) + 4 || o->size < offsetof(gc_step_out, counts) + 8)
+      fail(GC_E_ARG, "gc_step: null argument or struct size");
+    if (!in->n_work || !in->work) fail(GC_E_ARG, "gc_step: no work items");
+    if (in->n_work > static_cast<uint32_t>(h->max_seqs))
+      fail(GC_E_ARG, "gc_step: %u items, the bucket runs %d sequences", in->n_work, h->max_seqs);
+    std::vector<WorkIn> ws;
+    bool greedy = true;
+    uint64_t T = 0, R = 0;
+    for (uint32_t i = 0; i < in->n_work; i++) {
+      const gc_work *w = in->work[i];
+      if (!w) fail(GC_E_ARG, "work item %u is null", i);
+      gc_work W{};
+      std::memcpy(&W, w, std::min<size_t>(w->size, sizeof W));
+      if (w->size < offsetof(gc_work, want) + 4) fail(GC_E_ARG, "work item %u: struct size %u", i, w->size);
+      if (!W.n_tokens || !W.tokens || W.want > W.n_tokens) fail(GC_E_ARG, "work item %u: bad token count or want", i);
+      if (W.flags & GC_W_SPEC) fail(GC_E_UNSUPPORTED, "work item %u: speculative rounds need a spec pair", i);
+      if (W.flags & GC_W_FEATS) fail(GC_E_UNSUPPORTED, "work item %u: this pack has no tap features", i);
+      if (!W.blocks || static_cast<uint64_t>(W.n_blocks) * kBlock < static_cast<uint64_t>(W.pos) + W.n_tokens)
+        fail(GC_E_ARG, "work item %u: block table does not cover rows 0 .. %u", i, W.pos + W.n_tokens - 1);
+      if (static_cast<uint64_t>(W.pos) + W.n_tokens > static_cast<uint64_t>(h->max_ctx))
+        fail(GC_E_ARG, "work item %u: position %u past the context %d", i, W.pos + W.n_tokens, h->max_ctx);
+      uint32_t used_blocks = (W.pos + W.n_tokens + kBlock - 1) / kBlock;
+      for (uint32_t b = 0; b < W.n_blocks; b++)
+        if (W.blocks[b] >= static_cast<uint32_t>(h->nblk))
+          fail(GC_E_ARG, "work item %u: block %u out of pool (%d blocks)", i, W.blocks[b], h->nblk);
+      (void)used_blocks;
+      for (uint32_t j = 0; j < W.n_tokens; j++) {
+        if (W.tokens[j] < 0 || W.tokens[j] >= h->vocab) fail(GC_E_ARG, "work item %u: token %d outside the vocabulary", i, W.tokens[j]);
+        if (W.parents && (W.parents[j] < -1 || W.parents[j] >= static_cast<int32_t>(j)))
+          fail(GC_E_ARG, "work item %u: parent of token %u must be -1 or an earlier token", i, j);
+      }
+      for (auto &p : ws)
+        if (p.sid == W.sid) fail(GC_E_ARG, "sequence %llu appears twice in one step", static_cast<unsigned long long>(W.sid));
+      greedy = greedy && (W.flags & GC_W_GREEDY);
+      T += W.n_tokens;
+      R += W.want;
+      ws.push_back(WorkIn{W.flags, W.sid, W.pos, W.n_tokens, W.tokens, W.parents, W.blocks, W.n_blocks, W.want});
+    }
+    if (T > static_cast<uint64_t>(h->max_cols)) fail(GC_E_ARG, "gc_step: %llu tokens, at most %d", static_cast<unsigned long long>(T), h->max_cols);
+    gc_step_out O{};
+    std::memcpy(&O, o, std::min<size_t>(o->size, sizeof O));
+    o->n_rows = static_cast<uint32_t>(R);
+    if (greedy) {
+      if (O.tokens_cap < R || (R && !O.tokens) || !O.counts) fail(GC_E_CAPACITY, "tokens buffer too small (%llu rows)", static_cast<unsigned long long>(R));
+    } else if (in->flags & GC_S_HOST_LOGITS) {
+      if (O.logits_cap < R * static_cast<uint64_t>(h->vocab) || (R && !O.logits))
+        fail(GC_E_CAPACITY, "logits buffer too small (%llu rows of %d)", static_cast<unsigned long long>(R), h->vocab);
+    }
+    // sequence slots
+    for (auto &w : ws)
+      if (!find_slot(h, w.sid, true)) fail(GC_E_STATE, "no free sequence slot (%d in use)", h->max_seqs);
+    for (auto &w : ws) {
+      Slot *sl = find_slot(h, w.sid, false);
+      sl->blocks.assign(w.blocks, w.blocks + w.nblocks);
+      sl->last_pos = w.pos;
+      sl->last_n = w.n;
+    }
+    ck(cudaSetDevice(h->dev), "cudaSetDevice");
+    HostPlan pl;
+    build_plan(h, ws, pl);
+    PlanView pv = upload_plan(h, pl);
+    forward(h, pv, pl.nw);
+    if (greedy) {
+      if (R) {
+        launch_argmax(h->logits, static_cast<int>(R), h->vocab, h->argmax, h->st);
+        ck(cudaMemcpyAsync(h->tok_host, h->argmax, R * 4, cudaMemcpyDeviceToHost, h->st), "tokens");
+      }
+      ck(cudaStreamSynchronize(h->st), "step");
+      std::memcpy(O.tokens, h->tok_host, R * 4);
+      for (uint32_t i = 0; i < in->n_work; i++) O.counts[i] = ws[i].want;
+    } else if (in->flags & GC_S_HOST_LOGITS) {
+      if (R) ck(cudaMemcpyAsync(O.logits, h->logits, R * h->vocab * 4, cudaMemcpyDeviceToHost, h->st), "logits");
+      ck(cudaStreamSynchronize(h->st), "step");
+    } else {
+      ck(cudaStreamSynchronize(h->st), "step");
+      if (o->size >= offsetof(gc_step_out, logits_dev) + 8) o->logits_dev = reinterpret_cast<uint64_t>(h->logits);
+    }
+    ck(cudaGetLastError(), "step");
+    return GC_OK;
+  } catch (const GcError &e) {
+    h->err = e.msg;
+    return e.code;
+  }
+}
+
+GC_API int gc_commit(gc_handle *h, uint64_t sid, uint32_t base, const uint32_t *path, uint32_t n) {
+  if (!h) return GC_E_ARG;
+  try {
+    Slot *sl = find_slot(h, sid, false);
+    if (!sl) fail(GC_E_STATE, "gc_commit: unknown sequence %llu", static_cast<unsigned long long>(sid));
+    if (n && !path) fail(GC_E_ARG, "gc_commit: null path");
+    std::vector<int> moves;
+    uint64_t rows = static_cast<uint64_t>(sl->blocks.size()) * kBlock;
+    for (uint32_t j = 0; j < n; j++) {
+      if (path[j] < j || (j && path[j] <= path[j - 1])) fail(GC_E_ARG, "gc_commit: path must increase and path[j] >= j");
+      if (static_cast<uint64_t>(base) + path[j] >= rows) fail(GC_E_ARG, "gc_commit: row %u outside the table", base + path[j]);
+      if (path[j] == j) continue;
+      uint32_t a = base + path[j], b = base + j;
+      moves.push_back(static_cast<int>(sl->blocks[a / kBlock] * kBlock + a % kBlock));
+      moves.push_back(static_cast<int>(sl->blocks[b / kBlock] * kBlock + b % kBlock));
+    }
+    if (moves.empty()) return GC_OK;
+    ck(cudaSetDevice(h->dev), "cudaSetDevice");
+    int nm = static_cast<int>(moves.size() / 2);
+    h->pairs = grow(h, h->pairs, h->pairs_cap, vbytes(moves), "commit moves");
+    h->commit_tmp = grow(h, h->commit_tmp, h->commit_cap, static_cast<size_t>(nm) * h->L * 2 * h->KVH * h->dh * 4, "commit rows");
+    ck(cudaMemcpyAsync(h->pairs, moves.data(), vbytes(moves), cudaMemcpyHostToDevice, h->st), "commit moves");
+    launch_commit(h->pairs, nm, h->L, h->KVH, h->dh, h->kc, h->vc, h->page_scale ? h->exps : nullptr, h->kv_fp8,
+                  h->layer_bytes, h->exps_layer, h->commit_tmp, h->st);
+    ck(cudaStreamSynchronize(h->st), "commit");
+    ck(cudaGetLastError(), "commit");
+    return GC_OK;
+  } catch (const GcError &e) {
+    h->err = e.msg;
+    return e.code;
+  }
+}
+
+GC_API int gc_copy_blocks(gc_handle *h, const uint32_t *src, const uint32_t *dst, uint32_t n) {
+  if (!h) return GC_E_ARG;
+  try {
+    if (n && (!src || !dst)) fail(GC_E_ARG, "gc_copy_blocks: null array");
+    std::vector<int> pairs;
+    for (uint32_t i = 0; i < n; i++) {
+      if (src[i] >= static_cast<uint32_t>(h->nblk) || dst[i] >= static_cast<uint32_t>(h->nblk))
+        fail(GC_E_ARG, "gc_copy_blocks: block out of pool (%u -> %u, %d blocks)", src[i], dst[i], h->nblk);
+      pairs.push_back(static_cast<int>(src[i]));
+      pairs.push_back(static_cast<int>(dst[i]));
+    }
+    if (!n) return GC_OK;
+    ck(cudaSetDevice(h->dev), "cudaSetDevice");
+    h->pairs = grow(h, h->pairs, h->pairs_cap, vbytes(pairs), "copy pairs");
+    ck(cudaMemcpyAsync(h->pairs, pairs.data(), vbytes(pairs), cudaMemcpyHostToDevice, h->st), "copy pairs");
+    // pairs run in order; a batch runs in one launch while no destination is read or written again in it
+    size_t i = 0;
+    while (i < n) {
+      size_t j = i;
+      std::vector<uint32_t> touched;
+      while (j < n) {
+        bool clash = false;
+        for (uint32_t x : touched)
+          if (x == src[j] || x == dst[j]) clash = true;
+        if (clash) break;
+        touched.push_back(dst[j]);
+        j++;
+      }
+      launch_copy_blocks(h->pairs + 2 * i, static_cast<int>(j - i), h->L, h->page_bytes, h->layer_bytes, h->kc, h->vc,
+                         h->exps, h->exps_layer, h->KVH * 2, h->st);
+      i = j;
+    }
+    ck(cudaStreamSynchronize(h->st), "copy_blocks");
+    ck(cudaGetLastError(), "copy_blocks");
+    return GC_OK;
+  } catch (const GcError &e) {
+    h->err = e.msg;
+    return e.code;
+  }
+}
+
+GC_API int gc_state_save(gc_handle *h, uint64_t, uint32_t) {
+  if (h) h->err = "gc_state_save: this pack has no bounded state (GC_L_BOUNDED)";
+  return GC_E_ARG;
+}
+
+GC_API int gc_state_restore(gc_handle *h, uint32_t, uint64_t) {
+  if (h) h->err = "gc_state_restore: this pack has no bounded state (GC_L_BOUNDED)";
+  return GC_E_ARG;
+}
+
+GC_API int gc_release(gc_handle *h, uint64_t sid) {
+  if (!h) return GC_E_ARG;
+  Slot *sl = find_slot(h, sid, false);
+  if (sl) *sl = Slot{};
+  return GC_OK;
+}
+
+GC_API void gc_close(gc_handle *h) {
+  if (!h) return;
+  cudaSetDevice(h->dev);
+  delete h;
+}
+
+}  // extern "C"

@@ -1,0 +1,192 @@
+"""Host-side binding of libgck.so through its C ABI (ctypes), mirroring the engine's own backend interface.
+
+The reference engine binds a pack runtime with ``goethe_engine/gc_c.py`` (``bind`` at gc_c.py:58-77, the struct
+mirrors at gc_c.py:27-55, ``GcBackend.step/commit/copy_blocks/release`` at gc_c.py:262-316). This module is this
+project's own binding of the same ABI so that tests, the benchmark and users without the engine can drive the
+library the way the engine does: ``Backend.step(work)`` takes ``Work`` items (``goethe_engine/backend.py:19-29``) and
+returns per-item token lists (device argmax, all items greedy) or float32 logits ``[sum(want), vocab]``.
+
+Nothing here computes: every step runs in libgck.so on the GPU. A missing library or a machine without the device
+fails loudly (``GcError``); there is no fallback.
+"""
+import ctypes as C
+import os
+from dataclasses import dataclass
+
+import numpy as np
+
+ABI_MAJOR, ABI_MINOR = 1, 2
+OK, E_ARG, E_MANIFEST, E_WEIGHTS, E_DEVICE, E_UNSUPPORTED, E_STATE, E_CAPACITY = 0, -1, -2, -3, -4, -5, -6, -7
+W_GREEDY, W_SPEC, W_FEATS = 1, 2, 4
+S_HOST_LOGITS = 1
+L_PAGED, L_DEVICE_ARGMAX = 1, 2
+KV_DTYPE = {0: "f16", 1: "fp8"}
+P_ = C.POINTER
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libgck.so")
+# every symbol include/gc.h declares
+SYMBOLS = ("gc_abi_version", "gc_open", "gc_layout_get", "gc_step", "gc_commit", "gc_copy_blocks", "gc_state_save",
+           "gc_state_restore", "gc_release", "gc_last_error", "gc_close")
+
+
+class GcError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__(f"gc call failed ({code}): {msg}")
+        self.code = code
+
+
+class OpenParams(C.Structure):
+    _fields_ = [("size", C.c_uint32), ("flags", C.c_uint32), ("pack_dir", C.c_char_p), ("weights", P_(C.c_char_p)),
+                ("n_weights", C.c_uint32), ("device", C.c_int32), ("buckets", P_(C.c_char_p)),
+                ("n_buckets", C.c_uint32), ("pool_blocks", C.c_uint32), ("spec_policy", C.c_char_p),
+                ("scratch_dir", C.c_char_p), ("state_pages", C.c_uint32)]
+
+
+class Layout(C.Structure):
+    _fields_ = [("size", C.c_uint32)] + [(k, C.c_uint32) for k in (
+        "flags", "vocab", "max_cols", "max_seqs", "max_ctx", "block_size", "num_blocks", "layers", "kv_heads",
+        "head_dim", "kv_dtype", "spec_width", "feat_width")] + [(k, C.c_uint64) for k in (
+        "kv_bytes", "state_bytes", "device_bytes")] + [(k, C.c_uint32) for k in (
+        "state_pages", "pad1", "embd_dim", "embd_pool", "enc_frames", "enc_feat")]
+
+
+class WorkS(C.Structure):
+    _fields_ = [("size", C.c_uint32), ("flags", C.c_uint32), ("sid", C.c_uint64), ("pos", C.c_uint32),
+                ("n_tokens", C.c_uint32), ("tokens", P_(C.c_int32)), ("parents", P_(C.c_int32)),
+                ("blocks", P_(C.c_uint32)), ("n_blocks", C.c_uint32), ("want", C.c_uint32)]
+
+
+class StepIn(C.Structure):
+    _fields_ = [("size", C.c_uint32), ("flags", C.c_uint32), ("work", P_(P_(WorkS))), ("n_work", C.c_uint32),
+                ("pad", C.c_uint32)]
+
+
+class StepOut(C.Structure):
+    _fields_ = [("size", C.c_uint32), ("n_rows", C.c_uint32), ("tokens", P_(C.c_int32)), ("tokens_cap", C.c_uint32),
+                ("pad0", C.c_uint32), ("counts", P_(C.c_uint32)), ("logits", C.c_void_p), ("logits_cap", C.c_uint64),
+                ("logits_dev", C.c_uint64), ("feats", C.c_void_p), ("feats_cap", C.c_uint64)]
+
+
+@dataclass
+class Work:
+    """One sequence's tokens for a step (goethe_engine/backend.py:19-29)."""
+    sid: int
+    tokens: list
+    pos: int
+    blocks: list
+    want: int
+    greedy: bool = False
+    spec: bool = False
+    parents: list = None
+    feats: bool = False
+
+
+def load(path=LIB_PATH):
+    """The library with its gc.h signatures; refuses a different ABI major or an older minor."""
+    if not os.path.exists(path):
+        raise GcError(E_DEVICE, f"{path} is not built (python -m goethe_engine_b200.build)")
+    L = C.CDLL(path)
+    sig = dict(gc_abi_version=(C.c_uint32, []), gc_open=(C.c_int, [P_(OpenParams), P_(C.c_void_p)]),
+               gc_layout_get=(C.c_int, [C.c_void_p, P_(Layout)]),
+               gc_step=(C.c_int, [C.c_void_p, P_(StepIn), P_(StepOut)]),
+               gc_commit=(C.c_int, [C.c_void_p, C.c_uint64, C.c_uint32, P_(C.c_uint32), C.c_uint32]),
+               gc_copy_blocks=(C.c_int, [C.c_void_p, P_(C.c_uint32), P_(C.c_uint32), C.c_uint32]),
+               gc_state_save=(C.c_int, [C.c_void_p, C.c_uint64, C.c_uint32]),
+               gc_state_restore=(C.c_int, [C.c_void_p, C.c_uint32, C.c_uint64]),
+               gc_release=(C.c_int, [C.c_void_p, C.c_uint64]), gc_last_error=(C.c_char_p, [C.c_void_p]),
+               gc_close=(None, [C.c_void_p]))
+    for n, (res, args) in sig.items():
+        f = getattr(L, n)
+        f.restype, f.argtypes = res, args
+    v = L.gc_abi_version()
+    if v >> 16 != ABI_MAJOR or (v & 0xFFFF) < ABI_MINOR:
+        raise GcError(E_ARG, f"{path}: C ABI {v >> 16}.{v & 0xFFFF}, need {ABI_MAJOR}.{ABI_MINOR}+")
+    return L
+
+
+def arr(ctype, xs):
+    return (ctype * len(xs))(*xs)
+
+
+class Backend:
+    """One gc_open handle: the engine-facing step / commit / copy_blocks / release of gc_c.GcBackend."""
+
+    def __init__(self, pack_dir, weights, buckets=("b200.BI.main",), pool_blocks=0, device=-1, lib=None):
+        self.L = lib or load()
+        self.h = None
+        ws = [weights] if isinstance(weights, str) else list(weights)
+        keep = [arr(C.c_char_p, [os.fsencode(w) for w in ws]), arr(C.c_char_p, [b.encode() for b in buckets])]
+        p = OpenParams(C.sizeof(OpenParams), 2, os.fsencode(pack_dir), keep[0], len(ws), device, keep[1], len(buckets),
+                       pool_blocks, None, None, 0)
+        h = C.c_void_p()
+        rc = self.L.gc_open(C.byref(p), C.byref(h))
+        if rc:
+            raise GcError(rc, (self.L.gc_last_error(None) or b"").decode())
+        self.h = h.value
+        lo = Layout(size=C.sizeof(Layout))
+        self._ck(self.L.gc_layout_get(self.h, C.byref(lo)))
+        self.layout = lo
+        self.vocab_size, self.max_seqs, self.max_len = lo.vocab, lo.max_seqs, lo.max_ctx
+        self.block_size, self.num_blocks = lo.block_size, lo.num_blocks
+        self.kv_dtype = KV_DTYPE.get(lo.kv_dtype, "f16")
+        self.device_argmax = bool(lo.flags & L_DEVICE_ARGMAX)
+
+    def _ck(self, rc):
+        if rc < 0:
+            raise GcError(rc, (self.L.gc_last_error(self.h) or b"").decode())
+
+    def step(self, work, logits=None):
+        """Tokens per item (every item greedy) or float32 logits [sum(want), vocab] (into `logits` if given)."""
+        n = len(work)
+        greedy = self.device_argmax and all(w.greedy for w in work)
+        keep, ws = [], []
+        for w in work:
+            fl = (1 if greedy else 0) | (2 if w.spec else 0) | (4 if w.feats else 0)
+            toks = np.ascontiguousarray(w.tokens, np.int32)
+            blk = np.ascontiguousarray(w.blocks, np.uint32)
+            par = np.ascontiguousarray(w.parents, np.int32) if w.parents is not None else None
+            keep += [toks, blk, par]
+            ws.append(WorkS(C.sizeof(WorkS), fl, w.sid, w.pos, len(toks), toks.ctypes.data_as(P_(C.c_int32)),
+                            par.ctypes.data_as(P_(C.c_int32)) if par is not None else None,
+                            blk.ctypes.data_as(P_(C.c_uint32)), len(blk), w.want))
+        pw = arr(P_(WorkS), [C.pointer(x) for x in ws])
+        rows = sum(w.want for w in work)
+        out = StepOut(size=C.sizeof(StepOut))
+        counts = (C.c_uint32 * n)()
+        if greedy:
+            tok = (C.c_int32 * max(rows, 1))()
+            out.tokens, out.tokens_cap, out.counts = tok, rows, counts
+        else:
+            lg = logits if logits is not None else np.empty((rows, self.vocab_size), np.float32)
+            out.logits, out.logits_cap = lg.ctypes.data, lg.size
+        self._ck(self.L.gc_step(self.h, C.byref(StepIn(C.sizeof(StepIn), 0 if greedy else S_HOST_LOGITS, pw, n, 0)),
+                                C.byref(out)))
+        if greedy:
+            res, o = [], 0
+            for c in counts:
+                res.append(list(tok[o:o + c]))
+                o += c
+            return res
+        return lg[:out.n_rows]
+
+    def commit(self, sid, base, path):
+        self._ck(self.L.gc_commit(self.h, sid, base, arr(C.c_uint32, path), len(path)))
+
+    def copy_blocks(self, pairs):
+        self._ck(self.L.gc_copy_blocks(self.h, arr(C.c_uint32, [s for s, _ in pairs]),
+                                       arr(C.c_uint32, [d for _, d in pairs]), len(pairs)))
+
+    def release(self, sid):
+        self._ck(self.L.gc_release(self.h, sid))
+
+    def close(self):
+        if self.h:
+            self.L.gc_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    __del__ = close

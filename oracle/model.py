@@ -66,7 +66,8 @@ def page_scale_exp(row_amax):
     the largest e with amax * 2^e <= PAGE_TARGET, clamped to [-8, 15]. A stored value is code(x * 2^e)."""
     if not row_amax > 0 or not math.isfinite(row_amax):
         return 0
-    e = math.floor(math.log2(PAGE_TARGET / row_amax))
+    m, k = math.frexp(row_amax)            # amax = m * 2^k, m in [0.5, 1): exact, no log rounding
+    e = 6 - k + (1 if m == 0.5 else 0)     # PAGE_TARGET = 2^6
     return int(min(max(e, PAGE_EXP_MIN), PAGE_EXP_MAX))
 
 

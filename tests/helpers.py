@@ -1,0 +1,67 @@
+"""Shared test helpers: synthetic checkpoints, the scripted golden session, and the logits comparison rule."""
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(HERE, "golden"))
+from make_golden import SCENARIO  # noqa: E402,F401
+
+from goethe_engine_b200 import gck, synth  # noqa: E402
+from oracle.load import weights_from_gguf  # noqa: E402
+from oracle.model import PagedOracle  # noqa: E402
+
+SMALL = dict(vocab=512, d=256, layers=2, heads=4, kv_heads=2, ffn=512)      # dh 64, GQA 2
+SMALL128 = dict(vocab=512, d=512, layers=2, heads=4, kv_heads=1, ffn=768)   # dh 128, GQA 4
+# a16 with f16 KV: the north-star tolerance on logits, max |a - b| / max |b| per row
+TOL_F16 = 1e-2
+TOL_FP8 = 3e-2
+
+
+def model(tmp, spec, **bucket):
+    pack, ws = synth.make(str(tmp), spec, **bucket)
+    return pack, ws
+
+
+def work(d, greedy=False):
+    return gck.Work(d["sid"], d["tokens"], d["pos"], d["blocks"], d["want"], greedy=greedy, parents=d.get("parents"))
+
+
+def replay(be, scenario=SCENARIO):
+    """Run the scripted session through a backend with the engine's interface (gck.Backend or PagedOracle)."""
+    out = []
+    for op, a in scenario:
+        if op == "step":
+            if isinstance(be, PagedOracle):
+                out.append(be.step(a))
+            else:
+                out.append(be.step([work(d) for d in a]))
+        elif op == "commit":
+            be.commit(*a)
+        elif op == "copy":
+            be.copy_blocks(a)
+    return out
+
+
+def rel_err(a, b):
+    """max |a - b| / max |b| per row."""
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return np.abs(a - b).max(-1) / np.maximum(np.abs(b).max(-1), 1e-30)
+
+
+def assert_logits_close(got, ref, tol):
+    assert got.shape == ref.shape, (got.shape, ref.shape)
+    if not ref.size:
+        return
+    e = rel_err(got, ref)
+    assert (e <= tol).all(), f"relative error {e.max():.3g} > {tol}"
+    # greedy tokens identical wherever the reference's top-2 margin exceeds the tolerance
+    top2 = np.sort(ref, -1)[:, -2:]
+    margin = (top2[:, 1] - top2[:, 0]) / np.maximum(np.abs(ref).max(-1), 1e-30)
+    sure = margin > 2 * tol
+    assert (got.argmax(-1)[sure] == ref.argmax(-1)[sure]).all()
+
+
+def oracle_for(ws, num_blocks=16, kv="f16", kv_scale="unit"):
+    return PagedOracle(weights_from_gguf(ws[0]), num_blocks=num_blocks, block_size=16, kv=kv, kv_scale=kv_scale)
