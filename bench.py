@@ -1,0 +1,385 @@
+"""Benchmark: decode tok/s of the 8B-shaped Q4_K decoder at batch 64 with fp8 paged KV, and % of the HBM roofline.
+
+Workload: Llama-3-8B shape (32 layers, d 4096, 32/8 heads of 128, FFN 14336, vocab 128256),
+random N(0, 0.02) weights quantized to Q4_K (every matrix, embedding and head included), fp8 e4m3 KV with per-page
+scales in 16-token pages; 64 sequences with contexts log-normal over 512-8192 (numpy default_rng(0), median 2147,
+sum 168,356); sequences 0-31 share a 1024-token radix prefix (the same 64 pages in every table). Synthetic data: there
+is no network for checkpoints or datasets.
+
+One step = one gc_step of 64 one-token greedy decode items (device argmax) through the C ABI of libgck.so.
+  value  tok/s from the device time of the steps' kernels (CUDA events on the library's stream, gck_ext.h)
+  e2e    tok/s from the host clock around the synchronous gc_step calls: plan upload (tokens, block tables) H2D,
+         the kernels, the argmax tokens D2H
+Inputs (13 GB of weights and KV) are far larger than L2 (126 MB), so no flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+Under torchrun (N > 1) every rank runs an independent replica on its GPU (the 8B configs do not shard).
+"""
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+SPEC8B = dict(vocab=128256, d=4096, layers=32, heads=32, kv_heads=8, ffn=14336, eps=1e-5, theta=5e5, wtype="q4_k",
+              std=0.02, seed=0, ctx=8192 + 64, name="llama3-8b-shape-q4k")
+B, PREFIX = 64, 1024
+METRIC = "decode tok/s (8B Q4_K, batch 64, fp8 KV)"
+
+
+def contexts():
+    rng = np.random.default_rng(0)
+    ctx = np.clip(np.rint(np.exp(rng.normal(math.log(2048), math.log(4) / 2, B))), 512, 8192).astype(int)
+    ctx[:32] = np.maximum(ctx[:32], PREFIX + 16)
+    return ctx
+
+
+def peaks():
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except OSError:
+        return {}
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region."""
+
+    def __init__(self, gpu):
+        self.gpu, self.rows, self.p = gpu, [], None
+
+    def __enter__(self):
+        q = "clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown," \
+            "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown," \
+            "clocks_event_reasons.sw_power_cap"
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.p = None
+        return self
+
+    def _read(self):
+        for line in self.p.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.p:
+            self.p.terminate()
+            self.p.wait()
+            self.t.join(timeout=2)
+
+    def summary(self):
+        sm = [float(r[0]) for r in self.rows if r and r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in self.rows if len(r) > 1 and r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[4:8]) if v.lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(sm)}
+
+
+def model_dir():
+    from goethe_engine_b200 import synth
+    spec = synth.Spec(**SPEC8B)
+    d = os.path.join(os.environ.get("GCK_BENCH_DIR", "/tmp/gck_bench"), f"{spec.name}-s{spec.seed}")
+    return spec, d
+
+
+def ensure_model(rank, world, barrier):
+    from goethe_engine_b200 import synth
+    spec, d = model_dir()
+    if rank == 0:
+        t0 = time.time()
+        synth.make(d, spec, ncol=B, maxctx=spec.ctx, kv="fp8", tune=dict(max_cols=2048, kv_scale="page"))
+        print(f"[bench] model ready in {d} ({time.time() - t0:.1f}s)", file=sys.stderr, flush=True)
+    if world > 1:
+        barrier()
+    return spec, d, [os.path.join(d, "model.gguf")]
+
+
+def setup_sequences(be, ctx, steps_total):
+    """Block tables and the prefill of every sequence's context (the shared prefix once)."""
+    from goethe_engine_b200 import gck
+    bs = be.block_size
+    nxt = [0]
+
+    def alloc(n):
+        out = list(range(nxt[0], nxt[0] + n))
+        nxt[0] += n
+        return out
+    rng = np.random.default_rng(1)
+    prefix_tok = [int(x) for x in rng.integers(1, 128000, PREFIX)]
+    shared = alloc(PREFIX // bs)
+    tables, toks, start = [], [], []
+    for i, c in enumerate(ctx):
+        own = -(-(int(c) + steps_total + 1) // bs)
+        if i < 32:
+            tables.append(shared + alloc(own - len(shared)))
+            toks.append(prefix_tok + [int(x) for x in rng.integers(1, 128000, int(c) - PREFIX)])
+            start.append(PREFIX if i else 0)
+        else:
+            tables.append(alloc(own))
+            toks.append([int(x) for x in rng.integers(1, 128000, int(c))])
+            start.append(0)
+    assert nxt[0] <= be.num_blocks, (nxt[0], be.num_blocks)
+    # prefill: chunks packed into steps of at most max_cols tokens; the last token of each context is left for decode
+    queue = [[i, start[i], int(ctx[i]) - 1] for i in range(len(ctx))]
+    queue[0][2] = int(ctx[0]) - 1
+    # sequence 0 computes the shared prefix before anyone else reads it
+    order = [queue[0]] + queue[1:]
+    cap = be.layout.max_cols
+    t0 = time.time()
+    while any(q[1] < q[2] for q in order):
+        budget, items = cap, []
+        for q in order:
+            if q[1] >= q[2] or budget == 0:
+                continue
+            if q[0] in range(1, 32) and order[0][1] < PREFIX:
+                continue
+            n = min(budget, q[2] - q[1])
+            items.append(gck.Work(q[0], toks[q[0]][q[1]:q[1] + n], q[1], tables[q[0]], 0))
+            q[1] += n
+            budget -= n
+        be.step(items)
+    return tables, toks, time.time() - t0
+
+
+def kv_unique_bytes(ctx_now, layout):
+    """Algorithmic KV bytes one decode step reads over all layers: every distinct row once (the shared prefix once)."""
+    rows = int(np.sum(ctx_now + 1)) - 31 * PREFIX
+    per_row = 2 * layout.kv_heads * layout.head_dim * 1        # K and V, fp8
+    return rows * per_row * layout.layers
+
+
+def weight_bytes(spec):
+    from goethe_engine_b200.synth import Spec
+    s = Spec(**spec)
+    n = sum(r * c for _, (r, c), t in s.tensors() if t != "f32" and _ != "token_embd.weight")
+    return n * 144 // 256
+
+
+def run_mine(args, rank, world, barrier, maxreduce):
+    import ctypes as C
+    from goethe_engine_b200 import build, gck
+    if rank == 0:
+        build.build()
+    if world > 1:
+        barrier()
+    spec, d, ws = ensure_model(rank, world, barrier)
+    ctx = contexts()
+    steps_total = args.warmup + args.steps
+    dev = int(os.environ.get("LOCAL_RANK", 0))
+    t0 = time.time()
+    be = gck.Backend(d, ws, pool_blocks=int(np.sum(ctx)) // 16 + 2 * B + 64, device=dev)
+    t_open = time.time() - t0
+    L = be.L
+    L.gck_stats_enable.argtypes = [C.c_void_p, C.c_uint32]
+    L.gck_stats_read.argtypes = [C.c_void_p, C.c_void_p]
+
+    class Stats(C.Structure):
+        _fields_ = [("size", C.c_uint32), ("steps", C.c_uint32), ("launches", C.c_uint64), ("forward_ms", C.c_double),
+                    ("class_ms", C.c_double * 16), ("class_launches", C.c_uint64 * 16)]
+    tables, toks, t_prefill = setup_sequences(be, ctx, steps_total)
+    last = [t[-1] for t in toks]
+    pos = [int(c) - 1 for c in ctx]
+
+    def step():
+        out = be.step([gck.Work(i, [last[i]], pos[i], tables[i], 1, greedy=True) for i in range(B)])
+        for i in range(B):
+            last[i] = out[i][0]
+            pos[i] += 1
+    for _ in range(args.warmup):
+        step()
+    kv_bytes = np.mean([kv_unique_bytes(np.array(pos) + k, be.layout) for k in range(args.steps)])
+    import torch
+    torch.cuda.synchronize()
+    if world > 1:
+        barrier()
+    ATTN = 4
+    L.gck_stats_enable(be.h, 1 << ATTN)
+    with Clocks(dev) as clk:
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            step()
+        wall = time.perf_counter() - t0
+    st = Stats(size=C.sizeof(Stats))
+    L.gck_stats_read(be.h, C.byref(st))
+    torch.cuda.synchronize()
+    if world > 1:
+        barrier()
+    dev_s = maxreduce(st.forward_ms / 1e3)
+    wall = maxreduce(wall)
+    tokens = B * args.steps * world
+    value = tokens / dev_s
+    e2e = tokens / wall
+    pk = peaks()
+    hbm = pk.get("hbm_gbs", 6650.0)
+    attn_ms = st.class_ms[ATTN] / max(1, st.class_launches[ATTN])
+    attn_bytes = kv_bytes / be.layout.layers
+    wbytes = weight_bytes(SPEC8B)
+    step_bytes = kv_bytes + wbytes
+    ms_step = dev_s / args.steps * 1e3
+    res = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "q4_k x f16 -> f32; fp8 e4m3 KV", "data": "synthetic (seeded N(0,0.02) weights, uniform tokens)",
+        "config": {"workload": "C3: Llama-3-8B shape, Q4_K weights, fp8 paged KV (per-page scale), 64-sequence greedy "
+                               "decode, log-normal contexts 512-8192 (sum 168356), 32 sequences share a 1024-token prefix",
+                   "batch": B, "context_sum": int(np.sum(ctx)), "block_size": be.block_size,
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2 (13 GB per step), no flush"},
+        "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": int(sum(len(t) for t in tables) * 4 + B * 4 * 3 + B * 48),
+                "d2h_bytes_per_step": B * 4, "path": "gc_step through the C ABI (ctypes), host buffers"},
+        "roofline": {"bound": "hbm", "kernel": "attn_kernel (paged fp8 KV attention)", "achieved": round(attn_bytes / (attn_ms / 1e3) / 1e9, 1),
+                     "peak": hbm, "unit": "GB/s", "frac": round(attn_bytes / (attn_ms / 1e3) / 1e9 / hbm, 4),
+                     "traffic": None, "algorithmic_bytes_per_launch": int(attn_bytes), "launch_ms": round(attn_ms, 4),
+                     "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in pk else "fallback 6650 GB/s"},
+        "step_roofline": {"algorithmic_bytes": int(step_bytes), "weights_bytes": int(wbytes), "kv_bytes": int(kv_bytes),
+                          "achieved_gbs": round(step_bytes / (ms_step / 1e3) / 1e9, 1),
+                          "frac_of_measured": round(step_bytes / (ms_step / 1e3) / 1e9 / hbm, 4),
+                          "frac_of_8tbs": round(step_bytes / (ms_step / 1e3) / 1e9 / 8000, 4)},
+        "gpu_launches": int(st.launches),
+        "clocks": clk.summary(),
+        "setup": {"open_s": round(t_open, 1), "prefill_s": round(t_prefill, 1), "prefill_tokens": int(np.sum(ctx) - 31 * PREFIX)},
+    }
+    be.close()
+    if rank == 0:
+        if world == 1 and not args.no_cpu:
+            res["cpu_baseline"] = cpu_baseline(args)
+        print(json.dumps(res), flush=True)
+
+
+class CpuSample:
+    """The oracle (numpy restatement of ref.py) on a bounded sample of the same decode step: `seqs` sequences with the
+    first C3 contexts, `layers` of the 32 layers (dequantized from the same GGUF), the head on 8192 of the 128256
+    vocabulary rows; the step time is scaled to 32 layers and the full head. KV pages hold random fp8 codes (a decode
+    step's time does not depend on their values)."""
+
+    VS = 8192
+
+    def __init__(self, seqs=8, layers=2):
+        from oracle import quants as Q
+        from oracle.model import PagedOracle, Weights
+        import gguf
+        _, d = model_dir()
+        r = gguf.GGUFReader(os.path.join(d, "model.gguf"))
+        T = {t.name: t for t in r.tensors}
+
+        def mat(name, rows=None):
+            t = T[name]
+            ne = [int(x) for x in t.shape]
+            raw = np.asarray(t.data).view(np.uint8).reshape(ne[1], -1)
+            if rows:
+                raw = raw[:rows]
+            return Q.dequant(int(t.tensor_type), raw.tobytes(), (raw.shape[0], ne[0]))
+        lw = []
+        for i in range(layers):
+            b = f"blk.{i}."
+            lw.append(dict(q=mat(b + "attn_q.weight"), k=mat(b + "attn_k.weight"), v=mat(b + "attn_v.weight"),
+                           o=mat(b + "attn_output.weight"), g=mat(b + "ffn_gate.weight"), u=mat(b + "ffn_up.weight"),
+                           dn=mat(b + "ffn_down.weight")))
+        self.head = mat("output.weight", self.VS)
+        w = Weights(self.head.copy(), self.head, lw, eps=1e-5, theta=5e5, heads=32, kv_heads=8)
+        self.ctx = contexts()[:seqs]
+        nb = int(sum(-(-(c + 1) // 16) for c in self.ctx))
+        self.o = PagedOracle(w, num_blocks=nb, kv="fp8", kv_scale="page")
+        rng = np.random.default_rng(2)
+        self.o.kc[:] = rng.integers(0, 0x78, self.o.kc.shape, dtype=np.uint8)
+        self.o.vc[:] = rng.integers(0, 0x78, self.o.vc.shape, dtype=np.uint8)
+        tabs, k = [], 0
+        for c in self.ctx:
+            n = -(-(int(c) + 1) // 16)
+            tabs.append(list(range(k, k + n)))
+            k += n
+        self.items = [dict(sid=i, tokens=[7], pos=int(c), blocks=tabs[i], want=1) for i, c in enumerate(self.ctx)]
+        self.seqs, self.layers = seqs, layers
+        self.o.step(self.items)          # warm
+
+    def run(self):
+        t0 = time.perf_counter()
+        self.o.step(self.items)
+        t_all = time.perf_counter() - t0
+        h = np.ones((self.seqs, 4096), np.float32)
+        t0 = time.perf_counter()
+        for _ in range(3):
+            h @ self.head.T
+        t_head = (time.perf_counter() - t0) / 3
+        per_step = max(t_all - t_head, 1e-9) * 32 / self.layers + t_head * 128256 / self.VS
+        return {"value": round(self.seqs / per_step, 3), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+                "sample": f"oracle decode step of {self.seqs} C3 sequences (contexts {list(map(int, self.ctx))}), "
+                          f"{self.layers}/32 layers and {self.VS}/128256 head rows timed ({t_all:.2f}s), scaled to "
+                          f"the full model: {per_step:.2f}s per step"}
+
+
+def cpu_baseline(args):
+    return CpuSample().run()
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    from goethe_engine_b200 import build
+    build.build_synth()
+    ensure_model(0, 1, lambda: None)
+    smp = CpuSample()
+    cb, vals = None, []
+    for _ in range(max(1, min(args.steps, 3))):
+        cb = smp.run()
+        vals.append(cb["value"])
+    v = float(np.median(vals))
+    cb["value"] = v
+    print(json.dumps({"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": world,
+                      "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                      "dtype": "f32 (numpy oracle of ref.py; fp8 KV)", "data": "synthetic",
+                      "config": {"workload": "C3 decode step, bounded CPU sample (see cpu_baseline.sample)"},
+                      "cpu_baseline": cb, "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0,
+                                                   "d2h_bytes_per_step": 0}}), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    rank = int(os.environ.get("RANK", 0))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    barrier = lambda: None  # noqa: E731
+    maxreduce = lambda x: x  # noqa: E731
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=1800))
+
+        def barrier():
+            dist.barrier()
+
+        def maxreduce(x):
+            t = torch.tensor([x], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+    try:
+        run_mine(args, rank, world, barrier, maxreduce)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -46,7 +46,7 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
 }
 
 template <int DH, bool FP8>
-__global__ void __launch_bounds__(128) attn_kernel(PlanView pv, AttnArgs a) {
+__global__ void __launch_bounds__(256) attn_kernel(PlanView pv, AttnArgs a) {
   using C = Cfg<DH, FP8>;
   extern __shared__ __align__(128) uint8_t sm[];
   int *sE = reinterpret_cast<int *>(sm + 2 * C::BUF);   // [2 bufs][16 entries][2] page exponents (K, V)
@@ -328,7 +328,6 @@ template <int DH, bool FP8>
 void launch_t(const PlanView &pv, const AttnArgs &a, int nw, cudaStream_t s) {
   using C = Cfg<DH, FP8>;
   if (pv.n_work > 0) attn_kernel<DH, FP8><<<pv.n_work, 32 * nw, C::SMEM, s>>>(pv, a);
-  if (pv.n_qg > 0) attn_combine<DH><<<dim3(pv.n_qg, a.KVH), 128, 0, s>>>(pv, a);
 }
 
 }  // namespace
@@ -341,6 +340,12 @@ void launch_attention(const PlanView &pv, const AttnArgs &a, int nw, cudaStream_
     if (a.kv_fp8) launch_t<64, true>(pv, a, nw, s);
     else launch_t<64, false>(pv, a, nw, s);
   }
+}
+
+void launch_attention_combine(const PlanView &pv, const AttnArgs &a, cudaStream_t s) {
+  if (pv.n_qg <= 0) return;
+  if (a.dh == 128) attn_combine<128><<<dim3(pv.n_qg, a.KVH), 128, 0, s>>>(pv, a);
+  else attn_combine<64><<<dim3(pv.n_qg, a.KVH), 128, 0, s>>>(pv, a);
 }
 
 }  // namespace gck

@@ -71,5 +71,6 @@ struct AttnArgs {
   float scale_log2;          // log2(e) / sqrt(dh)
 };
 void launch_attention(const PlanView &pv, const AttnArgs &a, int nw, cudaStream_t s);
+void launch_attention_combine(const PlanView &pv, const AttnArgs &a, cudaStream_t s);
 
 }  // namespace gck

@@ -19,6 +19,7 @@
 #include <vector>
 
 #include "gc.h"
+#include "gck_ext.h"
 #include "hostio.h"
 #include "kernels.h"
 
@@ -100,6 +101,24 @@ struct gc_handle {
   std::vector<Slot> slots;
   std::vector<void *> allocs;
   size_t device_bytes = 0;
+  // step statistics (gck_ext.h)
+  bool stats_on = false;
+  uint32_t stats_mask = 0;
+  gck_stats stats{};
+  std::vector<cudaEvent_t> ev_pool;
+  size_t ev_used = 0;
+  struct Mark { int cls; cudaEvent_t a, b; };
+  std::vector<Mark> marks;
+  uint64_t step_launches = 0;
+
+  cudaEvent_t event() {
+    if (ev_used == ev_pool.size()) {
+      cudaEvent_t e;
+      ck(cudaEventCreate(&e), "event");
+      ev_pool.push_back(e);
+    }
+    return ev_pool[ev_used++];
+  }
 
   void *dalloc(size_t n, const char *what) {
     void *p = nullptr;
@@ -119,6 +138,7 @@ struct gc_handle {
     for (void *p : allocs) cudaFree(p);
     if (plan_host) cudaFreeHost(plan_host);
     if (tok_host) cudaFreeHost(tok_host);
+    for (auto e : ev_pool) cudaEventDestroy(e);
     if (st) cudaStreamDestroy(st);
   }
 };
@@ -625,7 +645,7 @@ void build_plan(gc_handle *h, const std::vector<WorkIn> &ws, HostPlan &pl) {
     T += static_cast<int>(w.n);
   }
   (void)G;
-  pl.nw = multi ? 4 : 1;
+  pl.nw = multi ? 8 : 1;
   // work: per item, kv head, split: chain groups of the item packed nw to a CTA, tree groups one to a CTA
   for (size_t i = 0; i < pl.items.size(); i++) {
     int q0 = -1, q1 = -1;
@@ -722,8 +742,26 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
     h->attn_ml = static_cast<float2 *>(h->dalloc(cap * 16 * 8, "attention partials"));
     h->attn_parts_cap = cap;
   }
+  h->step_launches = 0;
+  // run(cls, kernels, fn): launch fn on the stream, bracketed by events when the class is being timed
+  auto run = [&](int cls, int nk, auto fn) {
+    bool rec = h->stats_on && ((h->stats_mask >> cls) & 1u);
+    cudaEvent_t a = nullptr, b = nullptr;
+    if (rec) {
+      a = h->event();
+      b = h->event();
+      cudaEventRecord(a, s);
+    }
+    fn();
+    if (rec) {
+      cudaEventRecord(b, s);
+      h->marks.push_back({cls, a, b});
+    }
+    h->step_launches += nk;
+  };
+  auto gemm_kernels = [](const QWeight &w) { return w.splits > 1 ? 2 : 1; };
 
-  launch_embed(pv, h->emb, h->emb_type, h->emb_row_bytes, h->d, h->x, s);
+  run(GCK_K_EMBED, 1, [&] { launch_embed(pv, h->emb, h->emb_type, h->emb_row_bytes, h->d, h->x, s); });
   const int wq = (h->H + 2 * h->KVH) * h->dh;
   AttnArgs aa{};
   aa.q = h->q;
@@ -737,24 +775,50 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
   aa.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(h->dh)));
   for (int l = 0; l < h->L; l++) {
     const Layer &ly = h->layers[l];
-    launch_rmsnorm(h->x, nullptr, T, ly.attn_norm, h->eps, h->d, h->d, h->h, s);
-    launch_gemm(ly.qkv, h->h, T, Epi{kEpiStore, wq, wq, h->qkv, nullptr}, h->part, s);
+    run(GCK_K_NORM, 1, [&] { launch_rmsnorm(h->x, nullptr, T, ly.attn_norm, h->eps, h->d, h->d, h->h, s); });
+    run(GCK_K_QKV, gemm_kernels(ly.qkv),
+        [&] { launch_gemm(ly.qkv, h->h, T, Epi{kEpiStore, wq, wq, h->qkv, nullptr}, h->part, s); });
     uint8_t *kc = h->kc + l * h->layer_bytes, *vc = h->vc + l * h->layer_bytes;
     int8_t *ex = h->exps ? h->exps + l * h->exps_layer : nullptr;
-    launch_rope_kv(pv, h->qkv, h->H, h->KVH, h->dh, h->rope, h->q, kc, vc, ex, h->kv_fp8, h->page_scale, s);
+    run(GCK_K_ROPE, 1, [&] {
+      launch_rope_kv(pv, h->qkv, h->H, h->KVH, h->dh, h->rope, h->q, kc, vc, ex, h->kv_fp8, h->page_scale, s);
+    });
     aa.kc = kc;
     aa.vc = vc;
     aa.exps = h->page_scale ? ex : nullptr;
-    launch_attention(pv, aa, nw, s);
-    launch_gemm(ly.o, h->att, T, Epi{kEpiAdd, h->d, h->d, h->x, nullptr}, h->part, s);
-    launch_rmsnorm(h->x, nullptr, T, ly.ffn_norm, h->eps, h->d, h->d, h->h, s);
-    launch_gemm(ly.gu, h->h, T, Epi{kEpiSwiGLU, h->F, ly.dn.KT * kBK, nullptr, h->act}, h->part, s);
-    launch_gemm(ly.dn, h->act, T, Epi{kEpiAdd, h->d, h->d, h->x, nullptr}, h->part, s);
+    run(GCK_K_ATTN, 1, [&] { launch_attention(pv, aa, nw, s); });
+    run(GCK_K_COMBINE, 1, [&] { launch_attention_combine(pv, aa, s); });
+    run(GCK_K_O, gemm_kernels(ly.o),
+        [&] { launch_gemm(ly.o, h->att, T, Epi{kEpiAdd, h->d, h->d, h->x, nullptr}, h->part, s); });
+    run(GCK_K_NORM, 1, [&] { launch_rmsnorm(h->x, nullptr, T, ly.ffn_norm, h->eps, h->d, h->d, h->h, s); });
+    run(GCK_K_GATEUP, gemm_kernels(ly.gu), [&] {
+      launch_gemm(ly.gu, h->h, T, Epi{kEpiSwiGLU, h->F, ly.dn.KT * kBK, nullptr, h->act}, h->part, s);
+    });
+    run(GCK_K_DOWN, gemm_kernels(ly.dn),
+        [&] { launch_gemm(ly.dn, h->act, T, Epi{kEpiAdd, h->d, h->d, h->x, nullptr}, h->part, s); });
   }
   if (pv.R > 0) {
-    launch_rmsnorm(h->x, pv.want_tok, pv.R, h->out_norm, h->eps, h->d, h->d, h->h, s);
-    launch_gemm(h->head, h->h, pv.R, Epi{kEpiStore, h->vocab, h->vocab, h->logits, nullptr}, h->part, s);
+    run(GCK_K_NORM, 1, [&] { launch_rmsnorm(h->x, pv.want_tok, pv.R, h->out_norm, h->eps, h->d, h->d, h->h, s); });
+    run(GCK_K_HEAD, gemm_kernels(h->head), [&] {
+      launch_gemm(h->head, h->h, pv.R, Epi{kEpiStore, h->vocab, h->vocab, h->logits, nullptr}, h->part, s);
+    });
   }
+}
+
+// after the step's synchronize: fold the recorded events into the statistics
+void collect_stats(gc_handle *h, cudaEvent_t f0, cudaEvent_t f1) {
+  if (!h->stats_on) return;
+  float ms = 0.f;
+  if (f0 && cudaEventElapsedTime(&ms, f0, f1) == cudaSuccess) h->stats.forward_ms += ms;
+  for (auto &m : h->marks)
+    if (cudaEventElapsedTime(&ms, m.a, m.b) == cudaSuccess) {
+      h->stats.class_ms[m.cls] += ms;
+      h->stats.class_launches[m.cls] += 1;
+    }
+  h->marks.clear();
+  h->ev_used = 0;
+  h->stats.steps += 1;
+  h->stats.launches += h->step_launches;
 }
 
 Slot *find_slot(gc_handle *h, uint64_t sid, bool make) {
@@ -839,10 +903,27 @@ GC_API int gc_step(gc_handle *h, const gc_step_in *in, gc_step_out *o) {
     HostPlan pl;
     build_plan(h, ws, pl);
     PlanView pv = upload_plan(h, pl);
+    cudaEvent_t f0 = nullptr, f1 = nullptr;
+    if (h->stats_on) {
+      f0 = h->event();
+      f1 = h->event();
+      cudaEventRecord(f0, h->st);
+    }
     forward(h, pv, pl.nw);
+    if (greedy && R) {
+      bool rec = h->stats_on && ((h->stats_mask >> GCK_K_ARGMAX) & 1u);
+      cudaEvent_t a = rec ? h->event() : nullptr, b = rec ? h->event() : nullptr;
+      if (rec) cudaEventRecord(a, h->st);
+      launch_argmax(h->logits, static_cast<int>(R), h->vocab, h->argmax, h->st);
+      if (rec) {
+        cudaEventRecord(b, h->st);
+        h->marks.push_back({GCK_K_ARGMAX, a, b});
+      }
+      h->step_launches += 1;
+    }
+    if (f1) cudaEventRecord(f1, h->st);
     if (greedy) {
       if (R) {
-        launch_argmax(h->logits, static_cast<int>(R), h->vocab, h->argmax, h->st);
         ck(cudaMemcpyAsync(h->tok_host, h->argmax, R * 4, cudaMemcpyDeviceToHost, h->st), "tokens");
       }
       ck(cudaStreamSynchronize(h->st), "step");
@@ -856,6 +937,7 @@ GC_API int gc_step(gc_handle *h, const gc_step_in *in, gc_step_out *o) {
       if (o->size >= offsetof(gc_step_out, logits_dev) + 8) o->logits_dev = reinterpret_cast<uint64_t>(h->logits);
     }
     ck(cudaGetLastError(), "step");
+    collect_stats(h, f0, f1);
     return GC_OK;
   } catch (const GcError &e) {
     h->err = e.msg;
@@ -951,6 +1033,27 @@ GC_API int gc_release(gc_handle *h, uint64_t sid) {
   if (!h) return GC_E_ARG;
   Slot *sl = find_slot(h, sid, false);
   if (sl) *sl = Slot{};
+  return GC_OK;
+}
+
+GC_API int gck_stats_enable(gc_handle *h, uint32_t class_mask) {
+  if (!h) return GC_E_ARG;
+  h->stats = gck_stats{};
+  h->stats.size = sizeof(gck_stats);
+  h->stats_mask = class_mask;
+  h->stats_on = true;
+  h->marks.clear();
+  h->ev_used = 0;
+  return GC_OK;
+}
+
+GC_API int gck_stats_read(gc_handle *h, gck_stats *out) {
+  if (!h || !out || out->size < 8) return GC_E_ARG;
+  h->stats_on = false;
+  uint32_t n = std::min<uint32_t>(out->size, sizeof(gck_stats));
+  gck_stats st = h->stats;
+  st.size = n;
+  std::memcpy(out, &st, n);
   return GC_OK;
 }
 
