@@ -188,7 +188,10 @@ def run_mine(args, rank, world, barrier, maxreduce):
     class Stats(C.Structure):
         _fields_ = [("size", C.c_uint32), ("steps", C.c_uint32), ("launches", C.c_uint64), ("forward_ms", C.c_double),
                     ("class_ms", C.c_double * 16), ("class_launches", C.c_uint64 * 16)]
+    L.gck_stats_enable(be.h, 0)
     tables, toks, t_prefill = setup_sequences(be, ctx, steps_total)
+    st0 = Stats(size=C.sizeof(Stats))
+    L.gck_stats_read(be.h, C.byref(st0))
     last = [t[-1] for t in toks]
     pos = [int(c) - 1 for c in ctx]
 
@@ -197,15 +200,18 @@ def run_mine(args, rank, world, barrier, maxreduce):
         for i in range(B):
             last[i] = out[i][0]
             pos[i] += 1
+    L.gck_stats_enable(be.h, 0)
     for _ in range(args.warmup):
         step()
+    stw = Stats(size=C.sizeof(Stats))
+    L.gck_stats_read(be.h, C.byref(stw))
     kv_bytes = np.mean([kv_unique_bytes(np.array(pos) + k, be.layout) for k in range(args.steps)])
     import torch
     torch.cuda.synchronize()
     if world > 1:
         barrier()
     ATTN = 4
-    L.gck_stats_enable(be.h, 1 << ATTN)
+    L.gck_stats_enable(be.h, 0xFFFF if args.profile else 1 << ATTN)
     with Clocks(dev) as clk:
         t0 = time.perf_counter()
         for _ in range(args.steps):
@@ -249,8 +255,17 @@ def run_mine(args, rank, world, barrier, maxreduce):
                           "frac_of_8tbs": round(step_bytes / (ms_step / 1e3) / 1e9 / 8000, 4)},
         "gpu_launches": int(st.launches),
         "clocks": clk.summary(),
-        "setup": {"open_s": round(t_open, 1), "prefill_s": round(t_prefill, 1), "prefill_tokens": int(np.sum(ctx) - 31 * PREFIX)},
+        "setup": {"open_s": round(t_open, 1), "prefill_s": round(t_prefill, 1), "prefill_tokens": int(np.sum(ctx) - 31 * PREFIX),
+                  "launches_before_timed": int(st0.launches + stw.launches)},
     }
+    if args.profile:
+        names = ["embed", "rmsnorm", "gemm_qkv", "rope_kv", "attention", "attn_combine", "gemm_o", "gemm_gateup",
+                 "gemm_down", "gemm_head", "argmax"]
+        tot = sum(st.class_ms[i] for i in range(len(names)))
+        lines = [f"{n:14s} {st.class_ms[i] / args.steps:8.3f} ms/step  {st.class_launches[i] // max(1, args.steps):5d} "
+                 f"launches/step  {100 * st.class_ms[i] / max(tot, 1e-9):5.1f}%" for i, n in enumerate(names)]
+        print("[bench] per-class device time (events around each launch):\n" + "\n".join(lines) +
+              f"\n  sum {tot / args.steps:.3f} ms/step, step {st.forward_ms / args.steps:.3f} ms", file=sys.stderr, flush=True)
     be.close()
     if rank == 0:
         if world == 1 and not args.no_cpu:
@@ -352,6 +367,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--profile", action="store_true", help="time every kernel class (stderr table)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", 1))
     rank = int(os.environ.get("RANK", 0))

@@ -12,6 +12,7 @@
 #include <cstdio>
 #include <fstream>
 #include <memory>
+#include <mutex>
 #include <sstream>
 #include <string>
 #include <thread>
@@ -393,6 +394,34 @@ std::string read_file(const std::string &path) {
   return ss.str();
 }
 
+}  // namespace
+
+// ============================================================================================== static commit scratch
+// gck_commit_static keeps its scratch (the move list and the staged rows) in this fixed device array instead of
+// memory the handle allocates, so that callers that may not allocate device memory can commit tree paths. Every GPU
+// that loads the library holds these 16 MiB until the process exits. In host code the name is only a stand-in: the
+// device address comes from cudaGetSymbolAddress, once per device, with that device current.
+constexpr size_t kCommitStaticBytes = static_cast<size_t>(16) << 20;
+static __device__ __align__(256) unsigned char g_commit_static[kCommitStaticBytes];
+
+namespace {
+std::mutex g_static_mu;
+void *g_static_addr[256] = {};
+
+void *commit_static_address(int dev) {
+  std::lock_guard<std::mutex> lk(g_static_mu);
+  if (dev < 0 || dev >= 256) fail(GC_E_DEVICE, "device ordinal %d", dev);
+  if (!g_static_addr[dev]) {
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_commit_static);
+    if (e != cudaSuccess || !p) {
+      cudaGetLastError();
+      fail(GC_E_DEVICE, "cudaGetSymbolAddress of the static commit scratch: %s", cudaGetErrorString(e));
+    }
+    g_static_addr[dev] = p;
+  }
+  return g_static_addr[dev];
+}
 }  // namespace
 
 // ============================================================================================== exported ABI
@@ -1012,6 +1041,50 @@ GC_API int gc_copy_blocks(gc_handle *h, const uint32_t *src, const uint32_t *dst
     }
     ck(cudaStreamSynchronize(h->st), "copy_blocks");
     ck(cudaGetLastError(), "copy_blocks");
+    return GC_OK;
+  } catch (const GcError &e) {
+    h->err = e.msg;
+    return e.code;
+  }
+}
+
+GC_API int gck_commit_static(gc_handle *h, uint64_t sid, uint32_t base, const uint32_t *path, uint32_t n) {
+  if (!h) return GC_E_ARG;
+  try {
+    Slot *sl = find_slot(h, sid, false);
+    if (!sl) fail(GC_E_STATE, "gck_commit_static: unknown sequence %llu", static_cast<unsigned long long>(sid));
+    if (n && !path) fail(GC_E_ARG, "gck_commit_static: null path");
+    std::vector<int> moves;
+    uint64_t rows = static_cast<uint64_t>(sl->blocks.size()) * kBlock;
+    for (uint32_t j = 0; j < n; j++) {
+      if (path[j] < j || (j && path[j] <= path[j - 1]))
+        fail(GC_E_ARG, "gck_commit_static: path must increase and path[j] >= j");
+      if (static_cast<uint64_t>(base) + path[j] >= rows)
+        fail(GC_E_ARG, "gck_commit_static: row %u outside the table", base + path[j]);
+      if (path[j] == j) continue;
+      uint32_t a = base + path[j], b = base + j;
+      moves.push_back(static_cast<int>(sl->blocks[a / kBlock] * kBlock + a % kBlock));
+      moves.push_back(static_cast<int>(sl->blocks[b / kBlock] * kBlock + b % kBlock));
+    }
+    if (moves.empty()) return GC_OK;
+    const int nm = static_cast<int>(moves.size() / 2);
+    // layout in the array: the move list (256-byte aligned), then the staged rows [moves][layers][K, V][KVH * dh] f32
+    const size_t list_bytes = (vbytes(moves) + 255) / 256 * 256;
+    const size_t row_bytes = static_cast<size_t>(h->L) * 2 * h->KVH * h->dh * 4;
+    const size_t need = list_bytes + static_cast<size_t>(nm) * row_bytes;
+    if (need > kCommitStaticBytes)
+      fail(GC_E_ARG, "gck_commit_static: %d moved rows need %zu bytes of scratch; the static array holds %zu (at most %zu "
+           "moved rows for this model)", nm, need, kCommitStaticBytes, (kCommitStaticBytes - 256) / (row_bytes + 8));
+    ck(cudaSetDevice(h->dev), "cudaSetDevice");
+    uint8_t *base_ptr = static_cast<uint8_t *>(commit_static_address(h->dev));
+    int *d_moves = reinterpret_cast<int *>(base_ptr);
+    float *d_rows = reinterpret_cast<float *>(base_ptr + list_bytes);
+    // nothing in the array has to start at zero: the list is copied whole and every staged row is written before read
+    ck(cudaMemcpyAsync(d_moves, moves.data(), vbytes(moves), cudaMemcpyHostToDevice, h->st), "commit moves");
+    launch_commit(d_moves, nm, h->L, h->KVH, h->dh, h->kc, h->vc, h->page_scale ? h->exps : nullptr, h->kv_fp8,
+                  h->layer_bytes, h->exps_layer, d_rows, h->st);
+    ck(cudaStreamSynchronize(h->st), "commit");
+    ck(cudaGetLastError(), "commit");
     return GC_OK;
   } catch (const GcError &e) {
     h->err = e.msg;

@@ -42,6 +42,26 @@ GC_API int gck_stats_enable(gc_handle *h, uint32_t class_mask);
 /* Stops recording and copies the statistics (up to out->size bytes). */
 GC_API int gck_stats_read(gc_handle *h, gck_stats *out);
 
+/* gc_commit without device allocation. No counterpart in the reference's abi/gc.h (an addition of this library).
+ *
+ * Some callers cannot allocate device memory while they run: a serving process that reserves all of the GPU's memory
+ * at start-up and treats any later cudaMalloc as a failure, or one that shares the GPU under a fixed memory budget
+ * enforced by an allocator it does not control. gc_commit grows its staging buffers with cudaMalloc on first use; this entry point does the
+ * same commit (row base + path[j] becomes row base + j in every layer, K and V; fp8 rows re-encoded into their new
+ * page's scale) with its scratch in a fixed 16 MiB device array inside the library instead, and allocates nothing.
+ *
+ * Limits and rules:
+ *  - the scratch holds the move list and every moved row of every layer as float32: (path entries that move) times
+ *    layers x 2 x kv_heads x head_dim x 4 bytes must fit 16 MiB less 256 bytes (an 8B-shaped model: about 63 rows;
+ *    a 70B-shaped one: about 25); a longer path returns GC_E_ARG and a text giving the limit;
+ *  - every GPU that loads the library holds the 16 MiB array until the process exits;
+ *  - the first call on a device looks the array's address up (cudaGetSymbolAddress); make that first call before any
+ *    stream capture on that device;
+ *  - all callers on one device share the array and it keeps the last call's contents; calls that overlap on the GPU
+ *    (two handles of one device committing from different threads at once) race, so serialize them. The call itself
+ *    returns only after its work on the handle's stream has finished. */
+GC_API int gck_commit_static(gc_handle *h, uint64_t sid, uint32_t base, const uint32_t *path, uint32_t n);
+
 #ifdef __cplusplus
 }
 #endif

@@ -27,16 +27,18 @@ def tiny(tmp_path_factory):
     return synth.make(str(d), spec, ncol=4, maxctx=256)
 
 
-def declared():
-    txt = open(os.path.join(ROOT, "include", "gc.h")).read()
-    return re.findall(r"GC_API\s+[\w\s\*]+?\b(gc_\w+)\s*\(", txt)
+def declared(header):
+    txt = open(os.path.join(ROOT, "include", header)).read()
+    return re.findall(r"GC_API\s+[\w\s\*]+?\b(gck?_\w+)\s*\(", txt)
 
 
 def test_exports_every_declared_symbol(lib):
-    names = declared()
-    assert set(names) == set(gck.SYMBOLS)
-    for n in names:
-        assert hasattr(lib, n), n
+    assert set(declared("gc.h")) == set(gck.SYMBOLS)
+    for h in sorted(os.listdir(os.path.join(ROOT, "include"))):
+        names = declared(h)
+        assert names, h
+        for n in names:
+            assert hasattr(lib, n), (h, n)
 
 
 def test_abi_version(lib):
