@@ -47,33 +47,60 @@ void launch_embed(const PlanView &pv, const uint8_t *emb, int type, size_t row_b
 
 // ----------------------------------------------------------------------------------------------------------------
 // RMSNorm: out[r, :] = f16(x[src(r), :] * rsqrt(mean(x^2) + eps) * gain); columns d .. ld-1 are zeroed.
-// The sum of squares has a fixed order (per-thread strided partials, then a fixed tree), independent of the batch.
-__global__ void rmsnorm_kernel(const float *x, const int *rows, const float *gain, float eps, int d, int ld,
-                               __half *out) {
+// One CTA per row; float4 loads, all issued before the first use. The sum of squares has a fixed order (each thread's
+// strided partials in index order, then a fixed shuffle tree, then the warps in index order), independent of the batch.
+constexpr int kNormThreads = 512;
+constexpr int kNormMaxVec = 4;    // float4 loads per thread: d <= 512 * 4 * 4 = 8192
+
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float *x, const int *rows, const float *gain,
+                                                               float eps, int d, int ld, __half *out) {
   int r = blockIdx.x;
   int src = rows ? rows[r] : r;
-  const float *xr = x + static_cast<size_t>(src) * d;
+  const float4 *xr = reinterpret_cast<const float4 *>(x + static_cast<size_t>(src) * d);
+  const float4 *gr = reinterpret_cast<const float4 *>(gain);
+  const int nv = d / 4;
+  float4 v[kNormMaxVec];
+#pragma unroll
+  for (int i = 0; i < kNormMaxVec; i++) {
+    int e = threadIdx.x + i * kNormThreads;
+    v[i] = e < nv ? xr[e] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   float ss = 0.f;
-  for (int e = threadIdx.x; e < d; e += blockDim.x) ss = fmaf(xr[e], xr[e], ss);
+#pragma unroll
+  for (int i = 0; i < kNormMaxVec; i++) {
+    ss = fmaf(v[i].x, v[i].x, ss);
+    ss = fmaf(v[i].y, v[i].y, ss);
+    ss = fmaf(v[i].z, v[i].z, ss);
+    ss = fmaf(v[i].w, v[i].w, ss);
+  }
   ss = warp_sum(ss);
   __shared__ float part[32];
   int w = threadIdx.x / 32, l = threadIdx.x % 32;
   if (l == 0) part[w] = ss;
   __syncthreads();
   if (w == 0) {
-    float v = l < blockDim.x / 32 ? part[l] : 0.f;
-    v = warp_sum(v);
-    if (l == 0) part[0] = v;
+    float s2 = l < kNormThreads / 32 ? part[l] : 0.f;
+    s2 = warp_sum(s2);
+    if (l == 0) part[0] = s2;
   }
   __syncthreads();
   float inv = rsqrtf(part[0] / static_cast<float>(d) + eps);
-  __half *o = out + static_cast<size_t>(r) * ld;
-  for (int e = threadIdx.x; e < ld; e += blockDim.x) o[e] = __float2half_rn(e < d ? xr[e] * inv * gain[e] : 0.f);
+  __half2 *o = reinterpret_cast<__half2 *>(out + static_cast<size_t>(r) * ld);
+#pragma unroll
+  for (int i = 0; i < kNormMaxVec; i++) {
+    int e = threadIdx.x + i * kNormThreads;
+    if (e < nv) {
+      float4 g = gr[e];
+      o[2 * e] = __floats2half2_rn(v[i].x * inv * g.x, v[i].y * inv * g.y);
+      o[2 * e + 1] = __floats2half2_rn(v[i].z * inv * g.z, v[i].w * inv * g.w);
+    }
+  }
+  for (int e = d / 2 + threadIdx.x; e < ld / 2; e += kNormThreads) o[e] = __floats2half2_rn(0.f, 0.f);
 }
 
 void launch_rmsnorm(const float *x, const int *rows, int n, const float *gain, float eps, int d, int ld, __half *out,
                     cudaStream_t s) {
-  if (n > 0) rmsnorm_kernel<<<n, 256, 0, s>>>(x, rows, gain, eps, d, ld, out);
+  if (n > 0) rmsnorm_kernel<<<n, kNormThreads, 0, s>>>(x, rows, gain, eps, d, ld, out);
 }
 
 // ----------------------------------------------------------------------------------------------------------------

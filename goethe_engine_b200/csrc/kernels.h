@@ -1,5 +1,6 @@
 // Launch wrappers of the decoder-step kernels (host-callable; all run on the caller's stream).
 #pragma once
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
@@ -24,6 +25,9 @@ __host__ __device__ inline size_t tile_bytes(int type) {
     default: return static_cast<size_t>(kBM) * kBK * 2;              // f16
   }
 }
+// Q4_K and Q8_0 tiles: the 128 rows' 16-byte headers (Q4_K: d, dmin, 12 scale bytes; Q8_0: the 8 block scales), then
+// the quants as [4 K-stages of 64][pieces][128 rows][16 B] (Q4_K 2 pieces: bytes 32j..32j+31 of each row's block;
+// Q8_0 4 pieces: the 64 int8 of blocks 2j, 2j+1), so that thread r of the dequant warps reads rows 16 B apart.
 
 enum EpiKind { kEpiStore = 0, kEpiAdd = 1, kEpiSwiGLU = 2 };
 struct Epi {
@@ -56,8 +60,20 @@ void launch_commit(const int *moves, int n, int L, int KVH, int dh, uint8_t *kc,
 
 // y = act[T, Kpad] (f16, row-major, Kpad = KT * kBK) times W^T, with the epilogue; part: split-K scratch
 // [splits, T, NT * kBM] f32 (unused when splits == 1).
+// F16 weights: mma.sync kernel (k_gemm.cu). Q4_K / Q8_0 weights: tcgen05 kernel (k_gemm_tc.cu), whose activation
+// tiles come through TMA tensor maps over the activation buffer, one map per token tile size.
 void gemm_init();   // once per device, before the first launch_gemm
 void launch_gemm(const QWeight &w, const __half *act, int T, const Epi &epi, float *part, cudaStream_t s);
+
+struct TmaSet {            // tensor maps over one activation buffer [rows, K] f16, boxes of 64 K x {16..256} rows
+  CUtensorMap m[5];
+  const CUtensorMap *map(int nt) const { return &m[nt <= 16 ? 0 : nt <= 32 ? 1 : nt <= 64 ? 2 : nt <= 128 ? 3 : 4]; }
+};
+int tc_token_tile(int T);
+size_t tc_tile_bytes(int type);
+void gemm_tc_init();      // once per device
+void launch_gemm_tc(const QWeight &w, const TmaSet &ts, const __half *act, int T, const Epi &epi, float *part,
+                    int *err, cudaStream_t s);
 
 // Paged attention over the plan's work list: q [T, H, dh] f16 -> out [T, H, dh] f16. part_o / part_ml: split partials.
 struct AttnArgs {

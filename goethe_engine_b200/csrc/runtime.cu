@@ -4,6 +4,7 @@
 // structs read and written up to min(caller size, own size); negative GC_E_* codes with a per-handle error text; a
 // thread-local gc_open error; block ids checked against the pool (GC_E_ARG); an unknown sid in gc_release accepted.
 // What happens inside a step follows goethe_engine/ref.py (RefModel.token, TorchBackend.step/commit/copy_blocks).
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -95,6 +96,8 @@ struct gc_handle {
   __half *h = nullptr, *q = nullptr, *att = nullptr, *act = nullptr;
   float2 *attn_ml = nullptr;
   int *argmax = nullptr, *pairs = nullptr;
+  int *kerr = nullptr, *kerr_host = nullptr;   // device error word of bounded waits, and its pinned mirror
+  TmaSet tma_h, tma_att, tma_act;               // activation tiles of the tcgen05 GEMMs
   size_t part_cap = 0, attn_parts_cap = 0, commit_cap = 0, pairs_cap = 0;
   uint8_t *plan_dev = nullptr, *plan_host = nullptr;
   size_t plan_cap = 0;
@@ -139,6 +142,7 @@ struct gc_handle {
     for (void *p : allocs) cudaFree(p);
     if (plan_host) cudaFreeHost(plan_host);
     if (tok_host) cudaFreeHost(tok_host);
+    if (kerr_host) cudaFreeHost(kerr_host);
     for (auto e : ev_pool) cudaEventDestroy(e);
     if (st) cudaStreamDestroy(st);
   }
@@ -192,7 +196,7 @@ QWeight relayout(gc_handle *h, int type, int N, int K, RowMap rowmap, const char
   w.K = K;
   w.NT = (N + kBM - 1) / kBM;
   w.KT = (K + kBK - 1) / kBK;
-  size_t tb = tile_bytes(w.type);
+  size_t tb = w.type == kF16 ? tile_bytes(kF16) : tc_tile_bytes(w.type);
   size_t total = tb * w.NT * w.KT;
   std::vector<uint8_t> host(total, 0);
   auto work = [&](int nt0, int nt1) {
@@ -208,19 +212,27 @@ QWeight relayout(gc_handle *h, int type, int N, int K, RowMap rowmap, const char
         for (int kt = 0; kt < w.KT; kt++) {
           uint8_t *tile = host.data() + (static_cast<size_t>(nt) * w.KT + kt) * tb;
           if (type == kQ4_K) {
+            // header (d, dmin, 12 scale bytes) at r*16; quant bytes 32j+16p .. +15 at [stage j][piece p][row r]
             int nsb = K / 256;
             if (kt >= nsb) continue;
             const uint8_t *src = row + (static_cast<size_t>(sr) * nsb + kt) * 144;
             std::memcpy(tile + r * 16, src, 16);
-            std::memcpy(tile + kBM * 16 + r * 128, src + 16, 128);
+            for (int j = 0; j < 4; j++)
+              for (int p = 0; p < 2; p++)
+                std::memcpy(tile + kBM * 16 + (j * 2 + p) * (kBM * 16) + r * 16, src + 16 + 32 * j + 16 * p, 16);
           } else if (type == kQ8_0) {
+            // the 8 block scales at r*16; quants of blocks 2j + p/2, bytes 16(p%2) .. +15 at [stage j][piece p][row r]
             int nb = K / 32;
             for (int i = 0; i < 8; i++) {
               int b = kt * 8 + i;
               if (b >= nb) break;
               const uint8_t *src = row + (static_cast<size_t>(sr) * nb + b) * 34;
-              std::memcpy(tile + (r * 8 + i) * 2, src, 2);
-              std::memcpy(tile + kBM * 16 + r * 256 + i * 32, src + 2, 32);
+              std::memcpy(tile + r * 16 + i * 2, src, 2);
+              int j = i / 2;
+              for (int h2 = 0; h2 < 2; h2++) {
+                int p = (i % 2) * 2 + h2;
+                std::memcpy(tile + kBM * 16 + (j * 4 + p) * (kBM * 16) + r * 16, src + 2 + 16 * h2, 16);
+              }
             }
           } else {
             uint16_t *dst = reinterpret_cast<uint16_t *>(tile) + r * kBK;
@@ -297,8 +309,8 @@ void load_model(gc_handle *h, const std::vector<std::unique_ptr<GgufFile>> &file
   int G = h->H / h->KVH;
   if (h->dh != 64 && h->dh != 128) fail(GC_E_UNSUPPORTED, "head dim %d: this library runs 64 and 128", h->dh);
   if (16 % G) fail(GC_E_UNSUPPORTED, "GQA group %d: must divide 16", G);
-  if (h->d % kBK || (h->H * h->dh) % kBK)
-    fail(GC_E_UNSUPPORTED, "model width %d: must be a multiple of %d", h->d, kBK);
+  if (h->d % kBK || (h->H * h->dh) % kBK || h->d > 8192)
+    fail(GC_E_UNSUPPORTED, "model width %d: must be a multiple of %d, at most 8192", h->d, kBK);
   h->qg_tokens = 16 / G;
   const GgufTensor &emb = tensor(files, "token_embd.weight");
   if (emb.dims.size() < 2 || static_cast<int>(emb.dims[0]) != h->d) fail(GC_E_WEIGHTS, "token_embd.weight shape");
@@ -355,6 +367,33 @@ void load_model(gc_handle *h, const std::vector<std::unique_ptr<GgufFile>> &file
 }  // namespace
 
 namespace {
+
+// TMA tensor maps over an activation buffer [rows, K] f16 row-major: boxes of 64 K (128 B, swizzled) x nt rows
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+void build_tma(TmaSet &ts, void *buf, int rows, int K) {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    ck(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q), "cuTensorMapEncodeTiled");
+    if (!p || q != cudaDriverEntryPointSuccess) fail(GC_E_DEVICE, "cuTensorMapEncodeTiled is not available");
+    fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  const int nts[5] = {16, 32, 64, 128, 256};
+  for (int i = 0; i < 5; i++) {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
+    cuuint32_t box[2] = {64, static_cast<cuuint32_t>(nts[i])};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = fn(&ts.m[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, buf, dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail(GC_E_DEVICE, "tensor map of an activation buffer: CUresult %d", static_cast<int>(r));
+  }
+}
 
 void build_rope(gc_handle *h) {
   // ref.py:31: inv = theta ** (-arange(0, dh, 2) / dh) in float32; angle = inv * p in float32
@@ -503,6 +542,7 @@ GC_API int gc_open(const gc_open_params *p, gc_handle **out) {
     h->dev = dev;
     ck(cudaStreamCreateWithFlags(&h->st, cudaStreamNonBlocking), "stream");
     gemm_init();
+    gemm_tc_init();
     load_model(h, files);
     files.clear();
     h->max_seqs = std::max(1, ncol);
@@ -530,6 +570,12 @@ GC_API int gc_open(const gc_open_params *p, gc_handle **out) {
     h->logits = static_cast<float *>(h->dalloc(static_cast<size_t>(T) * h->vocab * 4, "logits"));
     h->argmax = static_cast<int *>(h->dalloc(static_cast<size_t>(T) * 4, "argmax"));
     ck(cudaMallocHost(&h->tok_host, static_cast<size_t>(T) * 4), "pinned tokens");
+    h->kerr = static_cast<int *>(h->dalloc(16, "error word"));
+    ck(cudaMemset(h->kerr, 0, 16), "error word");
+    ck(cudaMallocHost(&h->kerr_host, 16), "pinned error word");
+    build_tma(h->tma_h, h->h, T, d);
+    build_tma(h->tma_att, h->att, T, h->H * h->dh);
+    build_tma(h->tma_act, h->act, T, Fpad);
     if (!nblk) {
       size_t fr = 0, tot = 0;
       ck(cudaMemGetInfo(&fr, &tot), "cudaMemGetInfo");
@@ -789,6 +835,10 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
     h->step_launches += nk;
   };
   auto gemm_kernels = [](const QWeight &w) { return w.splits > 1 ? 2 : 1; };
+  auto gemm = [&](const QWeight &w, const TmaSet &ts, const __half *act, int rows, const Epi &e) {
+    if (w.type == kF16) launch_gemm(w, act, rows, e, h->part, s);
+    else launch_gemm_tc(w, ts, act, rows, e, h->part, h->kerr, s);
+  };
 
   run(GCK_K_EMBED, 1, [&] { launch_embed(pv, h->emb, h->emb_type, h->emb_row_bytes, h->d, h->x, s); });
   const int wq = (h->H + 2 * h->KVH) * h->dh;
@@ -806,7 +856,7 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
     const Layer &ly = h->layers[l];
     run(GCK_K_NORM, 1, [&] { launch_rmsnorm(h->x, nullptr, T, ly.attn_norm, h->eps, h->d, h->d, h->h, s); });
     run(GCK_K_QKV, gemm_kernels(ly.qkv),
-        [&] { launch_gemm(ly.qkv, h->h, T, Epi{kEpiStore, wq, wq, h->qkv, nullptr}, h->part, s); });
+        [&] { gemm(ly.qkv, h->tma_h, h->h, T, Epi{kEpiStore, wq, wq, h->qkv, nullptr}); });
     uint8_t *kc = h->kc + l * h->layer_bytes, *vc = h->vc + l * h->layer_bytes;
     int8_t *ex = h->exps ? h->exps + l * h->exps_layer : nullptr;
     run(GCK_K_ROPE, 1, [&] {
@@ -818,18 +868,18 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
     run(GCK_K_ATTN, 1, [&] { launch_attention(pv, aa, nw, s); });
     run(GCK_K_COMBINE, 1, [&] { launch_attention_combine(pv, aa, s); });
     run(GCK_K_O, gemm_kernels(ly.o),
-        [&] { launch_gemm(ly.o, h->att, T, Epi{kEpiAdd, h->d, h->d, h->x, nullptr}, h->part, s); });
+        [&] { gemm(ly.o, h->tma_att, h->att, T, Epi{kEpiAdd, h->d, h->d, h->x, nullptr}); });
     run(GCK_K_NORM, 1, [&] { launch_rmsnorm(h->x, nullptr, T, ly.ffn_norm, h->eps, h->d, h->d, h->h, s); });
     run(GCK_K_GATEUP, gemm_kernels(ly.gu), [&] {
-      launch_gemm(ly.gu, h->h, T, Epi{kEpiSwiGLU, h->F, ly.dn.KT * kBK, nullptr, h->act}, h->part, s);
+      gemm(ly.gu, h->tma_h, h->h, T, Epi{kEpiSwiGLU, h->F, ly.dn.KT * kBK, nullptr, h->act});
     });
     run(GCK_K_DOWN, gemm_kernels(ly.dn),
-        [&] { launch_gemm(ly.dn, h->act, T, Epi{kEpiAdd, h->d, h->d, h->x, nullptr}, h->part, s); });
+        [&] { gemm(ly.dn, h->tma_act, h->act, T, Epi{kEpiAdd, h->d, h->d, h->x, nullptr}); });
   }
   if (pv.R > 0) {
     run(GCK_K_NORM, 1, [&] { launch_rmsnorm(h->x, pv.want_tok, pv.R, h->out_norm, h->eps, h->d, h->d, h->h, s); });
     run(GCK_K_HEAD, gemm_kernels(h->head), [&] {
-      launch_gemm(h->head, h->h, pv.R, Epi{kEpiStore, h->vocab, h->vocab, h->logits, nullptr}, h->part, s);
+      gemm(h->head, h->tma_h, h->h, pv.R, Epi{kEpiStore, h->vocab, h->vocab, h->logits, nullptr});
     });
   }
 }
@@ -951,6 +1001,7 @@ GC_API int gc_step(gc_handle *h, const gc_step_in *in, gc_step_out *o) {
       h->step_launches += 1;
     }
     if (f1) cudaEventRecord(f1, h->st);
+    ck(cudaMemcpyAsync(h->kerr_host, h->kerr, 4, cudaMemcpyDeviceToHost, h->st), "error word");
     if (greedy) {
       if (R) {
         ck(cudaMemcpyAsync(h->tok_host, h->argmax, R * 4, cudaMemcpyDeviceToHost, h->st), "tokens");
@@ -966,6 +1017,14 @@ GC_API int gc_step(gc_handle *h, const gc_step_in *in, gc_step_out *o) {
       if (o->size >= offsetof(gc_step_out, logits_dev) + 8) o->logits_dev = reinterpret_cast<uint64_t>(h->logits);
     }
     ck(cudaGetLastError(), "step");
+    if (*h->kerr_host) {
+      int code = *h->kerr_host;
+      *h->kerr_host = 0;
+      ck(cudaMemset(h->kerr, 0, 16), "error word");
+      h->marks.clear();
+      h->ev_used = 0;
+      fail(GC_E_DEVICE, "a kernel's wait ran out of time (code %d); the step's results are invalid", code);
+    }
     collect_stats(h, f0, f1);
     return GC_OK;
   } catch (const GcError &e) {
