@@ -5,13 +5,16 @@
 //
 // One CTA computes a 128-row band of W (the MMA's M) against a tile of NT token rows (the MMA's N) over a fixed range
 // of K (split-K, fixed per weight). Warp roles:
-//   warp 0       producer: one 1-D bulk copy per raw weight tile (128 rows x 256 K, the GGUF blocks as relaid at load)
-//                and one 2-D tensor-map copy per K stage of activations (NT rows x 64 K, 128-byte swizzle);
-//   warp 1       TMEM allocation; one elected thread issues 4 tcgen05.mma (K = 16 each) per 64-K stage and commits
-//                each stage back to the producers;
-//   warps 2-5    dequantize each stage of the raw tile (one weight row per thread; f16 arithmetic with one rounding)
-//                into the UMMA K-major 128-byte-swizzled layout, then read the accumulator with tcgen05.ld and apply
-//                the epilogue (store, residual add, SwiGLU, or the split-K partial).
+//   warp 0       producer of raw weight tiles: one 1-D bulk copy per tile (128 rows x 256 K, the GGUF blocks as relaid
+//                at load), up to 3-4 tiles ahead;
+//   warp 10      producer of activations: one 2-D tensor-map copy per 64-K stage (NT rows, 128-byte swizzle);
+//   warp 1       TMEM allocation; one elected thread issues 4 tcgen05.mma (K = 16 each, weights from TMEM,
+//                activations from shared memory) per 64-K stage and commits each stage back to the producers;
+//   warps 2-9    dequantize each 64-K stage of the raw tile (two threads per weight row; f16 arithmetic, one rounding)
+//                straight into tensor memory (tcgen05.st): the MMA reads its weight operand from TMEM, so shared
+//                memory carries only the raw tiles and the activations;
+//   warps 11-14  epilogue: tcgen05.ld of the accumulator (two buffers, so it overlaps the next unit's MMAs) and the
+//                store, residual add, SwiGLU or split-K partial.
 // Every output element accumulates its K range in one order whatever NT is, so a row's result does not depend on the
 // rest of the batch. Every copy here reads this GPU's global memory into this CTA's own shared memory.
 //
@@ -25,12 +28,11 @@
 namespace gck {
 namespace {
 
-constexpr int kStages = 3;                 // A/B stage ring
-constexpr int kRawSlots = 2;               // raw weight tile ring
-constexpr int kKS = 64;                    // K per stage: one 128-byte swizzle row of f16
-constexpr int kSub = kBK / kKS;            // stages per raw tile (4)
-constexpr int kThreads = 192;
-constexpr int kStageA = kBM * 128;         // 16 KB
+constexpr int kKS = 128;                   // K per stage: two 128-byte swizzle rows of f16 (8 MMAs of K = 16)
+constexpr int kSub = kBK / kKS;            // stages per raw tile (2)
+constexpr int kThreads = 480;              // 15 warps
+constexpr int kDeqWarps = 8;               // warps 2-9: two threads per weight row
+constexpr int kEpiWarp0 = 11;              // warps 11-14: epilogue (TMEM lane quarters 3, 0, 1, 2)
 constexpr unsigned long long kTimeoutNs = 2000000000ull;
 
 enum ErrCode { kErrRawFull = 1, kErrRawEmpty, kErrStageEmpty, kErrAFull, kErrBFull, kErrAcc };
@@ -59,9 +61,11 @@ GCK_DEV void mbar_arrive(uint64_t *b) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(b)) : "memory");
 }
 GCK_DEV bool mbar_try(uint64_t *b, uint32_t parity) {
+  // suspends the thread (up to ~1 us) until the phase completes instead of returning at once, so waiting warps leave
+  // the issue slots to the dequantizing warps
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 1000;\n selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
       : "r"(smem_u32(b)), "r"(parity)
       : "memory");
@@ -72,17 +76,30 @@ GCK_DEV unsigned long long now_ns() {
   asm volatile("mov.u64 %0, %globaltimer;\n" : "=l"(t));
   return t;
 }
-// bounded wait for the phase of the given parity; false (and the error word set) on timeout
+// Bounded wait for the phase of the given parity; false (and the error word set) on timeout. Each try suspends the
+// thread until the phase completes (or ~1 us); the global timer is read every 64 tries.
 GCK_DEV bool mbar_wait(uint64_t *b, uint32_t parity, int *err, int code) {
   if (mbar_try(b, parity)) return true;
-  unsigned long long t0 = now_ns();
-  while (true) {
+  const unsigned long long t0 = now_ns();
+  for (uint32_t n = 1;; n++) {
     if (mbar_try(b, parity)) return true;
-    if (now_ns() - t0 > kTimeoutNs) {
+    if ((n & 63u) == 0 && now_ns() - t0 > kTimeoutNs) {
       atomicCAS(err, 0, code);
       return false;
     }
-    if (*reinterpret_cast<volatile int *>(err)) return false;   // another CTA already failed: give up early
+  }
+}
+// the same for waits expected to be long (the epilogue waiting for a unit's accumulator): back off between tries
+GCK_DEV bool mbar_wait_sleep(uint64_t *b, uint32_t parity, int *err, int code) {
+  if (mbar_try(b, parity)) return true;
+  const unsigned long long t0 = now_ns();
+  for (uint32_t n = 1;; n++) {
+    __nanosleep(256);
+    if (mbar_try(b, parity)) return true;
+    if ((n & 63u) == 0 && now_ns() - t0 > kTimeoutNs) {
+      atomicCAS(err, 0, code);
+      return false;
+    }
   }
 }
 
@@ -167,9 +184,10 @@ GCK_DEV Q4kScales q4k_scales(uint32_t w0, uint32_t w1, uint32_t w2) {
   return q;
 }
 
-// Q4_K: stage j of row r -> 64 f16 into the swizzled A row
-GCK_DEV void dequant_q4k(const uint8_t *raw, int r, int j, uint32_t d_dm, const Q4kScales &qs, uint8_t *arow, int sw) {
-  // sub-blocks 2j (low nibbles) and 2j+1 (high nibbles) of quant bytes 32j .. 32j+31
+// Q4_K: stage j (64 K) of row r, half h: quant bytes 16h .. 16h+15 of the stage's 32 (one piece, read by this thread
+// only). Low nibbles are k = 16h .. 16h+15 (sub-block 2j), high nibbles k = 32 + 16h .. (sub-block 2j+1).
+// out[0..7] = TMEM columns 8h .. 8h+7, out[8..15] = columns 16 + 8h .. (two f16 per column, lower k in the low half).
+GCK_DEV void dequant_q4k(const uint8_t *raw, int r, int j, int h, uint32_t d_dm, const Q4kScales &qs, uint32_t (&out)[16]) {
   const uint32_t scw = j < 2 ? qs.sc_lo : qs.sc_hi, mw = j < 2 ? qs.m_lo : qs.m_hi;
   const int sh = 16 * (j & 1);
   const int sc0 = (scw >> sh) & 0xFF, sc1 = (scw >> (sh + 8)) & 0xFF;
@@ -181,270 +199,368 @@ GCK_DEV void dequant_q4k(const uint8_t *raw, int r, int j, uint32_t d_dm, const 
   const uint32_t S0 = *reinterpret_cast<uint32_t *>(&s0), O0 = *reinterpret_cast<uint32_t *>(&o0);
   const uint32_t S1 = *reinterpret_cast<uint32_t *>(&s1), O1 = *reinterpret_cast<uint32_t *>(&o1);
   const uint32_t K1024 = 0x64006400u;
+  const uint4 q = *reinterpret_cast<const uint4 *>(raw + kBM * 16 + (j * 2 + h) * (kBM * 16) + r * 16);
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-  for (int p = 0; p < 2; p++) {
-    uint4 q = *reinterpret_cast<const uint4 *>(raw + kBM * 16 + (j * 2 + p) * (kBM * 16) + r * 16);
-    uint32_t w[4] = {q.x, q.y, q.z, q.w};
-    uint32_t lo[8], hi[8];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-      uint32_t l4 = w[i] & 0x0F0F0F0Fu, h4 = (w[i] >> 4) & 0x0F0F0F0Fu;
-      uint32_t a0, a1, b0, b1;
-      bytes_to_h2(l4, a0, a1);
-      bytes_to_h2(h4, b0, b1);
-      lo[2 * i] = hfma2_u(hsub2_u(a0, K1024), S0, O0);
-      lo[2 * i + 1] = hfma2_u(hsub2_u(a1, K1024), S0, O0);
-      hi[2 * i] = hfma2_u(hsub2_u(b0, K1024), S1, O1);
-      hi[2 * i + 1] = hfma2_u(hsub2_u(b1, K1024), S1, O1);
-    }
-    // piece p holds bytes 16p .. 16p+15: k = 16p .. 16p+15 (low) and 32 + 16p .. (high): chunks 2p, 2p+1, 4+2p, 5+2p
-    int c0 = 2 * p, c1 = 4 + 2 * p;
-    *reinterpret_cast<uint4 *>(arow + (((c0) ^ sw) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-    *reinterpret_cast<uint4 *>(arow + (((c0 + 1) ^ sw) << 4)) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
-    *reinterpret_cast<uint4 *>(arow + (((c1) ^ sw) << 4)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-    *reinterpret_cast<uint4 *>(arow + (((c1 + 1) ^ sw) << 4)) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+  for (int i = 0; i < 4; i++) {
+    uint32_t a0, a1, b0, b1;
+    bytes_to_h2(w[i] & 0x0F0F0F0Fu, a0, a1);
+    bytes_to_h2((w[i] >> 4) & 0x0F0F0F0Fu, b0, b1);
+    out[2 * i] = hfma2_u(hsub2_u(a0, K1024), S0, O0);
+    out[2 * i + 1] = hfma2_u(hsub2_u(a1, K1024), S0, O0);
+    out[8 + 2 * i] = hfma2_u(hsub2_u(b0, K1024), S1, O1);
+    out[8 + 2 * i + 1] = hfma2_u(hsub2_u(b1, K1024), S1, O1);
   }
 }
 
-// Q8_0: stage j of row r (blocks 2j, 2j+1) -> 64 f16
-GCK_DEV void dequant_q80(const uint8_t *raw, int r, int j, const uint4 &hdr, uint8_t *arow, int sw) {
+// Q8_0: stage j of row r, half h: block 2j + h (k = 32h .. 32h+31) -> TMEM columns 16h .. 16h+15
+GCK_DEV void dequant_q80(const uint8_t *raw, int r, int j, int h, const uint4 &hdr, uint32_t (&out)[16]) {
   const uint32_t K1152 = 0x64806480u;   // 1024 + 128
-  // the row's 8 block scales: d[2j] and d[2j+1] are the two halves of header word j
   const uint32_t dw = j == 0 ? hdr.x : j == 1 ? hdr.y : j == 2 ? hdr.z : hdr.w;
-  const uint32_t D0 = (dw & 0xFFFFu) * 0x10001u, D1 = (dw >> 16) * 0x10001u;
+  const uint32_t D = (h ? (dw >> 16) : (dw & 0xFFFFu)) * 0x10001u;
 #pragma unroll
-  for (int p = 0; p < 4; p++) {
-    uint4 q = *reinterpret_cast<const uint4 *>(raw + kBM * 16 + (j * 4 + p) * (kBM * 16) + r * 16);
-    uint32_t w[4] = {q.x, q.y, q.z, q.w};
-    uint32_t o[8];
-    const uint32_t D = p < 2 ? D0 : D1;
+  for (int pp = 0; pp < 2; pp++) {
+    const uint4 q = *reinterpret_cast<const uint4 *>(raw + kBM * 16 + (j * 4 + 2 * h + pp) * (kBM * 16) + r * 16);
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
     for (int i = 0; i < 4; i++) {
       uint32_t a0, a1;
       bytes_to_h2(w[i] ^ 0x80808080u, a0, a1);
-      o[2 * i] = hmul2_u(hsub2_u(a0, K1152), D);
-      o[2 * i + 1] = hmul2_u(hsub2_u(a1, K1152), D);
+      out[8 * pp + 2 * i] = hmul2_u(hsub2_u(a0, K1152), D);
+      out[8 * pp + 2 * i + 1] = hmul2_u(hsub2_u(a1, K1152), D);
     }
-    *reinterpret_cast<uint4 *>(arow + (((2 * p) ^ sw) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
-    *reinterpret_cast<uint4 *>(arow + (((2 * p + 1) ^ sw) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
   }
 }
 
-template <int NT>
+GCK_DEV void tmem_st8(uint32_t taddr, const uint32_t *v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};\n" ::"r"(taddr), "r"(v[0]), "r"(v[1]),
+               "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+GCK_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+GCK_DEV void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(
+          tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// One ring of R stages. Stage s: 64 TMEM columns of dequantized weights (128 rows x 128 K, two f16 per column) after
+// the ACC accumulator buffers, and two shared-memory activation tiles of NT rows x 64 K (128-byte swizzle). Raw
+// weight tiles (HBM lookahead: 4 Q4_K = 72 KB or 3 Q8_0 = 102 KB per SM) have their own ring.
+template <int TYPE, int NT>
 struct Shape {
-  static constexpr int STAGE_B = NT * 128;
+  static constexpr int STAGE_B = 2 * NT * 128;
   static constexpr int NCOLS = NT <= 32 ? 32 : NT <= 64 ? 64 : NT <= 128 ? 128 : 256;
+  static constexpr int ACC = NT <= 128 ? 2 : 1;
+  static constexpr int RAW = TYPE == kQ4_K ? 4 : (NT >= 256 ? 2 : 3);
+  static constexpr int R_TMEM = (512 - ACC * NCOLS) / 64;
+  static constexpr int R_SMEM = (216 * 1024 - RAW * TileFmt<TYPE>::BYTES) / STAGE_B;
+  static constexpr int R0 = R_TMEM < R_SMEM ? R_TMEM : R_SMEM;
+  static constexpr int R = R0 > 8 ? 8 : R0;
+  static_assert(R >= 2, "stage ring too shallow");
 };
+
+constexpr int kXchg = 64 * 17 * 4;         // SwiGLU hand-off: 64 rows x 16 columns (+1 pad) of f32
 
 template <int TYPE, int NT>
 constexpr int smem_total() {
-  return 1024 + kStages * kStageA + kStages * Shape<NT>::STAGE_B + kRawSlots * TileFmt<TYPE>::BYTES + 256;
+  using S = Shape<TYPE, NT>;
+  // at least 120 KB: one CTA per SM, since each takes all 512 TMEM columns
+  constexpr int need = 1024 + S::R * S::STAGE_B + S::RAW * TileFmt<TYPE>::BYTES + kXchg + 512;
+  return need > 120 * 1024 ? need : 120 * 1024;
+}
+
+// Work unit w (0 .. units-1) = (token tile, weight tile, K split); a CTA takes units blockIdx.x, + gridDim.x, ...
+struct Unit {
+  int nt, split, tt, kt0, per;
+};
+GCK_DEV Unit unit_of(int w, int NTW, int KT, int splits) {
+  Unit u;
+  u.tt = w / (NTW * splits);
+  int rem = w % (NTW * splits);
+  u.nt = rem / splits;
+  u.split = rem % splits;
+  const int base = KT / splits, extra = KT % splits;   // the first KT % splits splits take one more raw tile
+  u.per = base + (u.split < extra ? 1 : 0);
+  u.kt0 = u.split * base + min(u.split, extra);
+  return u;
 }
 
 template <int TYPE, int NT>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_tc_kernel(const uint8_t *__restrict__ W, int KT, int splits, const __grid_constant__ CUtensorMap tmap, int T,
-                   Epi epi, float *part, int Npad, int *err) {
+    gemm_tc_kernel(const uint8_t *__restrict__ W, int NTW, int KT, int splits, int units,
+                   const __grid_constant__ CUtensorMap tmap, int T, Epi epi, float *part, int Npad, int *err) {
   using F = TileFmt<TYPE>;
-  using S = Shape<NT>;
+  using S = Shape<TYPE, NT>;
+  constexpr int RS = S::RAW, SR = S::R, ACC = S::ACC;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t *sA = smem;
-  uint8_t *sB = sA + kStages * kStageA;
-  uint8_t *sRaw = sB + kStages * S::STAGE_B;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(sRaw + kRawSlots * F::BYTES);
-  uint64_t *raw_full = bars, *raw_empty = bars + kRawSlots, *a_full = bars + 2 * kRawSlots;
-  uint64_t *b_full = a_full + kStages, *st_empty = b_full + kStages, *acc_full = st_empty + kStages;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
-
-  const int nt = blockIdx.x, split = blockIdx.y, t0 = blockIdx.z * NT;
-  const int per = KT / splits, kt0 = split * per, nstage = per * kSub;
+  uint8_t *sB = smem;
+  uint8_t *sRaw = sB + SR * S::STAGE_B;
+  float *xchg = reinterpret_cast<float *>(sRaw + RS * F::BYTES);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(xchg) + kXchg);
+  uint64_t *raw_full = bars, *raw_empty = raw_full + RS;
+  uint64_t *a_full = raw_empty + RS, *st_empty = a_full + SR, *b_full = st_empty + SR;
+  uint64_t *acc_full = b_full + SR, *acc_empty = acc_full + 2, *mma_done = acc_empty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kRawSlots; i++) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], 4); }
-    for (int i = 0; i < kStages; i++) { mbar_init(&a_full[i], 4); mbar_init(&b_full[i], 1); mbar_init(&st_empty[i], 1); }
-    mbar_init(acc_full, 1);
+    for (int i = 0; i < RS; i++) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], kDeqWarps); }
+    for (int i = 0; i < SR; i++) { mbar_init(&a_full[i], kDeqWarps); mbar_init(&st_empty[i], 1); mbar_init(&b_full[i], 1); }
+    for (int i = 0; i < 2; i++) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
+    mbar_init(mma_done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     fence_async_smem();
   }
-  if (warp == 1) {
+  if (warp == 1) {   // all 512 columns: ACC accumulator buffers, then the weight stages (one CTA per SM)
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
-                 "r"(S::NCOLS));
+                 "r"(512));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem_a = tmem + ACC * S::NCOLS;   // weight stage s at columns tmem_a + 64 * s
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---- producer
-      int issued_raw = 0, issued_b = 0;
+      // ---- raw weight tiles: one bulk copy each, up to RS tiles ahead, across unit boundaries
+      long c = 0;
       bool ok = true;
-      for (int u = 0; u < per && ok; u++) {
-        int rs = u % kRawSlots;
-        ok = mbar_wait(&raw_empty[rs], ((u / kRawSlots) & 1) ^ 1, err, kErrRawEmpty);
-        if (!ok) break;
-        mbar_expect_tx(&raw_full[rs], F::BYTES);
-        bulk_g2s(sRaw + rs * F::BYTES, W + (static_cast<size_t>(nt) * KT + kt0 + u) * F::BYTES, F::BYTES, &raw_full[rs]);
-        issued_raw++;
-        for (int j = 0; j < kSub; j++) {
-          int i = u * kSub + j, s = i % kStages;
-          ok = mbar_wait(&st_empty[s], ((i / kStages) & 1) ^ 1, err, kErrStageEmpty);
-          if (!ok) break;
-          mbar_expect_tx(&b_full[s], S::STAGE_B);
-          tma_2d(sB + s * S::STAGE_B, &tmap, (kt0 + u) * kBK + j * kKS, t0, &b_full[s]);
-          issued_b++;
+      for (int w = blockIdx.x; w < units && ok; w += gridDim.x) {
+        const Unit un = unit_of(w, NTW, KT, splits);
+        for (int u = 0; u < un.per; u++, c++) {
+          const int rs = static_cast<int>(c % RS);
+          if (!(ok = mbar_wait(&raw_empty[rs], static_cast<uint32_t>((c / RS) & 1) ^ 1, err, kErrRawEmpty))) break;
+          mbar_expect_tx(&raw_full[rs], F::BYTES);
+          bulk_g2s(sRaw + rs * F::BYTES, W + (static_cast<size_t>(un.nt) * KT + un.kt0 + u) * F::BYTES, F::BYTES,
+                   &raw_full[rs]);
         }
       }
-      // drain: every copy issued has landed before the CTA may exit (bounded)
-      for (int u = 0; u < issued_raw; u++) {
-        if (u + kRawSlots < issued_raw) continue;
-        mbar_wait(&raw_full[u % kRawSlots], (u / kRawSlots) & 1, err, kErrRawFull);
+      // every issued copy has landed before the CTA may exit (the last phase of each slot; bounded)
+      for (long i = c > RS ? c - RS : 0; i < c; i++) mbar_wait(&raw_full[i % RS], static_cast<uint32_t>((i / RS) & 1), err, kErrRawFull);
+    }
+  } else if (warp == 10) {
+    if (lane == 0) {
+      // ---- activation stages: two tensor-map copies (64 K each) per 128-K stage, up to SR stages ahead
+      long c = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < units && ok; w += gridDim.x) {
+        const Unit un = unit_of(w, NTW, KT, splits);
+        for (int i = 0; i < un.per * kSub; i++, c++) {
+          const int s = static_cast<int>(c % SR);
+          if (!(ok = mbar_wait(&st_empty[s], static_cast<uint32_t>((c / SR) & 1) ^ 1, err, kErrStageEmpty))) break;
+          mbar_expect_tx(&b_full[s], S::STAGE_B);
+          const int x = (un.kt0 + i / kSub) * kBK + (i % kSub) * kKS;
+          tma_2d(sB + s * S::STAGE_B, &tmap, x, un.tt * NT, &b_full[s]);
+          tma_2d(sB + s * S::STAGE_B + NT * 128, &tmap, x + 64, un.tt * NT, &b_full[s]);
+        }
       }
-      for (int i = (issued_b > kStages ? issued_b - kStages : 0); i < issued_b; i++)
-        mbar_wait(&b_full[i % kStages], (i / kStages) & 1, err, kErrBFull);
+      for (long i = c > SR ? c - SR : 0; i < c; i++) mbar_wait(&b_full[i % SR], static_cast<uint32_t>((i / SR) & 1), err, kErrBFull);
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      // ---- MMA issuer
+      // ---- MMA issuer: accumulator buffer (local unit index) % 2
       const uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(NT >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
-      for (int i = 0; i < nstage; i++) {
-        int s = i % kStages;
-        uint32_t ph = (i / kStages) & 1;
-        if (!mbar_wait(&a_full[s], ph, err, kErrAFull)) break;
-        if (!mbar_wait(&b_full[s], ph, err, kErrBFull)) break;
+      long ca = 0;
+      int lu = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < units && ok; w += gridDim.x, lu++) {
+        const Unit un = unit_of(w, NTW, KT, splits);
+        const int ab = ACC == 2 ? (lu & 1) : 0;
+        const uint32_t ph = ACC == 2 ? static_cast<uint32_t>((lu >> 1) & 1) : static_cast<uint32_t>(lu & 1);
+        if (!(ok = mbar_wait(&acc_empty[ab], ph ^ 1, err, kErrAcc))) break;
         tc_fence_after();
-        uint64_t ad = umma_desc(sA + s * kStageA), bd = umma_desc(sB + s * S::STAGE_B);
+        const uint32_t dt = tmem + ab * S::NCOLS;
+        for (int i = 0; i < un.per * kSub; i++, ca++) {
+          const int s = static_cast<int>(ca % SR);
+          // a_full covers both operands: the dequant warps signal it only after the stage's activations landed
+          if (!(ok = mbar_wait(&a_full[s], static_cast<uint32_t>((ca / SR) & 1), err, kErrAFull))) break;
+          tc_fence_after();
+          const uint64_t bd0 = umma_desc(sB + s * S::STAGE_B), bd1 = umma_desc(sB + s * S::STAGE_B + NT * 128);
+          const uint32_t at = tmem_a + 64 * s;
 #pragma unroll
-        for (int k = 0; k < kKS / 16; k++) umma_f16(tmem, ad + 2 * k, bd + 2 * k, idesc, (i | k) != 0);
-        umma_commit(&st_empty[s]);
+          for (int k = 0; k < kKS / 16; k++)
+            umma_f16_ts(dt, at + 8 * k, (k < 4 ? bd0 : bd1) + 2 * (k & 3), idesc, (i | k) != 0);
+          umma_commit(&st_empty[s]);
+        }
+        umma_commit(&acc_full[ab]);   // arrives once every MMA of this unit has completed
       }
-      umma_commit(acc_full);   // arrives once every MMA issued above has completed
+      // completes once every MMA issued above has: the exit below never frees tensor memory still being written
+      umma_commit(mma_done);
     }
-  } else {
-    // ---- dequant (one weight row per thread) then epilogue
-    const int q = warp & 3;                 // TMEM lane quarter of this warp
-    const int r = q * 32 + lane;            // weight row in the tile = accumulator lane
-    const int sw = r & 7;
+  } else if (warp < kEpiWarp0) {
+    // ---- dequant: two threads per weight row, one 32-element half each, into the TMEM stage ring. Software
+    // pipelined: stage i's TMEM stores are in flight while stage i+1 is computed, and only then waited for and
+    // signalled, so the store latency hides behind arithmetic.
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const int hsel = (warp - 2) >> 2;
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    long cr = 0, ca = 0;
+    int prev = -1;              // stage slot whose stores are in flight, not yet signalled
     bool ok = true;
-    for (int u = 0; u < per && ok; u++) {
-      int rs = u % kRawSlots;
-      ok = mbar_wait(&raw_full[rs], (u / kRawSlots) & 1, err, kErrRawFull);
-      if (!ok) break;
-      const uint8_t *raw = sRaw + rs * F::BYTES;
-      const uint4 hdr = *reinterpret_cast<const uint4 *>(raw + r * 16);
-      const Q4kScales qsc = q4k_scales(hdr.y, hdr.z, hdr.w);
-      for (int j = 0; j < kSub; j++) {
-        int i = u * kSub + j, s = i % kStages;
-        ok = mbar_wait(&st_empty[s], ((i / kStages) & 1) ^ 1, err, kErrStageEmpty);
-        if (!ok) break;
-        uint8_t *arow = sA + s * kStageA + r * 128;
-        if (TYPE == kQ4_K) dequant_q4k(raw, r, j, hdr.x, qsc, arow, sw);
-        else dequant_q80(raw, r, j, hdr, arow, sw);
-        fence_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&a_full[s]);
-      }
+    long prev_c = 0;
+    auto signal_prev = [&]() {
+      if (prev < 0) return;
+      tmem_st_wait();
+      tc_fence_before();
+      // the stage's activation tiles must have landed too: then one barrier tells the MMA thread both are ready
+      if (!mbar_wait(&b_full[prev], static_cast<uint32_t>((prev_c / SR) & 1), err, kErrBFull)) ok = false;
       __syncwarp();
-      if (lane == 0) mbar_arrive(&raw_empty[rs]);
-    }
-    // epilogue: the accumulator's lane r = weight row nt*128 + r, column c = token t0 + c
-    bool done = mbar_wait(acc_full, 0, err, kErrAcc);
-    tc_fence_after();
-    const bool good = done && ok;
-    const int row = nt * kBM + r;
-    const uint32_t tbase = tmem + (static_cast<uint32_t>(q * 32) << 16);
-    if (splits > 1) {
-      if (good) {
-        float *p = part + static_cast<size_t>(split) * T * Npad;
-        for (int c0 = 0; c0 < NT; c0 += 16) {
-          uint32_t v[16];
-          tmem_ld16(tbase + c0, v);
+      if (lane == 0) mbar_arrive(&a_full[prev]);
+      prev = -1;
+    };
+    for (int w = blockIdx.x; w < units && ok; w += gridDim.x) {
+      const Unit un = unit_of(w, NTW, KT, splits);
+      for (int u = 0; u < un.per && ok; u++, cr++) {
+        const int rs = static_cast<int>(cr % RS);
+        if (!(ok = mbar_wait(&raw_full[rs], static_cast<uint32_t>((cr / RS) & 1), err, kErrRawFull))) break;
+        const uint8_t *raw = sRaw + rs * F::BYTES;
+        const uint4 hdr = *reinterpret_cast<const uint4 *>(raw + r * 16);
+        const Q4kScales qsc = q4k_scales(hdr.y, hdr.z, hdr.w);
+        for (int j = 0; j < kSub; j++, ca++) {
+          const int s = static_cast<int>(ca % SR);
+          // 128 K = two 64-K halves (quarters 2j, 2j+1 of the raw tile) -> 4 runs of 8 TMEM columns
+          uint32_t v0[16], v1[16];
+          if (TYPE == kQ4_K) {
+            dequant_q4k(raw, r, 2 * j, hsel, hdr.x, qsc, v0);
+            dequant_q4k(raw, r, 2 * j + 1, hsel, hdr.x, qsc, v1);
+          } else {
+            dequant_q80(raw, r, 2 * j, hsel, hdr, v0);
+            dequant_q80(raw, r, 2 * j + 1, hsel, hdr, v1);
+          }
+          if (j == kSub - 1) {       // every byte of this raw tile is in registers: release the slot
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&raw_empty[rs]);
+          }
+          signal_prev();
+          if (!(ok = mbar_wait(&st_empty[s], static_cast<uint32_t>((ca / SR) & 1) ^ 1, err, kErrStageEmpty))) break;
+          tc_fence_after();
+          const uint32_t col = tmem_a + 64 * s + lane_base;
 #pragma unroll
-          for (int c = 0; c < 16; c++) {
-            int t = t0 + c0 + c;
-            if (t < T) p[static_cast<size_t>(t) * Npad + row] = __uint_as_float(v[c]);
+          for (int t = 0; t < 2; t++) {
+            const uint32_t *v = t ? v1 : v0;
+            const uint32_t c0 = col + 32 * t;
+            if (TYPE == kQ4_K) {
+              tmem_st8(c0 + 8 * hsel, v);
+              tmem_st8(c0 + 16 + 8 * hsel, v + 8);
+            } else {
+              tmem_st8(c0 + 16 * hsel, v);
+              tmem_st8(c0 + 16 * hsel + 8, v + 8);
+            }
+          }
+          prev = s;
+          prev_c = ca;
+        }
+      }
+    }
+    signal_prev();
+  } else {
+    // ---- epilogue: TMEM lane quarter q = weight rows 32q .. 32q+31 of the tile
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    int lu = 0;
+    for (int w = blockIdx.x; w < units; w += gridDim.x, lu++) {
+      const Unit un = unit_of(w, NTW, KT, splits);
+      const int ab = ACC == 2 ? (lu & 1) : 0;
+      const uint32_t ph = ACC == 2 ? static_cast<uint32_t>((lu >> 1) & 1) : static_cast<uint32_t>(lu & 1);
+      const bool good = mbar_wait_sleep(&acc_full[ab], ph, err, kErrAcc);
+      tc_fence_after();
+      const uint32_t tbase = tmem + ab * S::NCOLS + (static_cast<uint32_t>(q * 32) << 16);
+      const int row = un.nt * kBM + r, t0 = un.tt * NT;
+      if (splits > 1) {
+        if (good) {
+          float *p = part + static_cast<size_t>(un.split) * T * Npad;
+          for (int c0 = 0; c0 < NT; c0 += 16) {
+            uint32_t v[16];
+            tmem_ld16(tbase + c0, v);
+#pragma unroll
+            for (int c = 0; c < 16; c++) {
+              int t = t0 + c0 + c;
+              if (t < T) p[static_cast<size_t>(t) * Npad + row] = __uint_as_float(v[c]);
+            }
           }
         }
-      }
-    } else if (epi.kind == kEpiSwiGLU) {
-      // rows 64..127 (up) hand their values to rows 0..63 (gate) through shared memory (the finished stage ring);
-      // all four warps reach the named barrier whatever happened before it
-      float *xu = reinterpret_cast<float *>(sA);      // [64][NT + 1]
-      if (good && r >= 64) {
+      } else if (epi.kind == kEpiSwiGLU) {
+        // rows 64..127 (up) hand 16 columns at a time to rows 0..63 (gate); all four warps reach every barrier
+        const int f = un.nt * 64 + r;
         for (int c0 = 0; c0 < NT; c0 += 16) {
           uint32_t v[16];
-          tmem_ld16(tbase + c0, v);
+          if (good) tmem_ld16(tbase + c0, v);
+          if (good && r >= 64) {
 #pragma unroll
-          for (int c = 0; c < 16; c++) xu[(r - 64) * (NT + 1) + c0 + c] = __uint_as_float(v[c]);
+            for (int c = 0; c < 16; c++) xchg[(r - 64) * 17 + c] = __uint_as_float(v[c]);
+          }
+          asm volatile("bar.sync 1, 128;\n" ::: "memory");
+          if (good && r < 64) {
+#pragma unroll
+            for (int c = 0; c < 16; c++) {
+              int t = t0 + c0 + c;
+              if (t < T && f < epi.n) {
+                float g = __uint_as_float(v[c]), uu = xchg[r * 17 + c];
+                epi.out_h[static_cast<size_t>(t) * epi.ld + f] = __float2half_rn(g / (1.f + expf(-g)) * uu);
+              }
+            }
+          }
+          asm volatile("bar.sync 1, 128;\n" ::: "memory");
         }
-      }
-      asm volatile("bar.sync 1, 128;\n" ::: "memory");
-      if (good && r < 64) {
-        const int f = nt * 64 + r;
+      } else if (good) {
         for (int c0 = 0; c0 < NT; c0 += 16) {
           uint32_t v[16];
           tmem_ld16(tbase + c0, v);
 #pragma unroll
           for (int c = 0; c < 16; c++) {
             int t = t0 + c0 + c;
-            if (t < T && f < epi.n) {
-              float g = __uint_as_float(v[c]), uu = xu[r * (NT + 1) + c0 + c];
-              epi.out_h[static_cast<size_t>(t) * epi.ld + f] = __float2half_rn(g / (1.f + expf(-g)) * uu);
+            if (t < T && row < epi.n) {
+              float *o = epi.out_f + static_cast<size_t>(t) * epi.ld + row;
+              if (epi.kind == kEpiAdd) *o += __uint_as_float(v[c]);
+              else *o = __uint_as_float(v[c]);
             }
           }
         }
       }
-    } else if (good) {
-      for (int c0 = 0; c0 < NT; c0 += 16) {
-        uint32_t v[16];
-        tmem_ld16(tbase + c0, v);
-#pragma unroll
-        for (int c = 0; c < 16; c++) {
-          int t = t0 + c0 + c;
-          if (t < T && row < epi.n) {
-            float *o = epi.out_f + static_cast<size_t>(t) * epi.ld + row;
-            if (epi.kind == kEpiAdd) *o += __uint_as_float(v[c]);
-            else *o = __uint_as_float(v[c]);
-          }
-        }
-      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[ab]);
+      if (!good) break;
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
-    // no MMA may still write the accumulator when it is freed (bounded; returns at once after a normal run)
-    if (lane == 0) mbar_wait(acc_full, 0, err, kErrAcc);
+    // no MMA may still write the accumulators when they are freed (bounded; returns at once after a normal run)
+    if (lane == 0) mbar_wait(mma_done, 0, err, kErrAcc);
     __syncwarp();
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(S::NCOLS));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(512));
   }
 }
 
 template <int TYPE, int NT>
-void launch_nt(const QWeight &w, const CUtensorMap *maps, const __half *, int T, const Epi &epi, float *part, int *err,
+void launch_nt(const QWeight &w, const CUtensorMap *map, int T, const Epi &epi, float *part, int *err, int sms,
                cudaStream_t s) {
-  (void)maps;
-  dim3 grid(w.NT, w.splits, (T + NT - 1) / NT);
-  gemm_tc_kernel<TYPE, NT><<<grid, kThreads, smem_total<TYPE, NT>(), s>>>(w.data, w.KT, w.splits, *maps, T, epi, part,
-                                                                          w.NT * kBM, err);
+  const int units = w.NT * w.splits * ((T + NT - 1) / NT);
+  const int grid = units < sms ? units : sms;
+  gemm_tc_kernel<TYPE, NT><<<grid, kThreads, smem_total<TYPE, NT>(), s>>>(w.data, w.NT, w.KT, w.splits, units, *map, T,
+                                                                          epi, part, w.NT * kBM, err);
 }
 
 template <int TYPE>
-void launch_type(const QWeight &w, const TmaSet &ts, const __half *act, int T, const Epi &epi, float *part, int *err,
+void launch_type(const QWeight &w, const TmaSet &ts, int T, const Epi &epi, float *part, int *err, int sms,
                  cudaStream_t s) {
   int nt = tc_token_tile(T);
   const CUtensorMap *m = ts.map(nt);
   switch (nt) {
-    case 16: launch_nt<TYPE, 16>(w, m, act, T, epi, part, err, s); break;
-    case 32: launch_nt<TYPE, 32>(w, m, act, T, epi, part, err, s); break;
-    case 64: launch_nt<TYPE, 64>(w, m, act, T, epi, part, err, s); break;
-    case 128: launch_nt<TYPE, 128>(w, m, act, T, epi, part, err, s); break;
-    default: launch_nt<TYPE, 256>(w, m, act, T, epi, part, err, s); break;
+    case 16: launch_nt<TYPE, 16>(w, m, T, epi, part, err, sms, s); break;
+    case 32: launch_nt<TYPE, 32>(w, m, T, epi, part, err, sms, s); break;
+    case 64: launch_nt<TYPE, 64>(w, m, T, epi, part, err, sms, s); break;
+    case 128: launch_nt<TYPE, 128>(w, m, T, epi, part, err, sms, s); break;
+    default: launch_nt<TYPE, 256>(w, m, T, epi, part, err, sms, s); break;
   }
 }
 
@@ -470,11 +586,11 @@ void gemm_tc_init() {
 
 size_t tc_tile_bytes(int type) { return type == kQ4_K ? TileFmt<kQ4_K>::BYTES : TileFmt<kQ8_0>::BYTES; }
 
-void launch_gemm_tc(const QWeight &w, const TmaSet &ts, const __half *act, int T, const Epi &epi, float *part,
-                    int *err, cudaStream_t s) {
+void launch_gemm_tc(const QWeight &w, const TmaSet &ts, int T, const Epi &epi, float *part, int *err, int sms,
+                    cudaStream_t s) {
   if (T <= 0) return;
-  if (w.type == kQ4_K) launch_type<kQ4_K>(w, ts, act, T, epi, part, err, s);
-  else launch_type<kQ8_0>(w, ts, act, T, epi, part, err, s);
+  if (w.type == kQ4_K) launch_type<kQ4_K>(w, ts, T, epi, part, err, sms, s);
+  else launch_type<kQ8_0>(w, ts, T, epi, part, err, sms, s);
   if (w.splits > 1) launch_splitk_reduce(part, w.splits, T, w.NT * kBM, epi, s);
 }
 

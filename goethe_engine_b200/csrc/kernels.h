@@ -72,8 +72,8 @@ struct TmaSet {            // tensor maps over one activation buffer [rows, K] f
 int tc_token_tile(int T);
 size_t tc_tile_bytes(int type);
 void gemm_tc_init();      // once per device
-void launch_gemm_tc(const QWeight &w, const TmaSet &ts, const __half *act, int T, const Epi &epi, float *part,
-                    int *err, cudaStream_t s);
+void launch_gemm_tc(const QWeight &w, const TmaSet &ts, int T, const Epi &epi, float *part, int *err, int sms,
+                    cudaStream_t s);
 
 // Paged attention over the plan's work list: q [T, H, dh] f16 -> out [T, H, dh] f16. part_o / part_ml: split partials.
 struct AttnArgs {

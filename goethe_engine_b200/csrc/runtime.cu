@@ -71,7 +71,7 @@ size_t vbytes(const std::vector<T> &v) { return v.size() * sizeof(T); }
 }  // namespace
 
 struct gc_handle {
-  int dev = 0;
+  int dev = 0, sms = 148;
   cudaStream_t st = nullptr;
   std::string err;
   // model
@@ -257,12 +257,27 @@ QWeight relayout(gc_handle *h, int type, int N, int K, RowMap rowmap, const char
   uint8_t *dev = static_cast<uint8_t *>(h->dalloc(total, what));
   ck(cudaMemcpy(dev, host.data(), total, cudaMemcpyHostToDevice), what);
   w.data = dev;
-  // split-K: the fewest K slices (a divisor of KT, at most 8) that give at least one CTA per SM
-  w.splits = 1;
-  for (int s = 1; s <= std::min(8, w.KT); s++) {
-    if (w.KT % s) continue;
-    w.splits = s;
-    if (w.NT * s >= 148) break;
+  if (w.type == kF16) {
+    // split-K (mma.sync kernel): the fewest K slices (a divisor of KT, at most 8) that give at least one CTA per SM
+    w.splits = 1;
+    for (int sp = 1; sp <= std::min(8, w.KT); sp++) {
+      if (w.KT % sp) continue;
+      w.splits = sp;
+      if (w.NT * sp >= 148) break;
+    }
+  } else {
+    // split-K (tcgen05 kernel, one CTA per SM): the fewest K slices whose NT x S work units fill the SMs' rounds to
+    // at least 90% (else the best fill); slices may differ by one raw tile. Fixed per weight: batch invariant.
+    int best = 1;
+    double best_eff = 0;
+    for (int sp = 1; sp <= std::min(16, w.KT); sp++) {
+      long units = static_cast<long>(w.NT) * sp;
+      long rounds = (units + h->sms - 1) / h->sms;
+      double eff = static_cast<double>(units) / static_cast<double>(rounds * h->sms);
+      if (eff > best_eff + 1e-9) { best_eff = eff; best = sp; }
+      if (eff >= 0.9) { best = sp; break; }
+    }
+    w.splits = best;
   }
   return w;
 }
@@ -540,6 +555,7 @@ GC_API int gc_open(const gc_open_params *p, gc_handle **out) {
     ck(cudaSetDevice(dev), "cudaSetDevice");
     h = new gc_handle();
     h->dev = dev;
+    h->sms = prop.multiProcessorCount;
     ck(cudaStreamCreateWithFlags(&h->st, cudaStreamNonBlocking), "stream");
     gemm_init();
     gemm_tc_init();
@@ -837,7 +853,7 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
   auto gemm_kernels = [](const QWeight &w) { return w.splits > 1 ? 2 : 1; };
   auto gemm = [&](const QWeight &w, const TmaSet &ts, const __half *act, int rows, const Epi &e) {
     if (w.type == kF16) launch_gemm(w, act, rows, e, h->part, s);
-    else launch_gemm_tc(w, ts, act, rows, e, h->part, h->kerr, s);
+    else launch_gemm_tc(w, ts, rows, e, h->part, h->kerr, h->sms, s);
   };
 
   run(GCK_K_EMBED, 1, [&] { launch_embed(pv, h->emb, h->emb_type, h->emb_row_bytes, h->d, h->x, s); });
