@@ -157,7 +157,6 @@ void gemm_init() {
 void launch_gemm(const QWeight &w, const __half *act, int T, const Epi &epi, float *part, cudaStream_t s) {
   if (T <= 0) return;
   launch_t<kF16>(w, act, T, epi, part, s);
-  if (w.splits > 1) launch_splitk_reduce(part, w.splits, T, w.NT * kBM, epi, s);
 }
 
 }  // namespace gck

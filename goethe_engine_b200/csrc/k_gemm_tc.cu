@@ -3,18 +3,21 @@
 //
 //   y[t, n] = sum_k act[t, k] * W[n, k]          (the reference's `w @ h`, ref.py:51-59, for all token rows at once)
 //
-// One CTA computes a 128-row band of W (the MMA's M) against a tile of NT token rows (the MMA's N) over a fixed range
-// of K (split-K, fixed per weight). Warp roles:
+// A persistent CTA per SM (it takes all 512 TMEM columns) walks work units: a 128-row band of W (the MMA's M) against
+// a tile of NT token rows (the MMA's N) over a fixed range of K (split-K, fixed per weight). Warp roles:
 //   warp 0       producer of raw weight tiles: one 1-D bulk copy per tile (128 rows x 256 K, the GGUF blocks as relaid
-//                at load), up to 3-4 tiles ahead;
-//   warp 10      producer of activations: one 2-D tensor-map copy per 64-K stage (NT rows, 128-byte swizzle);
-//   warp 1       TMEM allocation; one elected thread issues 4 tcgen05.mma (K = 16 each, weights from TMEM,
-//                activations from shared memory) per 64-K stage and commits each stage back to the producers;
-//   warps 2-9    dequantize each 64-K stage of the raw tile (two threads per weight row; f16 arithmetic, one rounding)
-//                straight into tensor memory (tcgen05.st): the MMA reads its weight operand from TMEM, so shared
-//                memory carries only the raw tiles and the activations;
-//   warps 11-14  epilogue: tcgen05.ld of the accumulator (two buffers, so it overlaps the next unit's MMAs) and the
+//                at load), 2-4 tiles ahead, across unit boundaries;
+//   warp 2       producer of activations: 64-K x NT-row tensor-map copies (128-byte swizzle), a stage ahead;
+//   warp 1       TMEM allocation; one elected thread issues the stage's tcgen05.mma (K = 16 each, weights from TMEM,
+//                activations from shared memory) and one commit per stage back to the producers;
+//   warps 7-22   dequantize into tensor memory (tcgen05.st), in two groups of 8 warps that take alternate stages, so
+//                one group's barrier waits overlap the other's arithmetic (two threads per weight row in a group; f16
+//                arithmetic, one rounding): the MMA reads its weight operand from TMEM, so shared memory carries only
+//                the raw tiles and the activations;
+//   warps 3-6    epilogue: tcgen05.ld of the accumulator (two buffers, so it overlaps the next unit's MMAs) and the
 //                store, residual add, SwiGLU or split-K partial.
+// At a decode batch of 64 the M128 x N64 MMAs and the Q4_K weight stream need about the same time per tile, so the
+// MMA thread is kept fed by a stage ring of whole 256-K tiles.
 // Every output element accumulates its K range in one order whatever NT is, so a row's result does not depend on the
 // rest of the batch. Every copy here reads this GPU's global memory into this CTA's own shared memory.
 //
@@ -28,11 +31,10 @@
 namespace gck {
 namespace {
 
-constexpr int kKS = 128;                   // K per stage: two 128-byte swizzle rows of f16 (8 MMAs of K = 16)
-constexpr int kSub = kBK / kKS;            // stages per raw tile (2)
-constexpr int kThreads = 480;              // 15 warps
-constexpr int kDeqWarps = 8;               // warps 2-9: two threads per weight row
-constexpr int kEpiWarp0 = 11;              // warps 11-14: epilogue (TMEM lane quarters 3, 0, 1, 2)
+constexpr int kThreads = 736;              // 23 warps
+constexpr int kEpiWarp0 = 3;               // warps 3-6: epilogue (TMEM lane quarters 3, 0, 1, 2)
+constexpr int kDeqWarp0 = 7;               // warps 7-22: dequant, two groups
+constexpr int kGroupWarps = 8;             // per group: two threads per weight row
 constexpr unsigned long long kTimeoutNs = 2000000000ull;
 
 enum ErrCode { kErrRawFull = 1, kErrRawEmpty, kErrStageEmpty, kErrAFull, kErrBFull, kErrAcc };
@@ -41,13 +43,11 @@ template <int TYPE>
 struct TileFmt;
 template <>
 struct TileFmt<kQ4_K> {
-  static constexpr int BYTES = kBM * 144;   // 128 x 16 B headers, then [4 stages][2 pieces][128 rows][16 B]
-  static constexpr int PIECES = 2;
+  static constexpr int BYTES = kBM * 144;   // 128 x 16 B headers, then [8 sub-blocks][128 rows][16 B]
 };
 template <>
 struct TileFmt<kQ8_0> {
-  static constexpr int BYTES = kBM * 272;   // 128 x 16 B (8 fp16 d), then [4 stages][4 pieces][128 rows][16 B]
-  static constexpr int PIECES = 4;
+  static constexpr int BYTES = kBM * 272;   // 128 x 16 B (8 fp16 d), then [8 blocks][2 halves][128 rows][16 B]
 };
 
 // ---------------------------------------------------------------------------------------------------- PTX wrappers
@@ -125,13 +125,6 @@ GCK_DEV uint64_t umma_desc(const void *p) {
   uint64_t a = smem_u32(p);
   return ((a >> 4) & 0x3FFFull) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
 }
-GCK_DEV void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
-          tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
 GCK_DEV void umma_commit(uint64_t *bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_u32(bar))
                : "memory");
@@ -163,73 +156,50 @@ GCK_DEV uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   asm("prmt.b32 %0, %1, %2, %3;\n" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
   return d;
 }
-// 4 byte values 0..255 in x -> two half2 (1024 + b0, 1024 + b1), (1024 + b2, 1024 + b3): exact
-GCK_DEV void bytes_to_h2(uint32_t x, uint32_t &lo, uint32_t &hi) {
-  lo = prmt(x, 0x64646464u, 0x5140u);
-  hi = prmt(x, 0x64646464u, 0x5342u);
+
+constexpr uint32_t kMagic = 0x64006400u;   // f16 pair (1024, 1024): OR-ing an integer below 1024 into a half adds it
+constexpr uint32_t kP64 = 0x64646464u;     // byte source of prmt: 0x64 in every byte
+constexpr uint32_t kH1024 = 0x64006400u;
+constexpr uint32_t kH1152 = 0x64806480u;   // 1024 + 128
+constexpr uint32_t kH16th = 0x2C002C00u;   // 1/16
+constexpr uint32_t kHm64 = 0xD400D400u;    // -64
+
+// One Q4_K quant word of the relaid tile: 8 nibbles of k = 0..7 at bit positions 0, 16, 4, 20, 8, 24, 12, 28, so
+// that masking gives f16 pairs of consecutive k: (1024 + q) for the nibbles at bits 0/16 and 8/24, (1024 + 16q) for
+// those at 4/20 and 12/28 -> exact q by one subtraction or one fma, then q * S + O with one rounding.
+GCK_DEV void q4_word(uint32_t w, uint32_t S, uint32_t O, uint32_t *o) {
+  const uint32_t w8 = w >> 8;
+  const uint32_t a = (w & 0x000F000Fu) | kMagic, b = (w & 0x00F000F0u) | kMagic;
+  const uint32_t c = (w8 & 0x000F000Fu) | kMagic, d = (w8 & 0x00F000F0u) | kMagic;
+  o[0] = hfma2_u(hsub2_u(a, kH1024), S, O);
+  o[1] = hfma2_u(hfma2_u(b, kH16th, kHm64), S, O);
+  o[2] = hfma2_u(hsub2_u(c, kH1024), S, O);
+  o[3] = hfma2_u(hfma2_u(d, kH16th, kHm64), S, O);
+}
+// One Q8_0 quant word of the relaid tile: 4 bytes q + 128 of k = 0..3 -> two f16 pairs (q0, q1) * D, (q2, q3) * D
+GCK_DEV void q8_word(uint32_t w, uint32_t D, uint32_t *o) {
+  o[0] = hmul2_u(hsub2_u(prmt(w, kP64, 0x5140u), kH1152), D);
+  o[1] = hmul2_u(hsub2_u(prmt(w, kP64, 0x5342u), kH1152), D);
 }
 
-// Q4_K super-block header words (bytes 4..15 of the block) -> the 8 six-bit scales and mins, one per byte:
-// scales 0-3 / mins 0-3 are the low 6 bits of bytes 0-3 / 4-7; scales 4-7 / mins 4-7 take their low 4 bits from the
-// low / high nibbles of bytes 8-11 and their top 2 bits from the top 2 bits of bytes 0-3 / 4-7.
-struct Q4kScales {
-  uint32_t sc_lo, sc_hi, m_lo, m_hi;
-};
-GCK_DEV Q4kScales q4k_scales(uint32_t w0, uint32_t w1, uint32_t w2) {
-  Q4kScales q;
-  q.sc_lo = w0 & 0x3F3F3F3Fu;
-  q.m_lo = w1 & 0x3F3F3F3Fu;
-  q.sc_hi = (w2 & 0x0F0F0F0Fu) | ((w0 >> 2) & 0x30303030u);
-  q.m_hi = ((w2 >> 4) & 0x0F0F0F0Fu) | ((w1 >> 2) & 0x30303030u);
-  return q;
-}
-
-// Q4_K: stage j (64 K) of row r, half h: quant bytes 16h .. 16h+15 of the stage's 32 (one piece, read by this thread
-// only). Low nibbles are k = 16h .. 16h+15 (sub-block 2j), high nibbles k = 32 + 16h .. (sub-block 2j+1).
-// out[0..7] = TMEM columns 8h .. 8h+7, out[8..15] = columns 16 + 8h .. (two f16 per column, lower k in the low half).
-GCK_DEV void dequant_q4k(const uint8_t *raw, int r, int j, int h, uint32_t d_dm, const Q4kScales &qs, uint32_t (&out)[16]) {
-  const uint32_t scw = j < 2 ? qs.sc_lo : qs.sc_hi, mw = j < 2 ? qs.m_lo : qs.m_hi;
-  const int sh = 16 * (j & 1);
-  const int sc0 = (scw >> sh) & 0xFF, sc1 = (scw >> (sh + 8)) & 0xFF;
-  const int m0 = (mw >> sh) & 0xFF, m1 = (mw >> (sh + 8)) & 0xFF;
-  __half2 dd = *reinterpret_cast<__half2 *>(&d_dm);
-  float d = __low2float(dd), dm = __high2float(dd);
-  __half2 s0 = __float2half2_rn(d * static_cast<float>(sc0)), o0 = __float2half2_rn(-dm * static_cast<float>(m0));
-  __half2 s1 = __float2half2_rn(d * static_cast<float>(sc1)), o1 = __float2half2_rn(-dm * static_cast<float>(m1));
-  const uint32_t S0 = *reinterpret_cast<uint32_t *>(&s0), O0 = *reinterpret_cast<uint32_t *>(&o0);
-  const uint32_t S1 = *reinterpret_cast<uint32_t *>(&s1), O1 = *reinterpret_cast<uint32_t *>(&o1);
-  const uint32_t K1024 = 0x64006400u;
-  const uint4 q = *reinterpret_cast<const uint4 *>(raw + kBM * 16 + (j * 2 + h) * (kBM * 16) + r * 16);
-  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    uint32_t a0, a1, b0, b1;
-    bytes_to_h2(w[i] & 0x0F0F0F0Fu, a0, a1);
-    bytes_to_h2((w[i] >> 4) & 0x0F0F0F0Fu, b0, b1);
-    out[2 * i] = hfma2_u(hsub2_u(a0, K1024), S0, O0);
-    out[2 * i + 1] = hfma2_u(hsub2_u(a1, K1024), S0, O0);
-    out[8 + 2 * i] = hfma2_u(hsub2_u(b0, K1024), S1, O1);
-    out[8 + 2 * i + 1] = hfma2_u(hsub2_u(b1, K1024), S1, O1);
+// Q4_K super-block header words (bytes 4..15 of the block: 12 packed six-bit scales and mins) -> the scales and mins
+// of sub-blocks g0 and g0 + 1 (g0 even) as exact f16 pairs, then S = d * sc and O = -dmin * m, one rounding each (the
+// products are exact in f32, so this equals rounding the f32 product). dd = (d, d), mm = (-dmin, -dmin).
+// Sub-blocks 0-3: low 6 bits of bytes 0-3 (scales) / 4-7 (mins); 4-7: low / high nibbles of bytes 8-11 with the top
+// 2 bits of bytes 0-3 / 4-7.
+GCK_DEV void q4k_pair_scales(const uint4 &hdr, int g0, uint32_t dd, uint32_t mm, uint32_t &S01, uint32_t &O01) {
+  uint32_t scw, mw;
+  if (g0 < 4) {
+    scw = hdr.y & 0x3F3F3F3Fu;
+    mw = hdr.z & 0x3F3F3F3Fu;
+  } else {
+    scw = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
+    mw = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
   }
-}
-
-// Q8_0: stage j of row r, half h: block 2j + h (k = 32h .. 32h+31) -> TMEM columns 16h .. 16h+15
-GCK_DEV void dequant_q80(const uint8_t *raw, int r, int j, int h, const uint4 &hdr, uint32_t (&out)[16]) {
-  const uint32_t K1152 = 0x64806480u;   // 1024 + 128
-  const uint32_t dw = j == 0 ? hdr.x : j == 1 ? hdr.y : j == 2 ? hdr.z : hdr.w;
-  const uint32_t D = (h ? (dw >> 16) : (dw & 0xFFFFu)) * 0x10001u;
-#pragma unroll
-  for (int pp = 0; pp < 2; pp++) {
-    const uint4 q = *reinterpret_cast<const uint4 *>(raw + kBM * 16 + (j * 4 + 2 * h + pp) * (kBM * 16) + r * 16);
-    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-      uint32_t a0, a1;
-      bytes_to_h2(w[i] ^ 0x80808080u, a0, a1);
-      out[8 * pp + 2 * i] = hmul2_u(hsub2_u(a0, K1152), D);
-      out[8 * pp + 2 * i + 1] = hmul2_u(hsub2_u(a1, K1152), D);
-    }
-  }
+  // bytes g0 % 4 and g0 % 4 + 1 into the low bytes of two halves whose high bytes are 0x64: (1024 + x, 1024 + y)
+  const uint32_t sel = (g0 & 2) ? 0x5342u : 0x5140u;
+  S01 = hmul2_u(hsub2_u(prmt(scw, kP64, sel), kH1024), dd);
+  O01 = hmul2_u(hsub2_u(prmt(mw, kP64, sel), kH1024), mm);
 }
 
 GCK_DEV void tmem_st8(uint32_t taddr, const uint32_t *v) {
@@ -246,20 +216,27 @@ GCK_DEV void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint3
       : "memory");
 }
 
-// One ring of R stages. Stage s: 64 TMEM columns of dequantized weights (128 rows x 128 K, two f16 per column) after
-// the ACC accumulator buffers, and two shared-memory activation tiles of NT rows x 64 K (128-byte swizzle). Raw
-// weight tiles (HBM lookahead: 4 Q4_K = 72 KB or 3 Q8_0 = 102 KB per SM) have their own ring.
+// Stage geometry. A stage is KS of K: KS / 2 TMEM columns of dequantized weights (128 rows, two f16 per column)
+// after the ACC accumulator buffers, and KS / 64 shared-memory activation boxes of NT rows x 64 K (128-byte swizzle).
+// KS is a whole raw tile (256) up to NT = 128 and half of one at NT = 256 (so that two activation stages fit).
 template <int TYPE, int NT>
 struct Shape {
-  static constexpr int STAGE_B = 2 * NT * 128;
+  static constexpr int KS = NT >= 256 ? 128 : 256;
+  static constexpr int SPT = kBK / KS;                  // stages per raw tile
+  static constexpr int BOX_B = NT * 128;                // one 64-K activation box
+  static constexpr int STAGE_B = (KS / 64) * BOX_B;
   static constexpr int NCOLS = NT <= 32 ? 32 : NT <= 64 ? 64 : NT <= 128 ? 128 : 256;
   static constexpr int ACC = NT <= 128 ? 2 : 1;
-  static constexpr int RAW = TYPE == kQ4_K ? 4 : (NT >= 256 ? 2 : 3);
-  static constexpr int R_TMEM = (512 - ACC * NCOLS) / 64;
-  static constexpr int R_SMEM = (216 * 1024 - RAW * TileFmt<TYPE>::BYTES) / STAGE_B;
+  static constexpr int RAW = TYPE == kQ4_K ? 4 : (NT >= 128 ? 2 : 4);
+  static constexpr int R_TMEM = (512 - ACC * NCOLS) / (KS / 2);
+  static constexpr int R_SMEM = (204 * 1024 - RAW * TileFmt<TYPE>::BYTES) / STAGE_B;
   static constexpr int R0 = R_TMEM < R_SMEM ? R_TMEM : R_SMEM;
-  static constexpr int R = R0 > 8 ? 8 : R0;
+  static constexpr int R = R0 > 4 ? 4 : R0;
   static_assert(R >= 2, "stage ring too shallow");
+  // With one stage per raw tile the two dequant groups take alternate tiles. An even raw ring gives every slot a
+  // single consumer group, which waits on it in order, so a parity wait can never pass on a phase two behind (with an
+  // odd ring a group could see slot s "full" while the other group's earlier tile in s was still landing).
+  static_assert(SPT == 2 || RAW % 2 == 0, "raw ring slots must each belong to one dequant group");
 };
 
 constexpr int kXchg = 64 * 17 * 4;         // SwiGLU hand-off: 64 rows x 16 columns (+1 pad) of f32
@@ -294,7 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const __grid_constant__ CUtensorMap tmap, int T, Epi epi, float *part, int Npad, int *err) {
   using F = TileFmt<TYPE>;
   using S = Shape<TYPE, NT>;
-  constexpr int RS = S::RAW, SR = S::R, ACC = S::ACC;
+  constexpr int RS = S::RAW, SR = S::R, ACC = S::ACC, KS = S::KS, SPT = S::SPT;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *sB = smem;
@@ -308,8 +285,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < RS; i++) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], kDeqWarps); }
-    for (int i = 0; i < SR; i++) { mbar_init(&a_full[i], kDeqWarps); mbar_init(&st_empty[i], 1); mbar_init(&b_full[i], 1); }
+    // a raw tile is read by one dequant group (KS = 256) or by both (KS = 128)
+    for (int i = 0; i < RS; i++) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], kGroupWarps * SPT); }
+    for (int i = 0; i < SR; i++) { mbar_init(&a_full[i], kGroupWarps); mbar_init(&st_empty[i], 1); mbar_init(&b_full[i], 1); }
     for (int i = 0; i < 2; i++) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
     mbar_init(mma_done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
@@ -324,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_a = tmem + ACC * S::NCOLS;   // weight stage s at columns tmem_a + 64 * s
+  const uint32_t tmem_a = tmem + ACC * S::NCOLS;   // weight stage s at columns tmem_a + (KS / 2) * s
 
   if (warp == 0) {
     if (lane == 0) {
@@ -344,20 +322,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       // every issued copy has landed before the CTA may exit (the last phase of each slot; bounded)
       for (long i = c > RS ? c - RS : 0; i < c; i++) mbar_wait(&raw_full[i % RS], static_cast<uint32_t>((i / RS) & 1), err, kErrRawFull);
     }
-  } else if (warp == 10) {
+  } else if (warp == 2) {
     if (lane == 0) {
-      // ---- activation stages: two tensor-map copies (64 K each) per 128-K stage, up to SR stages ahead
+      // ---- activation stages: KS / 64 tensor-map copies (64 K each) per stage, up to SR stages ahead
       long c = 0;
       bool ok = true;
       for (int w = blockIdx.x; w < units && ok; w += gridDim.x) {
         const Unit un = unit_of(w, NTW, KT, splits);
-        for (int i = 0; i < un.per * kSub; i++, c++) {
+        for (int i = 0; i < un.per * SPT; i++, c++) {
           const int s = static_cast<int>(c % SR);
           if (!(ok = mbar_wait(&st_empty[s], static_cast<uint32_t>((c / SR) & 1) ^ 1, err, kErrStageEmpty))) break;
           mbar_expect_tx(&b_full[s], S::STAGE_B);
-          const int x = (un.kt0 + i / kSub) * kBK + (i % kSub) * kKS;
-          tma_2d(sB + s * S::STAGE_B, &tmap, x, un.tt * NT, &b_full[s]);
-          tma_2d(sB + s * S::STAGE_B + NT * 128, &tmap, x + 64, un.tt * NT, &b_full[s]);
+          const int x = (un.kt0 + i / SPT) * kBK + (i % SPT) * KS;
+#pragma unroll
+          for (int b = 0; b < KS / 64; b++) tma_2d(sB + s * S::STAGE_B + b * S::BOX_B, &tmap, x + 64 * b, un.tt * NT, &b_full[s]);
         }
       }
       for (long i = c > SR ? c - SR : 0; i < c; i++) mbar_wait(&b_full[i % SR], static_cast<uint32_t>((i / SR) & 1), err, kErrBFull);
@@ -376,16 +354,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(ok = mbar_wait(&acc_empty[ab], ph ^ 1, err, kErrAcc))) break;
         tc_fence_after();
         const uint32_t dt = tmem + ab * S::NCOLS;
-        for (int i = 0; i < un.per * kSub; i++, ca++) {
+        for (int i = 0; i < un.per * SPT; i++, ca++) {
           const int s = static_cast<int>(ca % SR);
-          // a_full covers both operands: the dequant warps signal it only after the stage's activations landed
-          if (!(ok = mbar_wait(&a_full[s], static_cast<uint32_t>((ca / SR) & 1), err, kErrAFull))) break;
+          const uint32_t par = static_cast<uint32_t>((ca / SR) & 1);
+          if (!(ok = mbar_wait(&a_full[s], par, err, kErrAFull))) break;
+          if (!(ok = mbar_wait(&b_full[s], par, err, kErrBFull))) break;
           tc_fence_after();
-          const uint64_t bd0 = umma_desc(sB + s * S::STAGE_B), bd1 = umma_desc(sB + s * S::STAGE_B + NT * 128);
-          const uint32_t at = tmem_a + 64 * s;
+          const uint32_t at = tmem_a + (KS / 2) * s;
+          const uint64_t bd = umma_desc(sB + s * S::STAGE_B);
 #pragma unroll
-          for (int k = 0; k < kKS / 16; k++)
-            umma_f16_ts(dt, at + 8 * k, (k < 4 ? bd0 : bd1) + 2 * (k & 3), idesc, (i | k) != 0);
+          for (int k = 0; k < KS / 16; k++)
+            umma_f16_ts(dt, at + 8 * k, bd + static_cast<uint64_t>((k >> 2) * (S::BOX_B >> 4) + 2 * (k & 3)), idesc,
+                        (i | k) != 0);
           umma_commit(&st_empty[s]);
         }
         umma_commit(&acc_full[ab]);   // arrives once every MMA of this unit has completed
@@ -393,74 +373,78 @@ __global__ void __launch_bounds__(kThreads, 1)
       // completes once every MMA issued above has: the exit below never frees tensor memory still being written
       umma_commit(mma_done);
     }
-  } else if (warp < kEpiWarp0) {
-    // ---- dequant: two threads per weight row, one 32-element half each, into the TMEM stage ring. Software
-    // pipelined: stage i's TMEM stores are in flight while stage i+1 is computed, and only then waited for and
-    // signalled, so the store latency hides behind arithmetic.
+  } else if (warp >= kDeqWarp0) {
+    // ---- dequant: two groups of 8 warps take alternate stages, so one group's waits overlap the other's arithmetic.
+    // In a group, two threads per weight row (TMEM lane = row), each KS / 2 of the stage's K, straight into TMEM.
+    const int dw = warp - kDeqWarp0;
+    const int grp = dw / kGroupWarps;
+    const int hsel = (dw / 4) & 1;
     const int q = warp & 3;
     const int r = q * 32 + lane;
-    const int hsel = (warp - 2) >> 2;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-    long cr = 0, ca = 0;
-    int prev = -1;              // stage slot whose stores are in flight, not yet signalled
+    long c = 0, cr = 0;
     bool ok = true;
-    long prev_c = 0;
-    auto signal_prev = [&]() {
-      if (prev < 0) return;
-      tmem_st_wait();
-      tc_fence_before();
-      // the stage's activation tiles must have landed too: then one barrier tells the MMA thread both are ready
-      if (!mbar_wait(&b_full[prev], static_cast<uint32_t>((prev_c / SR) & 1), err, kErrBFull)) ok = false;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&a_full[prev]);
-      prev = -1;
-    };
     for (int w = blockIdx.x; w < units && ok; w += gridDim.x) {
       const Unit un = unit_of(w, NTW, KT, splits);
       for (int u = 0; u < un.per && ok; u++, cr++) {
         const int rs = static_cast<int>(cr % RS);
-        if (!(ok = mbar_wait(&raw_full[rs], static_cast<uint32_t>((cr / RS) & 1), err, kErrRawFull))) break;
-        const uint8_t *raw = sRaw + rs * F::BYTES;
-        const uint4 hdr = *reinterpret_cast<const uint4 *>(raw + r * 16);
-        const Q4kScales qsc = q4k_scales(hdr.y, hdr.z, hdr.w);
-        for (int j = 0; j < kSub; j++, ca++) {
-          const int s = static_cast<int>(ca % SR);
-          // 128 K = two 64-K halves (quarters 2j, 2j+1 of the raw tile) -> 4 runs of 8 TMEM columns
-          uint32_t v0[16], v1[16];
-          if (TYPE == kQ4_K) {
-            dequant_q4k(raw, r, 2 * j, hsel, hdr.x, qsc, v0);
-            dequant_q4k(raw, r, 2 * j + 1, hsel, hdr.x, qsc, v1);
-          } else {
-            dequant_q80(raw, r, 2 * j, hsel, hdr, v0);
-            dequant_q80(raw, r, 2 * j + 1, hsel, hdr, v1);
-          }
-          if (j == kSub - 1) {       // every byte of this raw tile is in registers: release the slot
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&raw_empty[rs]);
-          }
-          signal_prev();
-          if (!(ok = mbar_wait(&st_empty[s], static_cast<uint32_t>((ca / SR) & 1) ^ 1, err, kErrStageEmpty))) break;
+        for (int sub = 0; sub < SPT; sub++, c++) {
+          if ((c & 1) != grp) continue;
+          const int s = static_cast<int>(c % SR);
+          if (!(ok = mbar_wait(&raw_full[rs], static_cast<uint32_t>((cr / RS) & 1), err, kErrRawFull))) break;
+          if (!(ok = mbar_wait(&st_empty[s], static_cast<uint32_t>((c / SR) & 1) ^ 1, err, kErrStageEmpty))) break;
           tc_fence_after();
-          const uint32_t col = tmem_a + 64 * s + lane_base;
+          const uint8_t *raw = sRaw + rs * F::BYTES;
+          const uint4 hdr = *reinterpret_cast<const uint4 *>(raw + r * 16);
+          const uint32_t col = tmem_a + (KS / 2) * s + lane_base + (KS / 4) * hsel;
+          const int g0 = (KS / 32) * sub + (KS / 64) * hsel;   // first 32-K block of this thread
+          if (TYPE == kQ4_K) {
+            const uint32_t dd = prmt(hdr.x, 0, 0x1010u);                 // (d, d)
+            const uint32_t mm = prmt(hdr.x, 0, 0x3232u) ^ 0x80008000u;   // (-dmin, -dmin)
 #pragma unroll
-          for (int t = 0; t < 2; t++) {
-            const uint32_t *v = t ? v1 : v0;
-            const uint32_t c0 = col + 32 * t;
-            if (TYPE == kQ4_K) {
-              tmem_st8(c0 + 8 * hsel, v);
-              tmem_st8(c0 + 16 + 8 * hsel, v + 8);
-            } else {
-              tmem_st8(c0 + 16 * hsel, v);
-              tmem_st8(c0 + 16 * hsel + 8, v + 8);
+            for (int gp = 0; gp < KS / 128; gp++) {
+              const int g = g0 + 2 * gp;
+              uint32_t S01, O01;
+              q4k_pair_scales(hdr, g, dd, mm, S01, O01);
+#pragma unroll
+              for (int e = 0; e < 2; e++) {
+                const uint32_t Sg = prmt(S01, 0, e ? 0x3232u : 0x1010u), Og = prmt(O01, 0, e ? 0x3232u : 0x1010u);
+                const uint4 qw = *reinterpret_cast<const uint4 *>(raw + kBM * 16 + ((g + e) * kBM + r) * 16);
+                uint32_t v[16];
+                q4_word(qw.x, Sg, Og, v);
+                q4_word(qw.y, Sg, Og, v + 4);
+                q4_word(qw.z, Sg, Og, v + 8);
+                q4_word(qw.w, Sg, Og, v + 12);
+                tmem_st8(col + 16 * (2 * gp + e), v);
+                tmem_st8(col + 16 * (2 * gp + e) + 8, v + 8);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int gi = 0; gi < KS / 64; gi++) {
+              const int g = g0 + gi;
+              const uint32_t dw2 = (g >> 1) == 0 ? hdr.x : (g >> 1) == 1 ? hdr.y : (g >> 1) == 2 ? hdr.z : hdr.w;
+              const uint32_t D = prmt(dw2, 0, (g & 1) ? 0x3232u : 0x1010u);
+              const uint4 q0 = *reinterpret_cast<const uint4 *>(raw + kBM * 16 + ((2 * g) * kBM + r) * 16);
+              const uint4 q1 = *reinterpret_cast<const uint4 *>(raw + kBM * 16 + ((2 * g + 1) * kBM + r) * 16);
+              uint32_t v[16];
+              q8_word(q0.x, D, v); q8_word(q0.y, D, v + 2); q8_word(q0.z, D, v + 4); q8_word(q0.w, D, v + 6);
+              q8_word(q1.x, D, v + 8); q8_word(q1.y, D, v + 10); q8_word(q1.z, D, v + 12); q8_word(q1.w, D, v + 14);
+              tmem_st8(col + 16 * gi, v);
+              tmem_st8(col + 16 * gi + 8, v + 8);
             }
           }
-          prev = s;
-          prev_c = ca;
+          // this group's last read of the raw tile (each group reads a tile once)
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&raw_empty[rs]);
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&a_full[s]);
         }
       }
     }
-    signal_prev();
-  } else {
+  } else if (warp >= kEpiWarp0) {
     // ---- epilogue: TMEM lane quarter q = weight rows 32q .. 32q+31 of the tile
     const int q = warp & 3;
     const int r = q * 32 + lane;
@@ -591,7 +575,6 @@ void launch_gemm_tc(const QWeight &w, const TmaSet &ts, int T, const Epi &epi, f
   if (T <= 0) return;
   if (w.type == kQ4_K) launch_type<kQ4_K>(w, ts, T, epi, part, err, sms, s);
   else launch_type<kQ8_0>(w, ts, T, epi, part, err, sms, s);
-  if (w.splits > 1) launch_splitk_reduce(part, w.splits, T, w.NT * kBM, epi, s);
 }
 
 }  // namespace gck

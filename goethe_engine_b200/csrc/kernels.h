@@ -13,7 +13,7 @@ namespace gck {
 enum WType { kF32 = 0, kF16 = 1, kQ8_0 = 8, kQ4_K = 12 };  // GGUF type ids
 
 // GEMM tiles: a weight matrix [N, K] is stored as tiles of kBM rows x kBK columns, tile (nt, kt) at
-// (nt * KT + kt) * tile_bytes. Inside a tile, scales/headers come first, then the quants (see weights.cpp).
+// (nt * KT + kt) * tile_bytes. Inside a tile, scales/headers come first, then the quants (runtime.cu relayout).
 constexpr int kBM = 128;
 constexpr int kBK = 256;
 constexpr int kBN = 64;   // tokens per CTA tile
@@ -26,8 +26,9 @@ __host__ __device__ inline size_t tile_bytes(int type) {
   }
 }
 // Q4_K and Q8_0 tiles: the 128 rows' 16-byte headers (Q4_K: d, dmin, 12 scale bytes; Q8_0: the 8 block scales), then
-// the quants as [4 K-stages of 64][pieces][128 rows][16 B] (Q4_K 2 pieces: bytes 32j..32j+31 of each row's block;
-// Q8_0 4 pieces: the 64 int8 of blocks 2j, 2j+1), so that thread r of the dequant warps reads rows 16 B apart.
+// the quants as [32-K block][pieces][128 rows][16 B] (Q4_K: one piece, the block's 32 nibbles reordered so that
+// masks give f16 pairs of consecutive k; Q8_0: two pieces of 16 quants stored as q + 128), so that thread r of the
+// dequant warps reads rows 16 B apart (runtime.cu relayout, k_gemm_tc.cu).
 
 enum EpiKind { kEpiStore = 0, kEpiAdd = 1, kEpiSwiGLU = 2 };
 struct Epi {
@@ -59,7 +60,8 @@ void launch_commit(const int *moves, int n, int L, int KVH, int dh, uint8_t *kc,
                    int kv_fp8, size_t layer_bytes, size_t exps_layer, float *tmp, cudaStream_t s);
 
 // y = act[T, Kpad] (f16, row-major, Kpad = KT * kBK) times W^T, with the epilogue; part: split-K scratch
-// [splits, T, NT * kBM] f32 (unused when splits == 1).
+// [splits, T, NT * kBM] f32 (unused when splits == 1). With splits > 1 the GEMM writes only the partials and the caller
+// launches launch_splitk_reduce (the sum in split order and the epilogue) after it.
 // F16 weights: mma.sync kernel (k_gemm.cu). Q4_K / Q8_0 weights: tcgen05 kernel (k_gemm_tc.cu), whose activation
 // tiles come through TMA tensor maps over the activation buffer, one map per token tile size.
 void gemm_init();   // once per device, before the first launch_gemm

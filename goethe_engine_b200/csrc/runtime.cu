@@ -212,26 +212,37 @@ QWeight relayout(gc_handle *h, int type, int N, int K, RowMap rowmap, const char
         for (int kt = 0; kt < w.KT; kt++) {
           uint8_t *tile = host.data() + (static_cast<size_t>(nt) * w.KT + kt) * tb;
           if (type == kQ4_K) {
-            // header (d, dmin, 12 scale bytes) at r*16; quant bytes 32j+16p .. +15 at [stage j][piece p][row r]
+            // header (d, dmin, 12 scale bytes) at r*16; then per 32-K sub-block g the row's 32 nibbles as 16 bytes at
+            // [g][row r]: four words of 8 consecutive k, k = 0..7 at nibble positions 0, 4, 1, 5, 2, 6, 3, 7 (so the
+            // kernel masks out f16 pairs of consecutive k). GGUF order: element 64j + l is the low nibble of quant byte
+            // 32j + l for l < 32 (sub-block 2j), else the high nibble of byte 32j + l - 32 (sub-block 2j + 1).
+            static const int kPos[8] = {0, 4, 1, 5, 2, 6, 3, 7};
             int nsb = K / 256;
             if (kt >= nsb) continue;
             const uint8_t *src = row + (static_cast<size_t>(sr) * nsb + kt) * 144;
             std::memcpy(tile + r * 16, src, 16);
-            for (int j = 0; j < 4; j++)
-              for (int p = 0; p < 2; p++)
-                std::memcpy(tile + kBM * 16 + (j * 2 + p) * (kBM * 16) + r * 16, src + 16 + 32 * j + 16 * p, 16);
+            const uint8_t *qs = src + 16;
+            for (int g = 0; g < 8; g++) {
+              uint32_t words[4] = {0, 0, 0, 0};
+              for (int e = 0; e < 32; e++) {
+                int j = g / 2;
+                uint8_t byte = qs[32 * j + e];
+                uint32_t nib = (g & 1) ? (byte >> 4) : (byte & 15);
+                words[e / 8] |= nib << (4 * kPos[e % 8]);
+              }
+              std::memcpy(tile + kBM * 16 + (g * kBM + r) * 16, words, 16);
+            }
           } else if (type == kQ8_0) {
-            // the 8 block scales at r*16; quants of blocks 2j + p/2, bytes 16(p%2) .. +15 at [stage j][piece p][row r]
+            // the 8 block scales at r*16; block b's 32 quants as q + 128 (unsigned), 16 bytes each at [2b + half][row r]
             int nb = K / 32;
             for (int i = 0; i < 8; i++) {
               int b = kt * 8 + i;
               if (b >= nb) break;
               const uint8_t *src = row + (static_cast<size_t>(sr) * nb + b) * 34;
               std::memcpy(tile + r * 16 + i * 2, src, 2);
-              int j = i / 2;
               for (int h2 = 0; h2 < 2; h2++) {
-                int p = (i % 2) * 2 + h2;
-                std::memcpy(tile + kBM * 16 + (j * 4 + p) * (kBM * 16) + r * 16, src + 2 + 16 * h2, 16);
+                uint8_t *dst = tile + kBM * 16 + ((2 * i + h2) * kBM + r) * 16;
+                for (int e = 0; e < 16; e++) dst[e] = static_cast<uint8_t>(src[2 + 16 * h2 + e] ^ 0x80);
               }
             }
           } else {
@@ -850,10 +861,14 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
     }
     h->step_launches += nk;
   };
-  auto gemm_kernels = [](const QWeight &w) { return w.splits > 1 ? 2 : 1; };
-  auto gemm = [&](const QWeight &w, const TmaSet &ts, const __half *act, int rows, const Epi &e) {
-    if (w.type == kF16) launch_gemm(w, act, rows, e, h->part, s);
-    else launch_gemm_tc(w, ts, rows, e, h->part, h->kerr, h->sms, s);
+  // a GEMM under class cls; with split-K its reduction (and epilogue) is a second launch, timed as GCK_K_REDUCE
+  auto gemm = [&](int cls, const QWeight &w, const TmaSet &ts, const __half *act, int rows, const Epi &e) {
+    run(cls, 1, [&] {
+      if (w.type == kF16) launch_gemm(w, act, rows, e, h->part, s);
+      else launch_gemm_tc(w, ts, rows, e, h->part, h->kerr, h->sms, s);
+    });
+    if (w.splits > 1 && rows > 0)
+      run(GCK_K_REDUCE, 1, [&] { launch_splitk_reduce(h->part, w.splits, rows, w.NT * kBM, e, s); });
   };
 
   run(GCK_K_EMBED, 1, [&] { launch_embed(pv, h->emb, h->emb_type, h->emb_row_bytes, h->d, h->x, s); });
@@ -871,8 +886,7 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
   for (int l = 0; l < h->L; l++) {
     const Layer &ly = h->layers[l];
     run(GCK_K_NORM, 1, [&] { launch_rmsnorm(h->x, nullptr, T, ly.attn_norm, h->eps, h->d, h->d, h->h, s); });
-    run(GCK_K_QKV, gemm_kernels(ly.qkv),
-        [&] { gemm(ly.qkv, h->tma_h, h->h, T, Epi{kEpiStore, wq, wq, h->qkv, nullptr}); });
+    gemm(GCK_K_QKV, ly.qkv, h->tma_h, h->h, T, Epi{kEpiStore, wq, wq, h->qkv, nullptr});
     uint8_t *kc = h->kc + l * h->layer_bytes, *vc = h->vc + l * h->layer_bytes;
     int8_t *ex = h->exps ? h->exps + l * h->exps_layer : nullptr;
     run(GCK_K_ROPE, 1, [&] {
@@ -883,20 +897,14 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
     aa.exps = h->page_scale ? ex : nullptr;
     run(GCK_K_ATTN, 1, [&] { launch_attention(pv, aa, nw, s); });
     run(GCK_K_COMBINE, 1, [&] { launch_attention_combine(pv, aa, s); });
-    run(GCK_K_O, gemm_kernels(ly.o),
-        [&] { gemm(ly.o, h->tma_att, h->att, T, Epi{kEpiAdd, h->d, h->d, h->x, nullptr}); });
+    gemm(GCK_K_O, ly.o, h->tma_att, h->att, T, Epi{kEpiAdd, h->d, h->d, h->x, nullptr});
     run(GCK_K_NORM, 1, [&] { launch_rmsnorm(h->x, nullptr, T, ly.ffn_norm, h->eps, h->d, h->d, h->h, s); });
-    run(GCK_K_GATEUP, gemm_kernels(ly.gu), [&] {
-      gemm(ly.gu, h->tma_h, h->h, T, Epi{kEpiSwiGLU, h->F, ly.dn.KT * kBK, nullptr, h->act});
-    });
-    run(GCK_K_DOWN, gemm_kernels(ly.dn),
-        [&] { gemm(ly.dn, h->tma_act, h->act, T, Epi{kEpiAdd, h->d, h->d, h->x, nullptr}); });
+    gemm(GCK_K_GATEUP, ly.gu, h->tma_h, h->h, T, Epi{kEpiSwiGLU, h->F, ly.dn.KT * kBK, nullptr, h->act});
+    gemm(GCK_K_DOWN, ly.dn, h->tma_act, h->act, T, Epi{kEpiAdd, h->d, h->d, h->x, nullptr});
   }
   if (pv.R > 0) {
     run(GCK_K_NORM, 1, [&] { launch_rmsnorm(h->x, pv.want_tok, pv.R, h->out_norm, h->eps, h->d, h->d, h->h, s); });
-    run(GCK_K_HEAD, gemm_kernels(h->head), [&] {
-      gemm(h->head, h->tma_h, h->h, pv.R, Epi{kEpiStore, h->vocab, h->vocab, h->logits, nullptr});
-    });
+    gemm(GCK_K_HEAD, h->head, h->tma_h, h->h, pv.R, Epi{kEpiStore, h->vocab, h->vocab, h->logits, nullptr});
   }
 }
 
