@@ -260,7 +260,7 @@ def run_mine(args, rank, world, barrier, maxreduce):
     }
     if args.profile:
         names = ["embed", "rmsnorm", "gemm_qkv", "rope_kv", "attention", "attn_combine", "gemm_o", "gemm_gateup",
-                 "gemm_down", "gemm_head", "argmax"]
+                 "gemm_down", "gemm_head", "argmax", "splitk_reduce"]
         tot = sum(st.class_ms[i] for i in range(len(names)))
         lines = [f"{n:14s} {st.class_ms[i] / args.steps:8.3f} ms/step  {st.class_launches[i] // max(1, args.steps):5d} "
                  f"launches/step  {100 * st.class_ms[i] / max(tot, 1e-9):5.1f}%" for i, n in enumerate(names)]

@@ -4,19 +4,18 @@
 // softmax, weighted sum of V. Visible rows (ref.py:102, abi/gc.h:139-146): the cached prefix rows 0 .. pos-1, then the
 // token's ancestors (a chain: rows pos .. pos+j).
 //
-// Work decomposition. A warp owns 16 MMA rows: the G = H / KVH query heads of one kv head for up to 16 / G consecutive
-// chain tokens of one item (a prefill chunk), or one token (decode, tree node). It walks the token's visible list in
-// fixed groups of 16 entries and fixed splits of kSplit entries; splits are merged by attn_combine in split order. A
-// group's K and V rows are gathered through the block table into shared memory with cp.async (double buffered); a CTA
-// of several warps shares them when its warps serve consecutive tokens of one item. Every row's arithmetic depends only
-// on its own list, so results are identical alone, batched, chunked or as tree nodes (batch invariance).
+// Work decomposition. A warp owns up to 16 query rows: the G = H / KVH query heads of one kv head for up to 16 / G
+// consecutive chain tokens of one item (a prefill chunk), or one token (decode, tree node). It walks the token's
+// visible list in fixed groups of 16 entries and fixed splits of kSplit entries; the last CTA of a (query group, kv
+// head) to finish merges the splits' partials in split order. A split's groups are resolved to pages once (block
+// table; a tree token's own rows through its path); groups' K and V rows are gathered with cp.async through a 3-4 deep
+// ring; a CTA of several warps shares them when its warps serve consecutive tokens of one item. Every row's arithmetic
+// depends only on its own list, so results are identical alone, batched, chunked or as tree nodes (batch invariance).
 //
-// Tensor cores (mma.sync m16n8k16, f16 x f16 -> f32):
-//   S[16 rows x 8 entries] = Q[16 x dh] . K^T     (K as the B operand: one 8-entry tile per half of the group)
-//   O[16 rows x dh] += P[16 x 16 entries] . V      (P straight from the S accumulators, V as the B operand)
-// The head dimension is permuted inside the MMAs so that every lane reads contiguous bytes: for S, lane quad t reads
-// dims [t*dh/4, (t+1)*dh/4) of its K row; for O, lane g owns output dims [g*dh/8, (g+1)*dh/8). A permutation of the
-// contraction dimension does not change the dot product; the output dims are written back in their true places.
+// Tensor cores (mma.sync m16n8k16, f16 x f16 -> f32), with the 16 entries of a group as M and the query rows as N in
+// tiles of 8 (a decode warp holds one tile: its G <= 8 heads):
+//   S^T[16 entries x 8 rows] = K . Q^T,      O^T[dh x 8 rows] += V^T . P^T
+// P^T comes from the S^T accumulators by an 8x8 transpose in registers (movmatrix).
 //
 // fp8 pages: K and V codes are exact in f16; the per-page exponents (scale 2^e, see k_misc.cu) come back as a 2^-ek
 // factor on each score and as a running exponent E on the accumulator (O is kept scaled by 2^E, E = the V exponent of
@@ -31,12 +30,18 @@ namespace {
 template <int DH, bool FP8>
 struct Cfg {
   static constexpr int ESZ = FP8 ? 1 : 2;
-  static constexpr int ROWB = DH * ESZ + 16;         // padded smem row: conflict-free fragment reads
+  static constexpr int RB = DH * ESZ;                // bytes of one KV row of one head
+  static constexpr int ROWB = RB + 16;               // padded smem row: conflict-free fragment reads
   static constexpr int BUF = 2 * kGroup * ROWB;      // K rows then V rows
-  static constexpr int CHUNKS = DH * ESZ / 16;       // 16-byte chunks per row
+  static constexpr int CHUNKS = RB / 16;             // 16-byte chunks per row
   static constexpr int NKS = DH / 16;                // QK k-steps
-  static constexpr int NNT = DH / 8;                 // PV n-tiles
-  static constexpr int SMEM = 2 * BUF + 2 * kGroup * 2 * 4;  // two buffers + page exponents
+  static constexpr int NMT = DH / 16;                // PV m-tiles (16 head dims each)
+  static constexpr int NST = FP8 ? 4 : 3;            // gather ring: groups in flight while one is computed
+  static constexpr int NGS = kSplit / kGroup;        // groups per split
+  static constexpr int PG_OFF = NST * BUF;           // [NGS] page of each group (-1: entries resolved one by one)
+  static constexpr int GE_OFF = PG_OFF + NGS * 4;    // [NGS][2] page exponents (K, V) of page groups
+  static constexpr int EE_OFF = GE_OFF + NGS * 2;    // [NST][16][2] per-entry exponents of resolved groups
+  static constexpr int SMEM = EE_OFF + NST * kGroup * 2;
 };
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
@@ -44,15 +49,34 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   asm("prmt.b32 %0, %1, %2, %3;\n" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
   return d;
 }
+// 8x8 b16 transpose across the warp: lane (g, t) gives row g, columns 2t, 2t+1 and gets row g of the transpose
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;\n" : "=r"(d) : "r"(x));
+  return d;
+}
+// 2^e as a float for an integer e in [-126, 127], built from its bits (exact)
+__device__ __forceinline__ float pow2i(int e) { return __int_as_float((127 + e) << 23); }
 
-template <int DH, bool FP8>
-__global__ void __launch_bounds__(256) attn_kernel(PlanView pv, AttnArgs a) {
+// One warp = up to 8 * NT query rows (row r: token r / G of the group, query head head * G + r % G) against one kv
+// head. Per 16-entry group, with the entries as the MMA's M and the query rows as its N (tiles of 8 rows):
+//   S^T[16 entries x 8 rows] = K[16 x dh] . Q^T           (A = K from shared memory, B = Q^T held in registers)
+//   O^T[dh x 8 rows]        += V^T[dh x 16 entries] . P^T  (A = V^T from shared memory, B = P^T: S^T transposed in
+//                                                           registers with movmatrix)
+// A row's arithmetic does not depend on how many rows or tiles the warp holds.
+// Head dims are permuted inside the MMAs so that lanes read contiguous bytes: in QK, lane t's k indices of k-step s
+// are dims t*dh/4 + 4s + {0,1,2,3}; in PV, lane g's output rows of m-tile mt are dims g*dh/8 + 2mt + {0, 1}.
+template <int DH, bool FP8, int NW, int NT>
+__global__ void __launch_bounds__(32 * NW, NW == 1 && NT == 1 ? 16 : 1) attn_kernel(PlanView pv, AttnArgs a) {
   using C = Cfg<DH, FP8>;
+  constexpr int NTHR = 32 * NW;
   extern __shared__ __align__(128) uint8_t sm[];
-  int *sE = reinterpret_cast<int *>(sm + 2 * C::BUF);   // [2 bufs][16 entries][2] page exponents (K, V)
+  int *sPg = reinterpret_cast<int *>(sm + C::PG_OFF);
+  int8_t *sGE = reinterpret_cast<int8_t *>(sm + C::GE_OFF);
+  int8_t *sEE = reinterpret_cast<int8_t *>(sm + C::EE_OFF);
 
   const AttnWork w = pv.work[blockIdx.x];
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, nthr = blockDim.x;
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   const int g = lane / 4, t = lane % 4;
   const QGroup q0 = pv.qgroups[w.qg0];
   const Item it = pv.items[q0.item];
@@ -61,30 +85,37 @@ __global__ void __launch_bounds__(256) attn_kernel(PlanView pv, AttnArgs a) {
   const int lo = w.split * kSplit, hi = min(lo + kSplit, nvis_max);
   const int ngroups = (hi - lo + kGroup - 1) / kGroup;
   const bool active = warp < w.nqg;
-  const QGroup qg = pv.qgroups[w.qg0 + (active ? warp : 0)];
+  const int qgi = w.qg0 + (active ? warp : 0);
+  const QGroup qg = pv.qgroups[qgi];
   const int G = a.H / a.KVH;
   const int head = w.head;
+  const int nrows = active ? qg.ntok * G : 0;
+  const bool page_exp = FP8 && a.exps;
 
-  // rows g and g + 8 of this lane: (token, query head), validity and list length
-  int tokr[2], qh[2], nvis[2];
-  bool valid[2];
-#pragma unroll
-  for (int h = 0; h < 2; h++) {
-    int r = g + 8 * h;
-    int tl = r / G;
-    valid[h] = active && tl < qg.ntok;
-    tokr[h] = it.tok0 + qg.j0 + tl;
-    qh[h] = head * G + r % G;
-    nvis[h] = qg.path_len ? it.pos + qg.path_len : it.pos + qg.j0 + tl + 1;
+  // ---- the split's groups: a group of plain rows (entry i is row i: every group of a chain, and a tree token's
+  // groups below its own rows) is one page, read from the block table once; the rest are resolved entry by entry
+  for (int gi = tid; gi < ngroups; gi += NTHR) {
+    const int i0 = lo + gi * kGroup;
+    const bool plain = !q0.path_len || i0 + kGroup <= it.pos;
+    const int pg = plain ? static_cast<int>(pv.blocks[it.blk_off + i0 / kBlock]) : -1;
+    sPg[gi] = pg;
+    if (page_exp && plain) {
+      const int8_t *pe = a.exps + (static_cast<size_t>(pg) * a.KVH + head) * 2;
+      sGE[2 * gi] = pe[0];
+      sGE[2 * gi + 1] = pe[1];
+    }
   }
+  __syncthreads();
 
-  // Q fragments: lane quad t holds dims [t*DH/4, (t+1)*DH/4) of rows g and g+8
-  uint32_t qa[C::NKS][4];
+  // ---- Q^T fragments: tile nt, lane (g, t): row nt*8 + g, dims t*dh/4 + 4s + {0,1} (b0) and {2,3} (b1)
+  uint32_t qb[NT][C::NKS][2];
 #pragma unroll
-  for (int h = 0; h < 2; h++) {
+  for (int nt = 0; nt < NT; nt++) {
+    const int r = nt * 8 + g;
     uint32_t v[DH / 8];
-    if (valid[h]) {
-      const uint4 *src = reinterpret_cast<const uint4 *>(a.q + (static_cast<size_t>(tokr[h]) * a.H + qh[h]) * DH + t * (DH / 4));
+    if (r < nrows) {
+      const int tok = it.tok0 + qg.j0 + r / G, qh = head * G + r % G;
+      const uint4 *src = reinterpret_cast<const uint4 *>(a.q + (static_cast<size_t>(tok) * a.H + qh) * DH + t * (DH / 4));
 #pragma unroll
       for (int i = 0; i < DH / 32; i++) {
         uint4 u = src[i];
@@ -96,256 +127,322 @@ __global__ void __launch_bounds__(256) attn_kernel(PlanView pv, AttnArgs a) {
     }
 #pragma unroll
     for (int s = 0; s < C::NKS; s++) {
-      qa[s][h] = v[2 * s];
-      qa[s][2 + h] = v[2 * s + 1];
+      qb[nt][s][0] = v[2 * s];
+      qb[nt][s][1] = v[2 * s + 1];
     }
   }
+  // this lane's softmax rows: r = nt*8 + 2t + c
+  int nvis[NT][2];
+  bool rvalid[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+    for (int c = 0; c < 2; c++) {
+      const int r = nt * 8 + 2 * t + c;
+      rvalid[nt][c] = r < nrows;
+      nvis[nt][c] = qg.path_len ? it.pos + qg.path_len : it.pos + qg.j0 + r / G + 1;
+    }
 
   const uint8_t *kbase = static_cast<const uint8_t *>(a.kc);
   const uint8_t *vbase = static_cast<const uint8_t *>(a.vc);
+  // gather group gi's K and V rows into ring slot buf (entries past the list end read real rows and are masked)
   auto issue = [&](int gi, int buf) {
     uint8_t *sK = sm + buf * C::BUF;
     uint8_t *sV = sK + kGroup * C::ROWB;
-    const int i0 = lo + gi * kGroup;
-    for (int c = threadIdx.x; c < 2 * kGroup * C::CHUNKS; c += nthr) {
-      int isv = c / (kGroup * C::CHUNKS), rem = c % (kGroup * C::CHUNKS);
-      int e = rem / C::CHUNKS, ch = rem % C::CHUNKS;
-      int i = i0 + e;
-      bool ok = i < hi;
-      int row = ok ? list_row(pv, it, q0, i) : 0;
-      size_t off = ((static_cast<size_t>(row / kBlock) * a.KVH + head) * kBlock + row % kBlock) * (DH * C::ESZ) + ch * 16;
-      uint8_t *dst = (isv ? sV : sK) + e * C::ROWB + ch * 16;
-      cp_async16_pred(dst, (isv ? vbase : kbase) + off, ok);
-    }
-    if (FP8 && a.exps) {
-      for (int e = threadIdx.x; e < kGroup; e += nthr) {
-        int i = i0 + e;
-        int ek = 0, ev = 0;
-        if (i < hi) {
-          int row = list_row(pv, it, q0, i);
+    const int pg = sPg[gi];
+    if (pg >= 0) {
+      const size_t pb = (static_cast<size_t>(pg) * a.KVH + head) * (kBlock * C::RB);
+#pragma unroll
+      for (int c = tid; c < 2 * kGroup * C::CHUNKS; c += NTHR) {
+        const int isv = c / (kGroup * C::CHUNKS), rem = c % (kGroup * C::CHUNKS);
+        const int e = rem / C::CHUNKS, ch = rem % C::CHUNKS;
+        cp_async16((isv ? sV : sK) + e * C::ROWB + ch * 16, (isv ? vbase : kbase) + pb + e * C::RB + ch * 16);
+      }
+    } else {
+      const int i0 = lo + gi * kGroup;
+#pragma unroll
+      for (int c = tid; c < 2 * kGroup * C::CHUNKS; c += NTHR) {
+        const int isv = c / (kGroup * C::CHUNKS), rem = c % (kGroup * C::CHUNKS);
+        const int e = rem / C::CHUNKS, ch = rem % C::CHUNKS;
+        const int row = list_row(pv, it, q0, min(i0 + e, hi - 1));
+        const size_t off = ((static_cast<size_t>(row / kBlock) * a.KVH + head) * kBlock + row % kBlock) * C::RB + ch * 16;
+        cp_async16((isv ? sV : sK) + e * C::ROWB + ch * 16, (isv ? vbase : kbase) + off);
+      }
+      if (page_exp) {
+        for (int e = tid; e < kGroup; e += NTHR) {
+          const int row = list_row(pv, it, q0, min(i0 + e, hi - 1));
           const int8_t *pe = a.exps + (static_cast<size_t>(row / kBlock) * a.KVH + head) * 2;
-          ek = pe[0];
-          ev = pe[1];
+          sEE[(buf * kGroup + e) * 2] = pe[0];
+          sEE[(buf * kGroup + e) * 2 + 1] = pe[1];
         }
-        sE[(buf * kGroup + e) * 2] = ek;
-        sE[(buf * kGroup + e) * 2 + 1] = ev;
       }
     }
-    cp_async_commit();
   };
 
-  float o[C::NNT][4];
+  float o[NT][C::NMT][4];
 #pragma unroll
-  for (int j = 0; j < C::NNT; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+  for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+    for (int j = 0; j < C::NMT; j++) o[nt][j][0] = o[nt][j][1] = o[nt][j][2] = o[nt][j][3] = 0.f;
+  float mrow[NT][2], lrow[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++) mrow[nt][0] = mrow[nt][1] = -INFINITY, lrow[nt][0] = lrow[nt][1] = 0.f;
   int E = 0;
   bool have_e = false;
 
-  if (ngroups > 0) issue(0, 0);
+  // ring: group gi sits in slot gi % NST; every iteration commits one cp.async group (empty past the end), so waiting
+  // for all but the newest NST - 1 groups means group gi has landed
+#pragma unroll
+  for (int st = 0; st < C::NST - 1; st++) {
+    if (st < ngroups) issue(st, st);
+    cp_async_commit();
+  }
   for (int gi = 0; gi < ngroups; gi++) {
-    const int buf = gi & 1;
-    if (gi + 1 < ngroups) {
-      issue(gi + 1, buf ^ 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
+    const int buf = gi % C::NST;
+    if (gi + C::NST - 1 < ngroups) issue(gi + C::NST - 1, (gi + C::NST - 1) % C::NST);
+    cp_async_commit();
+    cp_async_wait<C::NST - 1>();
     __syncthreads();
     const int i0 = lo + gi * kGroup;
     if (active && i0 < qg.nvis) {
       const uint8_t *sK = sm + buf * C::BUF;
       const uint8_t *sV = sK + kGroup * C::ROWB;
-      // ---- S = Q K^T for entries 0..7 (tile 0) and 8..15 (tile 1)
-      float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      // ---- S^T = K Q^T: A rows g, g+8 (entries), lane t's dim slice
+      constexpr int KW = C::RB / 4 / 4;   // words of a lane's K slice
+      uint32_t k0[KW], k1[KW];
 #pragma unroll
-      for (int tile = 0; tile < 2; tile++) {
-        const uint8_t *kr = sK + (tile * 8 + g) * C::ROWB + t * (DH / 4) * C::ESZ;
-        uint32_t kw[DH / 4 * C::ESZ / 4];
-#pragma unroll
-        for (int i = 0; i < DH / 4 * C::ESZ / 16; i++) {
-          uint4 u = reinterpret_cast<const uint4 *>(kr)[i];
-          kw[4 * i] = u.x; kw[4 * i + 1] = u.y; kw[4 * i + 2] = u.z; kw[4 * i + 3] = u.w;
-        }
-#pragma unroll
-        for (int s = 0; s < C::NKS; s++) {
-          uint32_t b[2];
-          if (FP8) {
-            b[0] = e4m3x2_to_h2(static_cast<uint16_t>(kw[s] & 0xffff));
-            b[1] = e4m3x2_to_h2(static_cast<uint16_t>(kw[s] >> 16));
-          } else {
-            b[0] = kw[2 * s];
-            b[1] = kw[2 * s + 1];
-          }
-          mma_f16(sc[tile], qa[s], b);
-        }
+      for (int i = 0; i < KW / 4; i++) {
+        uint4 u = reinterpret_cast<const uint4 *>(sK + g * C::ROWB + t * (C::RB / 4))[i];
+        k0[4 * i] = u.x; k0[4 * i + 1] = u.y; k0[4 * i + 2] = u.z; k0[4 * i + 3] = u.w;
+        u = reinterpret_cast<const uint4 *>(sK + (g + 8) * C::ROWB + t * (C::RB / 4))[i];
+        k1[4 * i] = u.x; k1[4 * i + 1] = u.y; k1[4 * i + 2] = u.z; k1[4 * i + 3] = u.w;
       }
-      // ---- scale, mask, online softmax (log2 domain)
+      float sc[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+#pragma unroll
+      for (int s = 0; s < C::NKS; s++) {
+        uint32_t af[4];
+        if (FP8) {
+          af[0] = e4m3x2_to_h2(static_cast<uint16_t>(k0[s] & 0xffff));
+          af[2] = e4m3x2_to_h2(static_cast<uint16_t>(k0[s] >> 16));
+          af[1] = e4m3x2_to_h2(static_cast<uint16_t>(k1[s] & 0xffff));
+          af[3] = e4m3x2_to_h2(static_cast<uint16_t>(k1[s] >> 16));
+        } else {
+          af[0] = k0[2 * s]; af[2] = k0[2 * s + 1];
+          af[1] = k1[2 * s]; af[3] = k1[2 * s + 1];
+        }
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) mma_f16(sc[nt], af, qb[nt][s]);
+      }
+      // ---- page scales of entries g and g + 8: 2^-ek on the scores, 2^(evref - ev) on the probabilities
+      float ks0 = a.scale_log2, ks1 = a.scale_log2, pv0 = 1.f, pv1 = 1.f;
       int evref = 0;
-      float pscale[2][2] = {{1.f, 1.f}, {1.f, 1.f}};   // [tile][entry parity]: 2^(evref - ev)
-      float kscale[2][2] = {{1.f, 1.f}, {1.f, 1.f}};
-      if (FP8 && a.exps) {
-        const int *ee = sE + buf * kGroup * 2;
-        evref = ee[1];
-#pragma unroll
-        for (int tile = 0; tile < 2; tile++)
-#pragma unroll
-          for (int c = 0; c < 2; c++) {
-            int e = tile * 8 + 2 * t + c;
-            kscale[tile][c] = exp2f(-static_cast<float>(ee[2 * e]));
-            pscale[tile][c] = exp2f(static_cast<float>(evref - ee[2 * e + 1]));
-          }
-      }
-      float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-      for (int tile = 0; tile < 2; tile++)
-#pragma unroll
-        for (int c = 0; c < 4; c++) {
-          int h = c / 2, e = tile * 8 + 2 * t + (c % 2);
-          bool ok = valid[h] && i0 + e < nvis[h];
-          float v = ok ? sc[tile][c] * a.scale_log2 * kscale[tile][c % 2] : -INFINITY;
-          sc[tile][c] = v;
-          mx[h] = fmaxf(mx[h], v);
+      if (page_exp) {
+        if (sPg[gi] >= 0) {
+          const float k = a.scale_log2 * pow2i(-sGE[2 * gi]);
+          ks0 = ks1 = k;
+          evref = sGE[2 * gi + 1];
+        } else {
+          const int8_t *ee = sEE + buf * kGroup * 2;
+          evref = ee[1];
+          ks0 = a.scale_log2 * pow2i(-ee[2 * g]);
+          ks1 = a.scale_log2 * pow2i(-ee[2 * (g + 8)]);
+          pv0 = pow2i(evref - ee[2 * g + 1]);
+          pv1 = pow2i(evref - ee[2 * (g + 8) + 1]);
         }
-      float alpha[2];
-#pragma unroll
-      for (int h = 0; h < 2; h++) {
-        mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
-        mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
-        float mn = fmaxf(mrow[h], mx[h]);
-        alpha[h] = mn == -INFINITY ? 1.f : exp2f(mrow[h] - mn);
-        mrow[h] = mn;
       }
-      float ps[2] = {0.f, 0.f};
-#pragma unroll
-      for (int tile = 0; tile < 2; tile++)
-#pragma unroll
-        for (int c = 0; c < 4; c++) {
-          int h = c / 2;
-          float p = mrow[h] == -INFINITY ? 0.f : exp2f(sc[tile][c] - mrow[h]);
-          ps[h] += p;
-          sc[tile][c] = p * pscale[tile][c % 2];
-        }
-#pragma unroll
-      for (int h = 0; h < 2; h++) {
-        ps[h] += __shfl_xor_sync(0xffffffffu, ps[h], 1);
-        ps[h] += __shfl_xor_sync(0xffffffffu, ps[h], 2);
-        lrow[h] = lrow[h] * alpha[h] + ps[h];
-      }
-      float f0 = alpha[0], f1 = alpha[1];
-      if (FP8 && a.exps) {
-        float fe = have_e ? exp2f(static_cast<float>(evref - E)) : 1.f;
-        f0 *= fe;
-        f1 *= fe;
+      float fe = 1.f;
+      if (page_exp) {
+        fe = have_e ? pow2i(evref - E) : 1.f;
         E = evref;
         have_e = true;
       }
+      // ---- online softmax per row (log2 domain); a row's 16 entries sit in the 8 lanes of one t
+      uint32_t pb[NT][2];
+      float f[NT][2];
 #pragma unroll
-      for (int j = 0; j < C::NNT; j++) {
-        o[j][0] *= f0; o[j][1] *= f0; o[j][2] *= f1; o[j][3] *= f1;
+      for (int nt = 0; nt < NT; nt++) {
+        float x[2][2];   // [entry g / g+8][row c]
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+          const bool ok0 = rvalid[nt][c] && i0 + g < nvis[nt][c];
+          const bool ok1 = rvalid[nt][c] && i0 + g + 8 < nvis[nt][c];
+          x[0][c] = ok0 ? sc[nt][c] * ks0 : -INFINITY;
+          x[1][c] = ok1 ? sc[nt][2 + c] * ks1 : -INFINITY;
+        }
+        float p[2][2];
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+          float mx = fmaxf(x[0][c], x[1][c]);
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+          const float mn = fmaxf(mrow[nt][c], mx);
+          const float alpha = mn == -INFINITY ? 1.f : exp2f(mrow[nt][c] - mn);
+          mrow[nt][c] = mn;
+          p[0][c] = mn == -INFINITY ? 0.f : exp2f(x[0][c] - mn);
+          p[1][c] = mn == -INFINITY ? 0.f : exp2f(x[1][c] - mn);
+          float ps = p[0][c] + p[1][c];
+          ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+          ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+          ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+          lrow[nt][c] = lrow[nt][c] * alpha + ps;
+          f[nt][c] = alpha * fe;
+        }
+        // P^T as the PV B operand: (entries 2t, 2t+1 | 2t+8, 2t+9) of row g
+        pb[nt][0] = movmatrix_t(pack_h2(p[0][0] * pv0, p[0][1] * pv0));
+        pb[nt][1] = movmatrix_t(pack_h2(p[1][0] * pv1, p[1][1] * pv1));
       }
-      uint32_t pa[4] = {pack_h2(sc[0][0], sc[0][1]), pack_h2(sc[0][2], sc[0][3]), pack_h2(sc[1][0], sc[1][1]),
-                        pack_h2(sc[1][2], sc[1][3])};
-      // ---- O += P V: lane g owns output dims [g*DH/8, (g+1)*DH/8)
-      constexpr int VB = DH / 8 * C::ESZ;   // bytes per entry per lane
-      uint32_t vr[4][VB / 4];
+      // rescaling by exactly 1 changes nothing: skipped when no row of the warp needs it
+      bool one = true;
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++) one = one && f[nt][0] == 1.f && f[nt][1] == 1.f;
+      if (!__all_sync(0xffffffffu, one)) {
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+          for (int j = 0; j < C::NMT; j++) {
+            o[nt][j][0] *= f[nt][0]; o[nt][j][1] *= f[nt][1]; o[nt][j][2] *= f[nt][0]; o[nt][j][3] *= f[nt][1];
+          }
+      }
+      // ---- O^T += V^T P^T: lane (g, t) reads entries 2t, 2t+1, 2t+8, 2t+9, dims [g*dh/8, (g+1)*dh/8)
+      constexpr int VW = C::RB / 8 / 4;   // words of a lane's V slice per entry
+      uint32_t vr[4][VW];
 #pragma unroll
       for (int q = 0; q < 4; q++) {
-        int e = 2 * t + (q & 1) + (q >> 1) * 8;      // entries 2t, 2t+1, 2t+8, 2t+9
-        if (VB >= 16) {
-          const uint4 *src = reinterpret_cast<const uint4 *>(sV + e * C::ROWB + g * VB);
+        const int e = 2 * t + (q & 1) + (q >> 1) * 8;
+        const uint8_t *src = sV + e * C::ROWB + g * (C::RB / 8);
+        if (VW >= 4) {
 #pragma unroll
-          for (int i = 0; i < VB / 16; i++) {
-            uint4 u = src[i];
+          for (int i = 0; i < VW / 4; i++) {
+            uint4 u = reinterpret_cast<const uint4 *>(src)[i];
             vr[q][4 * i] = u.x; vr[q][4 * i + 1] = u.y; vr[q][4 * i + 2] = u.z; vr[q][4 * i + 3] = u.w;
           }
         } else {   // 8 bytes: fp8 with dh 64
-          uint2 u = *reinterpret_cast<const uint2 *>(sV + e * C::ROWB + g * VB);
+          uint2 u = *reinterpret_cast<const uint2 *>(src);
           vr[q][0] = u.x;
-          vr[q][VB / 4 - 1] = u.y;
+          vr[q][VW - 1] = u.y;
         }
       }
 #pragma unroll
-      for (int j = 0; j < C::NNT; j++) {
-        uint32_t b[2];
+      for (int mt = 0; mt < C::NMT; mt++) {
+        uint32_t af[4];
         if (FP8) {
-          // byte j of entries (2t, 2t+1) and (2t+8, 2t+9)
-          uint32_t sel = (j % 4) | ((4 + j % 4) << 4);
-          b[0] = e4m3x2_to_h2(static_cast<uint16_t>(prmt(vr[0][j / 4], vr[1][j / 4], sel)));
-          b[1] = e4m3x2_to_h2(static_cast<uint16_t>(prmt(vr[2][j / 4], vr[3][j / 4], sel)));
+          // dims 2mt (rows g) and 2mt + 1 (rows g + 8) of the slice: byte 2mt % 4 (+1) of word mt / 2
+          const int wi = mt / 2, b0 = 2 * (mt % 2);
+          const uint32_t s0 = b0 | ((4 + b0) << 4), s1 = (b0 + 1) | ((5 + b0) << 4);
+          af[0] = e4m3x2_to_h2(static_cast<uint16_t>(prmt(vr[0][wi], vr[1][wi], s0)));
+          af[1] = e4m3x2_to_h2(static_cast<uint16_t>(prmt(vr[0][wi], vr[1][wi], s1)));
+          af[2] = e4m3x2_to_h2(static_cast<uint16_t>(prmt(vr[2][wi], vr[3][wi], s0)));
+          af[3] = e4m3x2_to_h2(static_cast<uint16_t>(prmt(vr[2][wi], vr[3][wi], s1)));
         } else {
-          uint32_t sel = (j % 2) ? 0x7632u : 0x5410u;
-          b[0] = prmt(vr[0][j / 2], vr[1][j / 2], sel);
-          b[1] = prmt(vr[2][j / 2], vr[3][j / 2], sel);
+          af[0] = prmt(vr[0][mt], vr[1][mt], 0x5410u);
+          af[1] = prmt(vr[0][mt], vr[1][mt], 0x7632u);
+          af[2] = prmt(vr[2][mt], vr[3][mt], 0x5410u);
+          af[3] = prmt(vr[2][mt], vr[3][mt], 0x7632u);
         }
-        mma_f16(o[j], pa, b);
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) mma_f16(o[nt][mt], af, pb[nt]);
       }
     }
     __syncthreads();
   }
+  cp_async_wait<0>();
 
   if (!active || w.split >= qg.nsplit) return;
-  const int pi = qg.part_base + head * qg.nsplit + w.split;
-  const float inv = (FP8 && a.exps && have_e) ? exp2f(-static_cast<float>(E)) : 1.f;
-#pragma unroll
-  for (int h = 0; h < 2; h++) {
-    if (!valid[h]) continue;
-    int r = g + 8 * h;
-    float *dst = a.part_o + (static_cast<size_t>(pi) * 16 + r) * DH;
-#pragma unroll
-    for (int j = 0; j < C::NNT; j++) {
-      dst[(2 * t) * (DH / 8) + j] = o[j][2 * h] * inv;
-      dst[(2 * t + 1) * (DH / 8) + j] = o[j][2 * h + 1] * inv;
-    }
-    if (t == 0) a.part_ml[static_cast<size_t>(pi) * 16 + r] = make_float2(mrow[h], lrow[h]);
-  }
-}
-
-// out[token, head, :] = sum_s O_s 2^(m_s - m) / sum_s l_s 2^(m_s - m), splits in order
-template <int DH>
-__global__ void attn_combine(PlanView pv, AttnArgs a) {
-  const QGroup qg = pv.qgroups[blockIdx.x];
-  const Item it = pv.items[qg.item];
-  const int head = blockIdx.y, G = a.H / a.KVH;
   const int rows = qg.ntok * G;
-  for (int i = threadIdx.x; i < rows * DH; i += blockDim.x) {
-    int r = i / DH, d = i % DH;
-    const int pb = qg.part_base + head * qg.nsplit;
+  const float inv = (page_exp && have_e) ? pow2i(-E) : 1.f;
+  if (qg.nsplit == 1) {
+    // the whole list in one split: out = (O 2^-E) / l, which is what the merge below computes for a single split
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+      for (int c = 0; c < 2; c++) {
+        if (!rvalid[nt][c]) continue;
+        const int r = nt * 8 + 2 * t + c;
+        const int tok = it.tok0 + qg.j0 + r / G, qo = head * G + r % G;
+        uint32_t wv[C::NMT];
+#pragma unroll
+        for (int mt = 0; mt < C::NMT; mt++)
+          wv[mt] = pack_h2((o[nt][mt][c] * inv) / lrow[nt][c], (o[nt][mt][2 + c] * inv) / lrow[nt][c]);
+        uint32_t *dst = reinterpret_cast<uint32_t *>(a.out + (static_cast<size_t>(tok) * a.H + qo) * DH + g * (DH / 8));
+#pragma unroll
+        for (int mt = 0; mt < C::NMT; mt++) dst[mt] = wv[mt];
+      }
+    return;
+  }
+  const int pi = qg.part_base + head * qg.nsplit + w.split;
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+    for (int c = 0; c < 2; c++) {
+      if (!rvalid[nt][c]) continue;
+      const int r = nt * 8 + 2 * t + c;
+      float2 *dst = reinterpret_cast<float2 *>(a.part_o + (static_cast<size_t>(pi) * 16 + r) * DH + g * (DH / 8));
+#pragma unroll
+      for (int mt = 0; mt < C::NMT; mt++) dst[mt] = make_float2(o[nt][mt][c] * inv, o[nt][mt][2 + c] * inv);
+      if (g == 0) a.part_ml[static_cast<size_t>(pi) * 16 + r] = make_float2(mrow[nt][c], lrow[nt][c]);
+    }
+  // ---- the last split of (query group, kv head) to finish merges them all, in split order:
+  // out = sum_s O_s 2^(m_s - m) / sum_s l_s 2^(m_s - m). Which split finishes last does not change the arithmetic.
+  __threadfence();
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) last = atomicAdd(&a.sem[qgi * a.KVH + head], 1) == qg.nsplit - 1;
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (!last) return;
+  __threadfence();
+  const int pb0 = qg.part_base + head * qg.nsplit;
+  for (int r = 0; r < rows; r++) {
     float m = -INFINITY;
-    for (int s = 0; s < qg.nsplit; s++) m = fmaxf(m, a.part_ml[static_cast<size_t>(pb + s) * 16 + r].x);
-    float num = 0.f, den = 0.f;
+    for (int s = 0; s < qg.nsplit; s++) m = fmaxf(m, __ldcg(&a.part_ml[static_cast<size_t>(pb0 + s) * 16 + r]).x);
+    float num[DH / 32], den = 0.f;
+#pragma unroll
+    for (int k = 0; k < DH / 32; k++) num[k] = 0.f;
     for (int s = 0; s < qg.nsplit; s++) {
-      float2 ml = a.part_ml[static_cast<size_t>(pb + s) * 16 + r];
-      float wgt = ml.x == -INFINITY ? 0.f : exp2f(ml.x - m);
-      num += a.part_o[(static_cast<size_t>(pb + s) * 16 + r) * DH + d] * wgt;
+      const float2 ml = __ldcg(&a.part_ml[static_cast<size_t>(pb0 + s) * 16 + r]);
+      const float wgt = ml.x == -INFINITY ? 0.f : exp2f(ml.x - m);
+      const float *po = a.part_o + (static_cast<size_t>(pb0 + s) * 16 + r) * DH;
+#pragma unroll
+      for (int k = 0; k < DH / 32; k++) num[k] += __ldcg(po + lane + 32 * k) * wgt;
       den += ml.y * wgt;
     }
-    int tok = it.tok0 + qg.j0 + r / G, qh = head * G + r % G;
-    a.out[(static_cast<size_t>(tok) * a.H + qh) * DH + d] = __float2half_rn(num / den);
+    const int tok = it.tok0 + qg.j0 + r / G, qo = head * G + r % G;
+    __half *dst = a.out + (static_cast<size_t>(tok) * a.H + qo) * DH;
+#pragma unroll
+    for (int k = 0; k < DH / 32; k++) dst[lane + 32 * k] = __float2half_rn(num[k] / den);
   }
+  if (lane == 0) a.sem[qgi * a.KVH + head] = 0;   // ready for the next launch
 }
 
-template <int DH, bool FP8>
-void launch_t(const PlanView &pv, const AttnArgs &a, int nw, cudaStream_t s) {
+template <int DH, bool FP8, int NW, int NT>
+void launch_t(const PlanView &pv, const AttnArgs &a, cudaStream_t s) {
   using C = Cfg<DH, FP8>;
-  if (pv.n_work > 0) attn_kernel<DH, FP8><<<pv.n_work, 32 * nw, C::SMEM, s>>>(pv, a);
+  if (pv.n_work > 0) attn_kernel<DH, FP8, NW, NT><<<pv.n_work, 32 * NW, C::SMEM, s>>>(pv, a);
+}
+template <int DH, bool FP8>
+void launch_dh(const PlanView &pv, const AttnArgs &a, int nw, cudaStream_t s) {
+  const bool wide = pv.max_rows > 8;
+  if (nw > 1) {
+    if (wide) launch_t<DH, FP8, 8, 2>(pv, a, s);
+    else launch_t<DH, FP8, 8, 1>(pv, a, s);
+  } else {
+    if (wide) launch_t<DH, FP8, 1, 2>(pv, a, s);
+    else launch_t<DH, FP8, 1, 1>(pv, a, s);
+  }
 }
 
 }  // namespace
 
 void launch_attention(const PlanView &pv, const AttnArgs &a, int nw, cudaStream_t s) {
   if (a.dh == 128) {
-    if (a.kv_fp8) launch_t<128, true>(pv, a, nw, s);
-    else launch_t<128, false>(pv, a, nw, s);
+    if (a.kv_fp8) launch_dh<128, true>(pv, a, nw, s);
+    else launch_dh<128, false>(pv, a, nw, s);
   } else {
-    if (a.kv_fp8) launch_t<64, true>(pv, a, nw, s);
-    else launch_t<64, false>(pv, a, nw, s);
+    if (a.kv_fp8) launch_dh<64, true>(pv, a, nw, s);
+    else launch_dh<64, false>(pv, a, nw, s);
   }
-}
-
-void launch_attention_combine(const PlanView &pv, const AttnArgs &a, cudaStream_t s) {
-  if (pv.n_qg <= 0) return;
-  if (a.dh == 128) attn_combine<128><<<dim3(pv.n_qg, a.KVH), 128, 0, s>>>(pv, a);
-  else attn_combine<64><<<dim3(pv.n_qg, a.KVH), 128, 0, s>>>(pv, a);
 }
 
 }  // namespace gck

@@ -77,7 +77,8 @@ void gemm_tc_init();      // once per device
 void launch_gemm_tc(const QWeight &w, const TmaSet &ts, int T, const Epi &epi, float *part, int *err, int sms,
                     cudaStream_t s);
 
-// Paged attention over the plan's work list: q [T, H, dh] f16 -> out [T, H, dh] f16. part_o / part_ml: split partials.
+// Paged attention over the plan's work list: q [T, H, dh] f16 -> out [T, H, dh] f16. part_o / part_ml: split partials,
+// merged by the last split to finish.
 struct AttnArgs {
   const __half *q;
   const void *kc, *vc;       // this layer's pages [nblk][KVH][16][dh]
@@ -85,10 +86,10 @@ struct AttnArgs {
   __half *out;
   float *part_o;             // [n_parts, 16, dh]
   float2 *part_ml;           // [n_parts, 16] (running max in log2 units, sum)
+  int *sem;                  // [n_qg, KVH] finished splits (zero between launches)
   int H, KVH, dh, kv_fp8;
   float scale_log2;          // log2(e) / sqrt(dh)
 };
 void launch_attention(const PlanView &pv, const AttnArgs &a, int nw, cudaStream_t s);
-void launch_attention_combine(const PlanView &pv, const AttnArgs &a, cudaStream_t s);
 
 }  // namespace gck

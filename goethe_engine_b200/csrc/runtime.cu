@@ -98,7 +98,8 @@ struct gc_handle {
   int *argmax = nullptr, *pairs = nullptr;
   int *kerr = nullptr, *kerr_host = nullptr;   // device error word of bounded waits, and its pinned mirror
   TmaSet tma_h, tma_att, tma_act;               // activation tiles of the tcgen05 GEMMs
-  size_t part_cap = 0, attn_parts_cap = 0, commit_cap = 0, pairs_cap = 0;
+  size_t part_cap = 0, attn_parts_cap = 0, attn_sem_cap = 0, commit_cap = 0, pairs_cap = 0;
+  int *attn_sem = nullptr;
   uint8_t *plan_dev = nullptr, *plan_host = nullptr;
   size_t plan_cap = 0;
   int *tok_host = nullptr;
@@ -822,6 +823,8 @@ PlanView upload_plan(gc_handle *h, HostPlan &pl) {
   pv.n_work = static_cast<int>(pl.work.size());
   pv.R = static_cast<int>(pl.want_tok.size());
   pv.n_parts = pl.n_parts;
+  pv.max_rows = 0;
+  for (const QGroup &q : pl.qgroups) pv.max_rows = std::max(pv.max_rows, q.ntok * (h->H / h->KVH));
   return pv;
 }
 
@@ -843,6 +846,16 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
     h->attn_o = static_cast<float *>(h->dalloc(cap * 16 * h->dh * 4, "attention partials"));
     h->attn_ml = static_cast<float2 *>(h->dalloc(cap * 16 * 8, "attention partials"));
     h->attn_parts_cap = cap;
+  }
+  // per (query group, kv head): splits finished so far; zero between launches (the merging split resets it)
+  const size_t nsem = static_cast<size_t>(pv.n_qg) * h->KVH;
+  if (nsem > h->attn_sem_cap) {
+    cudaStreamSynchronize(s);
+    if (h->attn_sem) h->dfree(h->attn_sem, h->attn_sem_cap * 4);
+    size_t cap = std::max<size_t>(nsem, h->attn_sem_cap * 3 / 2);
+    h->attn_sem = static_cast<int *>(h->dalloc(cap * 4, "attention split counters"));
+    ck(cudaMemsetAsync(h->attn_sem, 0, cap * 4, s), "attention split counters");
+    h->attn_sem_cap = cap;
   }
   h->step_launches = 0;
   // run(cls, kernels, fn): launch fn on the stream, bracketed by events when the class is being timed
@@ -878,6 +891,7 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
   aa.out = h->att;
   aa.part_o = h->attn_o;
   aa.part_ml = h->attn_ml;
+  aa.sem = h->attn_sem;
   aa.H = h->H;
   aa.KVH = h->KVH;
   aa.dh = h->dh;
@@ -896,7 +910,6 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
     aa.vc = vc;
     aa.exps = h->page_scale ? ex : nullptr;
     run(GCK_K_ATTN, 1, [&] { launch_attention(pv, aa, nw, s); });
-    run(GCK_K_COMBINE, 1, [&] { launch_attention_combine(pv, aa, s); });
     gemm(GCK_K_O, ly.o, h->tma_att, h->att, T, Epi{kEpiAdd, h->d, h->d, h->x, nullptr});
     run(GCK_K_NORM, 1, [&] { launch_rmsnorm(h->x, nullptr, T, ly.ffn_norm, h->eps, h->d, h->d, h->h, s); });
     gemm(GCK_K_GATEUP, ly.gu, h->tma_h, h->h, T, Epi{kEpiSwiGLU, h->F, ly.dn.KT * kBK, nullptr, h->act});
