@@ -47,16 +47,19 @@ void launch_embed(const PlanView &pv, const uint8_t *emb, int type, size_t row_b
 
 // ----------------------------------------------------------------------------------------------------------------
 // RMSNorm: out[r, :] = f16(x[src(r), :] * rsqrt(mean(x^2) + eps) * gain); columns d .. ld-1 are zeroed.
+// With residual partials (a split-K o_proj / down_proj before it): first x[src] += sum_s part[s, src, :] (splits in
+// order, from 0), written back, as that GEMM's residual-add epilogue would have.
 // One CTA per row; float4 loads, all issued before the first use. The sum of squares has a fixed order (each thread's
 // strided partials in index order, then a fixed shuffle tree, then the warps in index order), independent of the batch.
 constexpr int kNormThreads = 512;
 constexpr int kNormMaxVec = 4;    // float4 loads per thread: d <= 512 * 4 * 4 = 8192
 
-__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float *x, const int *rows, const float *gain,
-                                                               float eps, int d, int ld, __half *out) {
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float *x, const int *rows, const float *gain, float eps,
+                                                               int d, int ld, __half *out, const float *part, int S,
+                                                               int pld, int T) {
   int r = blockIdx.x;
   int src = rows ? rows[r] : r;
-  const float4 *xr = reinterpret_cast<const float4 *>(x + static_cast<size_t>(src) * d);
+  float4 *xr = reinterpret_cast<float4 *>(x + static_cast<size_t>(src) * d);
   const float4 *gr = reinterpret_cast<const float4 *>(gain);
   const int nv = d / 4;
   float4 v[kNormMaxVec];
@@ -64,6 +67,20 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float *x, c
   for (int i = 0; i < kNormMaxVec; i++) {
     int e = threadIdx.x + i * kNormThreads;
     v[i] = e < nv ? xr[e] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  if (part) {
+#pragma unroll
+    for (int i = 0; i < kNormMaxVec; i++) {
+      int e = threadIdx.x + i * kNormThreads;
+      if (e >= nv) continue;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int sp = 0; sp < S; sp++) {
+        const float4 pp = reinterpret_cast<const float4 *>(part + (static_cast<size_t>(sp) * T + src) * pld)[e];
+        a.x += pp.x; a.y += pp.y; a.z += pp.z; a.w += pp.w;
+      }
+      v[i].x += a.x; v[i].y += a.y; v[i].z += a.z; v[i].w += a.w;
+      xr[e] = v[i];
+    }
   }
   float ss = 0.f;
 #pragma unroll
@@ -74,17 +91,17 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float *x, c
     ss = fmaf(v[i].w, v[i].w, ss);
   }
   ss = warp_sum(ss);
-  __shared__ float part[32];
+  __shared__ float wsum[32];
   int w = threadIdx.x / 32, l = threadIdx.x % 32;
-  if (l == 0) part[w] = ss;
+  if (l == 0) wsum[w] = ss;
   __syncthreads();
   if (w == 0) {
-    float s2 = l < kNormThreads / 32 ? part[l] : 0.f;
+    float s2 = l < kNormThreads / 32 ? wsum[l] : 0.f;
     s2 = warp_sum(s2);
-    if (l == 0) part[0] = s2;
+    if (l == 0) wsum[0] = s2;
   }
   __syncthreads();
-  float inv = rsqrtf(part[0] / static_cast<float>(d) + eps);
+  float inv = rsqrtf(wsum[0] / static_cast<float>(d) + eps);
   __half2 *o = reinterpret_cast<__half2 *>(out + static_cast<size_t>(r) * ld);
 #pragma unroll
   for (int i = 0; i < kNormMaxVec; i++) {
@@ -98,13 +115,13 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float *x, c
   for (int e = d / 2 + threadIdx.x; e < ld / 2; e += kNormThreads) o[e] = __floats2half2_rn(0.f, 0.f);
 }
 
-void launch_rmsnorm(const float *x, const int *rows, int n, const float *gain, float eps, int d, int ld, __half *out,
-                    cudaStream_t s) {
-  if (n > 0) rmsnorm_kernel<<<n, kNormThreads, 0, s>>>(x, rows, gain, eps, d, ld, out);
+void launch_rmsnorm(float *x, const int *rows, int n, const float *gain, float eps, int d, int ld, __half *out,
+                    const float *part, int S, int pld, int T, cudaStream_t s) {
+  if (n > 0) rmsnorm_kernel<<<n, kNormThreads, 0, s>>>(x, rows, gain, eps, d, ld, out, part, S, pld, T);
 }
 
 // ----------------------------------------------------------------------------------------------------------------
-// RoPE and KV write. qkv [T, (H + 2 KVH) * dh] f32 -> q [T, H, dh] f16 (rotated); K (rotated) and V -> the layer's
+// RoPE and KV write. qkv [T, (H + 2 KVH) * dh] f32 (or its split-K partials) -> q [T, H, dh] f16 (rotated); K (rotated) and V -> the layer's
 // pages. fp8 page mode: a page's exponent e (scale 2^e) is set by the row that is its first (row % 16 == 0) from that
 // row's amax (the largest e with amax * 2^e <= 64, clamped to [-8, 15]); later rows of the page use it, also within
 // the same step (a token recomputes its page's first row from this step's qkv).
@@ -116,48 +133,57 @@ __device__ int page_exp(float amax) {
   return min(max(e, -8), 15);
 }
 
-__device__ void rope_pair(const float *src, const float2 *cs, int i, float &a, float &b) {
-  float x0 = src[2 * i], x1 = src[2 * i + 1];
+// the q/k/v projection output: the GEMM's rows, or its split-K partials summed in split order (from 0)
+struct QkvSrc {
+  const float *p;
+  int S;            // 1: p is [T, ld]; > 1: p is [S, T, ld] partials
+  int ld, T;
+  __device__ float operator()(int t, int c) const {
+    if (S == 1) return p[static_cast<size_t>(t) * ld + c];
+    float v = 0.f;
+    for (int s = 0; s < S; s++) v += p[(static_cast<size_t>(s) * T + t) * ld + c];
+    return v;
+  }
+};
+
+__device__ void rope_pair(const QkvSrc &q, int t, int c0, const float2 *cs, int i, float &a, float &b) {
+  float x0 = q(t, c0 + 2 * i), x1 = q(t, c0 + 2 * i + 1);
   float2 c = cs[i];
   a = x0 * c.x - x1 * c.y;
   b = x0 * c.y + x1 * c.x;
 }
 
 template <int DH>
-__device__ float head_amax(const float *src, const float2 *cs, bool rot) {
+__device__ float head_amax(const QkvSrc &q, int t, int c0, const float2 *cs, bool rot) {
   float m = 0.f;
   for (int i = threadIdx.x % 32; i < DH / 2; i += 32) {
     float a, b;
-    if (rot) rope_pair(src, cs, i, a, b);
-    else { a = src[2 * i]; b = src[2 * i + 1]; }
+    if (rot) rope_pair(q, t, c0, cs, i, a, b);
+    else { a = q(t, c0 + 2 * i); b = q(t, c0 + 2 * i + 1); }
     m = fmaxf(m, fmaxf(fabsf(a), fabsf(b)));
   }
   return warp_max(m);
 }
 
 template <int DH>
-__global__ void rope_kv_kernel(PlanView pv, const float *qkv, int H, int KVH, const float2 *rope_tab, __half *q,
-                               void *kc, void *vc, int8_t *exps, int kv_fp8, int page_scale) {
+__global__ void rope_kv_kernel(PlanView pv, QkvSrc qs, int H, int KVH, const float2 *rope_tab, __half *q, void *kc,
+                               void *vc, int8_t *exps, int kv_fp8, int page_scale) {
   int t = blockIdx.x;
   int hh = threadIdx.x / 32 + blockIdx.y * (blockDim.x / 32);  // head slot: [0, H) q heads, [H, H + KVH) kv heads
   if (hh >= H + KVH) return;
   int lane = threadIdx.x % 32;
-  const int W = (H + 2 * KVH) * DH;
-  const float *row = qkv + static_cast<size_t>(t) * W;
   const float2 *cs = rope_tab + static_cast<size_t>(pv.rope_pos[t]) * (DH / 2);
   if (hh < H) {
-    const float *src = row + hh * DH;
     __half2 *dst = reinterpret_cast<__half2 *>(q + (static_cast<size_t>(t) * H + hh) * DH);
     for (int i = lane; i < DH / 2; i += 32) {
       float a, b;
-      rope_pair(src, cs, i, a, b);
+      rope_pair(qs, t, hh * DH, cs, i, a, b);
       dst[i] = __floats2half2_rn(a, b);
     }
     return;
   }
   int h = hh - H;
-  const float *ks = row + H * DH + h * DH;
-  const float *vs = row + (H + KVH) * DH + h * DH;
+  const int kcol = H * DH + h * DH, vcol = (H + KVH) * DH + h * DH;
   int r = pv.kv_row[t];
   int blk = r / kBlock, rip = r % kBlock;
   size_t off = ((static_cast<size_t>(blk) * KVH + h) * kBlock + rip) * DH;
@@ -166,9 +192,9 @@ __global__ void rope_kv_kernel(PlanView pv, const float *qkv, int H, int KVH, co
     __half2 *vd = reinterpret_cast<__half2 *>(static_cast<__half *>(vc) + off);
     for (int i = lane; i < DH / 2; i += 32) {
       float a, b;
-      rope_pair(ks, cs, i, a, b);
+      rope_pair(qs, t, kcol, cs, i, a, b);
       kd[i] = __floats2half2_rn(a, b);
-      vd[i] = __floats2half2_rn(vs[2 * i], vs[2 * i + 1]);
+      vd[i] = __floats2half2_rn(qs(t, vcol + 2 * i), qs(t, vcol + 2 * i + 1));
     }
     return;
   }
@@ -178,10 +204,9 @@ __global__ void rope_kv_kernel(PlanView pv, const float *qkv, int H, int KVH, co
     int8_t *pe = exps + (static_cast<size_t>(blk) * KVH + h) * 2;
     if (ft >= 0) {
       // the page's first row is written in this step (possibly by this token): derive its exponents
-      const float *frow = qkv + static_cast<size_t>(ft) * W;
       const float2 *fcs = rope_tab + static_cast<size_t>(pv.rope_pos[ft]) * (DH / 2);
-      ek = page_exp(head_amax<DH>(frow + H * DH + h * DH, fcs, true));
-      ev = page_exp(head_amax<DH>(frow + (H + KVH) * DH + h * DH, fcs, false));
+      ek = page_exp(head_amax<DH>(qs, ft, kcol, fcs, true));
+      ev = page_exp(head_amax<DH>(qs, ft, vcol, fcs, false));
       if (ft == t && lane == 0) { pe[0] = static_cast<int8_t>(ek); pe[1] = static_cast<int8_t>(ev); }
     } else {
       ek = pe[0];
@@ -193,22 +218,24 @@ __global__ void rope_kv_kernel(PlanView pv, const float *qkv, int H, int KVH, co
   uint8_t *vd = static_cast<uint8_t *>(vc) + off;
   for (int i = lane; i < DH / 2; i += 32) {
     float a, b;
-    rope_pair(ks, cs, i, a, b);
+    rope_pair(qs, t, kcol, cs, i, a, b);
     kd[2 * i] = f32_to_e4m3(a * sk);
     kd[2 * i + 1] = f32_to_e4m3(b * sk);
-    vd[2 * i] = f32_to_e4m3(vs[2 * i] * sv);
-    vd[2 * i + 1] = f32_to_e4m3(vs[2 * i + 1] * sv);
+    vd[2 * i] = f32_to_e4m3(qs(t, vcol + 2 * i) * sv);
+    vd[2 * i + 1] = f32_to_e4m3(qs(t, vcol + 2 * i + 1) * sv);
   }
 }
 
-void launch_rope_kv(const PlanView &pv, const float *qkv, int H, int KVH, int dh, const float2 *rope_tab, __half *q,
-                    void *kc, void *vc, int8_t *exps, int kv_fp8, int page_scale, cudaStream_t s) {
+void launch_rope_kv(const PlanView &pv, const float *qkv, int S, int ld, int H, int KVH, int dh,
+                    const float2 *rope_tab, __half *q, void *kc, void *vc, int8_t *exps, int kv_fp8, int page_scale,
+                    cudaStream_t s) {
   int heads = H + KVH, per = 8;
   dim3 grid(pv.T, (heads + per - 1) / per);
+  QkvSrc qs{qkv, S, ld, pv.T};
   if (dh == 128)
-    rope_kv_kernel<128><<<grid, per * 32, 0, s>>>(pv, qkv, H, KVH, rope_tab, q, kc, vc, exps, kv_fp8, page_scale);
+    rope_kv_kernel<128><<<grid, per * 32, 0, s>>>(pv, qs, H, KVH, rope_tab, q, kc, vc, exps, kv_fp8, page_scale);
   else
-    rope_kv_kernel<64><<<grid, per * 32, 0, s>>>(pv, qkv, H, KVH, rope_tab, q, kc, vc, exps, kv_fp8, page_scale);
+    rope_kv_kernel<64><<<grid, per * 32, 0, s>>>(pv, qs, H, KVH, rope_tab, q, kc, vc, exps, kv_fp8, page_scale);
 }
 
 // ----------------------------------------------------------------------------------------------------------------

@@ -48,10 +48,13 @@ struct QWeight {            // a relaid-out weight on the device
 };
 
 void launch_embed(const PlanView &pv, const uint8_t *emb, int type, size_t row_bytes, int d, float *x, cudaStream_t s);
-void launch_rmsnorm(const float *x, const int *rows, int n, const float *gain, float eps, int d, int ld, __half *out,
+// part (nullable): S split-K partials [S, T, pld] of a residual-add GEMM, added into x before the norm
+void launch_rmsnorm(float *x, const int *rows, int n, const float *gain, float eps, int d, int ld, __half *out,
+                    const float *part, int S, int pld, int T, cudaStream_t s);
+// qkv: [T, ld] rows (S == 1) or [S, T, ld] split-K partials
+void launch_rope_kv(const PlanView &pv, const float *qkv, int S, int ld, int H, int KVH, int dh,
+                    const float2 *rope_tab, __half *q, void *kc, void *vc, int8_t *exps, int kv_fp8, int page_scale,
                     cudaStream_t s);
-void launch_rope_kv(const PlanView &pv, const float *qkv, int H, int KVH, int dh, const float2 *rope_tab, __half *q,
-                    void *kc, void *vc, int8_t *exps, int kv_fp8, int page_scale, cudaStream_t s);
 void launch_splitk_reduce(const float *part, int S, int T, int Npad, const Epi &epi, cudaStream_t s);
 void launch_argmax(const float *logits, int R, int V, int *out, cudaStream_t s);
 void launch_copy_blocks(const int *pairs, int n, int L, size_t page_bytes, size_t layer_bytes, uint8_t *kc,
@@ -60,7 +63,8 @@ void launch_commit(const int *moves, int n, int L, int KVH, int dh, uint8_t *kc,
                    int kv_fp8, size_t layer_bytes, size_t exps_layer, float *tmp, cudaStream_t s);
 
 // y = act[T, Kpad] (f16, row-major, Kpad = KT * kBK) times W^T, with the epilogue; part: split-K scratch
-// [splits, T, NT * kBM] f32 (unused when splits == 1). With splits > 1 the GEMM writes only the partials and the caller
+// [splits, T, NT * kBM] f32 (unused when splits == 1). With splits > 1 the GEMM writes only the partials: the
+// reader sums them in split order (launch_splitk_reduce, or the next RMSNorm / RoPE kernel). With splits > 1 the GEMM writes only the partials and the caller
 // launches launch_splitk_reduce (the sum in split order and the epilogue) after it.
 // F16 weights: mma.sync kernel (k_gemm.cu). Q4_K / Q8_0 weights: tcgen05 kernel (k_gemm_tc.cu), whose activation
 // tiles come through TMA tensor maps over the activation buffer, one map per token tile size.

@@ -874,14 +874,31 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
     }
     h->step_launches += nk;
   };
-  // a GEMM under class cls; with split-K its reduction (and epilogue) is a second launch, timed as GCK_K_REDUCE
-  auto gemm = [&](int cls, const QWeight &w, const TmaSet &ts, const __half *act, int rows, const Epi &e) {
+  // A GEMM under class cls. With split-K it writes partials; their reader sums them in split order: the RMSNorm after
+  // a residual-add projection (o_proj, down_proj), the RoPE kernel after q/k/v, else a reduce launch (GCK_K_REDUCE).
+  auto gemm = [&](int cls, const QWeight &w, const TmaSet &ts, const __half *act, int rows, const Epi &e,
+                  bool reader_reduces) {
     run(cls, 1, [&] {
       if (w.type == kF16) launch_gemm(w, act, rows, e, h->part, s);
       else launch_gemm_tc(w, ts, rows, e, h->part, h->kerr, h->sms, s);
     });
-    if (w.splits > 1 && rows > 0)
+    if (w.splits > 1 && rows > 0 && !reader_reduces)
       run(GCK_K_REDUCE, 1, [&] { launch_splitk_reduce(h->part, w.splits, rows, w.NT * kBM, e, s); });
+  };
+  // residual partials waiting for the next RMSNorm (splits of the last o_proj / down_proj, 0: none)
+  int pend_s = 0, pend_ld = 0;
+  auto norm = [&](const int *rows, int n, const float *gain) {
+    const float *pp = pend_s > 1 ? h->part : nullptr;
+    const int ps = pend_s, pl = pend_ld;
+    run(GCK_K_NORM, 1, [&] { launch_rmsnorm(h->x, rows, n, gain, h->eps, h->d, h->d, h->h, pp, ps, pl, T, s); });
+    pend_s = 0;
+  };
+  auto residual = [&](int cls, const QWeight &w, const TmaSet &ts, const __half *act) {
+    gemm(cls, w, ts, act, T, Epi{kEpiAdd, h->d, h->d, h->x, nullptr}, true);
+    if (w.splits > 1) {
+      pend_s = w.splits;
+      pend_ld = w.NT * kBM;
+    }
   };
 
   run(GCK_K_EMBED, 1, [&] { launch_embed(pv, h->emb, h->emb_type, h->emb_row_bytes, h->d, h->x, s); });
@@ -899,25 +916,27 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
   aa.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(h->dh)));
   for (int l = 0; l < h->L; l++) {
     const Layer &ly = h->layers[l];
-    run(GCK_K_NORM, 1, [&] { launch_rmsnorm(h->x, nullptr, T, ly.attn_norm, h->eps, h->d, h->d, h->h, s); });
-    gemm(GCK_K_QKV, ly.qkv, h->tma_h, h->h, T, Epi{kEpiStore, wq, wq, h->qkv, nullptr});
+    norm(nullptr, T, ly.attn_norm);
+    gemm(GCK_K_QKV, ly.qkv, h->tma_h, h->h, T, Epi{kEpiStore, wq, wq, h->qkv, nullptr}, true);
     uint8_t *kc = h->kc + l * h->layer_bytes, *vc = h->vc + l * h->layer_bytes;
     int8_t *ex = h->exps ? h->exps + l * h->exps_layer : nullptr;
+    const bool qsplit = ly.qkv.splits > 1;
     run(GCK_K_ROPE, 1, [&] {
-      launch_rope_kv(pv, h->qkv, h->H, h->KVH, h->dh, h->rope, h->q, kc, vc, ex, h->kv_fp8, h->page_scale, s);
+      launch_rope_kv(pv, qsplit ? h->part : h->qkv, ly.qkv.splits, qsplit ? ly.qkv.NT * kBM : wq, h->H, h->KVH, h->dh,
+                     h->rope, h->q, kc, vc, ex, h->kv_fp8, h->page_scale, s);
     });
     aa.kc = kc;
     aa.vc = vc;
     aa.exps = h->page_scale ? ex : nullptr;
     run(GCK_K_ATTN, 1, [&] { launch_attention(pv, aa, nw, s); });
-    gemm(GCK_K_O, ly.o, h->tma_att, h->att, T, Epi{kEpiAdd, h->d, h->d, h->x, nullptr});
-    run(GCK_K_NORM, 1, [&] { launch_rmsnorm(h->x, nullptr, T, ly.ffn_norm, h->eps, h->d, h->d, h->h, s); });
-    gemm(GCK_K_GATEUP, ly.gu, h->tma_h, h->h, T, Epi{kEpiSwiGLU, h->F, ly.dn.KT * kBK, nullptr, h->act});
-    gemm(GCK_K_DOWN, ly.dn, h->tma_act, h->act, T, Epi{kEpiAdd, h->d, h->d, h->x, nullptr});
+    residual(GCK_K_O, ly.o, h->tma_att, h->att);
+    norm(nullptr, T, ly.ffn_norm);
+    gemm(GCK_K_GATEUP, ly.gu, h->tma_h, h->h, T, Epi{kEpiSwiGLU, h->F, ly.dn.KT * kBK, nullptr, h->act}, false);
+    residual(GCK_K_DOWN, ly.dn, h->tma_act, h->act);
   }
   if (pv.R > 0) {
-    run(GCK_K_NORM, 1, [&] { launch_rmsnorm(h->x, pv.want_tok, pv.R, h->out_norm, h->eps, h->d, h->d, h->h, s); });
-    gemm(GCK_K_HEAD, h->head, h->tma_h, h->h, pv.R, Epi{kEpiStore, h->vocab, h->vocab, h->logits, nullptr});
+    norm(pv.want_tok, pv.R, h->out_norm);
+    gemm(GCK_K_HEAD, h->head, h->tma_h, h->h, pv.R, Epi{kEpiStore, h->vocab, h->vocab, h->logits, nullptr}, false);
   }
 }
 
