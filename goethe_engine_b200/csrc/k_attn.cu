@@ -8,9 +8,10 @@
 // consecutive chain tokens of one item (a prefill chunk), or one token (decode, tree node). It walks the token's
 // visible list in fixed groups of 16 entries and fixed splits of kSplit entries; the last CTA of a (query group, kv
 // head) to finish merges the splits' partials in split order. A split's groups are resolved to pages once (block
-// table; a tree token's own rows through its path); groups' K and V rows are gathered with cp.async through a 3-4 deep
-// ring; a CTA of several warps shares them when its warps serve consecutive tokens of one item. Every row's arithmetic
-// depends only on its own list, so results are identical alone, batched, chunked or as tree nodes (batch invariance).
+// table; a tree token's own rows through its path); groups' K and V rows are gathered with cp.async, double
+// buffered (decode warps: 20 resident per SM at <= 96 registers); a CTA of several warps shares them when its warps
+// serve consecutive tokens of one item. Every row's arithmetic depends only on its own list, so results are identical
+// alone, batched, chunked or as tree nodes (batch invariance).
 //
 // Tensor cores (mma.sync m16n8k16, f16 x f16 -> f32), with the 16 entries of a group as M and the query rows as N in
 // tiles of 8 (a decode warp holds one tile: its G <= 8 heads):
@@ -36,7 +37,7 @@ struct Cfg {
   static constexpr int CHUNKS = RB / 16;             // 16-byte chunks per row
   static constexpr int NKS = DH / 16;                // QK k-steps
   static constexpr int NMT = DH / 16;                // PV m-tiles (16 head dims each)
-  static constexpr int NST = FP8 ? 4 : 3;            // gather ring: groups in flight while one is computed
+  static constexpr int NST = 2;                      // gather ring: double buffered (occupancy beats lookahead)
   static constexpr int NGS = kSplit / kGroup;        // groups per split
   static constexpr int PG_OFF = NST * BUF;           // [NGS] page of each group (-1: entries resolved one by one)
   static constexpr int GE_OFF = PG_OFF + NGS * 4;    // [NGS][2] page exponents (K, V) of page groups
@@ -67,7 +68,7 @@ __device__ __forceinline__ float pow2i(int e) { return __int_as_float((127 + e) 
 // Head dims are permuted inside the MMAs so that lanes read contiguous bytes: in QK, lane t's k indices of k-step s
 // are dims t*dh/4 + 4s + {0,1,2,3}; in PV, lane g's output rows of m-tile mt are dims g*dh/8 + 2mt + {0, 1}.
 template <int DH, bool FP8, int NW, int NT>
-__global__ void __launch_bounds__(32 * NW, NW == 1 && NT == 1 ? 16 : 1) attn_kernel(PlanView pv, AttnArgs a) {
+__global__ void __launch_bounds__(32 * NW, NW == 1 && NT == 1 ? 20 : 1) attn_kernel(PlanView pv, AttnArgs a) {
   using C = Cfg<DH, FP8>;
   constexpr int NTHR = 32 * NW;
   extern __shared__ __align__(128) uint8_t sm[];
@@ -217,9 +218,11 @@ __global__ void __launch_bounds__(32 * NW, NW == 1 && NT == 1 ? 16 : 1) attn_ker
         u = reinterpret_cast<const uint4 *>(sK + (g + 8) * C::ROWB + t * (C::RB / 4))[i];
         k1[4 * i] = u.x; k1[4 * i + 1] = u.y; k1[4 * i + 2] = u.z; k1[4 * i + 3] = u.w;
       }
-      float sc[NT][4];
+      // two accumulator chains (even / odd k-steps), summed at the end: half the MMA dependency chain
+      float sc[NT][4], sc2[NT][4];
 #pragma unroll
-      for (int nt = 0; nt < NT; nt++) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+      for (int nt = 0; nt < NT; nt++)
+        sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = sc2[nt][0] = sc2[nt][1] = sc2[nt][2] = sc2[nt][3] = 0.f;
 #pragma unroll
       for (int s = 0; s < C::NKS; s++) {
         uint32_t af[4];
@@ -233,8 +236,12 @@ __global__ void __launch_bounds__(32 * NW, NW == 1 && NT == 1 ? 16 : 1) attn_ker
           af[1] = k1[2 * s]; af[3] = k1[2 * s + 1];
         }
 #pragma unroll
-        for (int nt = 0; nt < NT; nt++) mma_f16(sc[nt], af, qb[nt][s]);
+        for (int nt = 0; nt < NT; nt++) mma_f16((s & 1) ? sc2[nt] : sc[nt], af, qb[nt][s]);
       }
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int c = 0; c < 4; c++) sc[nt][c] += sc2[nt][c];
       // ---- page scales of entries g and g + 8: 2^-ek on the scores, 2^(evref - ev) on the probabilities
       float ks0 = a.scale_log2, ks1 = a.scale_log2, pv0 = 1.f, pv1 = 1.f;
       int evref = 0;
