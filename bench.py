@@ -33,6 +33,9 @@ SPEC8B = dict(vocab=128256, d=4096, layers=32, heads=32, kv_heads=8, ffn=14336, 
               std=0.02, seed=0, ctx=8192 + 64, name="llama3-8b-shape-q4k")
 B, PREFIX = 64, 1024
 METRIC = "decode tok/s (8B Q4_K, batch 64, fp8 KV)"
+# DRAM bytes (read + write) of one attention launch of this workload, from the ncu capture summarised in
+# profiles/attn_kernel_c3_decode_L2.md (a layer's launch there has the full-size KV of these 64 contexts)
+ATTN_TRAFFIC = 291_734_272
 
 
 def contexts():
@@ -212,10 +215,16 @@ def run_mine(args, rank, world, barrier, maxreduce):
         barrier()
     ATTN = 4
     L.gck_stats_enable(be.h, 0xFFFF if args.profile else 1 << ATTN)
+    # GCK_PROFILE_WINDOW=1: the CUDA profiler window covers the first timed step only (ncu --profile-from-start off)
+    window = bool(os.environ.get("GCK_PROFILE_WINDOW"))
     with Clocks(dev) as clk:
         t0 = time.perf_counter()
-        for _ in range(args.steps):
+        for k in range(args.steps):
+            if window and k == 0:
+                torch.cuda.profiler.start()
             step()
+            if window and k == 0:
+                torch.cuda.profiler.stop()
         wall = time.perf_counter() - t0
     st = Stats(size=C.sizeof(Stats))
     L.gck_stats_read(be.h, C.byref(st))
@@ -240,14 +249,16 @@ def run_mine(args, rank, world, barrier, maxreduce):
         "vs_baseline": None, "dtype": "q4_k x f16 -> f32; fp8 e4m3 KV", "data": "synthetic (seeded N(0,0.02) weights, uniform tokens)",
         "config": {"workload": "C3: Llama-3-8B shape, Q4_K weights, fp8 paged KV (per-page scale), 64-sequence greedy "
                                "decode, log-normal contexts 512-8192 (sum 168356), 32 sequences share a 1024-token prefix",
-                   "batch": B, "context_sum": int(np.sum(ctx)), "block_size": be.block_size,
+                   "batch": B, "context_sum": int(np.sum(ctx)), "block_size": be.block_size, "layers": SPEC8B["layers"],
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (13 GB per step), no flush"},
         "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": int(sum(len(t) for t in tables) * 4 + B * 4 * 3 + B * 48),
                 "d2h_bytes_per_step": B * 4, "path": "gc_step through the C ABI (ctypes), host buffers"},
         "roofline": {"bound": "hbm", "kernel": "attn_kernel (paged fp8 KV attention)", "achieved": round(attn_bytes / (attn_ms / 1e3) / 1e9, 1),
                      "peak": hbm, "unit": "GB/s", "frac": round(attn_bytes / (attn_ms / 1e3) / 1e9 / hbm, 4),
-                     "traffic": None, "algorithmic_bytes_per_launch": int(attn_bytes), "launch_ms": round(attn_ms, 4),
+                     "traffic": ATTN_TRAFFIC, "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch "
+                     "(profiles/attn_kernel_c3_decode_L2.md)",
+                     "algorithmic_bytes_per_launch": int(attn_bytes), "launch_ms": round(attn_ms, 4),
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in pk else "fallback 6650 GB/s"},
         "step_roofline": {"algorithmic_bytes": int(step_bytes), "weights_bytes": int(wbytes), "kv_bytes": int(kv_bytes),
                           "achieved_gbs": round(step_bytes / (ms_step / 1e3) / 1e9, 1),
@@ -368,7 +379,12 @@ def main():
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--profile", action="store_true", help="time every kernel class (stderr table)")
+    ap.add_argument("--layers", type=int, default=32,
+                    help="layers of the 8B shape (default 32; fewer only for small profiling cases, not a headline)")
     args = ap.parse_args()
+    if args.layers != 32:
+        SPEC8B["layers"] = args.layers
+        SPEC8B["name"] += f"-L{args.layers}"
     world = int(os.environ.get("WORLD_SIZE", 1))
     rank = int(os.environ.get("RANK", 0))
     if args.impl == "reference":
