@@ -277,8 +277,9 @@ void launch_splitk_reduce(const float *part, int S, int T, int Npad, const Epi &
 }
 
 // ----------------------------------------------------------------------------------------------------------------
-// argmax per row, first index of the maximum (torch.argmax); NaN never wins.
-__global__ void argmax_kernel(const float *logits, int V, int *out) {
+// argmax per row, first index of the maximum (torch.argmax); NaN never wins. With pick (a tensor-parallel rank's
+// vocabulary slice starting at row `offset`): the candidate (value bits, global index) instead of the index.
+__global__ void argmax_kernel(const float *logits, int V, int *out, int *pick, int offset) {
   int r = blockIdx.x;
   const float *row = logits + static_cast<size_t>(r) * V;
   float best = -INFINITY;
@@ -305,12 +306,39 @@ __global__ void argmax_kernel(const float *logits, int V, int *out) {
       int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
       if (b2 > best || (b2 == best && i2 < idx)) { best = b2; idx = i2; }
     }
-    if (l == 0) out[r] = idx == 0x7fffffff ? 0 : idx;
+    if (l == 0) {
+      if (pick) {
+        pick[2 * r] = __float_as_int(best);
+        pick[2 * r + 1] = idx == 0x7fffffff ? idx : idx + offset;
+      } else {
+        out[r] = idx == 0x7fffffff ? 0 : idx;
+      }
+    }
   }
 }
 
+// the ranks' candidates [tp][R][2] -> the first index of the maximum over the whole vocabulary (slices ascend by rank)
+__global__ void argmax_merge_kernel(const int *pick, int tp, int R, int *out) {
+  int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= R) return;
+  float best = -INFINITY;
+  int idx = 0x7fffffff;
+  for (int k = 0; k < tp; k++) {
+    float v = __int_as_float(pick[(static_cast<size_t>(k) * R + r) * 2]);
+    int i = pick[(static_cast<size_t>(k) * R + r) * 2 + 1];
+    if (i != 0x7fffffff && (v > best || (v == best && i < idx))) { best = v; idx = i; }
+  }
+  out[r] = idx == 0x7fffffff ? 0 : idx;
+}
+
 void launch_argmax(const float *logits, int R, int V, int *out, cudaStream_t s) {
-  if (R > 0) argmax_kernel<<<R, 1024, 0, s>>>(logits, V, out);
+  if (R > 0) argmax_kernel<<<R, 1024, 0, s>>>(logits, V, out, nullptr, 0);
+}
+void launch_argmax_pick(const float *logits, int R, int V, int offset, int *pick, cudaStream_t s) {
+  if (R > 0) argmax_kernel<<<R, 1024, 0, s>>>(logits, V, nullptr, pick, offset);
+}
+void launch_argmax_merge(const int *pick, int tp, int R, int *out, cudaStream_t s) {
+  if (R > 0) argmax_merge_kernel<<<(R + 127) / 128, 128, 0, s>>>(pick, tp, R, out);
 }
 
 // ----------------------------------------------------------------------------------------------------------------

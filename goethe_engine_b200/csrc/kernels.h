@@ -57,6 +57,9 @@ void launch_rope_kv(const PlanView &pv, const float *qkv, int S, int ld, int H, 
                     cudaStream_t s);
 void launch_splitk_reduce(const float *part, int S, int T, int Npad, const Epi &epi, cudaStream_t s);
 void launch_argmax(const float *logits, int R, int V, int *out, cudaStream_t s);
+// tensor parallelism: a rank's candidates (value bits, global index) of its vocabulary slice, and their merge
+void launch_argmax_pick(const float *logits, int R, int V, int offset, int *pick, cudaStream_t s);
+void launch_argmax_merge(const int *pick, int tp, int R, int *out, cudaStream_t s);
 void launch_copy_blocks(const int *pairs, int n, int L, size_t page_bytes, size_t layer_bytes, uint8_t *kc,
                         uint8_t *vc, int8_t *exps, size_t exps_layer, int exps_per_block, cudaStream_t s);
 void launch_commit(const int *moves, int n, int L, int KVH, int dh, uint8_t *kc, uint8_t *vc, int8_t *exps,

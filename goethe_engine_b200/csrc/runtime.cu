@@ -6,6 +6,8 @@
 // What happens inside a step follows goethe_engine/ref.py (RefModel.token, TorchBackend.step/commit/copy_blocks).
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <algorithm>
 #include <cmath>
@@ -72,6 +74,14 @@ size_t vbytes(const std::vector<T> &v) { return v.size() * sizeof(T); }
 
 struct gc_handle {
   int dev = 0, sms = 148;
+  // tensor parallelism: a group handle (tp > 1, ranks filled) drives one rank handle per device and holds no device
+  // state of its own; a rank handle holds its slices (H, KVH, F, head rows) and an NCCL communicator
+  int tp = 1, rank = 0;
+  std::vector<gc_handle *> ranks;
+  void *comm = nullptr;              // ncclComm_t of a rank handle
+  float *tp_y = nullptr;             // rank: o_proj / down_proj output, all-reduced [T, d]
+  int *tp_pick = nullptr;            // rank: argmax candidates (value bits, index) of every rank [tp][T][2]
+  int vocab0 = 0, vocab_rows = 0;    // head rows held here: [vocab0, vocab0 + vocab_rows)
   cudaStream_t st = nullptr;
   std::string err;
   // model
@@ -189,8 +199,9 @@ uint16_t h_f32_to_f16(float f) {
 // Build the tiled layout of a weight whose logical row n maps to (source, source row) by `rowmap`, on the host, and
 // upload it. Tile (nt, kt) of kBM x kBK: Q4_K = 128 x 16 B headers then 128 x 128 B quants; Q8_0 = 128 x 8 fp16
 // scales then 128 x 256 int8; F16 = 128 x 256 halves. Rows past N and columns past K are zero (weights of 0).
+// k0: first source column (a tensor-parallel rank's slice of the input dimension; a multiple of 256 for Q4_K).
 template <typename RowMap>
-QWeight relayout(gc_handle *h, int type, int N, int K, RowMap rowmap, const char *what) {
+QWeight relayout(gc_handle *h, int type, int N, int K, RowMap rowmap, const char *what, int k0 = 0) {
   QWeight w;
   w.type = type == kF32 ? kF16 : type;
   w.N = N;
@@ -210,6 +221,7 @@ QWeight relayout(gc_handle *h, int type, int N, int K, RowMap rowmap, const char
         rowmap(n, t, sr);
         if (!t) continue;   // a padding row: zeros
         const uint8_t *row = t->data;
+        const int Ksrc = static_cast<int>(t->dims[0]);   // the source row's full length
         for (int kt = 0; kt < w.KT; kt++) {
           uint8_t *tile = host.data() + (static_cast<size_t>(nt) * w.KT + kt) * tb;
           if (type == kQ4_K) {
@@ -220,7 +232,7 @@ QWeight relayout(gc_handle *h, int type, int N, int K, RowMap rowmap, const char
             static const int kPos[8] = {0, 4, 1, 5, 2, 6, 3, 7};
             int nsb = K / 256;
             if (kt >= nsb) continue;
-            const uint8_t *src = row + (static_cast<size_t>(sr) * nsb + kt) * 144;
+            const uint8_t *src = row + (static_cast<size_t>(sr) * (Ksrc / 256) + k0 / 256 + kt) * 144;
             std::memcpy(tile + r * 16, src, 16);
             const uint8_t *qs = src + 16;
             for (int g = 0; g < 8; g++) {
@@ -239,7 +251,7 @@ QWeight relayout(gc_handle *h, int type, int N, int K, RowMap rowmap, const char
             for (int i = 0; i < 8; i++) {
               int b = kt * 8 + i;
               if (b >= nb) break;
-              const uint8_t *src = row + (static_cast<size_t>(sr) * nb + b) * 34;
+              const uint8_t *src = row + (static_cast<size_t>(sr) * (Ksrc / 32) + k0 / 32 + b) * 34;
               std::memcpy(tile + r * 16 + i * 2, src, 2);
               for (int h2 = 0; h2 < 2; h2++) {
                 uint8_t *dst = tile + kBM * 16 + ((2 * i + h2) * kBM + r) * 16;
@@ -251,8 +263,9 @@ QWeight relayout(gc_handle *h, int type, int N, int K, RowMap rowmap, const char
             for (int c = 0; c < kBK; c++) {
               int k = kt * kBK + c;
               if (k >= K) break;
-              if (type == kF16) dst[c] = reinterpret_cast<const uint16_t *>(row)[static_cast<size_t>(sr) * K + k];
-              else dst[c] = h_f32_to_f16(reinterpret_cast<const float *>(row)[static_cast<size_t>(sr) * K + k]);
+              const size_t si = static_cast<size_t>(sr) * Ksrc + k0 + k;
+              if (type == kF16) dst[c] = reinterpret_cast<const uint16_t *>(row)[si];
+              else dst[c] = h_f32_to_f16(reinterpret_cast<const float *>(row)[si]);
             }
           }
         }
@@ -339,6 +352,15 @@ void load_model(gc_handle *h, const std::vector<std::unique_ptr<GgufFile>> &file
   if (h->d % kBK || (h->H * h->dh) % kBK || h->d > 8192)
     fail(GC_E_UNSUPPORTED, "model width %d: must be a multiple of %d, at most 8192", h->d, kBK);
   h->qg_tokens = 16 / G;
+  // tensor parallelism: this handle holds rank `rank` of `tp`: heads, kv heads and FFN columns split evenly, o_proj and
+  // down_proj by their input columns (on 256-column super-block bounds), the head by vocabulary rows
+  const int N = h->tp, rk = h->rank;
+  if (N > 1) {
+    if (h->KVH % N || h->H % N)
+      fail(GC_E_UNSUPPORTED, "tensor parallelism %d: heads %d and kv heads %d must divide evenly", N, h->H, h->KVH);
+    if ((h->H / N * h->dh) % kBK || (h->F / N) % kBK || h->F % N)
+      fail(GC_E_UNSUPPORTED, "tensor parallelism %d: per-rank o_proj and down_proj inputs must be multiples of %d", N, kBK);
+  }
   const GgufTensor &emb = tensor(files, "token_embd.weight");
   if (emb.dims.size() < 2 || static_cast<int>(emb.dims[0]) != h->d) fail(GC_E_WEIGHTS, "token_embd.weight shape");
   h->vocab = static_cast<int>(emb.dims[1]);
@@ -348,7 +370,8 @@ void load_model(gc_handle *h, const std::vector<std::unique_ptr<GgufFile>> &file
   uint8_t *e = static_cast<uint8_t *>(h->dalloc(emb.bytes, "token_embd"));
   ck(cudaMemcpy(e, emb.data, emb.bytes, cudaMemcpyHostToDevice), "token_embd");
   h->emb = e;
-  const int dq = h->H * h->dh, dkv = h->KVH * h->dh;
+  const int dq_all = h->H * h->dh, F_all = h->F;
+  const int dq = h->H / N * h->dh, dkv = h->KVH / N * h->dh, Fr = h->F / N;   // this rank's slices
   for (int l = 0; l < h->L; l++) {
     std::string b = "blk." + std::to_string(l) + ".";
     Layer ly;
@@ -357,29 +380,29 @@ void load_model(gc_handle *h, const std::vector<std::unique_ptr<GgufFile>> &file
                      &tg = tensor(files, b + "ffn_gate.weight"), &tu = tensor(files, b + "ffn_up.weight"),
                      &td = tensor(files, b + "ffn_down.weight");
     for (auto *t : {&tq, &tk, &tv, &tg, &tu}) check_type(*t, h->d);
-    check_type(to, dq);
-    check_type(td, h->F);
+    check_type(to, dq_all);
+    check_type(td, F_all);
     if (tq.type != tk.type || tq.type != tv.type || tg.type != tu.type)
       fail(GC_E_WEIGHTS, "layer %d: q/k/v (and gate/up) must share one type", l);
     ly.qkv = relayout(h, static_cast<int>(tq.type), dq + 2 * dkv, h->d, [&](int n, const GgufTensor *&t, int &r) {
-      if (n < dq) { t = &tq; r = n; }
-      else if (n < dq + dkv) { t = &tk; r = n - dq; }
-      else { t = &tv; r = n - dq - dkv; }
+      if (n < dq) { t = &tq; r = rk * dq + n; }
+      else if (n < dq + dkv) { t = &tk; r = rk * dkv + n - dq; }
+      else { t = &tv; r = rk * dkv + n - dq - dkv; }
     }, "attn_qkv");
     ly.o = relayout(h, static_cast<int>(to.type), h->d, dq, [&](int n, const GgufTensor *&t, int &r) { t = &to; r = n; },
-                    "attn_output");
+                    "attn_output", rk * dq);
     // gate/up interleaved in 64-row halves of each 128-row tile: the SwiGLU epilogue finds g and u in one tile
-    int Fp = (h->F + 63) / 64 * 64;
+    int Fp = (Fr + 63) / 64 * 64;
     ly.gu = relayout(h, static_cast<int>(tg.type), 2 * Fp, h->d, [&](int n, const GgufTensor *&t, int &r) {
       int tile = n / 128, w = n % 128;
       int f = tile * 64 + (w % 64);
       t = w < 64 ? &tg : &tu;
-      r = std::min(f, h->F - 1);
-      if (f >= h->F) t = nullptr;
+      r = rk * Fr + std::min(f, Fr - 1);
+      if (f >= Fr) t = nullptr;
     }, "ffn_gate_up");
     ly.gu.N = 2 * Fp;
-    ly.dn = relayout(h, static_cast<int>(td.type), h->d, h->F, [&](int n, const GgufTensor *&t, int &r) { t = &td; r = n; },
-                     "ffn_down");
+    ly.dn = relayout(h, static_cast<int>(td.type), h->d, Fr, [&](int n, const GgufTensor *&t, int &r) { t = &td; r = n; },
+                     "ffn_down", rk * Fr);
     ly.attn_norm = upload_f32(h, tensor(files, b + "attn_norm.weight"), h->d, "attn_norm");
     ly.ffn_norm = upload_f32(h, tensor(files, b + "ffn_norm.weight"), h->d, "ffn_norm");
     h->layers.push_back(ly);
@@ -387,8 +410,15 @@ void load_model(gc_handle *h, const std::vector<std::unique_ptr<GgufFile>> &file
   h->out_norm = upload_f32(h, tensor(files, "output_norm.weight"), h->d, "output_norm");
   const GgufTensor &th = tensor(files, "output.weight");
   check_type(th, h->d);
-  h->head = relayout(h, static_cast<int>(th.type), h->vocab, h->d,
-                     [&](int n, const GgufTensor *&t, int &r) { t = &th; r = n; }, "output");
+  const int Vr = (h->vocab + N - 1) / N;
+  h->vocab0 = rk * Vr;
+  h->vocab_rows = std::max(0, std::min(h->vocab, h->vocab0 + Vr) - h->vocab0);
+  h->head = relayout(h, static_cast<int>(th.type), h->vocab_rows, h->d,
+                     [&](int n, const GgufTensor *&t, int &r) { t = &th; r = h->vocab0 + n; }, "output");
+  // from here on the handle's head counts and FFN width are its own slices
+  h->H /= N;
+  h->KVH /= N;
+  h->F = Fr;
 }
 
 }  // namespace
@@ -491,6 +521,131 @@ void *commit_static_address(int dev) {
 }  // namespace
 
 // ============================================================================================== exported ABI
+namespace {
+
+struct OpenCfg {
+  int ncol = 0, maxctx = 0, max_cols = 0, pool_tune = 0, tp = 1;
+  uint32_t pool_blocks = 0;
+  std::string kv, kv_scale;
+};
+
+// One device's state: checks the device, loads (this rank's slices of) the weights, allocates scratch and the KV pool.
+void open_device(gc_handle *h, int dev, const std::vector<std::unique_ptr<GgufFile>> &files, const OpenCfg &c, int rank) {
+  cudaDeviceProp prop;
+  ck(cudaGetDeviceProperties(&prop, dev), "cudaGetDeviceProperties");
+  if (prop.major != 10 || prop.minor != 0)
+    fail(GC_E_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a (B200)", dev, prop.major, prop.minor);
+  ck(cudaSetDevice(dev), "cudaSetDevice");
+  h->dev = dev;
+  h->rank = rank;
+  h->tp = c.tp;
+  h->sms = prop.multiProcessorCount;
+  ck(cudaStreamCreateWithFlags(&h->st, cudaStreamNonBlocking), "stream");
+  gemm_init();
+  gemm_tc_init();
+  load_model(h, files);
+  h->max_seqs = std::max(1, c.ncol);
+  h->max_ctx = std::max(kBlock, c.maxctx);
+  h->max_cols = c.max_cols > 0 ? c.max_cols : 2048;
+  h->kv_fp8 = c.kv == "fp8";
+  h->page_scale = h->kv_fp8 && c.kv_scale != "unit";
+  build_rope(h);
+  // KV pool: [L][nblk][KVH][16][dh] for K and for V, plus fp8 page exponents [L][nblk][KVH][2]
+  const size_t esz = h->kv_fp8 ? 1 : 2;
+  h->page_bytes = static_cast<size_t>(h->KVH) * kBlock * h->dh * esz;
+  size_t per_block = 2 * h->page_bytes * h->L + (h->kv_fp8 ? static_cast<size_t>(h->L) * h->KVH * 2 : 0);
+  size_t nblk = c.pool_blocks ? c.pool_blocks : c.pool_tune;
+  // scratch first, so that "what fits" is measured after it
+  const int T = h->max_cols, d = h->d;
+  const int wq = (h->H + 2 * h->KVH) * h->dh;
+  int Fpad = h->layers[0].dn.KT * kBK;
+  h->x = static_cast<float *>(h->dalloc(static_cast<size_t>(T) * d * 4, "x"));
+  h->h = static_cast<__half *>(h->dalloc(static_cast<size_t>(T) * d * 2, "h"));
+  h->qkv = static_cast<float *>(h->dalloc(static_cast<size_t>(T) * wq * 4, "qkv"));
+  h->q = static_cast<__half *>(h->dalloc(static_cast<size_t>(T) * h->H * h->dh * 2, "q"));
+  h->att = static_cast<__half *>(h->dalloc(static_cast<size_t>(T) * h->H * h->dh * 2, "att"));
+  h->act = static_cast<__half *>(h->dalloc(static_cast<size_t>(T) * Fpad * 2, "act"));
+  ck(cudaMemset(h->act, 0, static_cast<size_t>(T) * Fpad * 2), "act");
+  h->logits = static_cast<float *>(h->dalloc(static_cast<size_t>(T) * std::max(1, h->vocab_rows) * 4, "logits"));
+  h->argmax = static_cast<int *>(h->dalloc(static_cast<size_t>(T) * 4, "argmax"));
+  if (h->tp > 1) {
+    h->tp_y = static_cast<float *>(h->dalloc(static_cast<size_t>(T) * d * 4, "tensor-parallel partial sums"));
+    h->tp_pick = static_cast<int *>(h->dalloc(static_cast<size_t>(h->tp + 1) * T * 2 * 4, "tensor-parallel argmax"));
+  }
+  ck(cudaMallocHost(&h->tok_host, static_cast<size_t>(T) * 4), "pinned tokens");
+  h->kerr = static_cast<int *>(h->dalloc(16, "error word"));
+  ck(cudaMemset(h->kerr, 0, 16), "error word");
+  ck(cudaMallocHost(&h->kerr_host, 16), "pinned error word");
+  build_tma(h->tma_h, h->h, T, d);
+  build_tma(h->tma_att, h->att, T, h->H * h->dh);
+  build_tma(h->tma_act, h->act, T, Fpad);
+  if (!nblk) {
+    size_t fr = 0, tot = 0;
+    ck(cudaMemGetInfo(&fr, &tot), "cudaMemGetInfo");
+    size_t reserve = static_cast<size_t>(4) << 30;
+    nblk = fr > reserve ? (fr - reserve) / per_block : 0;
+    nblk = std::min<size_t>(nblk, static_cast<size_t>(h->max_seqs) * ((h->max_ctx + kBlock - 1) / kBlock) + 64);
+  }
+  if (nblk < 1 || nblk > (1u << 26)) fail(GC_E_DEVICE, "KV pool of %zu blocks: out of memory", nblk);
+  h->nblk = static_cast<int>(nblk);
+  h->layer_bytes = h->page_bytes * nblk;
+  h->kc = static_cast<uint8_t *>(h->dalloc(h->layer_bytes * h->L, "KV pool K"));
+  h->vc = static_cast<uint8_t *>(h->dalloc(h->layer_bytes * h->L, "KV pool V"));
+  ck(cudaMemset(h->kc, 0, h->layer_bytes * h->L), "KV pool");
+  ck(cudaMemset(h->vc, 0, h->layer_bytes * h->L), "KV pool");
+  if (h->kv_fp8) {
+    h->exps_layer = nblk * h->KVH * 2;
+    h->exps = static_cast<int8_t *>(h->dalloc(h->exps_layer * h->L, "KV page exponents"));
+    ck(cudaMemset(h->exps, 0, h->exps_layer * h->L), "KV page exponents");
+  }
+  h->slots.resize(h->max_seqs);
+  ck(cudaStreamSynchronize(h->st), "open");
+}
+
+// NCCL, loaded when a handle first needs it (tensor parallelism): the library does not link it
+struct Nccl {
+  decltype(&ncclCommInitAll) init_all = nullptr;
+  decltype(&ncclCommDestroy) destroy = nullptr;
+  decltype(&ncclAllReduce) all_reduce = nullptr;
+  decltype(&ncclAllGather) all_gather = nullptr;
+  decltype(&ncclGetErrorString) error_string = nullptr;
+};
+const Nccl &nccl() {
+  static Nccl n;
+  static std::once_flag once;
+  static std::string why;
+  std::call_once(once, [] {
+    void *lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!lib) {
+      why = dlerror();
+      return;
+    }
+    n.init_all = reinterpret_cast<decltype(&ncclCommInitAll)>(dlsym(lib, "ncclCommInitAll"));
+    n.destroy = reinterpret_cast<decltype(&ncclCommDestroy)>(dlsym(lib, "ncclCommDestroy"));
+    n.all_reduce = reinterpret_cast<decltype(&ncclAllReduce)>(dlsym(lib, "ncclAllReduce"));
+    n.all_gather = reinterpret_cast<decltype(&ncclAllGather)>(dlsym(lib, "ncclAllGather"));
+    n.error_string = reinterpret_cast<decltype(&ncclGetErrorString)>(dlsym(lib, "ncclGetErrorString"));
+  });
+  if (!n.init_all || !n.destroy || !n.all_reduce || !n.all_gather || !n.error_string)
+    fail(GC_E_DEVICE, "tensor parallelism needs NCCL (libnccl.so.2): %s", why.empty() ? "symbols missing" : why.c_str());
+  return n;
+}
+void nck(ncclResult_t r, const char *what) {
+  if (r != ncclSuccess) fail(GC_E_DEVICE, "%s: NCCL error %d (%s)", what, static_cast<int>(r), nccl().error_string(r));
+}
+
+// one communicator per rank, all in this process
+void init_tp(gc_handle *g) {
+  const Nccl &n = nccl();
+  std::vector<ncclComm_t> comms(g->tp);
+  std::vector<int> devs(g->tp);
+  for (int r = 0; r < g->tp; r++) devs[r] = g->ranks[r]->dev;
+  nck(n.init_all(comms.data(), g->tp, devs.data()), "ncclCommInitAll");
+  for (int r = 0; r < g->tp; r++) g->ranks[r]->comm = comms[r];
+}
+
+}  // namespace
+
 extern "C" {
 
 GC_API uint32_t gc_abi_version(void) { return GC_ABI_VERSION; }
@@ -519,26 +674,30 @@ GC_API int gc_open(const gc_open_params *p, gc_handle **out) {
     }
     const Json *bl = m.get("buckets");
     if (!bl || bl->kind != Json::Arr) fail(GC_E_MANIFEST, "manifest.json has no buckets");
-    int ncol = 0, maxctx = 0, max_cols = 0, pool_tune = 0;
-    std::string kv, kv_scale;
+    OpenCfg c;
+    c.pool_blocks = P.pool_blocks;
     for (uint32_t i = 0; i < P.n_buckets; i++) {
       if (!P.buckets[i]) fail(GC_E_ARG, "gc_open: null bucket id");
       const Json *b = nullptr;
       for (auto &x : bl->arr)
         if (x.str_or("id", "") == P.buckets[i]) b = &x;
       if (!b) fail(GC_E_MANIFEST, "bucket %s is not in the manifest", P.buckets[i]);
-      ncol = std::max(ncol, static_cast<int>(b->num_or("ncol", 1)));
-      maxctx = std::max(maxctx, static_cast<int>(b->num_or("maxctx", 4096)));
+      c.ncol = std::max(c.ncol, static_cast<int>(b->num_or("ncol", 1)));
+      c.maxctx = std::max(c.maxctx, static_cast<int>(b->num_or("maxctx", 4096)));
       std::string bkv = b->str_or("kv", "f16");
-      if (!kv.empty() && bkv != kv) fail(GC_E_MANIFEST, "buckets disagree on the KV dtype");
-      kv = bkv;
+      if (!c.kv.empty() && bkv != c.kv) fail(GC_E_MANIFEST, "buckets disagree on the KV dtype");
+      c.kv = bkv;
+      const int btp = static_cast<int>(b->num_or("tp", 1));
+      if (i && btp != c.tp) fail(GC_E_MANIFEST, "buckets disagree on the tensor-parallel degree");
+      c.tp = btp;
       if (const Json *t = b->get("tune")) {
-        max_cols = std::max(max_cols, static_cast<int>(t->num_or("max_cols", 0)));
-        pool_tune = std::max(pool_tune, static_cast<int>(t->num_or("pool_blocks", 0)));
-        kv_scale = t->str_or("kv_scale", kv_scale);
+        c.max_cols = std::max(c.max_cols, static_cast<int>(t->num_or("max_cols", 0)));
+        c.pool_tune = std::max(c.pool_tune, static_cast<int>(t->num_or("pool_blocks", 0)));
+        c.kv_scale = t->str_or("kv_scale", c.kv_scale);
       }
     }
-    if (kv != "f16" && kv != "fp8") fail(GC_E_MANIFEST, "kv dtype %s: f16 or fp8", kv.c_str());
+    if (c.kv != "f16" && c.kv != "fp8") fail(GC_E_MANIFEST, "kv dtype %s: f16 or fp8", c.kv.c_str());
+    if (c.tp != 1 && c.tp != 2 && c.tp != 4 && c.tp != 8) fail(GC_E_MANIFEST, "tensor-parallel degree %d: 1, 2, 4 or 8", c.tp);
     // weights: the target's files (a NULL entry separates a drafter's, which a non-spec open has none of)
     std::vector<std::unique_ptr<GgufFile>> files;
     if (!P.weights || !P.n_weights) fail(GC_E_WEIGHTS, "no weight files");
@@ -551,7 +710,7 @@ GC_API int gc_open(const gc_open_params *p, gc_handle **out) {
       }
     }
     if (files.empty()) fail(GC_E_WEIGHTS, "no weight files");
-    // device
+    // devices: `device` (or the current one) and, with tensor parallelism, the next tp - 1
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
       cudaGetLastError();
@@ -559,81 +718,66 @@ GC_API int gc_open(const gc_open_params *p, gc_handle **out) {
     }
     int dev = P.device;
     if (dev < 0) ck(cudaGetDevice(&dev), "cudaGetDevice");
-    if (dev >= ndev) fail(GC_E_DEVICE, "device %d: no such device (%d present)", dev, ndev);
-    cudaDeviceProp prop;
-    ck(cudaGetDeviceProperties(&prop, dev), "cudaGetDeviceProperties");
-    if (prop.major != 10 || prop.minor != 0)
-      fail(GC_E_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a (B200)", dev, prop.major, prop.minor);
-    ck(cudaSetDevice(dev), "cudaSetDevice");
+    if (dev + c.tp > ndev)
+      fail(GC_E_DEVICE, "devices %d .. %d: only %d present", dev, dev + c.tp - 1, ndev);
     h = new gc_handle();
-    h->dev = dev;
-    h->sms = prop.multiProcessorCount;
-    ck(cudaStreamCreateWithFlags(&h->st, cudaStreamNonBlocking), "stream");
-    gemm_init();
-    gemm_tc_init();
-    load_model(h, files);
+    if (c.tp == 1) {
+      open_device(h, dev, files, c, 0);
+    } else {
+      h->tp = c.tp;
+      h->dev = dev;
+      for (int r = 0; r < c.tp; r++) {
+        h->ranks.push_back(new gc_handle());
+        h->ranks.back()->tp = c.tp;
+        h->ranks.back()->rank = r;
+      }
+      // the ranks load in parallel (each relays its own slices out)
+      std::vector<std::thread> th;
+      std::vector<std::string> errs(c.tp);
+      std::vector<int> codes(c.tp, GC_OK);
+      for (int r = 0; r < c.tp; r++)
+        th.emplace_back([&, r] {
+          try {
+            open_device(h->ranks[r], dev + r, files, c, r);
+          } catch (const GcError &e) {
+            codes[r] = e.code;
+            errs[r] = e.msg;
+          } catch (const std::exception &e) {
+            codes[r] = GC_E_DEVICE;
+            errs[r] = e.what();
+          }
+        });
+      for (auto &t : th) t.join();
+      for (int r = 0; r < c.tp; r++)
+        if (codes[r] != GC_OK) fail(codes[r], "rank %d (device %d): %s", r, dev + r, errs[r].c_str());
+      init_tp(h);
+      gc_handle *r0 = h->ranks[0];
+      h->vocab = r0->vocab;
+      h->max_seqs = r0->max_seqs;
+      h->max_cols = r0->max_cols;
+      h->max_ctx = r0->max_ctx;
+      h->nblk = r0->nblk;
+      h->L = r0->L;
+      h->KVH = r0->KVH * c.tp;
+      h->dh = r0->dh;
+      h->kv_fp8 = r0->kv_fp8;
+      for (gc_handle *r : h->ranks) {
+        h->layer_bytes += r->layer_bytes;
+        h->exps_layer += r->exps_layer;
+        h->device_bytes += r->device_bytes;
+      }
+      h->slots.resize(h->max_seqs);
+    }
     files.clear();
-    h->max_seqs = std::max(1, ncol);
-    h->max_ctx = std::max(kBlock, maxctx);
-    h->max_cols = max_cols > 0 ? max_cols : 2048;
-    h->kv_fp8 = kv == "fp8";
-    h->page_scale = h->kv_fp8 && kv_scale != "unit";
-    build_rope(h);
-    // KV pool: [L][nblk][KVH][16][dh] for K and for V, plus fp8 page exponents [L][nblk][KVH][2]
-    const size_t esz = h->kv_fp8 ? 1 : 2;
-    h->page_bytes = static_cast<size_t>(h->KVH) * kBlock * h->dh * esz;
-    size_t per_block = 2 * h->page_bytes * h->L + (h->kv_fp8 ? static_cast<size_t>(h->L) * h->KVH * 2 : 0);
-    size_t nblk = P.pool_blocks ? P.pool_blocks : pool_tune;
-    // scratch first, so that "what fits" is measured after it
-    const int T = h->max_cols, d = h->d;
-    const int wq = (h->H + 2 * h->KVH) * h->dh;
-    int Fpad = h->layers[0].dn.KT * kBK;
-    h->x = static_cast<float *>(h->dalloc(static_cast<size_t>(T) * d * 4, "x"));
-    h->h = static_cast<__half *>(h->dalloc(static_cast<size_t>(T) * d * 2, "h"));
-    h->qkv = static_cast<float *>(h->dalloc(static_cast<size_t>(T) * wq * 4, "qkv"));
-    h->q = static_cast<__half *>(h->dalloc(static_cast<size_t>(T) * h->H * h->dh * 2, "q"));
-    h->att = static_cast<__half *>(h->dalloc(static_cast<size_t>(T) * h->H * h->dh * 2, "att"));
-    h->act = static_cast<__half *>(h->dalloc(static_cast<size_t>(T) * Fpad * 2, "act"));
-    ck(cudaMemset(h->act, 0, static_cast<size_t>(T) * Fpad * 2), "act");
-    h->logits = static_cast<float *>(h->dalloc(static_cast<size_t>(T) * h->vocab * 4, "logits"));
-    h->argmax = static_cast<int *>(h->dalloc(static_cast<size_t>(T) * 4, "argmax"));
-    ck(cudaMallocHost(&h->tok_host, static_cast<size_t>(T) * 4), "pinned tokens");
-    h->kerr = static_cast<int *>(h->dalloc(16, "error word"));
-    ck(cudaMemset(h->kerr, 0, 16), "error word");
-    ck(cudaMallocHost(&h->kerr_host, 16), "pinned error word");
-    build_tma(h->tma_h, h->h, T, d);
-    build_tma(h->tma_att, h->att, T, h->H * h->dh);
-    build_tma(h->tma_act, h->act, T, Fpad);
-    if (!nblk) {
-      size_t fr = 0, tot = 0;
-      ck(cudaMemGetInfo(&fr, &tot), "cudaMemGetInfo");
-      size_t reserve = static_cast<size_t>(4) << 30;
-      nblk = fr > reserve ? (fr - reserve) / per_block : 0;
-      nblk = std::min<size_t>(nblk, static_cast<size_t>(h->max_seqs) * ((h->max_ctx + kBlock - 1) / kBlock) + 64);
-    }
-    if (nblk < 1 || nblk > (1u << 26)) fail(GC_E_DEVICE, "KV pool of %zu blocks: out of memory", nblk);
-    h->nblk = static_cast<int>(nblk);
-    h->layer_bytes = h->page_bytes * nblk;
-    h->kc = static_cast<uint8_t *>(h->dalloc(h->layer_bytes * h->L, "KV pool K"));
-    h->vc = static_cast<uint8_t *>(h->dalloc(h->layer_bytes * h->L, "KV pool V"));
-    ck(cudaMemset(h->kc, 0, h->layer_bytes * h->L), "KV pool");
-    ck(cudaMemset(h->vc, 0, h->layer_bytes * h->L), "KV pool");
-    if (h->kv_fp8) {
-      h->exps_layer = nblk * h->KVH * 2;
-      h->exps = static_cast<int8_t *>(h->dalloc(h->exps_layer * h->L, "KV page exponents"));
-      ck(cudaMemset(h->exps, 0, h->exps_layer * h->L), "KV page exponents");
-    }
-    h->slots.resize(h->max_seqs);
-    ck(cudaStreamSynchronize(h->st), "open");
     *out = h;
     return GC_OK;
   } catch (const GcError &e) {
     g_open_err = e.msg;
-    delete h;
+    gc_close(h);
     return e.code;
   } catch (const std::exception &e) {
     g_open_err = e.what();
-    delete h;
+    gc_close(h);
     return GC_E_DEVICE;
   }
 }
@@ -885,17 +1029,33 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
     if (w.splits > 1 && rows > 0 && !reader_reduces)
       run(GCK_K_REDUCE, 1, [&] { launch_splitk_reduce(h->part, w.splits, rows, w.NT * kBM, e, s); });
   };
-  // residual partials waiting for the next RMSNorm (splits of the last o_proj / down_proj, 0: none)
+  // residual contributions waiting for the next RMSNorm: the split-K partials of the last o_proj / down_proj, or (tensor
+  // parallelism) its all-reduced output
+  const float *pend = nullptr;
   int pend_s = 0, pend_ld = 0;
   auto norm = [&](const int *rows, int n, const float *gain) {
-    const float *pp = pend_s > 1 ? h->part : nullptr;
+    const float *pp = pend;
     const int ps = pend_s, pl = pend_ld;
     run(GCK_K_NORM, 1, [&] { launch_rmsnorm(h->x, rows, n, gain, h->eps, h->d, h->d, h->h, pp, ps, pl, T, s); });
+    pend = nullptr;
     pend_s = 0;
   };
   auto residual = [&](int cls, const QWeight &w, const TmaSet &ts, const __half *act) {
+    if (h->tp > 1) {
+      // this rank's share of the projection (its input columns), summed over the ranks in place
+      gemm(cls, w, ts, act, T, Epi{kEpiStore, h->d, h->d, h->tp_y, nullptr}, false);
+      run(GCK_K_ALLREDUCE, 1, [&] {
+        nck(nccl().all_reduce(h->tp_y, h->tp_y, static_cast<size_t>(T) * h->d, ncclFloat, ncclSum,
+                              static_cast<ncclComm_t>(h->comm), s), "all-reduce");
+      });
+      pend = h->tp_y;
+      pend_s = 1;
+      pend_ld = h->d;
+      return;
+    }
     gemm(cls, w, ts, act, T, Epi{kEpiAdd, h->d, h->d, h->x, nullptr}, true);
     if (w.splits > 1) {
+      pend = h->part;
       pend_s = w.splits;
       pend_ld = w.NT * kBM;
     }
@@ -936,7 +1096,8 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
   }
   if (pv.R > 0) {
     norm(pv.want_tok, pv.R, h->out_norm);
-    gemm(GCK_K_HEAD, h->head, h->tma_h, h->h, pv.R, Epi{kEpiStore, h->vocab, h->vocab, h->logits, nullptr}, false);
+    gemm(GCK_K_HEAD, h->head, h->tma_h, h->h, pv.R, Epi{kEpiStore, h->vocab_rows, h->vocab_rows, h->logits, nullptr},
+         false);
   }
 }
 
@@ -970,6 +1131,77 @@ Slot *find_slot(gc_handle *h, uint64_t sid, bool make) {
   return nullptr;
 }
 
+// The device part of a step on one handle (or one tensor-parallel rank): slots, plan, forward, argmax, outputs. o (may be
+// null for ranks other than 0) receives logits_dev; O holds the caller's host buffers.
+void step_device(gc_handle *h, const std::vector<WorkIn> &ws, bool greedy, uint64_t R, uint32_t flags,
+                 const gc_step_out &O, gc_step_out *o) {
+  for (auto &w : ws) {
+    Slot *sl = find_slot(h, w.sid, true);
+    if (!sl) fail(GC_E_STATE, "no free sequence slot (%d in use)", h->max_seqs);
+    sl->blocks.assign(w.blocks, w.blocks + w.nblocks);
+    sl->last_pos = w.pos;
+    sl->last_n = w.n;
+  }
+  ck(cudaSetDevice(h->dev), "cudaSetDevice");
+  HostPlan pl;
+  build_plan(h, ws, pl);
+  PlanView pv = upload_plan(h, pl);
+  cudaEvent_t f0 = nullptr, f1 = nullptr;
+  if (h->stats_on) {
+    f0 = h->event();
+    f1 = h->event();
+    cudaEventRecord(f0, h->st);
+  }
+  forward(h, pv, pl.nw);
+  if (greedy && R) {
+    bool rec = h->stats_on && ((h->stats_mask >> GCK_K_ARGMAX) & 1u);
+    cudaEvent_t a = rec ? h->event() : nullptr, b = rec ? h->event() : nullptr;
+    if (rec) cudaEventRecord(a, h->st);
+    if (h->tp > 1) {
+      // each rank's best of its vocabulary slice, gathered, then the first maximum overall
+      int *mine = h->tp_pick + static_cast<size_t>(h->tp) * h->max_cols * 2;
+      launch_argmax_pick(h->logits, static_cast<int>(R), h->vocab_rows, h->vocab0, mine, h->st);
+      nck(nccl().all_gather(mine, h->tp_pick, R * 2, ncclInt32, static_cast<ncclComm_t>(h->comm), h->st), "argmax gather");
+      launch_argmax_merge(h->tp_pick, h->tp, static_cast<int>(R), h->argmax, h->st);
+      h->step_launches += 2;
+    } else {
+      launch_argmax(h->logits, static_cast<int>(R), h->vocab_rows, h->argmax, h->st);
+    }
+    if (rec) {
+      cudaEventRecord(b, h->st);
+      h->marks.push_back({GCK_K_ARGMAX, a, b});
+    }
+    h->step_launches += 1;
+  }
+  if (f1) cudaEventRecord(f1, h->st);
+  ck(cudaMemcpyAsync(h->kerr_host, h->kerr, 4, cudaMemcpyDeviceToHost, h->st), "error word");
+  if (greedy) {
+    if (R && h->rank == 0) ck(cudaMemcpyAsync(h->tok_host, h->argmax, R * 4, cudaMemcpyDeviceToHost, h->st), "tokens");
+    ck(cudaStreamSynchronize(h->st), "step");
+    if (h->rank == 0) std::memcpy(O.tokens, h->tok_host, R * 4);
+  } else if (flags & GC_S_HOST_LOGITS) {
+    // this handle's vocabulary rows [vocab0, vocab0 + vocab_rows) of every wanted row
+    if (R)
+      ck(cudaMemcpy2DAsync(O.logits + h->vocab0, static_cast<size_t>(h->vocab) * 4, h->logits,
+                           static_cast<size_t>(h->vocab_rows) * 4, static_cast<size_t>(h->vocab_rows) * 4, R,
+                           cudaMemcpyDeviceToHost, h->st), "logits");
+    ck(cudaStreamSynchronize(h->st), "step");
+  } else {
+    ck(cudaStreamSynchronize(h->st), "step");
+    if (o && o->size >= offsetof(gc_step_out, logits_dev) + 8) o->logits_dev = reinterpret_cast<uint64_t>(h->logits);
+  }
+  ck(cudaGetLastError(), "step");
+  if (*h->kerr_host) {
+    int code = *h->kerr_host;
+    *h->kerr_host = 0;
+    ck(cudaMemset(h->kerr, 0, 16), "error word");
+    h->marks.clear();
+    h->ev_used = 0;
+    fail(GC_E_DEVICE, "a kernel's wait ran out of time (code %d); the step's results are invalid", code);
+  }
+  collect_stats(h, f0, f1);
+}
+
 }  // namespace
 
 extern "C" {
@@ -998,11 +1230,9 @@ GC_API int gc_step(gc_handle *h, const gc_step_in *in, gc_step_out *o) {
         fail(GC_E_ARG, "work item %u: block table does not cover rows 0 .. %u", i, W.pos + W.n_tokens - 1);
       if (static_cast<uint64_t>(W.pos) + W.n_tokens > static_cast<uint64_t>(h->max_ctx))
         fail(GC_E_ARG, "work item %u: position %u past the context %d", i, W.pos + W.n_tokens, h->max_ctx);
-      uint32_t used_blocks = (W.pos + W.n_tokens + kBlock - 1) / kBlock;
       for (uint32_t b = 0; b < W.n_blocks; b++)
         if (W.blocks[b] >= static_cast<uint32_t>(h->nblk))
           fail(GC_E_ARG, "work item %u: block %u out of pool (%d blocks)", i, W.blocks[b], h->nblk);
-      (void)used_blocks;
       for (uint32_t j = 0; j < W.n_tokens; j++) {
         if (W.tokens[j] < 0 || W.tokens[j] >= h->vocab) fail(GC_E_ARG, "work item %u: token %d outside the vocabulary", i, W.tokens[j]);
         if (W.parents && (W.parents[j] < -1 || W.parents[j] >= static_cast<int32_t>(j)))
@@ -1019,69 +1249,44 @@ GC_API int gc_step(gc_handle *h, const gc_step_in *in, gc_step_out *o) {
     gc_step_out O{};
     std::memcpy(&O, o, std::min<size_t>(o->size, sizeof O));
     o->n_rows = static_cast<uint32_t>(R);
+    const uint32_t flags = in->flags;
     if (greedy) {
       if (O.tokens_cap < R || (R && !O.tokens) || !O.counts) fail(GC_E_CAPACITY, "tokens buffer too small (%llu rows)", static_cast<unsigned long long>(R));
-    } else if (in->flags & GC_S_HOST_LOGITS) {
+    } else if (flags & GC_S_HOST_LOGITS) {
       if (O.logits_cap < R * static_cast<uint64_t>(h->vocab) || (R && !O.logits))
         fail(GC_E_CAPACITY, "logits buffer too small (%llu rows of %d)", static_cast<unsigned long long>(R), h->vocab);
+    } else if (h->tp > 1) {
+      fail(GC_E_UNSUPPORTED, "device logits are not gathered across tensor-parallel ranks: ask for host logits or greedy rows");
     }
-    // sequence slots
+    // sequence slots: the handle's table (a group's is kept for the checks, every rank holds the same one)
     for (auto &w : ws)
       if (!find_slot(h, w.sid, true)) fail(GC_E_STATE, "no free sequence slot (%d in use)", h->max_seqs);
-    for (auto &w : ws) {
-      Slot *sl = find_slot(h, w.sid, false);
-      sl->blocks.assign(w.blocks, w.blocks + w.nblocks);
-      sl->last_pos = w.pos;
-      sl->last_n = w.n;
-    }
-    ck(cudaSetDevice(h->dev), "cudaSetDevice");
-    HostPlan pl;
-    build_plan(h, ws, pl);
-    PlanView pv = upload_plan(h, pl);
-    cudaEvent_t f0 = nullptr, f1 = nullptr;
-    if (h->stats_on) {
-      f0 = h->event();
-      f1 = h->event();
-      cudaEventRecord(f0, h->st);
-    }
-    forward(h, pv, pl.nw);
-    if (greedy && R) {
-      bool rec = h->stats_on && ((h->stats_mask >> GCK_K_ARGMAX) & 1u);
-      cudaEvent_t a = rec ? h->event() : nullptr, b = rec ? h->event() : nullptr;
-      if (rec) cudaEventRecord(a, h->st);
-      launch_argmax(h->logits, static_cast<int>(R), h->vocab, h->argmax, h->st);
-      if (rec) {
-        cudaEventRecord(b, h->st);
-        h->marks.push_back({GCK_K_ARGMAX, a, b});
-      }
-      h->step_launches += 1;
-    }
-    if (f1) cudaEventRecord(f1, h->st);
-    ck(cudaMemcpyAsync(h->kerr_host, h->kerr, 4, cudaMemcpyDeviceToHost, h->st), "error word");
-    if (greedy) {
-      if (R) {
-        ck(cudaMemcpyAsync(h->tok_host, h->argmax, R * 4, cudaMemcpyDeviceToHost, h->st), "tokens");
-      }
-      ck(cudaStreamSynchronize(h->st), "step");
-      std::memcpy(O.tokens, h->tok_host, R * 4);
-      for (uint32_t i = 0; i < in->n_work; i++) O.counts[i] = ws[i].want;
-    } else if (in->flags & GC_S_HOST_LOGITS) {
-      if (R) ck(cudaMemcpyAsync(O.logits, h->logits, R * h->vocab * 4, cudaMemcpyDeviceToHost, h->st), "logits");
-      ck(cudaStreamSynchronize(h->st), "step");
+    if (h->tp == 1) {
+      step_device(h, ws, greedy, R, flags, O, o);
     } else {
-      ck(cudaStreamSynchronize(h->st), "step");
-      if (o->size >= offsetof(gc_step_out, logits_dev) + 8) o->logits_dev = reinterpret_cast<uint64_t>(h->logits);
+      for (auto &w : ws) {
+        Slot *sl = find_slot(h, w.sid, false);
+        sl->blocks.assign(w.blocks, w.blocks + w.nblocks);
+        sl->last_pos = w.pos;
+        sl->last_n = w.n;
+      }
+      std::vector<std::thread> th;
+      std::vector<int> codes(h->tp, GC_OK);
+      std::vector<std::string> errs(h->tp);
+      for (int r = 0; r < h->tp; r++)
+        th.emplace_back([&, r] {
+          try {
+            step_device(h->ranks[r], ws, greedy, R, flags, O, r == 0 ? o : nullptr);
+          } catch (const GcError &e) {
+            codes[r] = e.code;
+            errs[r] = e.msg;
+          }
+        });
+      for (auto &t : th) t.join();
+      for (int r = 0; r < h->tp; r++)
+        if (codes[r] != GC_OK) fail(codes[r], "rank %d: %s", r, errs[r].c_str());
     }
-    ck(cudaGetLastError(), "step");
-    if (*h->kerr_host) {
-      int code = *h->kerr_host;
-      *h->kerr_host = 0;
-      ck(cudaMemset(h->kerr, 0, 16), "error word");
-      h->marks.clear();
-      h->ev_used = 0;
-      fail(GC_E_DEVICE, "a kernel's wait ran out of time (code %d); the step's results are invalid", code);
-    }
-    collect_stats(h, f0, f1);
+    for (uint32_t i = 0; greedy && i < in->n_work; i++) O.counts[i] = ws[i].want;
     return GC_OK;
   } catch (const GcError &e) {
     h->err = e.msg;
@@ -1089,8 +1294,26 @@ GC_API int gc_step(gc_handle *h, const gc_step_in *in, gc_step_out *o) {
   }
 }
 
+}  // extern "C"
+
+// a tensor-parallel group applies a KV operation on every rank (each holds its kv heads of the same blocks)
+template <typename Fn>
+static int on_ranks(gc_handle *h, Fn fn) {
+  for (gc_handle *r : h->ranks) {
+    int rc = fn(r);
+    if (rc != GC_OK) {
+      h->err = "rank " + std::to_string(r->rank) + ": " + r->err;
+      return rc;
+    }
+  }
+  return GC_OK;
+}
+
+extern "C" {
+
 GC_API int gc_commit(gc_handle *h, uint64_t sid, uint32_t base, const uint32_t *path, uint32_t n) {
   if (!h) return GC_E_ARG;
+  if (!h->ranks.empty()) return on_ranks(h, [&](gc_handle *r) { return gc_commit(r, sid, base, path, n); });
   try {
     Slot *sl = find_slot(h, sid, false);
     if (!sl) fail(GC_E_STATE, "gc_commit: unknown sequence %llu", static_cast<unsigned long long>(sid));
@@ -1124,6 +1347,7 @@ GC_API int gc_commit(gc_handle *h, uint64_t sid, uint32_t base, const uint32_t *
 
 GC_API int gc_copy_blocks(gc_handle *h, const uint32_t *src, const uint32_t *dst, uint32_t n) {
   if (!h) return GC_E_ARG;
+  if (!h->ranks.empty()) return on_ranks(h, [&](gc_handle *r) { return gc_copy_blocks(r, src, dst, n); });
   try {
     if (n && (!src || !dst)) fail(GC_E_ARG, "gc_copy_blocks: null array");
     std::vector<int> pairs;
@@ -1165,6 +1389,7 @@ GC_API int gc_copy_blocks(gc_handle *h, const uint32_t *src, const uint32_t *dst
 
 GC_API int gck_commit_static(gc_handle *h, uint64_t sid, uint32_t base, const uint32_t *path, uint32_t n) {
   if (!h) return GC_E_ARG;
+  if (!h->ranks.empty()) return on_ranks(h, [&](gc_handle *r) { return gck_commit_static(r, sid, base, path, n); });
   try {
     Slot *sl = find_slot(h, sid, false);
     if (!sl) fail(GC_E_STATE, "gck_commit_static: unknown sequence %llu", static_cast<unsigned long long>(sid));
@@ -1221,11 +1446,13 @@ GC_API int gc_release(gc_handle *h, uint64_t sid) {
   if (!h) return GC_E_ARG;
   Slot *sl = find_slot(h, sid, false);
   if (sl) *sl = Slot{};
+  for (gc_handle *r : h->ranks) gc_release(r, sid);
   return GC_OK;
 }
 
 GC_API int gck_stats_enable(gc_handle *h, uint32_t class_mask) {
   if (!h) return GC_E_ARG;
+  if (!h->ranks.empty()) return gck_stats_enable(h->ranks[0], class_mask);   // rank 0's device times
   h->stats = gck_stats{};
   h->stats.size = sizeof(gck_stats);
   h->stats_mask = class_mask;
@@ -1237,6 +1464,7 @@ GC_API int gck_stats_enable(gc_handle *h, uint32_t class_mask) {
 
 GC_API int gck_stats_read(gc_handle *h, gck_stats *out) {
   if (!h || !out || out->size < 8) return GC_E_ARG;
+  if (!h->ranks.empty()) return gck_stats_read(h->ranks[0], out);
   h->stats_on = false;
   uint32_t n = std::min<uint32_t>(out->size, sizeof(gck_stats));
   gck_stats st = h->stats;
@@ -1247,6 +1475,25 @@ GC_API int gck_stats_read(gc_handle *h, gck_stats *out) {
 
 GC_API void gc_close(gc_handle *h) {
   if (!h) return;
+  if (!h->ranks.empty()) {
+    // communicators are released by every rank at once (as their collectives run), then the ranks' memory
+    std::vector<std::thread> th;
+    for (gc_handle *r : h->ranks)
+      th.emplace_back([r] {
+        cudaSetDevice(r->dev);
+        if (r->st) cudaStreamSynchronize(r->st);
+        if (r->comm) nccl().destroy(static_cast<ncclComm_t>(r->comm));
+        r->comm = nullptr;
+      });
+    for (auto &t : th) t.join();
+    for (gc_handle *r : h->ranks) {
+      cudaSetDevice(r->dev);
+      delete r;
+    }
+    h->ranks.clear();
+    delete h;
+    return;
+  }
   cudaSetDevice(h->dev);
   delete h;
 }

@@ -159,7 +159,8 @@ def write_gguf(spec, path):
 
 
 def pack_dir(d, spec, buckets, weights_file="model.gguf"):
-    """Write d/manifest.json for the given buckets: [{id, ncol, maxctx, kv, tune}] (tune: the library's knobs)."""
+    """Write d/manifest.json for the given buckets: [{id, ncol, maxctx, kv, tune, tp}] (tune: the library's knobs; tp: the
+    tensor-parallel degree, 1 when absent)."""
     os.makedirs(d, exist_ok=True)
     bs = []
     for b in buckets:
@@ -170,6 +171,8 @@ def pack_dir(d, spec, buckets, weights_file="model.gguf"):
                        spec_caps=dict(verify=["linear", "tree"], tree_mask=True, verify_widths=[], taps=[],
                                       recurrent_commit=[], accept=[], drafter_roles=[]),
                        tune=dict(b.get("tune", {}))))
+        if b.get("tp", 1) > 1:
+            bs[-1]["tp"] = b["tp"]   # tensor-parallel degree: devices device .. device + tp - 1
     m = dict(schema="gc-pack", abi="3.0.0", arch="sm_100a", cuda="12.9", runtime=dict(kind="gc-c", version=1),
              contracts=["BI"], buckets=bs, model=dict(name=spec.name, weights=[dict(file=weights_file)]),
              synth=asdict(spec))

@@ -24,6 +24,7 @@ enum {
   GCK_K_HEAD = 9,       /* LM head GEMM */
   GCK_K_ARGMAX = 10,    /* device argmax */
   GCK_K_REDUCE = 11,    /* split-K reduction + epilogue of a GEMM with K splits */
+  GCK_K_ALLREDUCE = 12, /* tensor parallelism: all-reduce of o_proj / down_proj, argmax gather */
   GCK_K_CLASSES = 16
 };
 

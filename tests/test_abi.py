@@ -72,6 +72,14 @@ def test_open_errors_are_codes(lib, tiny, tmp_path):
     assert rc == gck.E_WEIGHTS and "GGUF" in msg
 
 
+def test_open_rejects_bad_tensor_parallel_degree(lib, tiny, tmp_path):
+    pack, ws = tiny
+    spec = synth.Spec(vocab=512, d=256, layers=1, heads=4, kv_heads=2, ffn=512, wtype="q8_0")
+    bad = synth.pack_dir(str(tmp_path / "tp3"), spec, [dict(id="b200.BI.main", ncol=4, maxctx=256, tp=3)])
+    rc, h, msg = _open(lib, bad, ws)
+    assert rc == gck.E_MANIFEST and "tensor-parallel" in msg and not h.value
+
+
 def test_null_handles(lib):
     assert lib.gc_layout_get(None, None) == gck.E_ARG
     assert lib.gc_step(None, None, None) == gck.E_ARG
