@@ -350,6 +350,102 @@ def cpu_baseline(args):
     return CpuSample().run()
 
 
+SPEC70B = dict(vocab=128256, d=8192, layers=80, heads=64, kv_heads=8, ffn=28672, eps=1e-5, theta=5e5, wtype="q4_k",
+               std=0.02, seed=0, ctx=4096 + 64, name="llama3-70b-shape-q4k")
+B70, CTX70 = 128, 4096
+
+
+def run_c5(args):
+    """C5: the 70B shape (Q4_K, fp8 paged KV with per-page scales), 128 sequences at context 4096 each (uniform tokens,
+    seed 0), greedy decode on one tensor-parallel handle over --gpus devices (one process, NCCL all-reduces inside)."""
+    import ctypes as C
+    import torch
+    from goethe_engine_b200 import build, gck, synth
+    build.build()
+    tp = args.gpus
+    spec = synth.Spec(**SPEC70B)
+    d = os.path.join(os.environ.get("GCK_BENCH_DIR", "/tmp/gck_bench"), f"{spec.name}-s{spec.seed}")
+    t0 = time.time()
+    synth.make(d, spec, buckets=[dict(id="b200.BI.main", ncol=B70, maxctx=spec.ctx, kv="fp8", tp=tp,
+                                      tune=dict(max_cols=2048, kv_scale="page"))])
+    print(f"[bench] model ready in {d} ({time.time() - t0:.1f}s)", file=sys.stderr, flush=True)
+    steps_total = args.warmup + args.steps
+    per_seq = -(-(CTX70 + steps_total + 1) // 16)
+    t0 = time.time()
+    be = gck.Backend(d, [os.path.join(d, "model.gguf")], pool_blocks=B70 * per_seq + 16, device=0)
+    t_open = time.time() - t0
+    L = be.L
+    L.gck_stats_enable.argtypes = [C.c_void_p, C.c_uint32]
+    L.gck_stats_read.argtypes = [C.c_void_p, C.c_void_p]
+
+    class Stats(C.Structure):
+        _fields_ = [("size", C.c_uint32), ("steps", C.c_uint32), ("launches", C.c_uint64), ("forward_ms", C.c_double),
+                    ("class_ms", C.c_double * 16), ("class_launches", C.c_uint64 * 16)]
+    rng = np.random.default_rng(0)
+    toks = [[int(x) for x in rng.integers(1, 128000, CTX70)] for _ in range(B70)]
+    tables = [list(range(i * per_seq, (i + 1) * per_seq)) for i in range(B70)]
+    cap = be.layout.max_cols
+    t0 = time.time()
+    queue = [[i, 0] for i in range(B70)]
+    while any(q[1] < CTX70 - 1 for q in queue):
+        budget, items = cap, []
+        for q in queue:
+            if q[1] >= CTX70 - 1 or budget == 0:
+                continue
+            n = min(budget, CTX70 - 1 - q[1])
+            items.append(gck.Work(q[0], toks[q[0]][q[1]:q[1] + n], q[1], tables[q[0]], 0))
+            q[1] += n
+            budget -= n
+        be.step(items)
+    t_prefill = time.time() - t0
+    last = [t[-1] for t in toks]
+    pos = [CTX70 - 1] * B70
+
+    def step():
+        out = be.step([gck.Work(i, [last[i]], pos[i], tables[i], 1, greedy=True) for i in range(B70)])
+        for i in range(B70):
+            last[i] = out[i][0]
+            pos[i] += 1
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    L.gck_stats_enable(be.h, 1 << 4)
+    with Clocks(0) as clk:
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            step()
+        wall = time.perf_counter() - t0
+    st = Stats(size=C.sizeof(Stats))
+    L.gck_stats_read(be.h, C.byref(st))
+    dev_s = st.forward_ms / 1e3
+    value, e2e = B70 * args.steps / dev_s, B70 * args.steps / wall
+    ms_step = dev_s / args.steps * 1e3
+    wbytes = weight_bytes(SPEC70B)
+    kv = (CTX70 + args.warmup + args.steps / 2) * B70 * 2 * 8 * 128 * 80
+    per_gpu = (wbytes + kv) / tp
+    hbm = peaks().get("hbm_gbs", 6650.0)
+    res = {
+        "metric": "decode tok/s (70B Q4_K, batch 128, fp8 KV, tensor parallel)", "value": round(value, 1),
+        "unit": "tok/s", "n_gpus": tp, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "q4_k x f16 -> f32; fp8 e4m3 KV",
+        "data": "synthetic (seeded N(0,0.02) weights, uniform tokens)",
+        "config": {"workload": "C5: Llama-3-70B shape, Q4_K weights, fp8 paged KV (per-page scale), 128 sequences at "
+                               "context 4096, greedy decode", "batch": B70, "context": CTX70,
+                   "parallelism": f"tp{tp} (one handle, NCCL all-reduce after o_proj and down_proj)",
+                   "l2": "inputs larger than L2, no flush"},
+        "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": int(sum(len(t) for t in tables) * 4 + B70 * 64),
+                "d2h_bytes_per_step": B70 * 4, "path": "gc_step through the C ABI (ctypes), host buffers"},
+        "step_roofline": {"bytes_per_gpu": int(per_gpu), "weights_bytes": int(wbytes), "kv_bytes": int(kv),
+                          "achieved_gbs_per_gpu": round(per_gpu / (ms_step / 1e3) / 1e9, 1),
+                          "frac_of_measured": round(per_gpu / (ms_step / 1e3) / 1e9 / hbm, 4)},
+        "gpu_launches": int(st.launches),
+        "clocks": clk.summary(),
+        "setup": {"open_s": round(t_open, 1), "prefill_s": round(t_prefill, 1), "prefill_tokens": B70 * (CTX70 - 1)},
+    }
+    be.close()
+    print(json.dumps(res), flush=True)
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return
@@ -379,6 +475,8 @@ def main():
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--profile", action="store_true", help="time every kernel class (stderr table)")
+    ap.add_argument("--workload", default="c3", choices=["c3", "c5"],
+                    help="c3: the headline (8B, replicas over --gpus); c5: 70B tensor parallel over --gpus in one process")
     ap.add_argument("--layers", type=int, default=32,
                     help="layers of the 8B shape (default 32; fewer only for small profiling cases, not a headline)")
     args = ap.parse_args()
@@ -387,6 +485,12 @@ def main():
         SPEC8B["name"] += f"-L{args.layers}"
     world = int(os.environ.get("WORLD_SIZE", 1))
     rank = int(os.environ.get("RANK", 0))
+    if args.workload == "c5":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "C5 (70B) on the CPU needs about 278 GB of f32 weights: "
+                              "not run"}), flush=True)
+            return
+        return run_c5(args)
     if args.impl == "reference":
         return run_reference(args, rank, world)
     barrier = lambda: None  # noqa: E731

@@ -69,16 +69,28 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float *x, const i
     v[i] = e < nv ? xr[e] : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   if (part) {
+    // per element: ((0 + p_0) + p_1) + ... in split order, then added to x; the four vectors' loads are independent
+    float4 a[kNormMaxVec];
+#pragma unroll
+    for (int i = 0; i < kNormMaxVec; i++) a[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sp = 0; sp < S; sp++) {
+      const float4 *pr = reinterpret_cast<const float4 *>(part + (static_cast<size_t>(sp) * T + src) * pld);
+      float4 pp[kNormMaxVec];
+#pragma unroll
+      for (int i = 0; i < kNormMaxVec; i++) {
+        int e = threadIdx.x + i * kNormThreads;
+        pp[i] = e < nv ? pr[e] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int i = 0; i < kNormMaxVec; i++) {
+        a[i].x += pp[i].x; a[i].y += pp[i].y; a[i].z += pp[i].z; a[i].w += pp[i].w;
+      }
+    }
 #pragma unroll
     for (int i = 0; i < kNormMaxVec; i++) {
       int e = threadIdx.x + i * kNormThreads;
       if (e >= nv) continue;
-      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int sp = 0; sp < S; sp++) {
-        const float4 pp = reinterpret_cast<const float4 *>(part + (static_cast<size_t>(sp) * T + src) * pld)[e];
-        a.x += pp.x; a.y += pp.y; a.z += pp.z; a.w += pp.w;
-      }
-      v[i].x += a.x; v[i].y += a.y; v[i].z += a.z; v[i].w += a.w;
+      v[i].x += a[i].x; v[i].y += a[i].y; v[i].z += a[i].z; v[i].w += a[i].w;
       xr[e] = v[i];
     }
   }
@@ -144,10 +156,22 @@ struct QkvSrc {
     for (int s = 0; s < S; s++) v += p[(static_cast<size_t>(s) * T + t) * ld + c];
     return v;
   }
+  // columns c, c + 1 (c even): one 8-byte load per split
+  __device__ float2 pair(int t, int c) const {
+    if (S == 1) return *reinterpret_cast<const float2 *>(p + static_cast<size_t>(t) * ld + c);
+    float2 v = make_float2(0.f, 0.f);
+    for (int s = 0; s < S; s++) {
+      const float2 x = *reinterpret_cast<const float2 *>(p + (static_cast<size_t>(s) * T + t) * ld + c);
+      v.x += x.x;
+      v.y += x.y;
+    }
+    return v;
+  }
 };
 
 __device__ void rope_pair(const QkvSrc &q, int t, int c0, const float2 *cs, int i, float &a, float &b) {
-  float x0 = q(t, c0 + 2 * i), x1 = q(t, c0 + 2 * i + 1);
+  const float2 x = q.pair(t, c0 + 2 * i);
+  const float x0 = x.x, x1 = x.y;
   float2 c = cs[i];
   a = x0 * c.x - x1 * c.y;
   b = x0 * c.y + x1 * c.x;
@@ -159,7 +183,7 @@ __device__ float head_amax(const QkvSrc &q, int t, int c0, const float2 *cs, boo
   for (int i = threadIdx.x % 32; i < DH / 2; i += 32) {
     float a, b;
     if (rot) rope_pair(q, t, c0, cs, i, a, b);
-    else { a = q(t, c0 + 2 * i); b = q(t, c0 + 2 * i + 1); }
+    else { const float2 x = q.pair(t, c0 + 2 * i); a = x.x; b = x.y; }
     m = fmaxf(m, fmaxf(fabsf(a), fabsf(b)));
   }
   return warp_max(m);
@@ -194,7 +218,8 @@ __global__ void rope_kv_kernel(PlanView pv, QkvSrc qs, int H, int KVH, const flo
       float a, b;
       rope_pair(qs, t, kcol, cs, i, a, b);
       kd[i] = __floats2half2_rn(a, b);
-      vd[i] = __floats2half2_rn(qs(t, vcol + 2 * i), qs(t, vcol + 2 * i + 1));
+      const float2 x = qs.pair(t, vcol + 2 * i);
+      vd[i] = __floats2half2_rn(x.x, x.y);
     }
     return;
   }
@@ -221,8 +246,9 @@ __global__ void rope_kv_kernel(PlanView pv, QkvSrc qs, int H, int KVH, const flo
     rope_pair(qs, t, kcol, cs, i, a, b);
     kd[2 * i] = f32_to_e4m3(a * sk);
     kd[2 * i + 1] = f32_to_e4m3(b * sk);
-    vd[2 * i] = f32_to_e4m3(qs(t, vcol + 2 * i) * sv);
-    vd[2 * i + 1] = f32_to_e4m3(qs(t, vcol + 2 * i + 1) * sv);
+    const float2 x = qs.pair(t, vcol + 2 * i);
+    vd[2 * i] = f32_to_e4m3(x.x * sv);
+    vd[2 * i + 1] = f32_to_e4m3(x.y * sv);
   }
 }
 
@@ -243,20 +269,27 @@ void launch_rope_kv(const PlanView &pv, const float *qkv, int S, int ld, int H, 
 __device__ __forceinline__ float silu(float g) { return g / (1.f + expf(-g)); }
 
 __global__ void splitk_reduce_kernel(const float *part, int S, int T, int Npad, Epi epi) {
-  size_t total = static_cast<size_t>(T) * (epi.kind == kEpiSwiGLU ? Npad / 2 : Npad);
+  size_t total = static_cast<size_t>(T) * (epi.kind == kEpiSwiGLU ? Npad / 8 : Npad);
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
     if (epi.kind == kEpiSwiGLU) {
-      int half = Npad / 2;
-      int t = static_cast<int>(i / half), f = static_cast<int>(i % half);
+      // four consecutive features of one 64-row half per thread: float4 loads of the gate and up rows
+      int q4 = Npad / 2 / 4;
+      int t = static_cast<int>(i / q4), f = static_cast<int>(i % q4) * 4;
       int tile = f / 64, w = f % 64;
       int ng = tile * 128 + w, nu = ng + 64;
-      float g = 0.f, u = 0.f;
+      float4 g = make_float4(0.f, 0.f, 0.f, 0.f), u = g;
       for (int s = 0; s < S; s++) {
-        g += part[(static_cast<size_t>(s) * T + t) * Npad + ng];
-        u += part[(static_cast<size_t>(s) * T + t) * Npad + nu];
+        const float4 a = *reinterpret_cast<const float4 *>(part + (static_cast<size_t>(s) * T + t) * Npad + ng);
+        const float4 b = *reinterpret_cast<const float4 *>(part + (static_cast<size_t>(s) * T + t) * Npad + nu);
+        g.x += a.x; g.y += a.y; g.z += a.z; g.w += a.w;
+        u.x += b.x; u.y += b.y; u.z += b.z; u.w += b.w;
       }
-      if (f < epi.n) epi.out_h[static_cast<size_t>(t) * epi.ld + f] = __float2half_rn(silu(g) * u);
+      __half *o = epi.out_h + static_cast<size_t>(t) * epi.ld + f;
+      if (f < epi.n) o[0] = __float2half_rn(silu(g.x) * u.x);
+      if (f + 1 < epi.n) o[1] = __float2half_rn(silu(g.y) * u.y);
+      if (f + 2 < epi.n) o[2] = __float2half_rn(silu(g.z) * u.z);
+      if (f + 3 < epi.n) o[3] = __float2half_rn(silu(g.w) * u.w);
     } else {
       int t = static_cast<int>(i / Npad), n = static_cast<int>(i % Npad);
       if (n >= epi.n) continue;
@@ -331,8 +364,49 @@ __global__ void argmax_merge_kernel(const int *pick, int tp, int R, int *out) {
   out[r] = idx == 0x7fffffff ? 0 : idx;
 }
 
-void launch_argmax(const float *logits, int R, int V, int *out, cudaStream_t s) {
-  if (R > 0) argmax_kernel<<<R, 1024, 0, s>>>(logits, V, out, nullptr, 0);
+// a row's argmax in kArgChunks parts (one CTA each), then the first maximum of the parts (parts ascend in index)
+constexpr int kArgChunks = 8;
+__global__ void argmax_part_kernel(const float *logits, int V, int *pick) {
+  const int r = blockIdx.x, c = blockIdx.y;
+  const int per = (V + kArgChunks - 1) / kArgChunks;
+  const int v0 = c * per, v1 = min(V, v0 + per);
+  const float *row = logits + static_cast<size_t>(r) * V;
+  float best = -INFINITY;
+  int idx = 0x7fffffff;
+  for (int v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
+    float x = row[v];
+    if (x > best) { best = x; idx = v; }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    float b2 = __shfl_xor_sync(0xffffffffu, best, o);
+    int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (b2 > best || (b2 == best && i2 < idx)) { best = b2; idx = i2; }
+  }
+  __shared__ float sb[32];
+  __shared__ int si[32];
+  int w = threadIdx.x / 32, l = threadIdx.x % 32;
+  if (l == 0) { sb[w] = best; si[w] = idx; }
+  __syncthreads();
+  if (w == 0) {
+    best = l < blockDim.x / 32 ? sb[l] : -INFINITY;
+    idx = l < blockDim.x / 32 ? si[l] : 0x7fffffff;
+    for (int o = 16; o > 0; o >>= 1) {
+      float b2 = __shfl_xor_sync(0xffffffffu, best, o);
+      int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
+      if (b2 > best || (b2 == best && i2 < idx)) { best = b2; idx = i2; }
+    }
+    if (l == 0) {
+      pick[(static_cast<size_t>(c) * gridDim.x + r) * 2] = __float_as_int(best);
+      pick[(static_cast<size_t>(c) * gridDim.x + r) * 2 + 1] = idx;
+    }
+  }
+}
+
+void launch_argmax_merge(const int *pick, int tp, int R, int *out, cudaStream_t s);
+void launch_argmax(const float *logits, int R, int V, int *out, int *scratch, cudaStream_t s) {
+  if (R <= 0) return;
+  argmax_part_kernel<<<dim3(R, kArgChunks), 512, 0, s>>>(logits, V, scratch);
+  launch_argmax_merge(scratch, kArgChunks, R, out, s);
 }
 void launch_argmax_pick(const float *logits, int R, int V, int offset, int *pick, cudaStream_t s) {
   if (R > 0) argmax_kernel<<<R, 1024, 0, s>>>(logits, V, nullptr, pick, offset);

@@ -56,7 +56,8 @@ void launch_rope_kv(const PlanView &pv, const float *qkv, int S, int ld, int H, 
                     const float2 *rope_tab, __half *q, void *kc, void *vc, int8_t *exps, int kv_fp8, int page_scale,
                     cudaStream_t s);
 void launch_splitk_reduce(const float *part, int S, int T, int Npad, const Epi &epi, cudaStream_t s);
-void launch_argmax(const float *logits, int R, int V, int *out, cudaStream_t s);
+// scratch: [8][R][2] ints (the parts' candidates)
+void launch_argmax(const float *logits, int R, int V, int *out, int *scratch, cudaStream_t s);
 // tensor parallelism: a rank's candidates (value bits, global index) of its vocabulary slice, and their merge
 void launch_argmax_pick(const float *logits, int R, int V, int offset, int *pick, cudaStream_t s);
 void launch_argmax_merge(const int *pick, int tp, int R, int *out, cudaStream_t s);

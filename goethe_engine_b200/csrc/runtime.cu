@@ -105,7 +105,7 @@ struct gc_handle {
   float *x = nullptr, *qkv = nullptr, *logits = nullptr, *part = nullptr, *attn_o = nullptr, *commit_tmp = nullptr;
   __half *h = nullptr, *q = nullptr, *att = nullptr, *act = nullptr;
   float2 *attn_ml = nullptr;
-  int *argmax = nullptr, *pairs = nullptr;
+  int *argmax = nullptr, *pairs = nullptr, *arg_scratch = nullptr;
   int *kerr = nullptr, *kerr_host = nullptr;   // device error word of bounded waits, and its pinned mirror
   TmaSet tma_h, tma_att, tma_act;               // activation tiles of the tcgen05 GEMMs
   size_t part_cap = 0, attn_parts_cap = 0, attn_sem_cap = 0, commit_cap = 0, pairs_cap = 0;
@@ -568,6 +568,7 @@ void open_device(gc_handle *h, int dev, const std::vector<std::unique_ptr<GgufFi
   ck(cudaMemset(h->act, 0, static_cast<size_t>(T) * Fpad * 2), "act");
   h->logits = static_cast<float *>(h->dalloc(static_cast<size_t>(T) * std::max(1, h->vocab_rows) * 4, "logits"));
   h->argmax = static_cast<int *>(h->dalloc(static_cast<size_t>(T) * 4, "argmax"));
+  h->arg_scratch = static_cast<int *>(h->dalloc(static_cast<size_t>(T) * 8 * 2 * 4, "argmax parts"));
   if (h->tp > 1) {
     h->tp_y = static_cast<float *>(h->dalloc(static_cast<size_t>(T) * d * 4, "tensor-parallel partial sums"));
     h->tp_pick = static_cast<int *>(h->dalloc(static_cast<size_t>(h->tp + 1) * T * 2 * 4, "tensor-parallel argmax"));
@@ -1165,7 +1166,8 @@ void step_device(gc_handle *h, const std::vector<WorkIn> &ws, bool greedy, uint6
       launch_argmax_merge(h->tp_pick, h->tp, static_cast<int>(R), h->argmax, h->st);
       h->step_launches += 2;
     } else {
-      launch_argmax(h->logits, static_cast<int>(R), h->vocab_rows, h->argmax, h->st);
+      launch_argmax(h->logits, static_cast<int>(R), h->vocab_rows, h->argmax, h->arg_scratch, h->st);
+      h->step_launches += 1;
     }
     if (rec) {
       cudaEventRecord(b, h->st);
