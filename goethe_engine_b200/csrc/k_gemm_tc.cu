@@ -344,7 +344,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // ---- MMA issuer: accumulator buffer (local unit index) % 2
       const uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(NT >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
-      long ca = 0;
+      int s = 0;                 // stage slot and the parity of its current use
+      uint32_t par = 0;
       int lu = 0;
       bool ok = true;
       for (int w = blockIdx.x; w < units && ok; w += gridDim.x, lu++) {
@@ -354,11 +355,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(ok = mbar_wait(&acc_empty[ab], ph ^ 1, err, kErrAcc))) break;
         tc_fence_after();
         const uint32_t dt = tmem + ab * S::NCOLS;
-        for (int i = 0; i < un.per * SPT; i++, ca++) {
-          const int s = static_cast<int>(ca % SR);
-          const uint32_t par = static_cast<uint32_t>((ca / SR) & 1);
+        for (int i = 0; i < un.per * SPT; i++) {
+          // a_full covers both operands: the dequant group signals it only after the stage's activations landed
           if (!(ok = mbar_wait(&a_full[s], par, err, kErrAFull))) break;
-          if (!(ok = mbar_wait(&b_full[s], par, err, kErrBFull))) break;
           tc_fence_after();
           const uint32_t at = tmem_a + (KS / 2) * s;
           const uint64_t bd = umma_desc(sB + s * S::STAGE_B);
@@ -367,6 +366,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             umma_f16_ts(dt, at + 8 * k, bd + static_cast<uint64_t>((k >> 2) * (S::BOX_B >> 4) + 2 * (k & 3)), idesc,
                         (i | k) != 0);
           umma_commit(&st_empty[s]);
+          if (++s == SR) {
+            s = 0;
+            par ^= 1u;
+          }
         }
         umma_commit(&acc_full[ab]);   // arrives once every MMA of this unit has completed
       }
@@ -391,8 +394,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int sub = 0; sub < SPT; sub++, c++) {
           if ((c & 1) != grp) continue;
           const int s = static_cast<int>(c % SR);
-          if (!(ok = mbar_wait(&raw_full[rs], static_cast<uint32_t>((cr / RS) & 1), err, kErrRawFull))) break;
-          if (!(ok = mbar_wait(&st_empty[s], static_cast<uint32_t>((c / SR) & 1) ^ 1, err, kErrStageEmpty))) break;
+          // every lane waits; the warp leaves together if any lane's wait ran out (the stores below are warp-wide)
+          ok = mbar_wait(&raw_full[rs], static_cast<uint32_t>((cr / RS) & 1), err, kErrRawFull);
+          ok = ok && mbar_wait(&st_empty[s], static_cast<uint32_t>((c / SR) & 1) ^ 1, err, kErrStageEmpty);
+          if (!(ok = __all_sync(0xffffffffu, ok))) break;
           tc_fence_after();
           const uint8_t *raw = sRaw + rs * F::BYTES;
           const uint4 hdr = *reinterpret_cast<const uint4 *>(raw + r * 16);
@@ -439,7 +444,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) mbar_arrive(&raw_empty[rs]);
           tmem_st_wait();
           tc_fence_before();
-          __syncwarp();
+          // the stage's activation tiles must have landed too: then a_full alone tells the MMA thread both are ready
+          ok = mbar_wait(&b_full[s], static_cast<uint32_t>((c / SR) & 1), err, kErrBFull);
+          if (!(ok = __all_sync(0xffffffffu, ok))) break;
           if (lane == 0) mbar_arrive(&a_full[s]);
         }
       }
