@@ -153,7 +153,8 @@ def setup_sequences(be, ctx, steps_total):
             q[1] += n
             budget -= n
         be.step(items)
-    return tables, toks, time.time() - t0
+    # block tables as uint32 arrays: the binding hands them to gc_step without a copy
+    return [np.asarray(t, np.uint32) for t in tables], toks, time.time() - t0
 
 
 def kv_unique_bytes(ctx_now, layout):
@@ -383,7 +384,7 @@ def run_c5(args):
                     ("class_ms", C.c_double * 16), ("class_launches", C.c_uint64 * 16)]
     rng = np.random.default_rng(0)
     toks = [[int(x) for x in rng.integers(1, 128000, CTX70)] for _ in range(B70)]
-    tables = [list(range(i * per_seq, (i + 1) * per_seq)) for i in range(B70)]
+    tables = [np.arange(i * per_seq, (i + 1) * per_seq, dtype=np.uint32) for i in range(B70)]
     cap = be.layout.max_cols
     t0 = time.time()
     queue = [[i, 0] for i in range(B70)]

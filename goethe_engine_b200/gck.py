@@ -55,6 +55,24 @@ class WorkS(C.Structure):
                 ("blocks", P_(C.c_uint32)), ("n_blocks", C.c_uint32), ("want", C.c_uint32)]
 
 
+# the same record as a numpy dtype (gc.h gc_work: natural alignment, 56 bytes): a step's records are filled in one array
+WORK_DTYPE = np.dtype([("size", "<u4"), ("flags", "<u4"), ("sid", "<u8"), ("pos", "<u4"), ("n_tokens", "<u4"),
+                       ("tokens", "<u8"), ("parents", "<u8"), ("blocks", "<u8"), ("n_blocks", "<u4"), ("want", "<u4")])
+assert WORK_DTYPE.itemsize == C.sizeof(WorkS) and all(
+    WORK_DTYPE.fields[n][1] == getattr(WorkS, n).offset for n, _ in WorkS._fields_)
+
+
+def _addr(a):
+    return a.__array_interface__["data"][0]
+
+
+def _u32(x):
+    # block tables: a contiguous uint32 array passes through; anything else is converted
+    if isinstance(x, np.ndarray) and x.dtype == np.uint32 and x.flags.c_contiguous:
+        return x
+    return np.ascontiguousarray(x, np.uint32)
+
+
 class StepIn(C.Structure):
     _fields_ = [("size", C.c_uint32), ("flags", C.c_uint32), ("work", P_(P_(WorkS))), ("n_work", C.c_uint32),
                 ("pad", C.c_uint32)]
@@ -138,17 +156,29 @@ class Backend:
         """Tokens per item (every item greedy) or float32 logits [sum(want), vocab] (into `logits` if given)."""
         n = len(work)
         greedy = self.device_argmax and all(w.greedy for w in work)
-        keep, ws = [], []
-        for w in work:
-            fl = (1 if greedy else 0) | (2 if w.spec else 0) | (4 if w.feats else 0)
-            toks = np.ascontiguousarray(w.tokens, np.int32)
-            blk = np.ascontiguousarray(w.blocks, np.uint32)
-            par = np.ascontiguousarray(w.parents, np.int32) if w.parents is not None else None
-            keep += [toks, blk, par]
-            ws.append(WorkS(C.sizeof(WorkS), fl, w.sid, w.pos, len(toks), toks.ctypes.data_as(P_(C.c_int32)),
-                            par.ctypes.data_as(P_(C.c_int32)) if par is not None else None,
-                            blk.ctypes.data_as(P_(C.c_uint32)), len(blk), w.want))
-        pw = arr(P_(WorkS), [C.pointer(x) for x in ws])
+        # every item's tokens in one int32 array, the records in one structured array (filled a column at a time), their
+        # addresses in another
+        ntok = np.fromiter((len(w.tokens) for w in work), np.int64, n)
+        toks = np.fromiter((t for w in work for t in w.tokens), np.int32, int(ntok.sum()))
+        blks = [_u32(w.blocks) for w in work]
+        rec = np.zeros(n, WORK_DTYPE)
+        keep = [toks, rec, blks]
+        rec["size"] = WORK_DTYPE.itemsize
+        rec["flags"] = [(1 if greedy else 0) | (2 if w.spec else 0) | (4 if w.feats else 0) for w in work]
+        rec["sid"] = [w.sid for w in work]
+        rec["pos"] = [w.pos for w in work]
+        rec["want"] = [w.want for w in work]
+        rec["n_tokens"] = ntok
+        rec["tokens"] = _addr(toks) + 4 * (np.cumsum(ntok) - ntok).astype(np.uint64)
+        rec["blocks"] = [_addr(x) for x in blks]
+        rec["n_blocks"] = [len(x) for x in blks]
+        for i, w in enumerate(work):
+            if w.parents is not None:
+                par = np.ascontiguousarray(w.parents, np.int32)
+                keep.append(par)
+                rec["parents"][i] = _addr(par)
+        ptrs = _addr(rec) + WORK_DTYPE.itemsize * np.arange(n, dtype=np.uint64)
+        pw = C.cast(C.c_void_p(_addr(ptrs)), P_(P_(WorkS)))
         rows = sum(w.want for w in work)
         out = StepOut(size=C.sizeof(StepOut))
         counts = (C.c_uint32 * n)()
@@ -160,6 +190,7 @@ class Backend:
             out.logits, out.logits_cap = lg.ctypes.data, lg.size
         self._ck(self.L.gc_step(self.h, C.byref(StepIn(C.sizeof(StepIn), 0 if greedy else S_HOST_LOGITS, pw, n, 0)),
                                 C.byref(out)))
+        del keep, ptrs
         if greedy:
             res, o = [], 0
             for c in counts:

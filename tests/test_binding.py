@@ -1,0 +1,56 @@
+"""The Python binding's step marshalling (no GPU): the gc_work records handed to gc_step carry each Work item's sid,
+position, tokens, block table, parents, want and flags (gc.h:133-157), with block tables as lists or uint32 arrays."""
+import numpy as np
+
+from goethe_engine_b200 import gck
+
+
+class FakeLib:
+    """Stands in for libgck.so: records what gc_step receives and answers greedy tokens."""
+
+    def __init__(self):
+        self.seen = None
+
+    def gc_step(self, h, pin, pout):
+        si, so = pin._obj, pout._obj
+        self.seen = []
+        for i in range(si.n_work):
+            r = si.work[i].contents
+            self.seen.append(dict(size=r.size, flags=r.flags, sid=r.sid, pos=r.pos, want=r.want,
+                                  tokens=[r.tokens[j] for j in range(r.n_tokens)],
+                                  blocks=[r.blocks[j] for j in range(r.n_blocks)],
+                                  parents=[r.parents[j] for j in range(r.n_tokens)] if r.parents else None))
+        if so.tokens:
+            for k in range(so.tokens_cap):
+                so.tokens[k] = 100 + k
+            for i, x in enumerate(self.seen):
+                so.counts[i] = x["want"]
+        so.n_rows = sum(x["want"] for x in self.seen)
+        return 0
+
+
+def backend(greedy):
+    b = gck.Backend.__new__(gck.Backend)
+    b.L, b.h, b.device_argmax, b.vocab_size = FakeLib(), None, greedy, 1000
+    b._ck = lambda rc: None
+    return b
+
+
+def test_records_match_work_items():
+    b = backend(True)
+    work = [gck.Work(7, [3, 4, 5], 32, [9, 8, 2], 2, greedy=True),
+            gck.Work(2, [11], 17, np.array([4, 6], np.uint32), 1, greedy=True),
+            gck.Work(5, [1, 2, 3, 4], 0, np.arange(10, 14, dtype=np.int64), 4, greedy=True, parents=[-1, 0, 0, 1])]
+    out = b.step(work)
+    assert out == [[100, 101], [102], [103, 104, 105, 106]]
+    for w, r in zip(work, b.L.seen):
+        assert r["size"] == 56 and r["flags"] == gck.W_GREEDY
+        assert (r["sid"], r["pos"], r["want"]) == (w.sid, w.pos, w.want)
+        assert r["tokens"] == list(w.tokens) and r["blocks"] == [int(x) for x in w.blocks]
+        assert r["parents"] == (list(w.parents) if w.parents is not None else None)
+
+
+def test_logits_request_without_device_argmax():
+    b = backend(False)
+    lg = b.step([gck.Work(1, [3], 0, [0], 1)])
+    assert lg.shape == (1, 1000) and b.L.seen[0]["flags"] == 0
