@@ -422,7 +422,7 @@ def run_c5(args):
     value, e2e = B70 * args.steps / dev_s, B70 * args.steps / wall
     ms_step = dev_s / args.steps * 1e3
     wbytes = weight_bytes(SPEC70B)
-    kv = (CTX70 + args.warmup + args.steps / 2) * B70 * 2 * 8 * 128 * 80
+    kv = (CTX70 + args.warmup + args.steps / 2) * B70 * 2 * 8 * 128 * SPEC70B["layers"]
     per_gpu = (wbytes + kv) / tp
     hbm = peaks().get("hbm_gbs", 6650.0)
     res = {
@@ -431,7 +431,7 @@ def run_c5(args):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "q4_k x f16 -> f32; fp8 e4m3 KV",
         "data": "synthetic (seeded N(0,0.02) weights, uniform tokens)",
         "config": {"workload": "C5: Llama-3-70B shape, Q4_K weights, fp8 paged KV (per-page scale), 128 sequences at "
-                               "context 4096, greedy decode", "batch": B70, "context": CTX70,
+                               "context 4096, greedy decode", "batch": B70, "context": CTX70, "layers": SPEC70B["layers"],
                    "parallelism": f"tp{tp} (one handle, NCCL all-reduce after o_proj and down_proj)",
                    "l2": "inputs larger than L2, no flush"},
         "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": int(sum(len(t) for t in tables) * 4 + B70 * 64),
@@ -482,8 +482,9 @@ def main():
                     help="layers of the 8B shape (default 32; fewer only for small profiling cases, not a headline)")
     args = ap.parse_args()
     if args.layers != 32:
-        SPEC8B["layers"] = args.layers
-        SPEC8B["name"] += f"-L{args.layers}"
+        for sp, full in ((SPEC8B, 32), (SPEC70B, 80)):
+            sp["layers"] = min(args.layers, full)
+            sp["name"] += f"-L{sp['layers']}"
     world = int(os.environ.get("WORLD_SIZE", 1))
     rank = int(os.environ.get("RANK", 0))
     if args.workload == "c5":
