@@ -1501,3 +1501,107 @@ GC_API void gc_close(gc_handle *h) {
 }
 
 }  // extern "C"
+
+// ============================================================================================== pricing
+// gc_probe / gc_price (abi/gc.h:232-237): the constants a device's step time follows (HBM copy bandwidth, per-launch
+// latency, SMs, clock), and a roofline prediction from them. The library serves any llama GGUF, and gc_price sees only
+// a bucket id, so the price is that of one reference step on the device: a single-sequence decode of the 8B Q4_K shape
+// (4.221 GB of weights streamed once at the measured bandwidth, plus the step's kernel launches).
+namespace {
+
+struct PriceBlob {
+  uint32_t magic = 0x45435250u;   // "PRCE"
+  uint32_t version = 1;
+  double hbm_gbs = 0;            // device copy bandwidth (read + write bytes / time)
+  double launch_us = 0;          // back-to-back empty-kernel launch interval on one stream
+  uint32_t sms = 0, clock_mhz = 0;
+};
+
+__global__ void probe_copy_kernel(const float4 *a, float4 *b, size_t n) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n; i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    b[i] = a[i];
+}
+__global__ void probe_empty_kernel() {}
+
+constexpr double kRefWeightBytes = 4.221e9;   // 8B shape, Q4_K linear weights and head
+constexpr double kRefLaunches = 292;          // kernels of one such decode step
+constexpr double kRefStreamEff = 0.85;        // fraction of copy bandwidth a weight-streaming step reaches
+
+}  // namespace
+
+extern "C" {
+
+GC_API int gc_probe(int device, void *constants, uint64_t cap, uint64_t *size) {
+  if (!size) return GC_E_ARG;
+  *size = sizeof(PriceBlob);
+  if (cap < sizeof(PriceBlob) || !constants) return GC_E_CAPACITY;
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
+    cudaGetLastError();
+    return GC_E_DEVICE;
+  }
+  int prev = 0;
+  cudaGetDevice(&prev);
+  PriceBlob b;
+  int rc = GC_OK;
+  float4 *x = nullptr, *y = nullptr;
+  cudaStream_t st = nullptr;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  do {
+    if (cudaSetDevice(device) != cudaSuccess) { rc = GC_E_DEVICE; break; }
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) { rc = GC_E_DEVICE; break; }
+    b.sms = static_cast<uint32_t>(prop.multiProcessorCount);
+    int clk = 0;
+    cudaDeviceGetAttribute(&clk, cudaDevAttrClockRate, device);
+    b.clock_mhz = static_cast<uint32_t>(clk / 1000);
+    const size_t bytes = static_cast<size_t>(512) << 20;   // 512 MiB each way: well past L2
+    const size_t n = bytes / sizeof(float4);
+    if (cudaMalloc(&x, bytes) != cudaSuccess || cudaMalloc(&y, bytes) != cudaSuccess) { rc = GC_E_DEVICE; break; }
+    cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaMemsetAsync(x, 0, bytes, st);
+    const int grid = static_cast<int>(b.sms) * 8;
+    float best = 1e30f;
+    for (int it = 0; it < 5; it++) {
+      cudaEventRecord(e0, st);
+      probe_copy_kernel<<<grid, 512, 0, st>>>(x, y, n);
+      cudaEventRecord(e1, st);
+      cudaEventSynchronize(e1);
+      float ms = 0;
+      cudaEventElapsedTime(&ms, e0, e1);
+      if (it > 0) best = std::min(best, ms);
+    }
+    b.hbm_gbs = 2.0 * bytes / (best * 1e-3) / 1e9;
+    const int nl = 200;
+    probe_empty_kernel<<<1, 32, 0, st>>>();
+    cudaEventRecord(e0, st);
+    for (int i = 0; i < nl; i++) probe_empty_kernel<<<1, 32, 0, st>>>();
+    cudaEventRecord(e1, st);
+    cudaEventSynchronize(e1);
+    float ms = 0;
+    cudaEventElapsedTime(&ms, e0, e1);
+    b.launch_us = ms * 1e3 / nl;
+    if (cudaGetLastError() != cudaSuccess) rc = GC_E_DEVICE;
+  } while (false);
+  if (e0) cudaEventDestroy(e0);
+  if (e1) cudaEventDestroy(e1);
+  if (st) cudaStreamDestroy(st);
+  if (x) cudaFree(x);
+  if (y) cudaFree(y);
+  cudaSetDevice(prev);
+  if (rc == GC_OK) std::memcpy(constants, &b, sizeof b);
+  return rc;
+}
+
+GC_API int gc_price(const void *constants, uint64_t size, const char *bucket_id, double *step_us) {
+  if (!constants || !bucket_id || !step_us || size != sizeof(PriceBlob)) return GC_E_ARG;
+  PriceBlob b;
+  std::memcpy(&b, constants, sizeof b);
+  if (b.magic != PriceBlob{}.magic || b.version != 1 || !(b.hbm_gbs > 0)) return GC_E_ARG;
+  *step_us = kRefWeightBytes / (b.hbm_gbs * 1e9 * kRefStreamEff) * 1e6 + kRefLaunches * b.launch_us;
+  return GC_OK;
+}
+
+}  // extern "C"

@@ -25,7 +25,7 @@ P_ = C.POINTER
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libgck.so")
 # every symbol include/gc.h declares
 SYMBOLS = ("gc_abi_version", "gc_open", "gc_layout_get", "gc_step", "gc_commit", "gc_copy_blocks", "gc_state_save",
-           "gc_state_restore", "gc_release", "gc_last_error", "gc_close")
+           "gc_state_restore", "gc_release", "gc_last_error", "gc_close", "gc_probe", "gc_price")
 
 
 class GcError(RuntimeError):

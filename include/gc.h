@@ -186,6 +186,13 @@ GC_API const char *gc_last_error(gc_handle *h);
 /* abi/gc.h:229-230: frees everything; NULL is accepted. */
 GC_API void gc_close(gc_handle *h);
 
+/* Pricing (optional in the ABI, abi/gc.h:232-237, bound by goethe_engine/pack.py lib_price:928-961). gc_probe measures a
+ * device's cost constants once into an opaque blob (it times bounded probe kernels; no handle, KV or weights are
+ * touched); a too-small cap gives GC_E_CAPACITY with *size set. gc_price is host math only: the predicted step time of
+ * a bucket on the device the blob describes. */
+GC_API int gc_probe(int device, void *constants, uint64_t cap, uint64_t *size);
+GC_API int gc_price(const void *constants, uint64_t size, const char *bucket_id, double *step_us);
+
 #ifdef __cplusplus
 }
 #endif

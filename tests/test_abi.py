@@ -80,6 +80,37 @@ def test_open_rejects_bad_tensor_parallel_degree(lib, tiny, tmp_path):
     assert rc == gck.E_MANIFEST and "tensor-parallel" in msg and not h.value
 
 
+def _blob(hbm_gbs, launch_us, sms=148, clock=1965):
+    import struct
+    return struct.pack("<IIddII", 0x45435250, 1, hbm_gbs, launch_us, sms, clock)
+
+
+def test_price_is_host_math_over_the_probe_constants(lib):
+    """gc_price (abi/gc.h:232-237): the reference step's weight stream at the probed bandwidth plus its launches;
+    a faster device prices lower; a blob of the wrong size or kind is an argument error."""
+    lib.gc_price.restype = C.c_int
+    lib.gc_price.argtypes = [C.c_void_p, C.c_uint64, C.c_char_p, C.POINTER(C.c_double)]
+    us = C.c_double()
+    b = _blob(6000.0, 2.0)
+    assert lib.gc_price(b, len(b), b"b200.BI.main", C.byref(us)) == gck.OK
+    assert abs(us.value - (4.221e9 / (6000e9 * 0.85) * 1e6 + 292 * 2.0)) < 1e-6
+    fast = C.c_double()
+    b2 = _blob(8000.0, 1.5)
+    assert lib.gc_price(b2, len(b2), b"b200.BI.main", C.byref(fast)) == gck.OK and fast.value < us.value
+    assert lib.gc_price(b, len(b) - 1, b"b200.BI.main", C.byref(us)) == gck.E_ARG
+    assert lib.gc_price(b"x" * len(b), len(b), b"b200.BI.main", C.byref(us)) == gck.E_ARG
+
+
+def test_probe_reports_its_size_first(lib):
+    lib.gc_probe.restype = C.c_int
+    lib.gc_probe.argtypes = [C.c_int, C.c_void_p, C.c_uint64, C.POINTER(C.c_uint64)]
+    n = C.c_uint64()
+    assert lib.gc_probe(0, None, 0, C.byref(n)) == gck.E_CAPACITY and n.value == 32
+    if not __import__("torch").cuda.is_available():
+        buf = C.create_string_buffer(n.value)
+        assert lib.gc_probe(0, buf, n.value, C.byref(n)) == gck.E_DEVICE
+
+
 def test_null_handles(lib):
     assert lib.gc_layout_get(None, None) == gck.E_ARG
     assert lib.gc_step(None, None, None) == gck.E_ARG

@@ -187,3 +187,21 @@ def test_greedy_decode_matches_the_oracle(tmp_path):
                 break           # a near tie may diverge; the rest is not comparable
             toks.append(t)
             lg = o.step([dict(sid=0, tokens=[t], pos=len(toks) - 1, blocks=[0, 1, 2, 3], want=1)])
+
+
+def test_probe_measures_the_device():
+    """gc_probe on the B200: copy bandwidth and launch interval in a plausible range, and gc_price over them."""
+    import ctypes as C
+    L = gck.load()
+    L.gc_probe.restype = L.gc_price.restype = C.c_int
+    L.gc_probe.argtypes = [C.c_int, C.c_void_p, C.c_uint64, C.POINTER(C.c_uint64)]
+    L.gc_price.argtypes = [C.c_void_p, C.c_uint64, C.c_char_p, C.POINTER(C.c_double)]
+    n = C.c_uint64()
+    assert L.gc_probe(0, None, 0, C.byref(n)) == gck.E_CAPACITY
+    buf = C.create_string_buffer(n.value)
+    assert L.gc_probe(0, buf, n.value, C.byref(n)) == gck.OK
+    import struct
+    magic, ver, hbm, launch, sms, clock = struct.unpack("<IIddII", buf.raw[:n.value])
+    assert 2000 < hbm < 10000 and 0 < launch < 50 and sms == 148
+    us = C.c_double()
+    assert L.gc_price(buf, n.value, b"b200.BI.main", C.byref(us)) == gck.OK and 300 < us.value < 5000
