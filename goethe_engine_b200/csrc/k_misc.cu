@@ -4,6 +4,8 @@
 //
 // Reference math (goethe_engine/ref.py): rms ref.py:14-15, RoPE ref.py:31-37 (interleaved pairs), KV write ref.py:54,
 // SwiGLU ref.py:59, commit ref.py:114-120, copy_blocks ref.py:122-126.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -51,14 +53,92 @@ void launch_embed(const PlanView &pv, const uint8_t *emb, int type, size_t row_b
 // order, from 0), written back, as that GEMM's residual-add epilogue would have.
 // One CTA per row; float4 loads, all issued before the first use. The sum of squares has a fixed order (each thread's
 // strided partials in index order, then a fixed shuffle tree, then the warps in index order), independent of the batch.
+// ---- tensor-parallel peer-memory reduction (declared in kernels.h)
+constexpr int kErrTpWait = 16;                    // error word: a peer's flag did not arrive within the limit
+constexpr unsigned long long kTpTimeoutNs = 2000000000ull;
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;\n" : "=l"(t));
+  return t;
+}
+// thread 0: until flag[k][b] >= need for ranks k in [k0, k1) (bounded: sets the error word and returns false)
+__device__ bool tp_wait_flags(const TpPeers &p, int k0, int k1, int b, unsigned long long need) {
+  const unsigned long long t0 = global_ns();
+  for (int k = k0; k < k1; k++)
+    while (ld_acquire_sys(p.flag[k] + b) < need) {
+      if (global_ns() - t0 > kTpTimeoutNs) {
+        atomicCAS(p.err, 0, kErrTpWait);
+        return false;
+      }
+      __nanosleep(64);
+    }
+  return true;
+}
+
+__global__ void tp_signal_kernel(unsigned long long *flag, unsigned long long value) {
+  // the stream's earlier kernels have completed: make their writes visible system-wide, then publish
+  __threadfence_system();
+  asm volatile("st.release.sys.global.u64 [%0], %1;\n" ::"l"(flag), "l"(value) : "memory");
+}
+
+// rows [r0, r1) of this rank: the sum over ranks 0 .. n-1 (in that order) of their partials, into this rank's buffer
+__global__ void tp_reduce_scatter_kernel(TpPeers p, int b, unsigned long long epoch, int T, int d) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = tp_wait_flags(p, 0, p.n, b, epoch * 4 + 1);
+  __syncthreads();
+  if (!ok) return;
+  int r0, r1;
+  tp_rows(T, p.n, p.rank, r0, r1);
+  const int nv = d / 4;
+  const size_t total = static_cast<size_t>(r1 - r0) * nv;
+  float4 *dst = reinterpret_cast<float4 *>(p.buf[p.rank][b]);
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t e = static_cast<size_t>(r0) * nv + i;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < p.n; k++) {
+      const float4 x = __ldcv(reinterpret_cast<const float4 *>(p.buf[k][b]) + e);
+      a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
+    }
+    dst[e] = a;
+  }
+}
+
+void launch_tp_signal(unsigned long long *flag, unsigned long long value, cudaStream_t s) {
+  tp_signal_kernel<<<1, 1, 0, s>>>(flag, value);
+}
+void launch_tp_reduce_scatter(const TpPeers &p, int b, unsigned long long epoch, int T, int d, cudaStream_t s) {
+  int r0, r1;
+  tp_rows(T, p.n, p.rank, r0, r1);
+  const size_t total = static_cast<size_t>(std::max(0, r1 - r0)) * (d / 4);
+  int blocks = static_cast<int>(std::min<size_t>((total + 255) / 256, 148 * 8));
+  tp_reduce_scatter_kernel<<<std::max(blocks, 1), 256, 0, s>>>(p, b, epoch, T, d);
+}
+
 constexpr int kNormThreads = 512;
 constexpr int kNormMaxVec = 4;    // float4 loads per thread: d <= 512 * 4 * 4 = 8192
 
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float *x, const int *rows, const float *gain, float eps,
                                                                int d, int ld, __half *out, const float *part, int S,
-                                                               int pld, int T) {
+                                                               int pld, int T, TpPeers tp, int tpb,
+                                                               unsigned long long tp_epoch) {
   int r = blockIdx.x;
   int src = rows ? rows[r] : r;
+  const float *tpsum = nullptr;   // tensor parallelism: this row's all-reduced sum, at its owner rank
+  if (tp.n > 1) {
+    const int per = (T + tp.n - 1) / tp.n, owner = src / per;
+    __shared__ int ok;
+    if (threadIdx.x == 0) ok = tp_wait_flags(tp, owner, owner + 1, tpb, tp_epoch * 4 + 2);
+    __syncthreads();
+    if (!ok) return;
+    tpsum = tp.buf[owner][tpb] + static_cast<size_t>(src) * d;
+  }
   float4 *xr = reinterpret_cast<float4 *>(x + static_cast<size_t>(src) * d);
   const float4 *gr = reinterpret_cast<const float4 *>(gain);
   const int nv = d / 4;
@@ -67,6 +147,16 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float *x, const i
   for (int i = 0; i < kNormMaxVec; i++) {
     int e = threadIdx.x + i * kNormThreads;
     v[i] = e < nv ? xr[e] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  if (tpsum) {
+#pragma unroll
+    for (int i = 0; i < kNormMaxVec; i++) {
+      int e = threadIdx.x + i * kNormThreads;
+      if (e >= nv) continue;
+      const float4 a = __ldcv(reinterpret_cast<const float4 *>(tpsum) + e);
+      v[i].x += a.x; v[i].y += a.y; v[i].z += a.z; v[i].w += a.w;
+      xr[e] = v[i];
+    }
   }
   if (part) {
     // per element: ((0 + p_0) + p_1) + ... in split order, then added to x; the four vectors' loads are independent
@@ -128,8 +218,13 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float *x, const i
 }
 
 void launch_rmsnorm(float *x, const int *rows, int n, const float *gain, float eps, int d, int ld, __half *out,
-                    const float *part, int S, int pld, int T, cudaStream_t s) {
-  if (n > 0) rmsnorm_kernel<<<n, kNormThreads, 0, s>>>(x, rows, gain, eps, d, ld, out, part, S, pld, T);
+                    const float *part, int S, int pld, int T, const TpPeers *tp, int tp_buf,
+                    unsigned long long tp_epoch, cudaStream_t s) {
+  TpPeers none{};
+  none.n = 1;
+  if (n > 0)
+    rmsnorm_kernel<<<n, kNormThreads, 0, s>>>(x, rows, gain, eps, d, ld, out, part, S, pld, T, tp ? *tp : none, tp_buf,
+                                              tp_epoch);
 }
 
 // ----------------------------------------------------------------------------------------------------------------

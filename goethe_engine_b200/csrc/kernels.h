@@ -47,10 +47,32 @@ struct QWeight {            // a relaid-out weight on the device
   int splits = 1;           // split-K factor (fixed per weight: batch invariant)
 };
 
+// Tensor parallelism: a deterministic all-reduce of the ranks' [T, d] f32 partials over peer memory (NVLink), in two
+// phases on a pair of buffers (one per alternate reduction). Every rank sums the rows it owns from all ranks in rank order
+// (reduce-scatter, into its own buffer), then every reader takes each row's sum from its owner; the order of the f32 adds
+// never depends on T. Flags are 64-bit epoch * 4 + phase, written by the owner, polled by the peers (bounded waits).
+constexpr int kMaxTp = 8;
+struct TpPeers {
+  int n, rank;
+  float *buf[kMaxTp][2];        // every rank's two partial buffers (peer pointers; this rank's own at [rank])
+  unsigned long long *flag[kMaxTp];   // every rank's flags [2] (one per buffer)
+  int *err;                     // this rank's error word (a wait that ran out)
+};
+// rows [r0, r1) of T owned by rank k
+__host__ __device__ inline void tp_rows(int T, int n, int k, int &r0, int &r1) {
+  const int per = (T + n - 1) / n;
+  r0 = min(T, k * per);
+  r1 = min(T, r0 + per);
+}
+void launch_tp_signal(unsigned long long *flag, unsigned long long value, cudaStream_t s);
+void launch_tp_reduce_scatter(const TpPeers &p, int b, unsigned long long epoch, int T, int d, cudaStream_t s);
+
 void launch_embed(const PlanView &pv, const uint8_t *emb, int type, size_t row_bytes, int d, float *x, cudaStream_t s);
-// part (nullable): S split-K partials [S, T, pld] of a residual-add GEMM, added into x before the norm
+// part (nullable): S split-K partials [S, T, pld] of a residual-add GEMM, added into x before the norm.
+// tp (nullable): instead, the tensor-parallel sum of buffer tp_buf for this epoch, gathered from the rows' owners.
 void launch_rmsnorm(float *x, const int *rows, int n, const float *gain, float eps, int d, int ld, __half *out,
-                    const float *part, int S, int pld, int T, cudaStream_t s);
+                    const float *part, int S, int pld, int T, const TpPeers *tp, int tp_buf,
+                    unsigned long long tp_epoch, cudaStream_t s);
 // qkv: [T, ld] rows (S == 1) or [S, T, ld] split-K partials
 void launch_rope_kv(const PlanView &pv, const float *qkv, int S, int ld, int H, int KVH, int dh,
                     const float2 *rope_tab, __half *q, void *kc, void *vc, int8_t *exps, int kv_fp8, int page_scale,
@@ -84,6 +106,7 @@ size_t tc_tile_bytes(int type);
 void gemm_tc_init();      // once per device
 void launch_gemm_tc(const QWeight &w, const TmaSet &ts, int T, const Epi &epi, float *part, int *err, int sms,
                     cudaStream_t s);
+
 
 // Paged attention over the plan's work list: q [T, H, dh] f16 -> out [T, H, dh] f16. part_o / part_ml: split partials,
 // merged by the last split to finish.

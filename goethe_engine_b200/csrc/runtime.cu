@@ -79,7 +79,12 @@ struct gc_handle {
   int tp = 1, rank = 0;
   std::vector<gc_handle *> ranks;
   void *comm = nullptr;              // ncclComm_t of a rank handle
-  float *tp_y = nullptr;             // rank: o_proj / down_proj output, all-reduced [T, d]
+  float *tp_y = nullptr;             // rank: o_proj / down_proj output, all-reduced [T, d] (NCCL path)
+  float *tp_bufs[2] = {nullptr, nullptr};   // rank: partial / summed rows of alternate reductions (peer-memory path)
+  unsigned long long *tp_flags = nullptr;   // rank: the two buffers' flags (epoch * 4 + phase), read by the peers
+  unsigned long long tp_epoch = 0;          // reductions so far (the same on every rank)
+  bool tp_p2p = false;                      // all ranks reach each other's memory: the peer-memory reduction
+  TpPeers peers{};
   int *tp_pick = nullptr;            // rank: argmax candidates (value bits, index) of every rank [tp][T][2]
   int vocab0 = 0, vocab_rows = 0;    // head rows held here: [vocab0, vocab0 + vocab_rows)
   cudaStream_t st = nullptr;
@@ -571,6 +576,10 @@ void open_device(gc_handle *h, int dev, const std::vector<std::unique_ptr<GgufFi
   h->arg_scratch = static_cast<int *>(h->dalloc(static_cast<size_t>(T) * 8 * 2 * 4, "argmax parts"));
   if (h->tp > 1) {
     h->tp_y = static_cast<float *>(h->dalloc(static_cast<size_t>(T) * d * 4, "tensor-parallel partial sums"));
+    for (int b = 0; b < 2; b++)
+      h->tp_bufs[b] = static_cast<float *>(h->dalloc(static_cast<size_t>(T) * d * 4, "tensor-parallel partials"));
+    h->tp_flags = static_cast<unsigned long long *>(h->dalloc(2 * sizeof(unsigned long long), "tensor-parallel flags"));
+    ck(cudaMemset(h->tp_flags, 0, 2 * sizeof(unsigned long long)), "tensor-parallel flags");
     h->tp_pick = static_cast<int *>(h->dalloc(static_cast<size_t>(h->tp + 1) * T * 2 * 4, "tensor-parallel argmax"));
   }
   ck(cudaMallocHost(&h->tok_host, static_cast<size_t>(T) * 4), "pinned tokens");
@@ -643,6 +652,35 @@ void init_tp(gc_handle *g) {
   for (int r = 0; r < g->tp; r++) devs[r] = g->ranks[r]->dev;
   nck(n.init_all(comms.data(), g->tp, devs.data()), "ncclCommInitAll");
   for (int r = 0; r < g->tp; r++) g->ranks[r]->comm = comms[r];
+  if (g->tp > kMaxTp) fail(GC_E_UNSUPPORTED, "tensor parallelism above %d", kMaxTp);
+  // peer access between every pair: the all-reduce reads the other ranks' buffers over NVLink (plain loads, no multicast)
+  bool p2p = true;
+  for (int i = 0; i < g->tp && p2p; i++)
+    for (int j = 0; j < g->tp && p2p; j++) {
+      if (i == j) continue;
+      int can = 0;
+      ck(cudaDeviceCanAccessPeer(&can, devs[i], devs[j]), "cudaDeviceCanAccessPeer");
+      if (!can) {
+        p2p = false;
+        break;
+      }
+      ck(cudaSetDevice(devs[i]), "cudaSetDevice");
+      cudaError_t e = cudaDeviceEnablePeerAccess(devs[j], 0);
+      if (e == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+      else ck(e, "cudaDeviceEnablePeerAccess");
+    }
+  for (int r = 0; r < g->tp; r++) {
+    gc_handle *h = g->ranks[r];
+    h->tp_p2p = p2p;
+    h->peers.n = g->tp;
+    h->peers.rank = r;
+    h->peers.err = h->kerr;
+    for (int k = 0; k < g->tp; k++) {
+      h->peers.buf[k][0] = g->ranks[k]->tp_bufs[0];
+      h->peers.buf[k][1] = g->ranks[k]->tp_bufs[1];
+      h->peers.flag[k] = g->ranks[k]->tp_flags;
+    }
+  }
 }
 
 }  // namespace
@@ -1034,14 +1072,37 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
   // parallelism) its all-reduced output
   const float *pend = nullptr;
   int pend_s = 0, pend_ld = 0;
+  bool pend_tp = false;              // the peer-memory reduction of buffer pend_b, epoch pend_ep
+  int pend_b = 0;
+  unsigned long long pend_ep = 0;
   auto norm = [&](const int *rows, int n, const float *gain) {
     const float *pp = pend;
     const int ps = pend_s, pl = pend_ld;
-    run(GCK_K_NORM, 1, [&] { launch_rmsnorm(h->x, rows, n, gain, h->eps, h->d, h->d, h->h, pp, ps, pl, T, s); });
+    const TpPeers *tp = pend_tp ? &h->peers : nullptr;
+    run(GCK_K_NORM, 1, [&] {
+      launch_rmsnorm(h->x, rows, n, gain, h->eps, h->d, h->d, h->h, pp, ps, pl, T, tp, pend_b, pend_ep, s);
+    });
     pend = nullptr;
     pend_s = 0;
+    pend_tp = false;
   };
   auto residual = [&](int cls, const QWeight &w, const TmaSet &ts, const __half *act) {
+    if (h->tp > 1 && h->tp_p2p) {
+      // this rank's share of the projection into buffer b; then the ranks' deterministic sum over peer memory: flag,
+      // reduce-scatter of the rows this rank owns, flag; the next RMSNorm gathers each row's sum from its owner
+      const unsigned long long ep = ++h->tp_epoch;
+      const int b = static_cast<int>(ep & 1);
+      gemm(cls, w, ts, act, T, Epi{kEpiStore, h->d, h->d, h->tp_bufs[b], nullptr}, false);
+      run(GCK_K_ALLREDUCE, 3, [&] {
+        launch_tp_signal(h->tp_flags + b, ep * 4 + 1, s);
+        launch_tp_reduce_scatter(h->peers, b, ep, T, h->d, s);
+        launch_tp_signal(h->tp_flags + b, ep * 4 + 2, s);
+      });
+      pend_tp = true;
+      pend_b = b;
+      pend_ep = ep;
+      return;
+    }
     if (h->tp > 1) {
       // this rank's share of the projection (its input columns), summed over the ranks in place
       gemm(cls, w, ts, act, T, Epi{kEpiStore, h->d, h->d, h->tp_y, nullptr}, false);
