@@ -410,7 +410,7 @@ def run_c5(args):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    L.gck_stats_enable(be.h, 1 << 4)
+    L.gck_stats_enable(be.h, 0xFFFF if args.profile else 1 << 4)
     with Clocks(0) as clk:
         t0 = time.perf_counter()
         for _ in range(args.steps):
@@ -420,6 +420,14 @@ def run_c5(args):
     L.gck_stats_read(be.h, C.byref(st))
     dev_s = st.forward_ms / 1e3
     value, e2e = B70 * args.steps / dev_s, B70 * args.steps / wall
+    if args.profile:
+        names = ["embed", "rmsnorm", "gemm_qkv", "rope_kv", "attention", "attn_combine", "gemm_o", "gemm_gateup",
+                 "gemm_down", "gemm_head", "argmax", "splitk_reduce", "allreduce"]
+        tot = sum(st.class_ms[i] for i in range(len(names)))
+        print("[bench] rank 0 per-class device time (events around each launch):\n" + "\n".join(
+            f"{n:14s} {st.class_ms[i] / args.steps:8.3f} ms/step  {st.class_launches[i] // max(1, args.steps):5d} launches/step"
+            for i, n in enumerate(names)) + f"\n  sum {tot / args.steps:.3f} ms/step, step {st.forward_ms / args.steps:.3f} ms",
+            file=sys.stderr, flush=True)
     ms_step = dev_s / args.steps * 1e3
     wbytes = weight_bytes(SPEC70B)
     kv = (CTX70 + args.warmup + args.steps / 2) * B70 * 2 * 8 * 128 * SPEC70B["layers"]

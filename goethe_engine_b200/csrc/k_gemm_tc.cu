@@ -268,7 +268,7 @@ GCK_DEV Unit unit_of(int w, int NTW, int KT, int splits) {
 template <int TYPE, int NT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const uint8_t *__restrict__ W, int NTW, int KT, int splits, int units,
-                   const __grid_constant__ CUtensorMap tmap, int T, Epi epi, float *part, int Npad, int *err) {
+                   const __grid_constant__ CUtensorMap tmap, int T, Epi epi, float *part, int Npad, int *err, Signal sig) {
   using F = TileFmt<TYPE>;
   using S = Shape<TYPE, NT>;
   constexpr int RS = S::RAW, SR = S::R, ACC = S::ACC, KS = S::KS, SPT = S::SPT;
@@ -521,8 +521,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!good) break;
     }
   }
+  // with a signal: every thread's stores are made visible system-wide; the last CTA to get here publishes the flag
+  if (sig.flag) __threadfence_system();
   tc_fence_before();
   __syncthreads();
+  if (sig.flag && threadIdx.x == 0) signal_if_last(sig);
   if (warp == 1) {
     // no MMA may still write the accumulators when they are freed (bounded; returns at once after a normal run)
     if (lane == 0) mbar_wait(mma_done, 0, err, kErrAcc);
@@ -534,24 +537,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <int TYPE, int NT>
 void launch_nt(const QWeight &w, const CUtensorMap *map, int T, const Epi &epi, float *part, int *err, int sms,
-               cudaStream_t s) {
+               const Signal &sig, cudaStream_t s) {
   const int units = w.NT * w.splits * ((T + NT - 1) / NT);
   const int grid = units < sms ? units : sms;
   gemm_tc_kernel<TYPE, NT><<<grid, kThreads, smem_total<TYPE, NT>(), s>>>(w.data, w.NT, w.KT, w.splits, units, *map, T,
-                                                                          epi, part, w.NT * kBM, err);
+                                                                          epi, part, w.NT * kBM, err, sig);
 }
 
 template <int TYPE>
 void launch_type(const QWeight &w, const TmaSet &ts, int T, const Epi &epi, float *part, int *err, int sms,
-                 cudaStream_t s) {
+                 const Signal &sig, cudaStream_t s) {
   int nt = tc_token_tile(T);
   const CUtensorMap *m = ts.map(nt);
   switch (nt) {
-    case 16: launch_nt<TYPE, 16>(w, m, T, epi, part, err, sms, s); break;
-    case 32: launch_nt<TYPE, 32>(w, m, T, epi, part, err, sms, s); break;
-    case 64: launch_nt<TYPE, 64>(w, m, T, epi, part, err, sms, s); break;
-    case 128: launch_nt<TYPE, 128>(w, m, T, epi, part, err, sms, s); break;
-    default: launch_nt<TYPE, 256>(w, m, T, epi, part, err, sms, s); break;
+    case 16: launch_nt<TYPE, 16>(w, m, T, epi, part, err, sms, sig, s); break;
+    case 32: launch_nt<TYPE, 32>(w, m, T, epi, part, err, sms, sig, s); break;
+    case 64: launch_nt<TYPE, 64>(w, m, T, epi, part, err, sms, sig, s); break;
+    case 128: launch_nt<TYPE, 128>(w, m, T, epi, part, err, sms, sig, s); break;
+    default: launch_nt<TYPE, 256>(w, m, T, epi, part, err, sms, sig, s); break;
   }
 }
 
@@ -578,10 +581,10 @@ void gemm_tc_init() {
 size_t tc_tile_bytes(int type) { return type == kQ4_K ? TileFmt<kQ4_K>::BYTES : TileFmt<kQ8_0>::BYTES; }
 
 void launch_gemm_tc(const QWeight &w, const TmaSet &ts, int T, const Epi &epi, float *part, int *err, int sms,
-                    cudaStream_t s) {
+                    cudaStream_t s, const Signal &sig) {
   if (T <= 0) return;
-  if (w.type == kQ4_K) launch_type<kQ4_K>(w, ts, T, epi, part, err, sms, s);
-  else launch_type<kQ8_0>(w, ts, T, epi, part, err, sms, s);
+  if (w.type == kQ4_K) launch_type<kQ4_K>(w, ts, T, epi, part, err, sms, sig, s);
+  else launch_type<kQ8_0>(w, ts, T, epi, part, err, sms, sig, s);
 }
 
 }  // namespace gck

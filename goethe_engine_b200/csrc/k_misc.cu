@@ -88,11 +88,11 @@ __global__ void tp_signal_kernel(unsigned long long *flag, unsigned long long va
 }
 
 // rows [r0, r1) of this rank: the sum over ranks 0 .. n-1 (in that order) of their partials, into this rank's buffer
-__global__ void tp_reduce_scatter_kernel(TpPeers p, int b, unsigned long long epoch, int T, int d) {
+__global__ void tp_reduce_scatter_kernel(TpPeers p, int b, unsigned long long epoch, int T, int d, int S, Signal sig) {
   __shared__ int ok;
   if (threadIdx.x == 0) ok = tp_wait_flags(p, 0, p.n, b, epoch * 4 + 1);
   __syncthreads();
-  if (!ok) return;
+  if (!ok) return;   // the flag is not published: the readers' waits run out too and the step reports the error
   int r0, r1;
   tp_rows(T, p.n, p.rank, r0, r1);
   const int nv = d / 4;
@@ -102,23 +102,31 @@ __global__ void tp_reduce_scatter_kernel(TpPeers p, int b, unsigned long long ep
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
     const size_t e = static_cast<size_t>(r0) * nv + i;
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int k = 0; k < p.n; k++) {
-      const float4 x = __ldcv(reinterpret_cast<const float4 *>(p.buf[k][b]) + e);
-      a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
-    }
-    dst[e] = a;
+    const size_t slice = static_cast<size_t>(T) * nv;   // float4s of one split-K slice
+    for (int k = 0; k < p.n; k++)
+      for (int sp = 0; sp < S; sp++) {
+        const float4 x = __ldcv(reinterpret_cast<const float4 *>(p.buf[k][b]) + sp * slice + e);
+        a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
+      }
+    dst[e] = a;   // into slice 0 of this rank's rows: no other rank reads them in this phase
+  }
+  if (sig.flag) {
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) signal_if_last(sig);
   }
 }
 
 void launch_tp_signal(unsigned long long *flag, unsigned long long value, cudaStream_t s) {
   tp_signal_kernel<<<1, 1, 0, s>>>(flag, value);
 }
-void launch_tp_reduce_scatter(const TpPeers &p, int b, unsigned long long epoch, int T, int d, cudaStream_t s) {
+void launch_tp_reduce_scatter(const TpPeers &p, int b, unsigned long long epoch, int T, int d, int S, const Signal &sig,
+                              cudaStream_t s) {
   int r0, r1;
   tp_rows(T, p.n, p.rank, r0, r1);
   const size_t total = static_cast<size_t>(std::max(0, r1 - r0)) * (d / 4);
   int blocks = static_cast<int>(std::min<size_t>((total + 255) / 256, 148 * 8));
-  tp_reduce_scatter_kernel<<<std::max(blocks, 1), 256, 0, s>>>(p, b, epoch, T, d);
+  tp_reduce_scatter_kernel<<<std::max(blocks, 1), 256, 0, s>>>(p, b, epoch, T, d, S, sig);
 }
 
 constexpr int kNormThreads = 512;

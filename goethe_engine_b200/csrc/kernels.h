@@ -64,8 +64,29 @@ __host__ __device__ inline void tp_rows(int T, int n, int k, int &r0, int &r1) {
   r0 = min(T, k * per);
   r1 = min(T, r0 + per);
 }
+// A kernel's completion published to other GPUs: the last CTA to finish (counter, reset by it) fences system-wide and
+// stores value to flag with release semantics. flag null: no signal.
+struct Signal {
+  unsigned long long *flag = nullptr;
+  unsigned long long value = 0;
+  unsigned *counter = nullptr;   // zero between launches
+};
+#ifdef __CUDACC__
+// thread 0 of a CTA, after the CTA's threads fenced their stores system-wide and synchronized
+__device__ __forceinline__ void signal_if_last(const Signal &sg) {
+  const unsigned total = gridDim.x * gridDim.y * gridDim.z;
+  if (atomicAdd(sg.counter, 1u) == total - 1) {
+    __threadfence_system();
+    *sg.counter = 0;
+    asm volatile("st.release.sys.global.u64 [%0], %1;\n" ::"l"(sg.flag), "l"(sg.value) : "memory");
+  }
+}
+#endif
 void launch_tp_signal(unsigned long long *flag, unsigned long long value, cudaStream_t s);
-void launch_tp_reduce_scatter(const TpPeers &p, int b, unsigned long long epoch, int T, int d, cudaStream_t s);
+// sig: published when every row of this rank is summed (phase 2)
+// S: split-K slices per rank ([S][T][d] in each buffer); sums over ranks, then slices, in order
+void launch_tp_reduce_scatter(const TpPeers &p, int b, unsigned long long epoch, int T, int d, int S, const Signal &sig,
+                              cudaStream_t s);
 
 void launch_embed(const PlanView &pv, const uint8_t *emb, int type, size_t row_bytes, int d, float *x, cudaStream_t s);
 // part (nullable): S split-K partials [S, T, pld] of a residual-add GEMM, added into x before the norm.
@@ -104,8 +125,9 @@ struct TmaSet {            // tensor maps over one activation buffer [rows, K] f
 int tc_token_tile(int T);
 size_t tc_tile_bytes(int type);
 void gemm_tc_init();      // once per device
+// sig (optional): the GEMM's completion published to other GPUs (tensor parallelism, phase 1 of the all-reduce)
 void launch_gemm_tc(const QWeight &w, const TmaSet &ts, int T, const Epi &epi, float *part, int *err, int sms,
-                    cudaStream_t s);
+                    cudaStream_t s, const Signal &sig = Signal{});
 
 
 // Paged attention over the plan's work list: q [T, H, dh] f16 -> out [T, H, dh] f16. part_o / part_ml: split partials,

@@ -84,6 +84,8 @@ struct gc_handle {
   unsigned long long *tp_flags = nullptr;   // rank: the two buffers' flags (epoch * 4 + phase), read by the peers
   unsigned long long tp_epoch = 0;          // reductions so far (the same on every rank)
   bool tp_p2p = false;                      // all ranks reach each other's memory: the peer-memory reduction
+  unsigned *sig_counter = nullptr;          // rank: finished CTAs of a signalling kernel (zero between launches)
+  int tp_splits = 1;                        // rank: most split-K slices of o_proj / down_proj (buffer depth)
   TpPeers peers{};
   int *tp_pick = nullptr;            // rank: argmax candidates (value bits, index) of every rank [tp][T][2]
   int vocab0 = 0, vocab_rows = 0;    // head rows held here: [vocab0, vocab0 + vocab_rows)
@@ -420,6 +422,10 @@ void load_model(gc_handle *h, const std::vector<std::unique_ptr<GgufFile>> &file
   h->vocab_rows = std::max(0, std::min(h->vocab, h->vocab0 + Vr) - h->vocab0);
   h->head = relayout(h, static_cast<int>(th.type), h->vocab_rows, h->d,
                      [&](int n, const GgufTensor *&t, int &r) { t = &th; r = h->vocab0 + n; }, "output");
+  // tensor parallelism: o_proj and down_proj in one K slice each. Their split-K partials would cross NVLink in the
+  // all-reduce (splits times the bytes), and a rank's slice of K is already N times shorter.
+  if (N > 1)
+    for (auto &ly : h->layers) ly.o.splits = ly.dn.splits = 1;
   // from here on the handle's head counts and FFN width are its own slices
   h->H /= N;
   h->KVH /= N;
@@ -576,10 +582,15 @@ void open_device(gc_handle *h, int dev, const std::vector<std::unique_ptr<GgufFi
   h->arg_scratch = static_cast<int *>(h->dalloc(static_cast<size_t>(T) * 8 * 2 * 4, "argmax parts"));
   if (h->tp > 1) {
     h->tp_y = static_cast<float *>(h->dalloc(static_cast<size_t>(T) * d * 4, "tensor-parallel partial sums"));
+    // o_proj / down_proj split-K partials of this rank go straight into the buffer: [splits][T][d]
+    for (auto &ly : h->layers) h->tp_splits = std::max({h->tp_splits, ly.o.splits, ly.dn.splits});
     for (int b = 0; b < 2; b++)
-      h->tp_bufs[b] = static_cast<float *>(h->dalloc(static_cast<size_t>(T) * d * 4, "tensor-parallel partials"));
+      h->tp_bufs[b] = static_cast<float *>(
+          h->dalloc(static_cast<size_t>(h->tp_splits) * T * d * 4, "tensor-parallel partials"));
     h->tp_flags = static_cast<unsigned long long *>(h->dalloc(2 * sizeof(unsigned long long), "tensor-parallel flags"));
     ck(cudaMemset(h->tp_flags, 0, 2 * sizeof(unsigned long long)), "tensor-parallel flags");
+    h->sig_counter = static_cast<unsigned *>(h->dalloc(16, "signal counter"));
+    ck(cudaMemset(h->sig_counter, 0, 16), "signal counter");
     h->tp_pick = static_cast<int *>(h->dalloc(static_cast<size_t>(h->tp + 1) * T * 2 * 4, "tensor-parallel argmax"));
   }
   ck(cudaMallocHost(&h->tok_host, static_cast<size_t>(T) * 4), "pinned tokens");
@@ -1092,12 +1103,17 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
       // reduce-scatter of the rows this rank owns, flag; the next RMSNorm gathers each row's sum from its owner
       const unsigned long long ep = ++h->tp_epoch;
       const int b = static_cast<int>(ep & 1);
-      gemm(cls, w, ts, act, T, Epi{kEpiStore, h->d, h->d, h->tp_bufs[b], nullptr}, false);
-      run(GCK_K_ALLREDUCE, 3, [&] {
-        launch_tp_signal(h->tp_flags + b, ep * 4 + 1, s);
-        launch_tp_reduce_scatter(h->peers, b, ep, T, h->d, s);
-        launch_tp_signal(h->tp_flags + b, ep * 4 + 2, s);
-      });
+      const Epi e{kEpiStore, h->d, h->d, h->tp_bufs[b], nullptr};
+      Signal s1{h->tp_flags + b, ep * 4 + 1, h->sig_counter}, s2{h->tp_flags + b, ep * 4 + 2, h->sig_counter};
+      if (w.type != kF16) {
+        // the rank's split-K partials [splits][T][d] (or its output) straight into buffer b; publishes phase 1
+        run(cls, 1, [&] { launch_gemm_tc(w, ts, T, e, h->tp_bufs[b], h->kerr, h->sms, s, s1); });
+      } else {
+        gemm(cls, w, ts, act, T, e, false);
+        run(GCK_K_ALLREDUCE, 1, [&] { launch_tp_signal(s1.flag, s1.value, s); });
+      }
+      const int sp = w.type != kF16 ? w.splits : 1;
+      run(GCK_K_ALLREDUCE, 1, [&] { launch_tp_reduce_scatter(h->peers, b, ep, T, h->d, sp, s2, s); });   // phase 2
       pend_tp = true;
       pend_b = b;
       pend_ep = ep;
