@@ -242,28 +242,34 @@ __global__ void __launch_bounds__(32 * NW, NW == 1 && NT == 1 ? 20 : 1) attn_ker
       for (int nt = 0; nt < NT; nt++)
 #pragma unroll
         for (int c = 0; c < 4; c++) sc[nt][c] += sc2[nt][c];
-      // ---- page scales of entries g and g + 8: 2^-ek on the scores, 2^(evref - ev) on the probabilities
-      float ks0 = a.scale_log2, ks1 = a.scale_log2, pv0 = 1.f, pv1 = 1.f;
-      int evref = 0;
+      // ---- page scales of entries g and g + 8: 2^-ek on the scores, 2^(E - ev) on the probabilities. O stays in one
+      // exponent frame E (O is kept scaled by 2^E); E moves (and O is rescaled) only when a page's V exponent is more
+      // than kRebase away, so the f16 probabilities times 2^(E - ev) neither overflow nor lose their bits
+      float ks0 = a.scale_log2, ks1 = a.scale_log2, pv0 = 1.f, pv1 = 1.f, fe = 1.f;
       if (page_exp) {
+        int ev0, ev1, evref;
         if (sPg[gi] >= 0) {
           const float k = a.scale_log2 * pow2i(-sGE[2 * gi]);
           ks0 = ks1 = k;
-          evref = sGE[2 * gi + 1];
+          evref = ev0 = ev1 = sGE[2 * gi + 1];
         } else {
           const int8_t *ee = sEE + buf * kGroup * 2;
           evref = ee[1];
           ks0 = a.scale_log2 * pow2i(-ee[2 * g]);
           ks1 = a.scale_log2 * pow2i(-ee[2 * (g + 8)]);
-          pv0 = pow2i(evref - ee[2 * g + 1]);
-          pv1 = pow2i(evref - ee[2 * (g + 8) + 1]);
+          ev0 = ee[2 * g + 1];
+          ev1 = ee[2 * (g + 8) + 1];
         }
-      }
-      float fe = 1.f;
-      if (page_exp) {
-        fe = have_e ? pow2i(evref - E) : 1.f;
-        E = evref;
-        have_e = true;
+        constexpr int kRebase = 10;
+        if (!have_e) {
+          E = evref;
+          have_e = true;
+        } else if (evref - E > kRebase || E - evref > kRebase) {
+          fe = pow2i(evref - E);
+          E = evref;
+        }
+        pv0 = pow2i(E - ev0);
+        pv1 = pow2i(E - ev1);
       }
       // ---- online softmax per row (log2 domain); a row's 16 entries sit in the 8 lanes of one t
       uint32_t pb[NT][2];
