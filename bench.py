@@ -351,6 +351,174 @@ def cpu_baseline(args):
     return CpuSample().run()
 
 
+SPEC8B_Q8 = dict(SPEC8B, wtype="q8_0", ctx=4096, name="llama3-8b-shape-q80")
+
+
+def open_q8(tune, ncol):
+    """The 8B shape with Q8_0 weights (C2, C4) and f16 KV; returns (backend, dir)."""
+    from goethe_engine_b200 import build, gck, synth
+    build.build()
+    spec = synth.Spec(**SPEC8B_Q8)
+    d = os.path.join(os.environ.get("GCK_BENCH_DIR", "/tmp/gck_bench"), f"{spec.name}-s{spec.seed}")
+    t0 = time.time()
+    synth.make(d, spec, buckets=[dict(id="b200.BI.main", ncol=ncol, maxctx=spec.ctx, kv="f16", tune=tune)])
+    print(f"[bench] model ready in {d} ({time.time() - t0:.1f}s)", file=sys.stderr, flush=True)
+    return d, [os.path.join(d, "model.gguf")]
+
+
+def stats_api(be):
+    import ctypes as C
+
+    class Stats(C.Structure):
+        _fields_ = [("size", C.c_uint32), ("steps", C.c_uint32), ("launches", C.c_uint64), ("forward_ms", C.c_double),
+                    ("class_ms", C.c_double * 16), ("class_launches", C.c_uint64 * 16)]
+    be.L.gck_stats_enable.argtypes = [C.c_void_p, C.c_uint32]
+    be.L.gck_stats_read.argtypes = [C.c_void_p, C.c_void_p]
+
+    def read():
+        st = Stats(size=C.sizeof(Stats))
+        be.L.gck_stats_read(be.h, C.byref(st))
+        return st
+    return lambda prof=False: be.L.gck_stats_enable(be.h, 0xFFFF if prof else 1 << 4), read
+
+
+CLASS_NAMES = ["embed", "rmsnorm", "gemm_qkv", "rope_kv", "attention", "attn_combine", "gemm_o", "gemm_gateup",
+               "gemm_down", "gemm_head", "argmax", "splitk_reduce", "tp_allreduce"]
+
+
+def print_classes(st, steps, label=""):
+    """The per-class device-time table (events around each launch) on stderr."""
+    tot = sum(st.class_ms[i] for i in range(len(CLASS_NAMES)))
+    lines = [f"{n:14s} {st.class_ms[i] / steps:8.3f} ms/step  {st.class_launches[i] // max(1, steps):5d} "
+             f"launches/step  {100 * st.class_ms[i] / max(tot, 1e-9):5.1f}%" for i, n in enumerate(CLASS_NAMES)]
+    print(f"[bench] {label}per-class device time (events around each launch):\n" + "\n".join(lines) +
+          f"\n  sum {tot / steps:.3f} ms/step, step {st.forward_ms / steps:.3f} ms", file=sys.stderr, flush=True)
+
+
+def run_c2(args):
+    """C2: the 8B shape, Q8_0 weights, f16 KV, one sequence decoding at context 2048 (HBM-bound: every weight byte and
+    the KV once per token)."""
+    import torch
+    from goethe_engine_b200 import gck
+    d, ws = open_q8(dict(max_cols=2048), 1)
+    ctx, steps_total = 2048, args.warmup + args.steps
+    per_seq = -(-(ctx + steps_total + 1) // 16)
+    be = gck.Backend(d, ws, pool_blocks=per_seq + 4)
+    on, read = stats_api(be)
+    rng = np.random.default_rng(0)
+    toks = [int(x) for x in rng.integers(1, 128000, ctx)]
+    tab = np.arange(per_seq, dtype=np.uint32)
+    be.step([gck.Work(0, toks[:-1], 0, tab, 0)])
+    last, pos = toks[-1], ctx - 1
+    for _ in range(args.warmup):
+        last = be.step([gck.Work(0, [last], pos, tab, 1, greedy=True)])[0][0]
+        pos += 1
+    torch.cuda.synchronize()
+    on(args.profile)
+    with Clocks(0) as clk:
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            last = be.step([gck.Work(0, [last], pos, tab, 1, greedy=True)])[0][0]
+            pos += 1
+        wall = time.perf_counter() - t0
+    st = read()
+    if args.profile:
+        print_classes(st, args.steps)
+    be.close()
+    ms = st.forward_ms / args.steps
+    wbytes = weight_bytes(SPEC8B_Q8) * 272 // 144         # Q8_0: 34 B per 32 weights
+    kv = (ctx + args.warmup + args.steps / 2) * 32 * 8 * 128 * 2 * 2
+    hbm = peaks().get("hbm_gbs", 6650.0)
+    gbs = (wbytes + kv) / (ms / 1e3) / 1e9
+    print(json.dumps({
+        "metric": "decode tok/s (8B Q8_0, batch 1, f16 KV)", "value": round(1e3 / ms, 2), "unit": "tok/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "q8_0 x f16 -> f32; f16 KV",
+        "data": "synthetic (seeded N(0,0.02) weights, uniform tokens)",
+        "config": {"workload": "C2: Llama-3-8B shape, Q8_0 weights, a16, f16 paged KV, one sequence at context 2048",
+                   "batch": 1, "context": ctx, "l2": "inputs larger than L2, no flush"},
+        "e2e": {"value": round(args.steps / wall, 2), "unit": "tok/s", "h2d_bytes_per_step": int(per_seq * 4 + 64),
+                "d2h_bytes_per_step": 4, "path": "gc_step through the C ABI (ctypes), host buffers"},
+        "step_roofline": {"algorithmic_bytes": int(wbytes + kv), "achieved_gbs": round(gbs, 1),
+                          "frac_of_measured": round(gbs / hbm, 4), "frac_of_8tbs": round(gbs / 8000, 4)},
+        "gpu_launches": int(st.launches), "clocks": clk.summary()}), flush=True)
+
+
+def run_c4(args):
+    """C4 (a16 here: the library has no a8 activations): the 8B shape, Q8_0 weights, f16 KV; prefill of 32 sequences x
+    2048 uniform tokens in 2048-token steps (tensor-bound), then one tree verify of a 16-node draft tree per sequence
+    (anchor + 15 drafts, each parent uniform over earlier nodes of depth < 4, random.Random(1) per sequence)."""
+    import random
+    import torch
+    from goethe_engine_b200 import gck
+    d, ws = open_q8(dict(max_cols=2048), 32)
+    n_seq, ctx = 32, 2048
+    per_seq = -(-(ctx + 64) // 16)
+    be = gck.Backend(d, ws, pool_blocks=n_seq * per_seq + 4)
+    on, read = stats_api(be)
+    rng = np.random.default_rng(0)
+    toks = [[int(x) for x in rng.integers(1, 128000, ctx)] for _ in range(n_seq)]
+    tabs = [np.arange(i * per_seq, (i + 1) * per_seq, dtype=np.uint32) for i in range(n_seq)]
+    # warm-up: one sequence's prefill
+    be.step([gck.Work(99, toks[0], 0, tabs[0], 0)])
+    be.release(99)
+    torch.cuda.synchronize()
+    on(args.profile)
+    with Clocks(0) as clk:
+        t0 = time.perf_counter()
+        for i in range(n_seq):
+            be.step([gck.Work(i, toks[i], 0, tabs[i], 1, greedy=True)])
+        wall_p = time.perf_counter() - t0
+    st_p = read()
+    if args.profile:
+        print_classes(st_p, n_seq, "prefill ")
+    parents = []
+    r = random.Random(1)
+    depth = [0]
+    par = [-1]
+    for i in range(1, 16):
+        cands = [j for j in range(i) if depth[j] < 4]
+        pj = r.choice(cands)
+        par.append(pj)
+        depth.append(depth[pj] + 1)
+    parents = par
+    draft = [[int(x) for x in rng.integers(1, 128000, 16)] for _ in range(n_seq)]
+    verify = [gck.Work(i, draft[i], ctx, tabs[i], 16, greedy=True, parents=parents) for i in range(n_seq)]
+    be.step(verify)                      # warm
+    on(args.profile)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        be.step(verify)
+    wall_v = time.perf_counter() - t0
+    st_v = read()
+    if args.profile:
+        print_classes(st_v, args.steps, "verify ")
+    be.close()
+    pre_ms = st_p.forward_ms
+    sp = SPEC8B_Q8
+    lin = sp["layers"] * sp["d"] * (sp["d"] * 2 + 2 * sp["d"] // sp["heads"] * sp["kv_heads"] + 3 * sp["ffn"])
+    # linear layers for every token, causal QK^T and PV (2 x 2 x pos x d per layer), the head for the wanted row
+    flop = n_seq * (2 * lin * ctx + sp["layers"] * 4 * sp["d"] * ctx * (ctx + 1) / 2 + 2 * sp["d"] * sp["vocab"])
+    tc = peaks().get("bf16_tflops_sustained", 1400.0)
+    ver_ms = st_v.forward_ms / args.steps
+    print(json.dumps({
+        "metric": "prefill tok/s (8B Q8_0, 32 x 2048, a16) and tree-verify step ms (32 x 16-node trees)",
+        "value": round(n_seq * ctx / (pre_ms / 1e3), 1), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": 1, "ms_per_step": round(pre_ms / n_seq, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "q8_0 x f16 -> f32 (a16; the C4 a8 activations are not built); f16 KV",
+        "data": "synthetic (seeded N(0,0.02) weights, uniform tokens, seeded draft trees)",
+        "config": {"workload": "C4: Llama-3-8B shape, Q8_0 weights, prefill 32 x 2048 then verify 32 x 16-node trees",
+                   "batch": n_seq, "context": ctx, "tree_parents": parents, "l2": "inputs larger than L2, no flush"},
+        "roofline": {"bound": "tensor", "achieved": round(flop / (pre_ms / 1e3) / 1e12, 1), "peak": tc, "unit": "TFLOP/s",
+                     "frac": round(flop / (pre_ms / 1e3) / 1e12 / tc, 4),
+                     "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained"},
+        "verify": {"ms_per_step": round(ver_ms, 4), "tokens_per_step": n_seq * 16,
+                   "tok_per_s": round(n_seq * 16 / (ver_ms / 1e3), 1), "e2e_ms_per_step": round(wall_v / args.steps * 1e3, 4)},
+        "e2e": {"value": round(n_seq * ctx / wall_p, 1), "unit": "tok/s", "h2d_bytes_per_step": int(ctx * 4 + per_seq * 4),
+                "d2h_bytes_per_step": 4, "path": "gc_step through the C ABI (ctypes), host buffers"},
+        "gpu_launches": int(st_p.launches + st_v.launches), "clocks": clk.summary()}), flush=True)
+
+
 SPEC70B = dict(vocab=128256, d=8192, layers=80, heads=64, kv_heads=8, ffn=28672, eps=1e-5, theta=5e5, wtype="q4_k",
                std=0.02, seed=0, ctx=4096 + 64, name="llama3-70b-shape-q4k")
 B70, CTX70 = 128, 4096
@@ -484,8 +652,9 @@ def main():
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--profile", action="store_true", help="time every kernel class (stderr table)")
-    ap.add_argument("--workload", default="c3", choices=["c3", "c5"],
-                    help="c3: the headline (8B, replicas over --gpus); c5: 70B tensor parallel over --gpus in one process")
+    ap.add_argument("--workload", default="c3", choices=["c2", "c3", "c4", "c5"],
+                    help="c3: the headline (8B, replicas over --gpus); c2: 8B Q8_0 batch-1 decode; c4: 8B Q8_0 prefill "
+                         "and tree verify; c5: 70B tensor parallel over --gpus in one process")
     ap.add_argument("--layers", type=int, default=32,
                     help="layers of the 8B shape (default 32; fewer only for small profiling cases, not a headline)")
     args = ap.parse_args()
@@ -495,6 +664,12 @@ def main():
             sp["name"] += f"-L{sp['layers']}"
     world = int(os.environ.get("WORLD_SIZE", 1))
     rank = int(os.environ.get("RANK", 0))
+    if args.workload in ("c2", "c4"):
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": f"{args.workload}: the CPU baseline is measured on C3 "
+                              "(bench.py --impl reference)"}), flush=True)
+            return
+        return run_c2(args) if args.workload == "c2" else run_c4(args)
     if args.workload == "c5":
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "C5 (70B) on the CPU needs about 278 GB of f32 weights: "
