@@ -2,6 +2,7 @@
 // mbarrier with bounded waits) and small numeric utilities.
 #pragma once
 #include <cuda_fp16.h>
+#include <cuda_runtime.h>
 #include <stdint.h>
 
 #include "plan.h"
@@ -11,6 +12,34 @@ namespace gck {
 #define GCK_DEV __device__ __forceinline__
 
 GCK_DEV uint32_t smem_u32(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+// Programmatic dependent launch. A forward kernel started by launch_pdl may begin while the kernel before it in the
+// stream still runs: it calls dep_wait() before its first access of memory that an earlier kernel writes or reads
+// (dep_wait returns once the earlier kernels have completed and their writes are visible), and dep_launch() so that
+// the next kernel's CTAs may start early (its prologue, or a weight stream that depends on nothing, overlaps this
+// kernel's tail). Launched without the attribute, both return at once.
+GCK_DEV void dep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+GCK_DEV void dep_launch() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
+extern bool g_pdl;   // programmatic dependent launch of the forward kernels (on unless GCK_PDL=0)
+template <typename... P, typename... A>
+inline void launch_pdl(void (*k)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, A... args) {
+  if (!g_pdl) {
+    k<<<grid, block, smem, s>>>(args...);
+    return;
+  }
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, k, args...);
+}
 
 GCK_DEV void cp_async16(void *smem, const void *gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(smem)), "l"(gmem));

@@ -43,6 +43,8 @@ struct Cfg {
   static constexpr int GE_OFF = PG_OFF + NGS * 4;    // [NGS][2] page exponents (K, V) of page groups
   static constexpr int EE_OFF = GE_OFF + NGS * 2;    // [NST][16][2] per-entry exponents of resolved groups
   static constexpr int SMEM = EE_OFF + NST * kGroup * 2;
+  static constexpr int TAIL_OFF = (SMEM + 15) / 16 * 16;   // per-warp tail buffers of tree CTAs: K, V rows, exponents
+  static constexpr int TAIL_B = BUF + 2 * kGroup;
 };
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
@@ -68,9 +70,11 @@ __device__ __forceinline__ float pow2i(int e) { return __int_as_float((127 + e) 
 // Head dims are permuted inside the MMAs so that lanes read contiguous bytes: in QK, lane t's k indices of k-step s
 // are dims t*dh/4 + 4s + {0,1,2,3}; in PV, lane g's output rows of m-tile mt are dims g*dh/8 + 2mt + {0, 1}.
 template <int DH, bool FP8, int NW, int NT>
-__global__ void __launch_bounds__(32 * NW, NW == 1 && NT == 1 ? 20 : 1) attn_kernel(PlanView pv, AttnArgs a) {
+__global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn_kernel(PlanView pv, AttnArgs a) {
   using C = Cfg<DH, FP8>;
   constexpr int NTHR = 32 * NW;
+  dep_wait();
+  dep_launch();
   extern __shared__ __align__(128) uint8_t sm[];
   int *sPg = reinterpret_cast<int *>(sm + C::PG_OFF);
   int8_t *sGE = reinterpret_cast<int8_t *>(sm + C::GE_OFF);
@@ -84,7 +88,11 @@ __global__ void __launch_bounds__(32 * NW, NW == 1 && NT == 1 ? 20 : 1) attn_ker
   int nvis_max = 0;
   for (int i = 0; i < w.nqg; i++) nvis_max = max(nvis_max, pv.qgroups[w.qg0 + i].nvis);
   const int lo = w.split * kSplit, hi = min(lo + kSplit, nvis_max);
-  const int ngroups = (hi - lo + kGroup - 1) / kGroup;
+  // a CTA of several tree nodes shares only the groups of plain rows below the item's own rows; each warp then walks
+  // the groups that reach its own path (its tail) from a private buffer, in the same order a lone warp would
+  const bool tree_cta = NW > 1 && q0.path_len > 0;
+  const int shared_hi = tree_cta ? min(hi, it.pos / kGroup * kGroup) : hi;
+  const int ngroups = shared_hi > lo ? (shared_hi - lo + kGroup - 1) / kGroup : 0;
   const bool active = warp < w.nqg;
   const int qgi = w.qg0 + (active ? warp : 0);
   const QGroup qg = pv.qgroups[qgi];
@@ -198,6 +206,161 @@ __global__ void __launch_bounds__(32 * NW, NW == 1 && NT == 1 ? 20 : 1) attn_ker
     if (st < ngroups) issue(st, st);
     cp_async_commit();
   }
+  // one 16-entry group of the row list starting at list index i0, staged at sK (K rows, then V rows): page groups
+  // carry their (K, V) exponents in ge, resolved groups per-entry exponents in ee
+  auto consume = [&](const uint8_t *sK, int i0, const int8_t *ge, const int8_t *ee) {
+    const uint8_t *sV = sK + kGroup * C::ROWB;
+    // ---- S^T = K Q^T: A rows g, g+8 (entries), lane t's dim slice
+    constexpr int KW = C::RB / 4 / 4;   // words of a lane's K slice
+    uint32_t k0[KW], k1[KW];
+#pragma unroll
+    for (int i = 0; i < KW / 4; i++) {
+      uint4 u = reinterpret_cast<const uint4 *>(sK + g * C::ROWB + t * (C::RB / 4))[i];
+      k0[4 * i] = u.x; k0[4 * i + 1] = u.y; k0[4 * i + 2] = u.z; k0[4 * i + 3] = u.w;
+      u = reinterpret_cast<const uint4 *>(sK + (g + 8) * C::ROWB + t * (C::RB / 4))[i];
+      k1[4 * i] = u.x; k1[4 * i + 1] = u.y; k1[4 * i + 2] = u.z; k1[4 * i + 3] = u.w;
+    }
+    // two accumulator chains (even / odd k-steps), summed at the end: half the MMA dependency chain
+    float sc[NT][4], sc2[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+      sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = sc2[nt][0] = sc2[nt][1] = sc2[nt][2] = sc2[nt][3] = 0.f;
+#pragma unroll
+    for (int s = 0; s < C::NKS; s++) {
+      uint32_t af[4];
+      if (FP8) {
+        af[0] = e4m3x2_to_h2(static_cast<uint16_t>(k0[s] & 0xffff));
+        af[2] = e4m3x2_to_h2(static_cast<uint16_t>(k0[s] >> 16));
+        af[1] = e4m3x2_to_h2(static_cast<uint16_t>(k1[s] & 0xffff));
+        af[3] = e4m3x2_to_h2(static_cast<uint16_t>(k1[s] >> 16));
+      } else {
+        af[0] = k0[2 * s]; af[2] = k0[2 * s + 1];
+        af[1] = k1[2 * s]; af[3] = k1[2 * s + 1];
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++) mma_f16((s & 1) ? sc2[nt] : sc[nt], af, qb[nt][s]);
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+      for (int c = 0; c < 4; c++) sc[nt][c] += sc2[nt][c];
+    // ---- page scales of entries g and g + 8: 2^-ek on the scores, 2^(E - ev) on the probabilities. O stays in one
+    // exponent frame E (O is kept scaled by 2^E); E moves (and O is rescaled) only when a page's V exponent is more
+    // than kRebase away, so the f16 probabilities times 2^(E - ev) neither overflow nor lose their bits
+    float ks0 = a.scale_log2, ks1 = a.scale_log2, pv0 = 1.f, pv1 = 1.f, fe = 1.f;
+    if (page_exp) {
+      int ev0, ev1, evref;
+      if (ge) {
+        const float k = a.scale_log2 * pow2i(-ge[0]);
+        ks0 = ks1 = k;
+        evref = ev0 = ev1 = ge[1];
+      } else {
+        evref = ee[1];
+        ks0 = a.scale_log2 * pow2i(-ee[2 * g]);
+        ks1 = a.scale_log2 * pow2i(-ee[2 * (g + 8)]);
+        ev0 = ee[2 * g + 1];
+        ev1 = ee[2 * (g + 8) + 1];
+      }
+      constexpr int kRebase = 10;
+      if (!have_e) {
+        E = evref;
+        have_e = true;
+      } else if (evref - E > kRebase || E - evref > kRebase) {
+        fe = pow2i(evref - E);
+        E = evref;
+      }
+      pv0 = pow2i(E - ev0);
+      pv1 = pow2i(E - ev1);
+    }
+    // ---- online softmax per row (log2 domain); a row's 16 entries sit in the 8 lanes of one t
+    uint32_t pb[NT][2];
+    float f[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {
+      float x[2][2];   // [entry g / g+8][row c]
+#pragma unroll
+      for (int c = 0; c < 2; c++) {
+        const bool ok0 = rvalid[nt][c] && i0 + g < nvis[nt][c];
+        const bool ok1 = rvalid[nt][c] && i0 + g + 8 < nvis[nt][c];
+        x[0][c] = ok0 ? sc[nt][c] * ks0 : -INFINITY;
+        x[1][c] = ok1 ? sc[nt][2 + c] * ks1 : -INFINITY;
+      }
+      float p[2][2];
+#pragma unroll
+      for (int c = 0; c < 2; c++) {
+        float mx = fmaxf(x[0][c], x[1][c]);
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float mn = fmaxf(mrow[nt][c], mx);
+        const float alpha = mn == -INFINITY ? 1.f : exp2f(mrow[nt][c] - mn);
+        mrow[nt][c] = mn;
+        p[0][c] = mn == -INFINITY ? 0.f : exp2f(x[0][c] - mn);
+        p[1][c] = mn == -INFINITY ? 0.f : exp2f(x[1][c] - mn);
+        float ps = p[0][c] + p[1][c];
+        ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+        lrow[nt][c] = lrow[nt][c] * alpha + ps;
+        f[nt][c] = alpha * fe;
+      }
+      // P^T as the PV B operand: (entries 2t, 2t+1 | 2t+8, 2t+9) of row g
+      pb[nt][0] = movmatrix_t(pack_h2(p[0][0] * pv0, p[0][1] * pv0));
+      pb[nt][1] = movmatrix_t(pack_h2(p[1][0] * pv1, p[1][1] * pv1));
+    }
+    // rescaling by exactly 1 changes nothing: skipped when no row of the warp needs it
+    bool one = true;
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) one = one && f[nt][0] == 1.f && f[nt][1] == 1.f;
+    if (!__all_sync(0xffffffffu, one)) {
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int j = 0; j < C::NMT; j++) {
+          o[nt][j][0] *= f[nt][0]; o[nt][j][1] *= f[nt][1]; o[nt][j][2] *= f[nt][0]; o[nt][j][3] *= f[nt][1];
+        }
+    }
+    // ---- O^T += V^T P^T: lane (g, t) reads entries 2t, 2t+1, 2t+8, 2t+9, dims [g*dh/8, (g+1)*dh/8)
+    constexpr int VW = C::RB / 8 / 4;   // words of a lane's V slice per entry
+    uint32_t vr[4][VW];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const int e = 2 * t + (q & 1) + (q >> 1) * 8;
+      const uint8_t *src = sV + e * C::ROWB + g * (C::RB / 8);
+      if (VW >= 4) {
+#pragma unroll
+        for (int i = 0; i < VW / 4; i++) {
+          uint4 u = reinterpret_cast<const uint4 *>(src)[i];
+          vr[q][4 * i] = u.x; vr[q][4 * i + 1] = u.y; vr[q][4 * i + 2] = u.z; vr[q][4 * i + 3] = u.w;
+        }
+      } else {   // 8 bytes: fp8 with dh 64
+        uint2 u = *reinterpret_cast<const uint2 *>(src);
+        vr[q][0] = u.x;
+        vr[q][VW - 1] = u.y;
+      }
+    }
+#pragma unroll
+    for (int mt = 0; mt < C::NMT; mt++) {
+      uint32_t af[4];
+      if (FP8) {
+        // dims 2mt (rows g) and 2mt + 1 (rows g + 8) of the slice: byte 2mt % 4 (+1) of word mt / 2
+        const int wi = mt / 2, b0 = 2 * (mt % 2);
+        const uint32_t s0 = b0 | ((4 + b0) << 4), s1 = (b0 + 1) | ((5 + b0) << 4);
+        af[0] = e4m3x2_to_h2(static_cast<uint16_t>(prmt(vr[0][wi], vr[1][wi], s0)));
+        af[1] = e4m3x2_to_h2(static_cast<uint16_t>(prmt(vr[0][wi], vr[1][wi], s1)));
+        af[2] = e4m3x2_to_h2(static_cast<uint16_t>(prmt(vr[2][wi], vr[3][wi], s0)));
+        af[3] = e4m3x2_to_h2(static_cast<uint16_t>(prmt(vr[2][wi], vr[3][wi], s1)));
+      } else {
+        af[0] = prmt(vr[0][mt], vr[1][mt], 0x5410u);
+        af[1] = prmt(vr[0][mt], vr[1][mt], 0x7632u);
+        af[2] = prmt(vr[2][mt], vr[3][mt], 0x5410u);
+        af[3] = prmt(vr[2][mt], vr[3][mt], 0x7632u);
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++) mma_f16(o[nt][mt], af, pb[nt]);
+    }
+  };
+
   for (int gi = 0; gi < ngroups; gi++) {
     const int buf = gi % C::NST;
     if (gi + C::NST - 1 < ngroups) issue(gi + C::NST - 1, (gi + C::NST - 1) % C::NST);
@@ -205,163 +368,41 @@ __global__ void __launch_bounds__(32 * NW, NW == 1 && NT == 1 ? 20 : 1) attn_ker
     cp_async_wait<C::NST - 1>();
     __syncthreads();
     const int i0 = lo + gi * kGroup;
-    if (active && i0 < qg.nvis) {
-      const uint8_t *sK = sm + buf * C::BUF;
-      const uint8_t *sV = sK + kGroup * C::ROWB;
-      // ---- S^T = K Q^T: A rows g, g+8 (entries), lane t's dim slice
-      constexpr int KW = C::RB / 4 / 4;   // words of a lane's K slice
-      uint32_t k0[KW], k1[KW];
-#pragma unroll
-      for (int i = 0; i < KW / 4; i++) {
-        uint4 u = reinterpret_cast<const uint4 *>(sK + g * C::ROWB + t * (C::RB / 4))[i];
-        k0[4 * i] = u.x; k0[4 * i + 1] = u.y; k0[4 * i + 2] = u.z; k0[4 * i + 3] = u.w;
-        u = reinterpret_cast<const uint4 *>(sK + (g + 8) * C::ROWB + t * (C::RB / 4))[i];
-        k1[4 * i] = u.x; k1[4 * i + 1] = u.y; k1[4 * i + 2] = u.z; k1[4 * i + 3] = u.w;
-      }
-      // two accumulator chains (even / odd k-steps), summed at the end: half the MMA dependency chain
-      float sc[NT][4], sc2[NT][4];
-#pragma unroll
-      for (int nt = 0; nt < NT; nt++)
-        sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = sc2[nt][0] = sc2[nt][1] = sc2[nt][2] = sc2[nt][3] = 0.f;
-#pragma unroll
-      for (int s = 0; s < C::NKS; s++) {
-        uint32_t af[4];
-        if (FP8) {
-          af[0] = e4m3x2_to_h2(static_cast<uint16_t>(k0[s] & 0xffff));
-          af[2] = e4m3x2_to_h2(static_cast<uint16_t>(k0[s] >> 16));
-          af[1] = e4m3x2_to_h2(static_cast<uint16_t>(k1[s] & 0xffff));
-          af[3] = e4m3x2_to_h2(static_cast<uint16_t>(k1[s] >> 16));
-        } else {
-          af[0] = k0[2 * s]; af[2] = k0[2 * s + 1];
-          af[1] = k1[2 * s]; af[3] = k1[2 * s + 1];
-        }
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++) mma_f16((s & 1) ? sc2[nt] : sc[nt], af, qb[nt][s]);
-      }
-#pragma unroll
-      for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-        for (int c = 0; c < 4; c++) sc[nt][c] += sc2[nt][c];
-      // ---- page scales of entries g and g + 8: 2^-ek on the scores, 2^(E - ev) on the probabilities. O stays in one
-      // exponent frame E (O is kept scaled by 2^E); E moves (and O is rescaled) only when a page's V exponent is more
-      // than kRebase away, so the f16 probabilities times 2^(E - ev) neither overflow nor lose their bits
-      float ks0 = a.scale_log2, ks1 = a.scale_log2, pv0 = 1.f, pv1 = 1.f, fe = 1.f;
-      if (page_exp) {
-        int ev0, ev1, evref;
-        if (sPg[gi] >= 0) {
-          const float k = a.scale_log2 * pow2i(-sGE[2 * gi]);
-          ks0 = ks1 = k;
-          evref = ev0 = ev1 = sGE[2 * gi + 1];
-        } else {
-          const int8_t *ee = sEE + buf * kGroup * 2;
-          evref = ee[1];
-          ks0 = a.scale_log2 * pow2i(-ee[2 * g]);
-          ks1 = a.scale_log2 * pow2i(-ee[2 * (g + 8)]);
-          ev0 = ee[2 * g + 1];
-          ev1 = ee[2 * (g + 8) + 1];
-        }
-        constexpr int kRebase = 10;
-        if (!have_e) {
-          E = evref;
-          have_e = true;
-        } else if (evref - E > kRebase || E - evref > kRebase) {
-          fe = pow2i(evref - E);
-          E = evref;
-        }
-        pv0 = pow2i(E - ev0);
-        pv1 = pow2i(E - ev1);
-      }
-      // ---- online softmax per row (log2 domain); a row's 16 entries sit in the 8 lanes of one t
-      uint32_t pb[NT][2];
-      float f[NT][2];
-#pragma unroll
-      for (int nt = 0; nt < NT; nt++) {
-        float x[2][2];   // [entry g / g+8][row c]
-#pragma unroll
-        for (int c = 0; c < 2; c++) {
-          const bool ok0 = rvalid[nt][c] && i0 + g < nvis[nt][c];
-          const bool ok1 = rvalid[nt][c] && i0 + g + 8 < nvis[nt][c];
-          x[0][c] = ok0 ? sc[nt][c] * ks0 : -INFINITY;
-          x[1][c] = ok1 ? sc[nt][2 + c] * ks1 : -INFINITY;
-        }
-        float p[2][2];
-#pragma unroll
-        for (int c = 0; c < 2; c++) {
-          float mx = fmaxf(x[0][c], x[1][c]);
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-          const float mn = fmaxf(mrow[nt][c], mx);
-          const float alpha = mn == -INFINITY ? 1.f : exp2f(mrow[nt][c] - mn);
-          mrow[nt][c] = mn;
-          p[0][c] = mn == -INFINITY ? 0.f : exp2f(x[0][c] - mn);
-          p[1][c] = mn == -INFINITY ? 0.f : exp2f(x[1][c] - mn);
-          float ps = p[0][c] + p[1][c];
-          ps += __shfl_xor_sync(0xffffffffu, ps, 4);
-          ps += __shfl_xor_sync(0xffffffffu, ps, 8);
-          ps += __shfl_xor_sync(0xffffffffu, ps, 16);
-          lrow[nt][c] = lrow[nt][c] * alpha + ps;
-          f[nt][c] = alpha * fe;
-        }
-        // P^T as the PV B operand: (entries 2t, 2t+1 | 2t+8, 2t+9) of row g
-        pb[nt][0] = movmatrix_t(pack_h2(p[0][0] * pv0, p[0][1] * pv0));
-        pb[nt][1] = movmatrix_t(pack_h2(p[1][0] * pv1, p[1][1] * pv1));
-      }
-      // rescaling by exactly 1 changes nothing: skipped when no row of the warp needs it
-      bool one = true;
-#pragma unroll
-      for (int nt = 0; nt < NT; nt++) one = one && f[nt][0] == 1.f && f[nt][1] == 1.f;
-      if (!__all_sync(0xffffffffu, one)) {
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-          for (int j = 0; j < C::NMT; j++) {
-            o[nt][j][0] *= f[nt][0]; o[nt][j][1] *= f[nt][1]; o[nt][j][2] *= f[nt][0]; o[nt][j][3] *= f[nt][1];
-          }
-      }
-      // ---- O^T += V^T P^T: lane (g, t) reads entries 2t, 2t+1, 2t+8, 2t+9, dims [g*dh/8, (g+1)*dh/8)
-      constexpr int VW = C::RB / 8 / 4;   // words of a lane's V slice per entry
-      uint32_t vr[4][VW];
-#pragma unroll
-      for (int q = 0; q < 4; q++) {
-        const int e = 2 * t + (q & 1) + (q >> 1) * 8;
-        const uint8_t *src = sV + e * C::ROWB + g * (C::RB / 8);
-        if (VW >= 4) {
-#pragma unroll
-          for (int i = 0; i < VW / 4; i++) {
-            uint4 u = reinterpret_cast<const uint4 *>(src)[i];
-            vr[q][4 * i] = u.x; vr[q][4 * i + 1] = u.y; vr[q][4 * i + 2] = u.z; vr[q][4 * i + 3] = u.w;
-          }
-        } else {   // 8 bytes: fp8 with dh 64
-          uint2 u = *reinterpret_cast<const uint2 *>(src);
-          vr[q][0] = u.x;
-          vr[q][VW - 1] = u.y;
-        }
-      }
-#pragma unroll
-      for (int mt = 0; mt < C::NMT; mt++) {
-        uint32_t af[4];
-        if (FP8) {
-          // dims 2mt (rows g) and 2mt + 1 (rows g + 8) of the slice: byte 2mt % 4 (+1) of word mt / 2
-          const int wi = mt / 2, b0 = 2 * (mt % 2);
-          const uint32_t s0 = b0 | ((4 + b0) << 4), s1 = (b0 + 1) | ((5 + b0) << 4);
-          af[0] = e4m3x2_to_h2(static_cast<uint16_t>(prmt(vr[0][wi], vr[1][wi], s0)));
-          af[1] = e4m3x2_to_h2(static_cast<uint16_t>(prmt(vr[0][wi], vr[1][wi], s1)));
-          af[2] = e4m3x2_to_h2(static_cast<uint16_t>(prmt(vr[2][wi], vr[3][wi], s0)));
-          af[3] = e4m3x2_to_h2(static_cast<uint16_t>(prmt(vr[2][wi], vr[3][wi], s1)));
-        } else {
-          af[0] = prmt(vr[0][mt], vr[1][mt], 0x5410u);
-          af[1] = prmt(vr[0][mt], vr[1][mt], 0x7632u);
-          af[2] = prmt(vr[2][mt], vr[3][mt], 0x5410u);
-          af[3] = prmt(vr[2][mt], vr[3][mt], 0x7632u);
-        }
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++) mma_f16(o[nt][mt], af, pb[nt]);
-      }
-    }
+    if (active && i0 < qg.nvis)
+      consume(sm + buf * C::BUF, i0, sPg[gi] >= 0 ? sGE + 2 * gi : nullptr, sEE + buf * kGroup * 2);
     __syncthreads();
   }
   cp_async_wait<0>();
+
+  if constexpr (NW > 1) {
+    if (tree_cta && active) {
+      // this warp's tail: list entries from the item's last plain group boundary, resolved through its own path
+      uint8_t *tK = sm + C::TAIL_OFF + warp * C::TAIL_B;
+      uint8_t *tV = tK + kGroup * C::ROWB;
+      int8_t *tE = reinterpret_cast<int8_t *>(tK + C::BUF);
+      const int hiw = min(lo + kSplit, qg.nvis);
+      for (int i0 = max(lo, shared_hi); i0 < hiw; i0 += kGroup) {
+        for (int c = lane; c < 2 * kGroup * C::CHUNKS; c += 32) {
+          const int isv = c / (kGroup * C::CHUNKS), rem = c % (kGroup * C::CHUNKS);
+          const int e = rem / C::CHUNKS, ch = rem % C::CHUNKS;
+          const int row = list_row(pv, it, qg, min(i0 + e, hiw - 1));
+          const size_t off = ((static_cast<size_t>(row / kBlock) * a.KVH + head) * kBlock + row % kBlock) * C::RB + ch * 16;
+          cp_async16((isv ? tV : tK) + e * C::ROWB + ch * 16, (isv ? vbase : kbase) + off);
+        }
+        if (page_exp && lane < kGroup) {
+          const int row = list_row(pv, it, qg, min(i0 + lane, hiw - 1));
+          const int8_t *pe = a.exps + (static_cast<size_t>(row / kBlock) * a.KVH + head) * 2;
+          tE[2 * lane] = pe[0];
+          tE[2 * lane + 1] = pe[1];
+        }
+        cp_async_commit();
+        cp_async_wait<0>();
+        __syncwarp();
+        consume(tK, i0, nullptr, tE);
+        __syncwarp();
+      }
+    }
+  }
 
   if (!active || w.split >= qg.nsplit) return;
   const int rows = qg.ntok * G;
@@ -432,7 +473,12 @@ __global__ void __launch_bounds__(32 * NW, NW == 1 && NT == 1 ? 20 : 1) attn_ker
 template <int DH, bool FP8, int NW, int NT>
 void launch_t(const PlanView &pv, const AttnArgs &a, cudaStream_t s) {
   using C = Cfg<DH, FP8>;
-  if (pv.n_work > 0) attn_kernel<DH, FP8, NW, NT><<<pv.n_work, 32 * NW, C::SMEM, s>>>(pv, a);
+  constexpr int kMaxSmem = C::TAIL_OFF + NW * C::TAIL_B;
+  const int smem = NW > 1 && pv.tree_cta ? kMaxSmem : C::SMEM;
+  // per device (tensor-parallel ranks launch on theirs from their own threads)
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(attn_kernel<DH, FP8, NW, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (pv.n_work > 0) launch_pdl(attn_kernel<DH, FP8, NW, NT>, pv.n_work, 32 * NW, smem, s, pv, a);
 }
 template <int DH, bool FP8>
 void launch_dh(const PlanView &pv, const AttnArgs &a, int nw, cudaStream_t s) {

@@ -24,6 +24,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const uint8_t *__restrict__ W, int KT, int splits, const __half *__restrict__ act, int T, Epi epi,
                 float *part, int Npad) {
   static_assert(TYPE == kF16, "quantized weights run on the tcgen05 kernel");
+  dep_wait();
+  dep_launch();
   extern __shared__ __align__(128) uint8_t smem[];
   __half *sA = reinterpret_cast<__half *>(smem);
   __half *sB = reinterpret_cast<__half *>(smem + kSA);
@@ -144,7 +146,7 @@ template <int TYPE>
 void launch_t(const QWeight &w, const __half *act, int T, const Epi &epi, float *part, cudaStream_t s) {
   size_t sm = smem_bytes<TYPE>();
   dim3 grid(w.NT, w.splits, (T + kBN - 1) / kBN);
-  gemm_kernel<TYPE><<<grid, kThreads, sm, s>>>(w.data, w.KT, w.splits, act, T, epi, part, w.NT * kBM);
+  launch_pdl(gemm_kernel<TYPE>, grid, kThreads, sm, s, w.data, w.KT, w.splits, act, T, epi, part, w.NT * kBM);
 }
 
 }  // namespace

@@ -273,7 +273,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   using S = Shape<TYPE, NT>;
   constexpr int RS = S::RAW, SR = S::R, ACC = S::ACC, KS = S::KS, SPT = S::SPT;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte aligned (the 128-byte swizzle atom) by an offset into the __shared__ array, so that every pointer derived
+  // from it stays a shared-memory pointer to the compiler (shared loads, not generic ones)
+  uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t *sB = smem;
   uint8_t *sRaw = sB + SR * S::STAGE_B;
   float *xchg = reinterpret_cast<float *>(sRaw + RS * F::BYTES);
@@ -283,6 +285,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *acc_full = b_full + SR, *acc_empty = acc_full + 2, *mma_done = acc_empty + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  // the next kernel may start as this one's CTAs run; the weight stream depends on no earlier kernel, so only the
+  // activation producer and the epilogue wait for the previous kernels (dep_wait)
+  dep_launch();
 
   if (threadIdx.x == 0) {
     // a raw tile is read by one dequant group (KS = 256) or by both (KS = 128)
@@ -325,6 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 2) {
     if (lane == 0) {
       // ---- activation stages: KS / 64 tensor-map copies (64 K each) per stage, up to SR stages ahead
+      dep_wait();
       long c = 0;
       bool ok = true;
       for (int w = blockIdx.x; w < units && ok; w += gridDim.x) {
@@ -453,6 +459,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= kEpiWarp0) {
     // ---- epilogue: TMEM lane quarter q = weight rows 32q .. 32q+31 of the tile
+    dep_wait();
     const int q = warp & 3;
     const int r = q * 32 + lane;
     int lu = 0;
@@ -540,8 +547,8 @@ void launch_nt(const QWeight &w, const CUtensorMap *map, int T, const Epi &epi, 
                const Signal &sig, cudaStream_t s) {
   const int units = w.NT * w.splits * ((T + NT - 1) / NT);
   const int grid = units < sms ? units : sms;
-  gemm_tc_kernel<TYPE, NT><<<grid, kThreads, smem_total<TYPE, NT>(), s>>>(w.data, w.NT, w.KT, w.splits, units, *map, T,
-                                                                          epi, part, w.NT * kBM, err, sig);
+  launch_pdl(gemm_tc_kernel<TYPE, NT>, grid, kThreads, smem_total<TYPE, NT>(), s, w.data, w.NT, w.KT, w.splits, units,
+             *map, T, epi, part, w.NT * kBM, err, sig);
 }
 
 template <int TYPE>

@@ -37,6 +37,8 @@ __device__ float dequant_elem(const uint8_t *row, int type, int e) {
 }
 
 __global__ void embed_kernel(PlanView pv, const uint8_t *emb, int type, size_t row_bytes, int d, float *x) {
+  dep_wait();
+  dep_launch();
   int t = blockIdx.x;
   const uint8_t *row = emb + static_cast<size_t>(pv.tok_id[t]) * row_bytes;
   for (int e = threadIdx.x; e < d; e += blockDim.x) x[static_cast<size_t>(t) * d + e] = dequant_elem(row, type, e);
@@ -44,7 +46,7 @@ __global__ void embed_kernel(PlanView pv, const uint8_t *emb, int type, size_t r
 
 void launch_embed(const PlanView &pv, const uint8_t *emb, int type, size_t row_bytes, int d, float *x,
                   cudaStream_t s) {
-  embed_kernel<<<pv.T, 256, 0, s>>>(pv, emb, type, row_bytes, d, x);
+  launch_pdl(embed_kernel, pv.T, 256, 0, s, pv, emb, type, row_bytes, d, x);
 }
 
 // ----------------------------------------------------------------------------------------------------------------
@@ -131,11 +133,15 @@ void launch_tp_reduce_scatter(const TpPeers &p, int b, unsigned long long epoch,
 
 constexpr int kNormThreads = 512;
 constexpr int kNormMaxVec = 4;    // float4 loads per thread: d <= 512 * 4 * 4 = 8192
+// split-K partials are read kSplitChunk slices at a time, all their loads in flight together, and summed in split order
+constexpr int kSplitChunk = 4;
 
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float *x, const int *rows, const float *gain, float eps,
                                                                int d, int ld, __half *out, const float *part, int S,
                                                                int pld, int T, TpPeers tp, int tpb,
                                                                unsigned long long tp_epoch) {
+  dep_wait();
+  dep_launch();
   int r = blockIdx.x;
   int src = rows ? rows[r] : r;
   const float *tpsum = nullptr;   // tensor parallelism: this row's all-reduced sum, at its owner rank
@@ -167,21 +173,28 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float *x, const i
     }
   }
   if (part) {
-    // per element: ((0 + p_0) + p_1) + ... in split order, then added to x; the four vectors' loads are independent
+    // per element: ((0 + p_0) + p_1) + ... in split order, then added to x; a chunk's loads are all issued first
     float4 a[kNormMaxVec];
 #pragma unroll
     for (int i = 0; i < kNormMaxVec; i++) a[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int sp = 0; sp < S; sp++) {
-      const float4 *pr = reinterpret_cast<const float4 *>(part + (static_cast<size_t>(sp) * T + src) * pld);
-      float4 pp[kNormMaxVec];
+    for (int sp0 = 0; sp0 < S; sp0 += kSplitChunk) {
+      float4 pp[kSplitChunk][kNormMaxVec];
 #pragma unroll
-      for (int i = 0; i < kNormMaxVec; i++) {
-        int e = threadIdx.x + i * kNormThreads;
-        pp[i] = e < nv ? pr[e] : make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int j = 0; j < kSplitChunk; j++) {
+        const float4 *pr = reinterpret_cast<const float4 *>(part + (static_cast<size_t>(sp0 + j) * T + src) * pld);
+#pragma unroll
+        for (int i = 0; i < kNormMaxVec; i++) {
+          int e = threadIdx.x + i * kNormThreads;
+          pp[j][i] = sp0 + j < S && e < nv ? pr[e] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
       }
 #pragma unroll
-      for (int i = 0; i < kNormMaxVec; i++) {
-        a[i].x += pp[i].x; a[i].y += pp[i].y; a[i].z += pp[i].z; a[i].w += pp[i].w;
+      for (int j = 0; j < kSplitChunk; j++) {
+        if (sp0 + j >= S) break;
+#pragma unroll
+        for (int i = 0; i < kNormMaxVec; i++) {
+          a[i].x += pp[j][i].x; a[i].y += pp[j][i].y; a[i].z += pp[j][i].z; a[i].w += pp[j][i].w;
+        }
       }
     }
 #pragma unroll
@@ -231,8 +244,8 @@ void launch_rmsnorm(float *x, const int *rows, int n, const float *gain, float e
   TpPeers none{};
   none.n = 1;
   if (n > 0)
-    rmsnorm_kernel<<<n, kNormThreads, 0, s>>>(x, rows, gain, eps, d, ld, out, part, S, pld, T, tp ? *tp : none, tp_buf,
-                                              tp_epoch);
+    launch_pdl(rmsnorm_kernel, n, kNormThreads, 0, s, x, rows, gain, eps, d, ld, out, part, S, pld, T, tp ? *tp : none,
+               tp_buf, tp_epoch);
 }
 
 // ----------------------------------------------------------------------------------------------------------------
@@ -256,17 +269,32 @@ struct QkvSrc {
   __device__ float operator()(int t, int c) const {
     if (S == 1) return p[static_cast<size_t>(t) * ld + c];
     float v = 0.f;
-    for (int s = 0; s < S; s++) v += p[(static_cast<size_t>(s) * T + t) * ld + c];
+    for (int s0 = 0; s0 < S; s0 += kSplitChunk) {
+      float x[kSplitChunk];
+#pragma unroll
+      for (int j = 0; j < kSplitChunk; j++) x[j] = s0 + j < S ? p[(static_cast<size_t>(s0 + j) * T + t) * ld + c] : 0.f;
+#pragma unroll
+      for (int j = 0; j < kSplitChunk; j++)
+        if (s0 + j < S) v += x[j];
+    }
     return v;
   }
   // columns c, c + 1 (c even): one 8-byte load per split
   __device__ float2 pair(int t, int c) const {
     if (S == 1) return *reinterpret_cast<const float2 *>(p + static_cast<size_t>(t) * ld + c);
     float2 v = make_float2(0.f, 0.f);
-    for (int s = 0; s < S; s++) {
-      const float2 x = *reinterpret_cast<const float2 *>(p + (static_cast<size_t>(s) * T + t) * ld + c);
-      v.x += x.x;
-      v.y += x.y;
+    for (int s0 = 0; s0 < S; s0 += kSplitChunk) {
+      float2 x[kSplitChunk];
+#pragma unroll
+      for (int j = 0; j < kSplitChunk; j++)
+        x[j] = s0 + j < S ? *reinterpret_cast<const float2 *>(p + (static_cast<size_t>(s0 + j) * T + t) * ld + c)
+                          : make_float2(0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < kSplitChunk; j++)
+        if (s0 + j < S) {
+          v.x += x[j].x;
+          v.y += x[j].y;
+        }
     }
     return v;
   }
@@ -295,6 +323,8 @@ __device__ float head_amax(const QkvSrc &q, int t, int c0, const float2 *cs, boo
 template <int DH>
 __global__ void rope_kv_kernel(PlanView pv, QkvSrc qs, int H, int KVH, const float2 *rope_tab, __half *q, void *kc,
                                void *vc, int8_t *exps, int kv_fp8, int page_scale) {
+  dep_wait();
+  dep_launch();
   int t = blockIdx.x;
   int hh = threadIdx.x / 32 + blockIdx.y * (blockDim.x / 32);  // head slot: [0, H) q heads, [H, H + KVH) kv heads
   if (hh >= H + KVH) return;
@@ -362,9 +392,9 @@ void launch_rope_kv(const PlanView &pv, const float *qkv, int S, int ld, int H, 
   dim3 grid(pv.T, (heads + per - 1) / per);
   QkvSrc qs{qkv, S, ld, pv.T};
   if (dh == 128)
-    rope_kv_kernel<128><<<grid, per * 32, 0, s>>>(pv, qs, H, KVH, rope_tab, q, kc, vc, exps, kv_fp8, page_scale);
+    launch_pdl(rope_kv_kernel<128>, grid, per * 32, 0, s, pv, qs, H, KVH, rope_tab, q, kc, vc, exps, kv_fp8, page_scale);
   else
-    rope_kv_kernel<64><<<grid, per * 32, 0, s>>>(pv, qs, H, KVH, rope_tab, q, kc, vc, exps, kv_fp8, page_scale);
+    launch_pdl(rope_kv_kernel<64>, grid, per * 32, 0, s, pv, qs, H, KVH, rope_tab, q, kc, vc, exps, kv_fp8, page_scale);
 }
 
 // ----------------------------------------------------------------------------------------------------------------
@@ -372,6 +402,8 @@ void launch_rope_kv(const PlanView &pv, const float *qkv, int S, int ld, int H, 
 __device__ __forceinline__ float silu(float g) { return g / (1.f + expf(-g)); }
 
 __global__ void splitk_reduce_kernel(const float *part, int S, int T, int Npad, Epi epi) {
+  dep_wait();
+  dep_launch();
   size_t total = static_cast<size_t>(T) * (epi.kind == kEpiSwiGLU ? Npad / 8 : Npad);
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -382,11 +414,20 @@ __global__ void splitk_reduce_kernel(const float *part, int S, int T, int Npad, 
       int tile = f / 64, w = f % 64;
       int ng = tile * 128 + w, nu = ng + 64;
       float4 g = make_float4(0.f, 0.f, 0.f, 0.f), u = g;
-      for (int s = 0; s < S; s++) {
-        const float4 a = *reinterpret_cast<const float4 *>(part + (static_cast<size_t>(s) * T + t) * Npad + ng);
-        const float4 b = *reinterpret_cast<const float4 *>(part + (static_cast<size_t>(s) * T + t) * Npad + nu);
-        g.x += a.x; g.y += a.y; g.z += a.z; g.w += a.w;
-        u.x += b.x; u.y += b.y; u.z += b.z; u.w += b.w;
+      for (int s0 = 0; s0 < S; s0 += kSplitChunk) {
+        float4 a[kSplitChunk], b[kSplitChunk];
+#pragma unroll
+        for (int j = 0; j < kSplitChunk; j++) {
+          const float *row = part + (static_cast<size_t>(s0 + j) * T + t) * Npad;
+          a[j] = s0 + j < S ? *reinterpret_cast<const float4 *>(row + ng) : make_float4(0.f, 0.f, 0.f, 0.f);
+          b[j] = s0 + j < S ? *reinterpret_cast<const float4 *>(row + nu) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int j = 0; j < kSplitChunk; j++) {
+          if (s0 + j >= S) break;
+          g.x += a[j].x; g.y += a[j].y; g.z += a[j].z; g.w += a[j].w;
+          u.x += b[j].x; u.y += b[j].y; u.z += b[j].z; u.w += b[j].w;
+        }
       }
       __half *o = epi.out_h + static_cast<size_t>(t) * epi.ld + f;
       if (f < epi.n) o[0] = __float2half_rn(silu(g.x) * u.x);
@@ -397,7 +438,14 @@ __global__ void splitk_reduce_kernel(const float *part, int S, int T, int Npad, 
       int t = static_cast<int>(i / Npad), n = static_cast<int>(i % Npad);
       if (n >= epi.n) continue;
       float v = 0.f;
-      for (int s = 0; s < S; s++) v += part[(static_cast<size_t>(s) * T + t) * Npad + n];
+      for (int s0 = 0; s0 < S; s0 += kSplitChunk) {
+        float x[kSplitChunk];
+#pragma unroll
+        for (int j = 0; j < kSplitChunk; j++) x[j] = s0 + j < S ? part[(static_cast<size_t>(s0 + j) * T + t) * Npad + n] : 0.f;
+#pragma unroll
+        for (int j = 0; j < kSplitChunk; j++)
+          if (s0 + j < S) v += x[j];
+      }
       float *o = epi.out_f + static_cast<size_t>(t) * epi.ld + n;
       if (epi.kind == kEpiAdd) *o += v;
       else *o = v;
@@ -409,13 +457,15 @@ void launch_splitk_reduce(const float *part, int S, int T, int Npad, const Epi &
   size_t total = static_cast<size_t>(T) * Npad;
   int blocks = static_cast<int>((total + 255) / 256);
   if (blocks > 148 * 16) blocks = 148 * 16;
-  splitk_reduce_kernel<<<blocks, 256, 0, s>>>(part, S, T, Npad, epi);
+  launch_pdl(splitk_reduce_kernel, blocks, 256, 0, s, part, S, T, Npad, epi);
 }
 
 // ----------------------------------------------------------------------------------------------------------------
 // argmax per row, first index of the maximum (torch.argmax); NaN never wins. With pick (a tensor-parallel rank's
 // vocabulary slice starting at row `offset`): the candidate (value bits, global index) instead of the index.
 __global__ void argmax_kernel(const float *logits, int V, int *out, int *pick, int offset) {
+  dep_wait();
+  dep_launch();
   int r = blockIdx.x;
   const float *row = logits + static_cast<size_t>(r) * V;
   float best = -INFINITY;
@@ -455,6 +505,8 @@ __global__ void argmax_kernel(const float *logits, int V, int *out, int *pick, i
 
 // the ranks' candidates [tp][R][2] -> the first index of the maximum over the whole vocabulary (slices ascend by rank)
 __global__ void argmax_merge_kernel(const int *pick, int tp, int R, int *out) {
+  dep_wait();
+  dep_launch();
   int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= R) return;
   float best = -INFINITY;
@@ -470,6 +522,8 @@ __global__ void argmax_merge_kernel(const int *pick, int tp, int R, int *out) {
 // a row's argmax in kArgChunks parts (one CTA each), then the first maximum of the parts (parts ascend in index)
 constexpr int kArgChunks = 8;
 __global__ void argmax_part_kernel(const float *logits, int V, int *pick) {
+  dep_wait();
+  dep_launch();
   const int r = blockIdx.x, c = blockIdx.y;
   const int per = (V + kArgChunks - 1) / kArgChunks;
   const int v0 = c * per, v1 = min(V, v0 + per);
@@ -508,14 +562,14 @@ __global__ void argmax_part_kernel(const float *logits, int V, int *pick) {
 void launch_argmax_merge(const int *pick, int tp, int R, int *out, cudaStream_t s);
 void launch_argmax(const float *logits, int R, int V, int *out, int *scratch, cudaStream_t s) {
   if (R <= 0) return;
-  argmax_part_kernel<<<dim3(R, kArgChunks), 512, 0, s>>>(logits, V, scratch);
+  launch_pdl(argmax_part_kernel, dim3(R, kArgChunks), 512, 0, s, logits, V, scratch);
   launch_argmax_merge(scratch, kArgChunks, R, out, s);
 }
 void launch_argmax_pick(const float *logits, int R, int V, int offset, int *pick, cudaStream_t s) {
-  if (R > 0) argmax_kernel<<<R, 1024, 0, s>>>(logits, V, nullptr, pick, offset);
+  if (R > 0) launch_pdl(argmax_kernel, R, 1024, 0, s, logits, V, static_cast<int *>(nullptr), pick, offset);
 }
 void launch_argmax_merge(const int *pick, int tp, int R, int *out, cudaStream_t s) {
-  if (R > 0) argmax_merge_kernel<<<(R + 127) / 128, 128, 0, s>>>(pick, tp, R, out);
+  if (R > 0) launch_pdl(argmax_merge_kernel, (R + 127) / 128, 128, 0, s, pick, tp, R, out);
 }
 
 // ----------------------------------------------------------------------------------------------------------------

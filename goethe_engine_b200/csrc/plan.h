@@ -57,6 +57,7 @@ struct PlanView {                   // device pointers into the plan buffer
   const int *want_tok;              // [R] step index of each wanted row's token
   int T, n_items, n_qg, n_work, R, n_parts;
   int max_rows;                     // most query rows (tokens x G) of any query group
+  int tree_cta;                     // 1: some attention CTA holds several tree nodes (private tail buffers needed)
 };
 
 }  // namespace gck

@@ -29,6 +29,10 @@
 
 using namespace gck;
 
+namespace gck {
+bool g_pdl = true;
+}
+
 namespace {
 
 thread_local std::string g_open_err;
@@ -203,12 +207,43 @@ uint16_t h_f32_to_f16(float f) {
   return *reinterpret_cast<uint16_t *>(&h);
 }
 
+// Split-K of a tcgen05 weight (one persistent CTA per SM takes units b, b + sms, ...; a unit is a 128-row band over one
+// K slice, slices differing by at most one 256-K tile). Chosen once per weight from its shape, never from the batch
+// (batch invariance), to minimise the estimated time of a decode step's launch in tile times (about 1 us each): the
+// busiest CTA's tiles, half a tile per unit (epilogue), and per slice the partials' write and read at 64 token rows
+// (64 x N x 8 B at about 5 TB/s), plus a reduce launch (about 4 tiles) when no later kernel sums the slices.
+int tc_splits(int NTW, int KT, int N, int sms, bool reader_sums) {
+  int best = 1;
+  double best_cost = 1e30;
+  for (int sp = 1; sp <= std::min(16, KT); sp++) {
+    const long units = static_cast<long>(NTW) * sp;
+    const int base = KT / sp, extra = KT % sp;
+    long max_tiles = 0, max_units = 0;
+    for (int b = 0; b < sms && b < units; b++) {
+      long tiles = 0, n = 0;
+      for (long u = b; u < units; u += sms, n++) tiles += base + ((u % sp) < extra ? 1 : 0);
+      max_tiles = std::max(max_tiles, tiles);
+      max_units = std::max(max_units, n);
+    }
+    double cost = static_cast<double>(max_tiles) + 0.5 * static_cast<double>(max_units);
+    if (sp > 1) cost += sp * (64.0 * N * 8.0 / 5e12 / 1.05e-6) + (reader_sums ? 0.0 : 4.0);
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = sp;
+    }
+  }
+  return best;
+}
+
 // Build the tiled layout of a weight whose logical row n maps to (source, source row) by `rowmap`, on the host, and
 // upload it. Tile (nt, kt) of kBM x kBK: Q4_K = 128 x 16 B headers then 128 x 128 B quants; Q8_0 = 128 x 8 fp16
 // scales then 128 x 256 int8; F16 = 128 x 256 halves. Rows past N and columns past K are zero (weights of 0).
 // k0: first source column (a tensor-parallel rank's slice of the input dimension; a multiple of 256 for Q4_K).
+// reader_sums: the kernel after this weight's GEMM sums its split-K partials (RoPE after q/k/v, RMSNorm after o_proj
+// and down_proj), so slices cost no reduce launch.
 template <typename RowMap>
-QWeight relayout(gc_handle *h, int type, int N, int K, RowMap rowmap, const char *what, int k0 = 0) {
+QWeight relayout(gc_handle *h, int type, int N, int K, RowMap rowmap, const char *what, int k0 = 0,
+                 bool reader_sums = true) {
   QWeight w;
   w.type = type == kF32 ? kF16 : type;
   w.N = N;
@@ -298,18 +333,7 @@ QWeight relayout(gc_handle *h, int type, int N, int K, RowMap rowmap, const char
       if (w.NT * sp >= 148) break;
     }
   } else {
-    // split-K (tcgen05 kernel, one CTA per SM): the fewest K slices whose NT x S work units fill the SMs' rounds to
-    // at least 90% (else the best fill); slices may differ by one raw tile. Fixed per weight: batch invariant.
-    int best = 1;
-    double best_eff = 0;
-    for (int sp = 1; sp <= std::min(16, w.KT); sp++) {
-      long units = static_cast<long>(w.NT) * sp;
-      long rounds = (units + h->sms - 1) / h->sms;
-      double eff = static_cast<double>(units) / static_cast<double>(rounds * h->sms);
-      if (eff > best_eff + 1e-9) { best_eff = eff; best = sp; }
-      if (eff >= 0.9) { best = sp; break; }
-    }
-    w.splits = best;
+    w.splits = tc_splits(w.NT, w.KT, N, h->sms, reader_sums);
   }
   return w;
 }
@@ -406,7 +430,7 @@ void load_model(gc_handle *h, const std::vector<std::unique_ptr<GgufFile>> &file
       t = w < 64 ? &tg : &tu;
       r = rk * Fr + std::min(f, Fr - 1);
       if (f >= Fr) t = nullptr;
-    }, "ffn_gate_up");
+    }, "ffn_gate_up", 0, false);
     ly.gu.N = 2 * Fp;
     ly.dn = relayout(h, static_cast<int>(td.type), h->d, Fr, [&](int n, const GgufTensor *&t, int &r) { t = &td; r = n; },
                      "ffn_down", rk * Fr);
@@ -421,7 +445,7 @@ void load_model(gc_handle *h, const std::vector<std::unique_ptr<GgufFile>> &file
   h->vocab0 = rk * Vr;
   h->vocab_rows = std::max(0, std::min(h->vocab, h->vocab0 + Vr) - h->vocab0);
   h->head = relayout(h, static_cast<int>(th.type), h->vocab_rows, h->d,
-                     [&](int n, const GgufTensor *&t, int &r) { t = &th; r = h->vocab0 + n; }, "output");
+                     [&](int n, const GgufTensor *&t, int &r) { t = &th; r = h->vocab0 + n; }, "output", 0, false);
   // tensor parallelism: o_proj and down_proj in one K slice each. Their split-K partials would cross NVLink in the
   // all-reduce (splits times the bytes), and a rank's slice of K is already N times shorter.
   if (N > 1)
@@ -712,6 +736,7 @@ GC_API int gc_open(const gc_open_params *p, gc_handle **out) {
     std::memcpy(&P, p, std::min<size_t>(p->size, sizeof P));
     if (p->size < offsetof(gc_open_params, pool_blocks) + sizeof(uint32_t)) fail(GC_E_ARG, "gc_open: struct size %u", p->size);
     if (P.flags & GC_OPEN_SPEC) fail(GC_E_UNSUPPORTED, "speculative pairs (GC_OPEN_SPEC) are not supported by this library");
+    if (const char *e = std::getenv("GCK_PDL")) g_pdl = std::atoi(e) != 0;
     if (!P.pack_dir) fail(GC_E_ARG, "gc_open: no pack_dir");
     if (!P.n_buckets || !P.buckets) fail(GC_E_ARG, "gc_open: no bucket ids");
     // manifest: the requested buckets
@@ -866,7 +891,7 @@ struct HostPlan {
   std::vector<QGroup> qgroups;
   std::vector<AttnWork> work;
   std::vector<unsigned> blocks;
-  int n_parts = 0, nw = 1;
+  int n_parts = 0, nw = 1, tree_cta = 0;
 };
 
 struct WorkIn {
@@ -924,6 +949,7 @@ void build_plan(gc_handle *h, const std::vector<WorkIn> &ws, HostPlan &pl) {
         q.path_off = poff[j]; q.path_len = plen[j];
         pl.qgroups.push_back(q);
       }
+      if (w.n > 1) multi = true;
     } else {
       for (uint32_t j = 0; j < w.n; j += QG) {
         QGroup q{};
@@ -943,7 +969,8 @@ void build_plan(gc_handle *h, const std::vector<WorkIn> &ws, HostPlan &pl) {
   }
   (void)G;
   pl.nw = multi ? 8 : 1;
-  // work: per item, kv head, split: chain groups of the item packed nw to a CTA, tree groups one to a CTA
+  // work: per item, kv head, split: the item's query groups (chain token groups or tree nodes) packed nw to a CTA, from
+  // the first that reaches the split (a tree node that does not idles in its CTA)
   for (size_t i = 0; i < pl.items.size(); i++) {
     int q0 = -1, q1 = -1;
     for (size_t k = 0; k < pl.qgroups.size(); k++)
@@ -955,17 +982,14 @@ void build_plan(gc_handle *h, const std::vector<WorkIn> &ws, HostPlan &pl) {
     for (int k = q0; k < q1; k++) maxs = std::max(maxs, pl.qgroups[k].nsplit);
     for (int head = 0; head < h->KVH; head++)
       for (int s = 0; s < maxs; s++) {
-        if (pl.items[i].tree) {
-          for (int k = q0; k < q1; k++)
-            if (s < pl.qgroups[k].nsplit) pl.work.push_back(AttnWork{k, 1, head, s});
-        } else {
-          int k = q0;
+        int k = q0;
+        while (k < q1) {
           while (k < q1 && pl.qgroups[k].nsplit <= s) k++;
-          while (k < q1) {
-            int n = std::min(pl.nw, q1 - k);
-            pl.work.push_back(AttnWork{k, n, head, s});
-            k += n;
-          }
+          if (k == q1) break;
+          int n = std::min(pl.nw, q1 - k);
+          pl.work.push_back(AttnWork{k, n, head, s});
+          if (pl.items[i].tree && pl.nw > 1) pl.tree_cta = 1;   // the kernel's tree warps use private tail buffers
+          k += n;
         }
       }
   }
@@ -1017,6 +1041,7 @@ PlanView upload_plan(gc_handle *h, HostPlan &pl) {
   pv.n_work = static_cast<int>(pl.work.size());
   pv.R = static_cast<int>(pl.want_tok.size());
   pv.n_parts = pl.n_parts;
+  pv.tree_cta = pl.tree_cta;
   pv.max_rows = 0;
   for (const QGroup &q : pl.qgroups) pv.max_rows = std::max(pv.max_rows, q.ntok * (h->H / h->KVH));
   return pv;

@@ -102,6 +102,39 @@ def test_tree_equals_chain_bitwise(small_model):
         assert np.array_equal(t2, c2)
 
 
+def test_tree_verify_shares_prefix_bitwise(small_model):
+    """A 16-node draft tree over a 1061-row prefix (three 512-entry splits, a prefix page shared with the tree's rows):
+    every node equals a chain decode of its path, bit for bit, whether the nodes share a CTA (8 warps over the prefix
+    pages, each walking its own path) or a node runs alone (one warp resolving every entry)."""
+    import random
+    pack, ws = small_model
+    rng = np.random.default_rng(5)
+    pre = [int(x) for x in rng.integers(1, 500, 1061)]
+    r, parents, depth = random.Random(1), [-1], [0]
+    for i in range(1, 16):
+        pj = r.choice([j for j in range(i) if depth[j] < 4])
+        parents.append(pj)
+        depth.append(depth[pj] + 1)
+    toks = [int(x) for x in rng.integers(1, 500, 16)]
+    pos = len(pre)
+    with backend(pack, ws, pool_blocks=256) as be:
+        ta, tb = list(range(0, 80)), list(range(80, 160))
+        be.step([gck.Work(1, pre, 0, ta, 0)])
+        be.step([gck.Work(2, pre, 0, tb, 0)])
+        tree = be.step([gck.Work(1, toks, pos, ta, 16, parents=parents)])
+        for j in range(16):
+            path = [j]
+            while parents[path[-1]] >= 0:
+                path.append(parents[path[-1]])
+            chain = be.step([gck.Work(2, [toks[k] for k in reversed(path)], pos, tb, 1)])
+            assert np.array_equal(tree[j], chain[0]), j
+        # the root alone (a one-warp launch) and beside a prefill chunk (8-warp CTAs, the tree warp on its tail path)
+        alone = be.step([gck.Work(1, toks[:1], pos, ta, 1, parents=[-1])])
+        mixed = be.step([gck.Work(3, pre[:40], 0, list(range(160, 164)), 1),
+                         gck.Work(1, toks[:1], pos, ta, 1, parents=[-1])])
+        assert np.array_equal(alone[0], tree[0]) and np.array_equal(mixed[1], tree[0])
+
+
 def test_batch_and_chunk_invariance_bitwise(small_model):
     pack, ws = small_model
     rng = np.random.default_rng(0)
