@@ -447,20 +447,42 @@ __global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn
   last = __shfl_sync(0xffffffffu, last, 0);
   if (!last) return;
   __threadfence();
-  const int pb0 = qg.part_base + head * qg.nsplit;
+  // the splits' (m, l) a lane each and their O rows kMergeChunk splits at a time are loaded together; the sums run in
+  // split order as before, so the loads are parallel and the arithmetic is unchanged
+  constexpr int kMergeChunk = 8;
+  const int pb0 = qg.part_base + head * qg.nsplit, S = qg.nsplit;
   for (int r = 0; r < rows; r++) {
     float m = -INFINITY;
-    for (int s = 0; s < qg.nsplit; s++) m = fmaxf(m, __ldcg(&a.part_ml[static_cast<size_t>(pb0 + s) * 16 + r]).x);
+    for (int s0 = 0; s0 < S; s0 += 32)
+      if (s0 + lane < S) m = fmaxf(m, __ldcg(&a.part_ml[static_cast<size_t>(pb0 + s0 + lane) * 16 + r]).x);
+    m = warp_max(m);
     float num[DH / 32], den = 0.f;
 #pragma unroll
     for (int k = 0; k < DH / 32; k++) num[k] = 0.f;
-    for (int s = 0; s < qg.nsplit; s++) {
-      const float2 ml = __ldcg(&a.part_ml[static_cast<size_t>(pb0 + s) * 16 + r]);
-      const float wgt = ml.x == -INFINITY ? 0.f : exp2f(ml.x - m);
-      const float *po = a.part_o + (static_cast<size_t>(pb0 + s) * 16 + r) * DH;
+    for (int s0 = 0; s0 < S; s0 += 32) {
+      const float2 ml = s0 + lane < S ? __ldcg(&a.part_ml[static_cast<size_t>(pb0 + s0 + lane) * 16 + r])
+                                      : make_float2(-INFINITY, 0.f);
+      const float w = ml.x == -INFINITY ? 0.f : exp2f(ml.x - m);
+      const int n = min(32, S - s0);
+      for (int j0 = 0; j0 < n; j0 += kMergeChunk) {
+        float po[kMergeChunk][DH / 32];
 #pragma unroll
-      for (int k = 0; k < DH / 32; k++) num[k] += __ldcg(po + lane + 32 * k) * wgt;
-      den += ml.y * wgt;
+        for (int j = 0; j < kMergeChunk; j++) {
+          const float *src = a.part_o + (static_cast<size_t>(pb0 + s0 + j0 + j) * 16 + r) * DH;
+#pragma unroll
+          for (int k = 0; k < DH / 32; k++) po[j][k] = j0 + j < n ? __ldcg(src + lane + 32 * k) : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < kMergeChunk; j++) {
+          const float wj = __shfl_sync(0xffffffffu, w, (j0 + j) & 31);
+          const float lj = __shfl_sync(0xffffffffu, ml.y, (j0 + j) & 31);
+          if (j0 + j < n) {
+#pragma unroll
+            for (int k = 0; k < DH / 32; k++) num[k] += po[j][k] * wj;
+            den += lj * wj;
+          }
+        }
+      }
     }
     const int tok = it.tok0 + qg.j0 + r / G, qo = head * G + r % G;
     __half *dst = a.out + (static_cast<size_t>(tok) * a.H + qo) * DH;

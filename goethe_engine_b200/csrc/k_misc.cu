@@ -300,88 +300,107 @@ struct QkvSrc {
   }
 };
 
-__device__ void rope_pair(const QkvSrc &q, int t, int c0, const float2 *cs, int i, float &a, float &b) {
-  const float2 x = q.pair(t, c0 + 2 * i);
-  const float x0 = x.x, x1 = x.y;
-  float2 c = cs[i];
-  a = x0 * c.x - x1 * c.y;
-  b = x0 * c.y + x1 * c.x;
+// RoPE of one (even, odd) pair, rounded step by step (no contraction), so that every kernel site that rotates a row
+// gets the same bits: the writer of a page's first row and the later rows of that page agree on its exponent
+__device__ __forceinline__ float2 rot(float2 x, float2 c) {
+  return make_float2(__fsub_rn(__fmul_rn(x.x, c.x), __fmul_rn(x.y, c.y)),
+                     __fadd_rn(__fmul_rn(x.x, c.y), __fmul_rn(x.y, c.x)));
 }
 
+// amax of row t's (rotated) k or v head at columns c0..: a warp reads it again (a page's first row from another token)
 template <int DH>
-__device__ float head_amax(const QkvSrc &q, int t, int c0, const float2 *cs, bool rot) {
+__device__ float head_amax(const QkvSrc &q, int t, int c0, const float2 *cs, bool rotate) {
   float m = 0.f;
   for (int i = threadIdx.x % 32; i < DH / 2; i += 32) {
-    float a, b;
-    if (rot) rope_pair(q, t, c0, cs, i, a, b);
-    else { const float2 x = q.pair(t, c0 + 2 * i); a = x.x; b = x.y; }
-    m = fmaxf(m, fmaxf(fabsf(a), fabsf(b)));
+    float2 v = q.pair(t, c0 + 2 * i);
+    if (rotate) v = rot(v, cs[i]);
+    m = fmaxf(m, fmaxf(fabsf(v.x), fabsf(v.y)));
   }
   return warp_max(m);
 }
 
+// One warp per (token, head): q heads are rotated into q (f16); kv heads are rotated (k) and written to the token's
+// page row (f16, or e4m3 with the page's exponents). Every input of the warp is loaded before its first store.
 template <int DH>
 __global__ void rope_kv_kernel(PlanView pv, QkvSrc qs, int H, int KVH, const float2 *rope_tab, __half *q, void *kc,
                                void *vc, int8_t *exps, int kv_fp8, int page_scale) {
   dep_wait();
   dep_launch();
-  int t = blockIdx.x;
-  int hh = threadIdx.x / 32 + blockIdx.y * (blockDim.x / 32);  // head slot: [0, H) q heads, [H, H + KVH) kv heads
+  constexpr int NP = DH / 64;   // (even, odd) pairs per lane: pair i = lane + 32 p
+  const int t = blockIdx.x;
+  const int hh = threadIdx.x / 32 + blockIdx.y * (blockDim.x / 32);  // head slot: [0, H) q heads, [H, H + KVH) kv
   if (hh >= H + KVH) return;
-  int lane = threadIdx.x % 32;
-  const float2 *cs = rope_tab + static_cast<size_t>(pv.rope_pos[t]) * (DH / 2);
-  if (hh < H) {
+  const int lane = threadIdx.x % 32;
+  const bool is_q = hh < H;
+  const int h = hh - H;
+  const int c0 = is_q ? hh * DH : (H + h) * DH, vcol = (H + KVH + h) * DH;
+  const bool fp8_page = !is_q && kv_fp8 && page_scale;
+  // plan entries, the head's q/k and v columns, the rotation table: all issued together
+  const int pos = pv.rope_pos[t];
+  const int r = is_q ? 0 : pv.kv_row[t];
+  const int ft = fp8_page ? pv.first_tok[t] : -1;
+  float2 x[NP], xv[NP], c[NP];
+#pragma unroll
+  for (int p = 0; p < NP; p++) x[p] = qs.pair(t, c0 + 2 * (lane + 32 * p));
+  if (!is_q) {
+#pragma unroll
+    for (int p = 0; p < NP; p++) xv[p] = qs.pair(t, vcol + 2 * (lane + 32 * p));
+  }
+  const float2 *cs = rope_tab + static_cast<size_t>(pos) * (DH / 2);
+#pragma unroll
+  for (int p = 0; p < NP; p++) c[p] = cs[lane + 32 * p];
+#pragma unroll
+  for (int p = 0; p < NP; p++) x[p] = rot(x[p], c[p]);
+  if (is_q) {
     __half2 *dst = reinterpret_cast<__half2 *>(q + (static_cast<size_t>(t) * H + hh) * DH);
-    for (int i = lane; i < DH / 2; i += 32) {
-      float a, b;
-      rope_pair(qs, t, hh * DH, cs, i, a, b);
-      dst[i] = __floats2half2_rn(a, b);
-    }
+#pragma unroll
+    for (int p = 0; p < NP; p++) dst[lane + 32 * p] = __floats2half2_rn(x[p].x, x[p].y);
     return;
   }
-  int h = hh - H;
-  const int kcol = H * DH + h * DH, vcol = (H + KVH) * DH + h * DH;
-  int r = pv.kv_row[t];
-  int blk = r / kBlock, rip = r % kBlock;
-  size_t off = ((static_cast<size_t>(blk) * KVH + h) * kBlock + rip) * DH;
+  const int blk = r / kBlock, rip = r % kBlock;
+  const size_t off = ((static_cast<size_t>(blk) * KVH + h) * kBlock + rip) * DH;
   if (!kv_fp8) {
     __half2 *kd = reinterpret_cast<__half2 *>(static_cast<__half *>(kc) + off);
     __half2 *vd = reinterpret_cast<__half2 *>(static_cast<__half *>(vc) + off);
-    for (int i = lane; i < DH / 2; i += 32) {
-      float a, b;
-      rope_pair(qs, t, kcol, cs, i, a, b);
-      kd[i] = __floats2half2_rn(a, b);
-      const float2 x = qs.pair(t, vcol + 2 * i);
-      vd[i] = __floats2half2_rn(x.x, x.y);
+#pragma unroll
+    for (int p = 0; p < NP; p++) {
+      kd[lane + 32 * p] = __floats2half2_rn(x[p].x, x[p].y);
+      vd[lane + 32 * p] = __floats2half2_rn(xv[p].x, xv[p].y);
     }
     return;
   }
   int ek = 0, ev = 0;
   if (page_scale) {
-    int ft = pv.first_tok[t];
     int8_t *pe = exps + (static_cast<size_t>(blk) * KVH + h) * 2;
-    if (ft >= 0) {
-      // the page's first row is written in this step (possibly by this token): derive its exponents
+    if (ft == t) {
+      // this token's row is its page's first: the exponents come from its own rotated k and its v
+      float mk = 0.f, mv = 0.f;
+#pragma unroll
+      for (int p = 0; p < NP; p++) {
+        mk = fmaxf(mk, fmaxf(fabsf(x[p].x), fabsf(x[p].y)));
+        mv = fmaxf(mv, fmaxf(fabsf(xv[p].x), fabsf(xv[p].y)));
+      }
+      ek = page_exp(warp_max(mk));
+      ev = page_exp(warp_max(mv));
+      if (lane == 0) { pe[0] = static_cast<int8_t>(ek); pe[1] = static_cast<int8_t>(ev); }
+    } else if (ft >= 0) {
+      // the page's first row is written in this step by token ft: derive its exponents from that row
       const float2 *fcs = rope_tab + static_cast<size_t>(pv.rope_pos[ft]) * (DH / 2);
-      ek = page_exp(head_amax<DH>(qs, ft, kcol, fcs, true));
+      ek = page_exp(head_amax<DH>(qs, ft, c0, fcs, true));
       ev = page_exp(head_amax<DH>(qs, ft, vcol, fcs, false));
-      if (ft == t && lane == 0) { pe[0] = static_cast<int8_t>(ek); pe[1] = static_cast<int8_t>(ev); }
     } else {
       ek = pe[0];
       ev = pe[1];
     }
   }
-  float sk = exp2f(static_cast<float>(ek)), sv = exp2f(static_cast<float>(ev));
-  uint8_t *kd = static_cast<uint8_t *>(kc) + off;
-  uint8_t *vd = static_cast<uint8_t *>(vc) + off;
-  for (int i = lane; i < DH / 2; i += 32) {
-    float a, b;
-    rope_pair(qs, t, kcol, cs, i, a, b);
-    kd[2 * i] = f32_to_e4m3(a * sk);
-    kd[2 * i + 1] = f32_to_e4m3(b * sk);
-    const float2 x = qs.pair(t, vcol + 2 * i);
-    vd[2 * i] = f32_to_e4m3(x.x * sv);
-    vd[2 * i + 1] = f32_to_e4m3(x.y * sv);
+  const float sk = exp2f(static_cast<float>(ek)), sv = exp2f(static_cast<float>(ev));
+  uint16_t *kd = reinterpret_cast<uint16_t *>(static_cast<uint8_t *>(kc) + off);
+  uint16_t *vd = reinterpret_cast<uint16_t *>(static_cast<uint8_t *>(vc) + off);
+#pragma unroll
+  for (int p = 0; p < NP; p++) {
+    const int i = lane + 32 * p;
+    kd[i] = static_cast<uint16_t>(f32_to_e4m3(x[p].x * sk) | (f32_to_e4m3(x[p].y * sk) << 8));
+    vd[i] = static_cast<uint16_t>(f32_to_e4m3(xv[p].x * sv) | (f32_to_e4m3(xv[p].y * sv) << 8));
   }
 }
 
