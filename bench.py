@@ -354,14 +354,14 @@ def cpu_baseline(args):
 SPEC8B_Q8 = dict(SPEC8B, wtype="q8_0", ctx=4096, name="llama3-8b-shape-q80")
 
 
-def open_q8(tune, ncol):
-    """The 8B shape with Q8_0 weights (C2, C4) and f16 KV; returns (backend, dir)."""
+def open_q8(tune, ncol, bucket="b200.BI.main", **extra):
+    """The 8B shape with Q8_0 weights (C2, C4) and f16 KV in one bucket; returns (pack dir, [weights])."""
     from goethe_engine_b200 import build, gck, synth
     build.build()
     spec = synth.Spec(**SPEC8B_Q8)
     d = os.path.join(os.environ.get("GCK_BENCH_DIR", "/tmp/gck_bench"), f"{spec.name}-s{spec.seed}")
     t0 = time.time()
-    synth.make(d, spec, buckets=[dict(id="b200.BI.main", ncol=ncol, maxctx=spec.ctx, kv="f16", tune=tune)])
+    synth.make(d, spec, buckets=[dict(id=bucket, ncol=ncol, maxctx=spec.ctx, kv="f16", tune=tune, **extra)])
     print(f"[bench] model ready in {d} ({time.time() - t0:.1f}s)", file=sys.stderr, flush=True)
     return d, [os.path.join(d, "model.gguf")]
 
@@ -397,13 +397,14 @@ def print_classes(st, steps, label=""):
 
 def run_c2(args):
     """C2: the 8B shape, Q8_0 weights, f16 KV, one sequence decoding at context 2048 (HBM-bound: every weight byte and
-    the KV once per token)."""
+    the KV once per token). A single-stream bucket (ncol 1, not batched) with "tolerance" determinism, the one the
+    reference's single-stream selection takes for one sequence (pack.py:619-633): its decode runs the GEMV."""
     import torch
     from goethe_engine_b200 import gck
-    d, ws = open_q8(dict(max_cols=2048), 1)
+    d, ws = open_q8(dict(max_cols=2048), 1, bucket="b200.FAST.single", determinism="tolerance", batch=False)
     ctx, steps_total = 2048, args.warmup + args.steps
     per_seq = -(-(ctx + steps_total + 1) // 16)
-    be = gck.Backend(d, ws, pool_blocks=per_seq + 4)
+    be = gck.Backend(d, ws, buckets=("b200.FAST.single",), pool_blocks=per_seq + 4)
     on, read = stats_api(be)
     rng = np.random.default_rng(0)
     toks = [int(x) for x in rng.integers(1, 128000, ctx)]
@@ -415,10 +416,15 @@ def run_c2(args):
         pos += 1
     torch.cuda.synchronize()
     on(args.profile)
+    window = bool(os.environ.get("GCK_PROFILE_WINDOW"))   # the CUDA profiler window covers the first timed step
     with Clocks(0) as clk:
         t0 = time.perf_counter()
-        for _ in range(args.steps):
+        for k in range(args.steps):
+            if window and k == 0:
+                torch.cuda.profiler.start()
             last = be.step([gck.Work(0, [last], pos, tab, 1, greedy=True)])[0][0]
+            if window and k == 0:
+                torch.cuda.profiler.stop()
             pos += 1
         wall = time.perf_counter() - t0
     st = read()
@@ -436,6 +442,7 @@ def run_c2(args):
         "scaling": "weak", "vs_baseline": None, "dtype": "q8_0 x f16 -> f32; f16 KV",
         "data": "synthetic (seeded N(0,0.02) weights, uniform tokens)",
         "config": {"workload": "C2: Llama-3-8B shape, Q8_0 weights, a16, f16 paged KV, one sequence at context 2048",
+                   "bucket": "single-stream, determinism tolerance (GEMV decode)",
                    "batch": 1, "context": ctx, "l2": "inputs larger than L2, no flush"},
         "e2e": {"value": round(args.steps / wall, 2), "unit": "tok/s", "h2d_bytes_per_step": int(per_seq * 4 + 64),
                 "d2h_bytes_per_step": 4, "path": "gc_step through the C ABI (ctypes), host buffers"},
@@ -464,10 +471,15 @@ def run_c4(args):
     be.release(99)
     torch.cuda.synchronize()
     on(args.profile)
+    window = bool(os.environ.get("GCK_PROFILE_WINDOW"))   # the CUDA profiler window: the first prefill, the first verify
     with Clocks(0) as clk:
         t0 = time.perf_counter()
         for i in range(n_seq):
+            if window and i == 0:
+                torch.cuda.profiler.start()
             be.step([gck.Work(i, toks[i], 0, tabs[i], 1, greedy=True)])
+            if window and i == 0:
+                torch.cuda.profiler.stop()
         wall_p = time.perf_counter() - t0
     st_p = read()
     if args.profile:
@@ -487,8 +499,12 @@ def run_c4(args):
     be.step(verify)                      # warm
     on(args.profile)
     t0 = time.perf_counter()
-    for _ in range(args.steps):
+    for k in range(args.steps):
+        if window and k == 0:
+            torch.cuda.profiler.start()
         be.step(verify)
+        if window and k == 0:
+            torch.cuda.profiler.stop()
     wall_v = time.perf_counter() - t0
     st_v = read()
     if args.profile:

@@ -20,7 +20,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden", "--expt-relaxed-constexpr",
          "-I", CSRC, "-I", os.path.join(ROOT, "include")]
-SOURCES = ["runtime.cu", "k_misc.cu", "k_gemm.cu", "k_gemm_tc.cu", "k_attn.cu"]
+SOURCES = ["runtime.cu", "k_misc.cu", "k_gemm.cu", "k_gemm_tc.cu", "k_gemv.cu", "k_attn.cu"]
 
 
 def _run(cmd):

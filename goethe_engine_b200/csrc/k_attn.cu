@@ -6,7 +6,8 @@
 //
 // Work decomposition. A warp owns up to 16 query rows: the G = H / KVH query heads of one kv head for up to 16 / G
 // consecutive chain tokens of one item (a prefill chunk), or one token (decode, tree node). It walks the token's
-// visible list in fixed groups of 16 entries and fixed splits of kSplit entries; the last CTA of a (query group, kv
+// visible list in fixed groups of 16 entries and fixed splits of pv.split entries (kSplit in batch-invariant buckets);
+// the last CTA of a (query group, kv
 // head) to finish merges the splits' partials in split order. A split's groups are resolved to pages once (block
 // table; a tree token's own rows through its path); groups' K and V rows are gathered with cp.async, double
 // buffered (decode warps: 20 resident per SM at <= 96 registers); a CTA of several warps shares them when its warps
@@ -87,7 +88,7 @@ __global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn
   const Item it = pv.items[q0.item];
   int nvis_max = 0;
   for (int i = 0; i < w.nqg; i++) nvis_max = max(nvis_max, pv.qgroups[w.qg0 + i].nvis);
-  const int lo = w.split * kSplit, hi = min(lo + kSplit, nvis_max);
+  const int lo = w.split * pv.split, hi = min(lo + pv.split, nvis_max);
   // a CTA of several tree nodes shares only the groups of plain rows below the item's own rows; each warp then walks
   // the groups that reach its own path (its tail) from a private buffer, in the same order a lone warp would
   const bool tree_cta = NW > 1 && q0.path_len > 0;
@@ -380,7 +381,7 @@ __global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn
       uint8_t *tK = sm + C::TAIL_OFF + warp * C::TAIL_B;
       uint8_t *tV = tK + kGroup * C::ROWB;
       int8_t *tE = reinterpret_cast<int8_t *>(tK + C::BUF);
-      const int hiw = min(lo + kSplit, qg.nvis);
+      const int hiw = min(lo + pv.split, qg.nvis);
       for (int i0 = max(lo, shared_hi); i0 < hiw; i0 += kGroup) {
         for (int c = lane; c < 2 * kGroup * C::CHUNKS; c += 32) {
           const int isv = c / (kGroup * C::CHUNKS), rem = c % (kGroup * C::CHUNKS);

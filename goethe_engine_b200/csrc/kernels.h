@@ -45,6 +45,7 @@ struct QWeight {            // a relaid-out weight on the device
   int N = 0, K = 0;         // logical rows (outputs) and columns (inputs)
   int NT = 0, KT = 0;       // tiles
   int splits = 1;           // split-K factor (fixed per weight: batch invariant)
+  int gslices = 1;          // K slices of the GEMV (tolerance buckets, a few token rows)
 };
 
 // Tensor parallelism: a deterministic all-reduce of the ranks' [T, d] f32 partials over peer memory (NVLink), in two
@@ -117,6 +118,13 @@ void launch_commit(const int *moves, int n, int L, int KVH, int dh, uint8_t *kc,
 // tiles come through TMA tensor maps over the activation buffer, one map per token tile size.
 void gemm_init();   // once per device, before the first launch_gemm
 void launch_gemm(const QWeight &w, const __half *act, int T, const Epi &epi, float *part, cudaStream_t s);
+
+// GEMV over Q4_K / Q8_0 tiles for T <= kGemvMaxT token rows: x [T, ldx] f16; gs K slices (partials [gs][T][Npad] when
+// gs > 1, else the epilogue)
+constexpr int kGemvMaxT = 4;
+int gemv_slices(int NTW, int KT, int sms, bool reader_sums);
+void launch_gemv(const QWeight &w, int gs, const __half *x, int ldx, int T, const Epi &epi, float *part,
+                 cudaStream_t s);
 
 struct TmaSet {            // tensor maps over one activation buffer [rows, K] f16, boxes of 64 K x {16..256} rows
   CUtensorMap m[5];

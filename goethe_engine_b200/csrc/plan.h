@@ -31,7 +31,7 @@ struct QGroup {                     // up to 16/G consecutive chain tokens of on
   int j0;                           // first token (index within the item)
   int ntok;
   int nvis;                         // list length of the group's last token
-  int nsplit;                       // ceil(nvis / kSplit)
+  int nsplit;                       // ceil(nvis / split)
   int part_base;                    // partial slot of (head 0, split 0); (head h, split s) = base + h * nsplit + s
   int path_off;                     // tree token: its path (token indices within the item, root .. self) in plan.paths
   int path_len;                     // tree token: depth + 1; chain: 0
@@ -58,6 +58,8 @@ struct PlanView {                   // device pointers into the plan buffer
   int T, n_items, n_qg, n_work, R, n_parts;
   int max_rows;                     // most query rows (tokens x G) of any query group
   int tree_cta;                     // 1: some attention CTA holds several tree nodes (private tail buffers needed)
+  int split;                        // list entries per split: kSplit, or (tolerance buckets, few rows of work) a
+                                    // shorter power of two, at least 64
 };
 
 }  // namespace gck

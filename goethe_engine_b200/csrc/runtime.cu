@@ -112,6 +112,7 @@ struct gc_handle {
   size_t page_bytes = 0, layer_bytes = 0, exps_layer = 0;
   // limits
   int max_seqs = 0, max_cols = 0, max_ctx = 0, qg_tokens = 1;
+  int gemv_max_t = 0;                       // tolerance buckets: steps of up to this many token rows run the GEMV
   // scratch
   float *x = nullptr, *qkv = nullptr, *logits = nullptr, *part = nullptr, *attn_o = nullptr, *commit_tmp = nullptr;
   __half *h = nullptr, *q = nullptr, *att = nullptr, *act = nullptr;
@@ -334,6 +335,7 @@ QWeight relayout(gc_handle *h, int type, int N, int K, RowMap rowmap, const char
     }
   } else {
     w.splits = tc_splits(w.NT, w.KT, N, h->sms, reader_sums);
+    w.gslices = gemv_slices(w.NT, w.KT, h->sms, reader_sums);
   }
   return w;
 }
@@ -560,6 +562,7 @@ namespace {
 
 struct OpenCfg {
   int ncol = 0, maxctx = 0, max_cols = 0, pool_tune = 0, tp = 1;
+  bool tolerance = true;   // every opened bucket's determinism is "tolerance" (the GEMV for a few token rows)
   uint32_t pool_blocks = 0;
   std::string kv, kv_scale;
 };
@@ -584,6 +587,8 @@ void open_device(gc_handle *h, int dev, const std::vector<std::unique_ptr<GgufFi
   h->max_cols = c.max_cols > 0 ? c.max_cols : 2048;
   h->kv_fp8 = c.kv == "fp8";
   h->page_scale = h->kv_fp8 && c.kv_scale != "unit";
+  // batch-invariant buckets run the tcgen05 GEMM at every width (a row's arithmetic never depends on the batch)
+  h->gemv_max_t = c.tolerance && c.tp == 1 ? kGemvMaxT : 0;
   build_rope(h);
   // KV pool: [L][nblk][KVH][16][dh] for K and for V, plus fp8 page exponents [L][nblk][KVH][2]
   const size_t esz = h->kv_fp8 ? 1 : 2;
@@ -762,6 +767,7 @@ GC_API int gc_open(const gc_open_params *p, gc_handle **out) {
       std::string bkv = b->str_or("kv", "f16");
       if (!c.kv.empty() && bkv != c.kv) fail(GC_E_MANIFEST, "buckets disagree on the KV dtype");
       c.kv = bkv;
+      c.tolerance = c.tolerance && b->str_or("determinism", "batch_invariant") == "tolerance";
       const int btp = static_cast<int>(b->num_or("tp", 1));
       if (i && btp != c.tp) fail(GC_E_MANIFEST, "buckets disagree on the tensor-parallel degree");
       c.tp = btp;
@@ -891,7 +897,7 @@ struct HostPlan {
   std::vector<QGroup> qgroups;
   std::vector<AttnWork> work;
   std::vector<unsigned> blocks;
-  int n_parts = 0, nw = 1, tree_cta = 0;
+  int n_parts = 0, nw = 1, tree_cta = 0, split = kSplit;
 };
 
 struct WorkIn {
@@ -959,13 +965,23 @@ void build_plan(gc_handle *h, const std::vector<WorkIn> &ws, HostPlan &pl) {
       }
       if (pl.qgroups.size() - qfirst > 1) multi = true;
     }
-    for (size_t k = qfirst; k < pl.qgroups.size(); k++) {
-      QGroup &q = pl.qgroups[k];
-      q.nsplit = (q.nvis + kSplit - 1) / kSplit;
-      q.part_base = pl.n_parts;
-      pl.n_parts += h->KVH * q.nsplit;
-    }
     T += static_cast<int>(w.n);
+  }
+  // splits: kSplit entries; a tolerance bucket's step with little attention work (fewer than two single-warp CTAs per
+  // SM) takes shorter splits, down to 64 entries, so that one sequence still spreads over the SMs
+  pl.split = kSplit;
+  if (h->gemv_max_t > 0) {
+    auto ctas = [&](int sp) {
+      long n = 0;
+      for (const QGroup &q : pl.qgroups) n += (q.nvis + sp - 1) / sp;
+      return n * h->KVH;
+    };
+    while (pl.split > 64 && ctas(pl.split) < 2L * h->sms) pl.split /= 2;
+  }
+  for (QGroup &q : pl.qgroups) {
+    q.nsplit = (q.nvis + pl.split - 1) / pl.split;
+    q.part_base = pl.n_parts;
+    pl.n_parts += h->KVH * q.nsplit;
   }
   (void)G;
   pl.nw = multi ? 8 : 1;
@@ -1042,6 +1058,7 @@ PlanView upload_plan(gc_handle *h, HostPlan &pl) {
   pv.R = static_cast<int>(pl.want_tok.size());
   pv.n_parts = pl.n_parts;
   pv.tree_cta = pl.tree_cta;
+  pv.split = pl.split;
   pv.max_rows = 0;
   for (const QGroup &q : pl.qgroups) pv.max_rows = std::max(pv.max_rows, q.ntok * (h->H / h->KVH));
   return pv;
@@ -1051,11 +1068,16 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
   const int T = pv.T;
   cudaStream_t s = h->st;
   // split-K and attention scratch for this step's sizes
+  // a GEMM of `rows` token rows: the GEMV (tolerance buckets, a few rows, quantized weights) or the tensor-core GEMM;
+  // its split-K slices (partials for the next kernel) either way
+  auto use_gemv = [&](const QWeight &w, int rows) { return rows > 0 && rows <= h->gemv_max_t && w.type != kF16; };
+  auto slices = [&](const QWeight &w, int rows) { return use_gemv(w, rows) ? w.gslices : w.splits; };
   size_t need = 0;
   for (auto &ly : h->layers)
     for (const QWeight *w : {&ly.qkv, &ly.o, &ly.gu, &ly.dn})
-      if (w->splits > 1) need = std::max(need, static_cast<size_t>(w->splits) * T * w->NT * kBM * 4);
-  if (h->head.splits > 1) need = std::max(need, static_cast<size_t>(h->head.splits) * pv.R * h->head.NT * kBM * 4);
+      if (slices(*w, T) > 1) need = std::max(need, static_cast<size_t>(slices(*w, T)) * T * w->NT * kBM * 4);
+  if (slices(h->head, pv.R) > 1)
+    need = std::max(need, static_cast<size_t>(slices(h->head, pv.R)) * pv.R * h->head.NT * kBM * 4);
   h->part = grow(h, h->part, h->part_cap, need, "split-K scratch");
   if (static_cast<size_t>(pv.n_parts) > h->attn_parts_cap) {
     cudaStreamSynchronize(s);
@@ -1095,14 +1117,16 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
   };
   // A GEMM under class cls. With split-K it writes partials; their reader sums them in split order: the RMSNorm after
   // a residual-add projection (o_proj, down_proj), the RoPE kernel after q/k/v, else a reduce launch (GCK_K_REDUCE).
-  auto gemm = [&](int cls, const QWeight &w, const TmaSet &ts, const __half *act, int rows, const Epi &e,
+  auto gemm = [&](int cls, const QWeight &w, const TmaSet &ts, const __half *act, int ldx, int rows, const Epi &e,
                   bool reader_reduces) {
     run(cls, 1, [&] {
-      if (w.type == kF16) launch_gemm(w, act, rows, e, h->part, s);
+      if (use_gemv(w, rows)) launch_gemv(w, w.gslices, act, ldx, rows, e, h->part, s);
+      else if (w.type == kF16) launch_gemm(w, act, rows, e, h->part, s);
       else launch_gemm_tc(w, ts, rows, e, h->part, h->kerr, h->sms, s);
     });
-    if (w.splits > 1 && rows > 0 && !reader_reduces)
-      run(GCK_K_REDUCE, 1, [&] { launch_splitk_reduce(h->part, w.splits, rows, w.NT * kBM, e, s); });
+    const int sl = slices(w, rows);
+    if (sl > 1 && rows > 0 && !reader_reduces)
+      run(GCK_K_REDUCE, 1, [&] { launch_splitk_reduce(h->part, sl, rows, w.NT * kBM, e, s); });
   };
   // residual contributions waiting for the next RMSNorm: the split-K partials of the last o_proj / down_proj, or (tensor
   // parallelism) its all-reduced output
@@ -1122,7 +1146,7 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
     pend_s = 0;
     pend_tp = false;
   };
-  auto residual = [&](int cls, const QWeight &w, const TmaSet &ts, const __half *act) {
+  auto residual = [&](int cls, const QWeight &w, const TmaSet &ts, const __half *act, int ldx) {
     if (h->tp > 1 && h->tp_p2p) {
       // this rank's share of the projection into buffer b; then the ranks' deterministic sum over peer memory: flag,
       // reduce-scatter of the rows this rank owns, flag; the next RMSNorm gathers each row's sum from its owner
@@ -1134,7 +1158,7 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
         // the rank's split-K partials [splits][T][d] (or its output) straight into buffer b; publishes phase 1
         run(cls, 1, [&] { launch_gemm_tc(w, ts, T, e, h->tp_bufs[b], h->kerr, h->sms, s, s1); });
       } else {
-        gemm(cls, w, ts, act, T, e, false);
+        gemm(cls, w, ts, act, ldx, T, e, false);
         run(GCK_K_ALLREDUCE, 1, [&] { launch_tp_signal(s1.flag, s1.value, s); });
       }
       const int sp = w.type != kF16 ? w.splits : 1;
@@ -1146,7 +1170,7 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
     }
     if (h->tp > 1) {
       // this rank's share of the projection (its input columns), summed over the ranks in place
-      gemm(cls, w, ts, act, T, Epi{kEpiStore, h->d, h->d, h->tp_y, nullptr}, false);
+      gemm(cls, w, ts, act, ldx, T, Epi{kEpiStore, h->d, h->d, h->tp_y, nullptr}, false);
       run(GCK_K_ALLREDUCE, 1, [&] {
         nck(nccl().all_reduce(h->tp_y, h->tp_y, static_cast<size_t>(T) * h->d, ncclFloat, ncclSum,
                               static_cast<ncclComm_t>(h->comm), s), "all-reduce");
@@ -1156,10 +1180,10 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
       pend_ld = h->d;
       return;
     }
-    gemm(cls, w, ts, act, T, Epi{kEpiAdd, h->d, h->d, h->x, nullptr}, true);
-    if (w.splits > 1) {
+    gemm(cls, w, ts, act, ldx, T, Epi{kEpiAdd, h->d, h->d, h->x, nullptr}, true);
+    if (slices(w, T) > 1) {
       pend = h->part;
-      pend_s = w.splits;
+      pend_s = slices(w, T);
       pend_ld = w.NT * kBM;
     }
   };
@@ -1180,27 +1204,28 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
   for (int l = 0; l < h->L; l++) {
     const Layer &ly = h->layers[l];
     norm(nullptr, T, ly.attn_norm);
-    gemm(GCK_K_QKV, ly.qkv, h->tma_h, h->h, T, Epi{kEpiStore, wq, wq, h->qkv, nullptr}, true);
+    gemm(GCK_K_QKV, ly.qkv, h->tma_h, h->h, h->d, T, Epi{kEpiStore, wq, wq, h->qkv, nullptr}, true);
     uint8_t *kc = h->kc + l * h->layer_bytes, *vc = h->vc + l * h->layer_bytes;
     int8_t *ex = h->exps ? h->exps + l * h->exps_layer : nullptr;
-    const bool qsplit = ly.qkv.splits > 1;
+    const int qs = slices(ly.qkv, T);
+    const bool qsplit = qs > 1;
     run(GCK_K_ROPE, 1, [&] {
-      launch_rope_kv(pv, qsplit ? h->part : h->qkv, ly.qkv.splits, qsplit ? ly.qkv.NT * kBM : wq, h->H, h->KVH, h->dh,
+      launch_rope_kv(pv, qsplit ? h->part : h->qkv, qs, qsplit ? ly.qkv.NT * kBM : wq, h->H, h->KVH, h->dh,
                      h->rope, h->q, kc, vc, ex, h->kv_fp8, h->page_scale, s);
     });
     aa.kc = kc;
     aa.vc = vc;
     aa.exps = h->page_scale ? ex : nullptr;
     run(GCK_K_ATTN, 1, [&] { launch_attention(pv, aa, nw, s); });
-    residual(GCK_K_O, ly.o, h->tma_att, h->att);
+    residual(GCK_K_O, ly.o, h->tma_att, h->att, h->H * h->dh);
     norm(nullptr, T, ly.ffn_norm);
-    gemm(GCK_K_GATEUP, ly.gu, h->tma_h, h->h, T, Epi{kEpiSwiGLU, h->F, ly.dn.KT * kBK, nullptr, h->act}, false);
-    residual(GCK_K_DOWN, ly.dn, h->tma_act, h->act);
+    gemm(GCK_K_GATEUP, ly.gu, h->tma_h, h->h, h->d, T, Epi{kEpiSwiGLU, h->F, ly.dn.KT * kBK, nullptr, h->act}, false);
+    residual(GCK_K_DOWN, ly.dn, h->tma_act, h->act, ly.dn.KT * kBK);
   }
   if (pv.R > 0) {
     norm(pv.want_tok, pv.R, h->out_norm);
-    gemm(GCK_K_HEAD, h->head, h->tma_h, h->h, pv.R, Epi{kEpiStore, h->vocab_rows, h->vocab_rows, h->logits, nullptr},
-         false);
+    gemm(GCK_K_HEAD, h->head, h->tma_h, h->h, h->d, pv.R,
+         Epi{kEpiStore, h->vocab_rows, h->vocab_rows, h->logits, nullptr}, false);
   }
 }
 

@@ -159,22 +159,24 @@ def write_gguf(spec, path):
 
 
 def pack_dir(d, spec, buckets, weights_file="model.gguf"):
-    """Write d/manifest.json for the given buckets: [{id, ncol, maxctx, kv, tune, tp}] (tune: the library's knobs; tp: the
-    tensor-parallel degree, 1 when absent)."""
+    """Write d/manifest.json for the given buckets: [{id, ncol, maxctx, kv, tune, tp, determinism}] (tune: the library's
+    knobs; tp: the tensor-parallel degree, 1 when absent; determinism: "batch_invariant" (default, contract "BI") or
+    "tolerance" (contract "FAST": the GEMV for steps of a few token rows, pack.py:639))."""
     os.makedirs(d, exist_ok=True)
     bs = []
     for b in buckets:
-        bs.append(dict(id=b["id"], role="target", variant="v", sku="b200", contract="BI", ncol=b.get("ncol", 64),
-                       batch=True, maxctx=b.get("maxctx", spec.ctx), weights=0, files={}, lib="libgck.so",
-                       requires=dict(arch="sm_100a", cc="10.0", sms=148, name="NVIDIA B200"),
-                       determinism="batch_invariant", act="a16", kv=b.get("kv", "f16"),
+        det = b.get("determinism", "batch_invariant")
+        bs.append(dict(id=b["id"], role="target", variant="v", sku="b200", contract="BI" if det != "tolerance" else "FAST",
+                       ncol=b.get("ncol", 64), batch=b.get("batch", True), maxctx=b.get("maxctx", spec.ctx), weights=0,
+                       files={}, lib="libgck.so", requires=dict(arch="sm_100a", cc="10.0", sms=148, name="NVIDIA B200"),
+                       determinism=det, act="a16", kv=b.get("kv", "f16"),
                        spec_caps=dict(verify=["linear", "tree"], tree_mask=True, verify_widths=[], taps=[],
                                       recurrent_commit=[], accept=[], drafter_roles=[]),
                        tune=dict(b.get("tune", {}))))
         if b.get("tp", 1) > 1:
             bs[-1]["tp"] = b["tp"]   # tensor-parallel degree: devices device .. device + tp - 1
     m = dict(schema="gc-pack", abi="3.0.0", arch="sm_100a", cuda="12.9", runtime=dict(kind="gc-c", version=1),
-             contracts=["BI"], buckets=bs, model=dict(name=spec.name, weights=[dict(file=weights_file)]),
+             contracts=sorted({x["contract"] for x in bs}), buckets=bs, model=dict(name=spec.name, weights=[dict(file=weights_file)]),
              synth=asdict(spec))
     with open(os.path.join(d, "manifest.json"), "w") as f:
         json.dump(m, f, indent=1, sort_keys=True)

@@ -41,6 +41,34 @@ def test_session_matches_oracle_f16_kv(tmp_path, shape, wtype):
         assert_logits_close(g, r, TOL_F16)
 
 
+@pytest.mark.parametrize("wtype", ["q8_0", "q4_k"])
+def test_gemv_tolerance_bucket(tmp_path, wtype):
+    """A "tolerance" bucket runs steps of up to four token rows on the GEMV: the scripted session matches the oracle,
+    and decodes of 1-4 rows match the batch-invariant bucket's tensor-core path within the tolerance but not bit for
+    bit (the GEMV's f16 sub-block sums), which shows the other path ran."""
+    spec = synth.Spec(**SMALL128, wtype=wtype, seed=9)
+    ws = synth.make(str(tmp_path / "w"), spec, ncol=8, maxctx=512)[1]
+    tol = synth.pack_dir(str(tmp_path / "tol"), spec, [dict(id="b200.FAST.main", ncol=8, maxctx=512,
+                                                            determinism="tolerance")], weights_file=ws[0])
+    bi = synth.pack_dir(str(tmp_path / "bi"), spec, [dict(id="b200.BI.main", ncol=8, maxctx=512)], weights_file=ws[0])
+    with backend(tol, ws, buckets=("b200.FAST.main",), pool_blocks=16) as be:
+        got = replay(be)
+    ref = replay(oracle_for(ws))
+    for g, r in zip(got, ref):
+        assert_logits_close(g, r, TOL_F16)
+    rng = np.random.default_rng(4)
+    prompts = [[int(x) for x in rng.integers(1, 500, 40 + 7 * i)] for i in range(4)]
+    outs = {}
+    for name, pack, bid in (("tol", tol, "b200.FAST.main"), ("bi", bi, "b200.BI.main")):
+        with backend(pack, ws, buckets=(bid,), pool_blocks=32) as be:
+            be.step([gck.Work(i, p[:-1], 0, list(range(4 * i, 4 * i + 4)), 0) for i, p in enumerate(prompts)])
+            outs[name] = [be.step([gck.Work(i, [p[-1]], len(p) - 1, list(range(4 * i, 4 * i + 4)), 1)
+                                   for i, p in enumerate(prompts[:n])]) for n in (1, 2, 3, 4)]
+    for a, b in zip(outs["tol"], outs["bi"]):
+        assert_logits_close(a, b, TOL_F16)
+    assert any(not np.array_equal(a, b) for a, b in zip(outs["tol"], outs["bi"]))
+
+
 @pytest.mark.parametrize("kv_scale", ["page", "unit"])
 def test_session_matches_oracle_fp8_kv(tmp_path, kv_scale):
     spec = synth.Spec(**SMALL128, wtype="q4_k", seed=5)
