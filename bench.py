@@ -53,12 +53,35 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi samples during the timed region."""
+    """SM clock and throttle reasons sampled during the timed region: NVML every 10 ms (reads only), else nvidia-smi
+    every 200 ms."""
 
     def __init__(self, gpu):
-        self.gpu, self.rows, self.p = gpu, [], None
+        self.gpu, self.rows, self.p, self.stop, self.t = gpu, [], None, None, None
 
     def __enter__(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.stop = threading.Event()
+            bits = [("hw_slowdown", pynvml.nvmlClocksEventReasonHwSlowdown),
+                    ("hw_thermal_slowdown", pynvml.nvmlClocksEventReasonHwThermalSlowdown),
+                    ("sw_thermal_slowdown", pynvml.nvmlClocksEventReasonSwThermalSlowdown),
+                    ("sw_power_cap", pynvml.nvmlClocksEventReasonSwPowerCap)]
+
+            def poll():
+                mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+                while not self.stop.is_set():
+                    sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                    r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.rows.append([str(sm), str(mx), "", ""] + ["Active" if r & m else "Not Active" for _, m in bits])
+                    time.sleep(0.01)
+            self.t = threading.Thread(target=poll, daemon=True)
+            self.t.start()
+            return self
+        except Exception:
+            self.stop = None
         q = "clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown," \
             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown," \
             "clocks_event_reasons.sw_power_cap"
@@ -76,6 +99,9 @@ class Clocks:
             self.rows.append([x.strip() for x in line.split(",")])
 
     def __exit__(self, *a):
+        if self.stop is not None:
+            self.stop.set()
+            self.t.join(timeout=2)
         if self.p:
             self.p.terminate()
             self.p.wait()
@@ -87,7 +113,7 @@ class Clocks:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({n for r in self.rows for n, v in zip(names, r[4:8]) if v.lower() == "active"})
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(sm)}
+                "reasons": reasons, "samples": len(sm), "source": "nvml 10 ms" if self.stop is not None else "nvidia-smi"}
 
 
 def model_dir():
@@ -675,7 +701,7 @@ def main():
                     help="layers of the 8B shape (default 32; fewer only for small profiling cases, not a headline)")
     args = ap.parse_args()
     if args.layers != 32:
-        for sp, full in ((SPEC8B, 32), (SPEC70B, 80)):
+        for sp, full in ((SPEC8B, 32), (SPEC8B_Q8, 32), (SPEC70B, 80)):
             sp["layers"] = min(args.layers, full)
             sp["name"] += f"-L{sp['layers']}"
     world = int(os.environ.get("WORLD_SIZE", 1))
