@@ -33,9 +33,10 @@ template <int DH, bool FP8>
 struct Cfg {
   static constexpr int ESZ = FP8 ? 1 : 2;
   static constexpr int RB = DH * ESZ;                // bytes of one KV row of one head
-  static constexpr int ROWB = RB + 16;               // padded smem row: conflict-free fragment reads
+  static constexpr int ROWB = RB;                    // smem row, its 16-byte chunks XOR-swizzled (chunk_at)
   static constexpr int BUF = 2 * kGroup * ROWB;      // K rows then V rows
   static constexpr int CHUNKS = RB / 16;             // 16-byte chunks per row
+  static constexpr int SWZ = CHUNKS >= 8 ? 7 : CHUNKS - 1;
   static constexpr int NKS = DH / 16;                // QK k-steps
   static constexpr int NMT = DH / 16;                // PV m-tiles (16 head dims each)
   static constexpr int NST = 2;                      // gather ring: double buffered (occupancy beats lookahead)
@@ -47,6 +48,13 @@ struct Cfg {
   static constexpr int TAIL_OFF = (SMEM + 15) / 16 * 16;   // per-warp tail buffers of tree CTAs: K, V rows, exponents
   static constexpr int TAIL_B = BUF + 2 * kGroup;
 };
+
+// byte offset of 16-byte chunk c of smem row `row`: chunks are XOR-swizzled by the row's low bits, so that the
+// fragment reads below (8 rows at one chunk column, or one row's chunks across 8 lanes) hit distinct bank groups
+template <class C>
+__device__ __forceinline__ int chunk_at(int row, int c) {
+  return row * C::ROWB + ((c ^ (row & C::SWZ)) << 4);
+}
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t d;
@@ -166,7 +174,7 @@ __global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn
       for (int c = tid; c < 2 * kGroup * C::CHUNKS; c += NTHR) {
         const int isv = c / (kGroup * C::CHUNKS), rem = c % (kGroup * C::CHUNKS);
         const int e = rem / C::CHUNKS, ch = rem % C::CHUNKS;
-        cp_async16((isv ? sV : sK) + e * C::ROWB + ch * 16, (isv ? vbase : kbase) + pb + e * C::RB + ch * 16);
+        cp_async16((isv ? sV : sK) + chunk_at<C>(e, ch), (isv ? vbase : kbase) + pb + e * C::RB + ch * 16);
       }
     } else {
       const int i0 = lo + gi * kGroup;
@@ -176,7 +184,7 @@ __global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn
         const int e = rem / C::CHUNKS, ch = rem % C::CHUNKS;
         const int row = list_row(pv, it, q0, min(i0 + e, hi - 1));
         const size_t off = ((static_cast<size_t>(row / kBlock) * a.KVH + head) * kBlock + row % kBlock) * C::RB + ch * 16;
-        cp_async16((isv ? sV : sK) + e * C::ROWB + ch * 16, (isv ? vbase : kbase) + off);
+        cp_async16((isv ? sV : sK) + chunk_at<C>(e, ch), (isv ? vbase : kbase) + off);
       }
       if (page_exp) {
         for (int e = tid; e < kGroup; e += NTHR) {
@@ -216,9 +224,10 @@ __global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn
     uint32_t k0[KW], k1[KW];
 #pragma unroll
     for (int i = 0; i < KW / 4; i++) {
-      uint4 u = reinterpret_cast<const uint4 *>(sK + g * C::ROWB + t * (C::RB / 4))[i];
+      const int c = t * (KW / 4) + i;   // the lane's chunks of the row
+      uint4 u = *reinterpret_cast<const uint4 *>(sK + chunk_at<C>(g, c));
       k0[4 * i] = u.x; k0[4 * i + 1] = u.y; k0[4 * i + 2] = u.z; k0[4 * i + 3] = u.w;
-      u = reinterpret_cast<const uint4 *>(sK + (g + 8) * C::ROWB + t * (C::RB / 4))[i];
+      u = *reinterpret_cast<const uint4 *>(sK + chunk_at<C>(g + 8, c));
       k1[4 * i] = u.x; k1[4 * i + 1] = u.y; k1[4 * i + 2] = u.z; k1[4 * i + 3] = u.w;
     }
     // two accumulator chains (even / odd k-steps), summed at the end: half the MMA dependency chain
@@ -327,15 +336,14 @@ __global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn
 #pragma unroll
     for (int q = 0; q < 4; q++) {
       const int e = 2 * t + (q & 1) + (q >> 1) * 8;
-      const uint8_t *src = sV + e * C::ROWB + g * (C::RB / 8);
       if (VW >= 4) {
 #pragma unroll
         for (int i = 0; i < VW / 4; i++) {
-          uint4 u = reinterpret_cast<const uint4 *>(src)[i];
+          const uint4 u = *reinterpret_cast<const uint4 *>(sV + chunk_at<C>(e, g * (VW / 4) + i));
           vr[q][4 * i] = u.x; vr[q][4 * i + 1] = u.y; vr[q][4 * i + 2] = u.z; vr[q][4 * i + 3] = u.w;
         }
-      } else {   // 8 bytes: fp8 with dh 64
-        uint2 u = *reinterpret_cast<const uint2 *>(src);
+      } else {   // 8 bytes: fp8 with dh 64 (half of chunk g / 2)
+        const uint2 u = *reinterpret_cast<const uint2 *>(sV + chunk_at<C>(e, g >> 1) + (g & 1) * 8);
         vr[q][0] = u.x;
         vr[q][VW - 1] = u.y;
       }
@@ -388,7 +396,7 @@ __global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn
           const int e = rem / C::CHUNKS, ch = rem % C::CHUNKS;
           const int row = list_row(pv, it, qg, min(i0 + e, hiw - 1));
           const size_t off = ((static_cast<size_t>(row / kBlock) * a.KVH + head) * kBlock + row % kBlock) * C::RB + ch * 16;
-          cp_async16((isv ? tV : tK) + e * C::ROWB + ch * 16, (isv ? vbase : kbase) + off);
+          cp_async16((isv ? tV : tK) + chunk_at<C>(e, ch), (isv ? vbase : kbase) + off);
         }
         if (page_exp && lane < kGroup) {
           const int row = list_row(pv, it, qg, min(i0 + lane, hiw - 1));
