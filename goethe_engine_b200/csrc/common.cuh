@@ -108,5 +108,10 @@ GCK_DEV int list_row(const PlanView &pv, const Item &it, const QGroup &qg, int i
   if (qg.path_len && i >= it.pos) r = it.pos + pv.paths[qg.path_off + (i - it.pos)];
   return static_cast<int>(pv.blocks[it.blk_off + r / kBlock]) * kBlock + (r % kBlock);
 }
+// the same for a tree token given by its path (offset, length) in plan.paths
+GCK_DEV int list_row_path(const PlanView &pv, const Item &it, int path_off, int i) {
+  const int r = i >= it.pos ? it.pos + pv.paths[path_off + (i - it.pos)] : i;
+  return static_cast<int>(pv.blocks[it.blk_off + r / kBlock]) * kBlock + (r % kBlock);
+}
 
 }  // namespace gck

@@ -158,7 +158,7 @@ __global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn
     for (int c = 0; c < 2; c++) {
       const int r = nt * 8 + 2 * t + c;
       rvalid[nt][c] = r < nrows;
-      nvis[nt][c] = qg.path_len ? it.pos + qg.path_len : it.pos + qg.j0 + r / G + 1;
+      nvis[nt][c] = qg.path_len ? it.pos + (r / G == 0 ? qg.path_len : qg.path_len1) : it.pos + qg.j0 + r / G + 1;
     }
 
   const uint8_t *kbase = static_cast<const uint8_t *>(a.kc);
@@ -217,7 +217,8 @@ __global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn
   }
   // one 16-entry group of the row list starting at list index i0, staged at sK (K rows, then V rows): page groups
   // carry their (K, V) exponents in ge, resolved groups per-entry exponents in ee
-  auto consume = [&](const uint8_t *sK, int i0, const int8_t *ge, const int8_t *ee) {
+  // rmask: the rows that take part (a tree node's own tail leaves the other node's rows out: an exact no-op for them)
+  auto consume = [&](const uint8_t *sK, int i0, const int8_t *ge, const int8_t *ee, uint32_t rmask) {
     const uint8_t *sV = sK + kGroup * C::ROWB;
     // ---- S^T = K Q^T: A rows g, g+8 (entries), lane t's dim slice
     constexpr int KW = C::RB / 4 / 4;   // words of a lane's K slice
@@ -290,8 +291,9 @@ __global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn
       float x[2][2];   // [entry g / g+8][row c]
 #pragma unroll
       for (int c = 0; c < 2; c++) {
-        const bool ok0 = rvalid[nt][c] && i0 + g < nvis[nt][c];
-        const bool ok1 = rvalid[nt][c] && i0 + g + 8 < nvis[nt][c];
+        const bool in = rvalid[nt][c] && ((rmask >> (nt * 8 + 2 * t + c)) & 1u);
+        const bool ok0 = in && i0 + g < nvis[nt][c];
+        const bool ok1 = in && i0 + g + 8 < nvis[nt][c];
         x[0][c] = ok0 ? sc[nt][c] * ks0 : -INFINITY;
         x[1][c] = ok1 ? sc[nt][2 + c] * ks1 : -INFINITY;
       }
@@ -378,37 +380,44 @@ __global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn
     __syncthreads();
     const int i0 = lo + gi * kGroup;
     if (active && i0 < qg.nvis)
-      consume(sm + buf * C::BUF, i0, sPg[gi] >= 0 ? sGE + 2 * gi : nullptr, sEE + buf * kGroup * 2);
+      consume(sm + buf * C::BUF, i0, sPg[gi] >= 0 ? sGE + 2 * gi : nullptr, sEE + buf * kGroup * 2, 0xFFFFFFFFu);
     __syncthreads();
   }
   cp_async_wait<0>();
 
   if constexpr (NW > 1) {
     if (tree_cta && active) {
-      // this warp's tail: list entries from the item's last plain group boundary, resolved through its own path
+      // this warp's tails: for each of its tree tokens (one or two), the list entries from the item's last plain group
+      // boundary, resolved through that token's path, with the other token's rows left out
       uint8_t *tK = sm + C::TAIL_OFF + warp * C::TAIL_B;
       uint8_t *tV = tK + kGroup * C::ROWB;
       int8_t *tE = reinterpret_cast<int8_t *>(tK + C::BUF);
-      const int hiw = min(lo + pv.split, qg.nvis);
-      for (int i0 = max(lo, shared_hi); i0 < hiw; i0 += kGroup) {
-        for (int c = lane; c < 2 * kGroup * C::CHUNKS; c += 32) {
-          const int isv = c / (kGroup * C::CHUNKS), rem = c % (kGroup * C::CHUNKS);
-          const int e = rem / C::CHUNKS, ch = rem % C::CHUNKS;
-          const int row = list_row(pv, it, qg, min(i0 + e, hiw - 1));
-          const size_t off = ((static_cast<size_t>(row / kBlock) * a.KVH + head) * kBlock + row % kBlock) * C::RB + ch * 16;
-          cp_async16((isv ? tV : tK) + chunk_at<C>(e, ch), (isv ? vbase : kbase) + off);
+      const int nnode = qg.path_len1 > 0 ? 2 : 1;
+      for (int nd = 0; nd < nnode; nd++) {
+        const int poff = nd ? qg.path_off1 : qg.path_off;
+        const int hiw = min(lo + pv.split, it.pos + (nd ? qg.path_len1 : qg.path_len));
+        const uint32_t rmask = nnode == 1 ? 0xFFFFFFFFu : ((1u << G) - 1u) << (nd * G);
+        for (int i0 = max(lo, shared_hi); i0 < hiw; i0 += kGroup) {
+          for (int c = lane; c < 2 * kGroup * C::CHUNKS; c += 32) {
+            const int isv = c / (kGroup * C::CHUNKS), rem = c % (kGroup * C::CHUNKS);
+            const int e = rem / C::CHUNKS, ch = rem % C::CHUNKS;
+            const int row = list_row_path(pv, it, poff, min(i0 + e, hiw - 1));
+            const size_t off =
+                ((static_cast<size_t>(row / kBlock) * a.KVH + head) * kBlock + row % kBlock) * C::RB + ch * 16;
+            cp_async16((isv ? tV : tK) + chunk_at<C>(e, ch), (isv ? vbase : kbase) + off);
+          }
+          if (page_exp && lane < kGroup) {
+            const int row = list_row_path(pv, it, poff, min(i0 + lane, hiw - 1));
+            const int8_t *pe = a.exps + (static_cast<size_t>(row / kBlock) * a.KVH + head) * 2;
+            tE[2 * lane] = pe[0];
+            tE[2 * lane + 1] = pe[1];
+          }
+          cp_async_commit();
+          cp_async_wait<0>();
+          __syncwarp();
+          consume(tK, i0, nullptr, tE, rmask);
+          __syncwarp();
         }
-        if (page_exp && lane < kGroup) {
-          const int row = list_row(pv, it, qg, min(i0 + lane, hiw - 1));
-          const int8_t *pe = a.exps + (static_cast<size_t>(row / kBlock) * a.KVH + head) * 2;
-          tE[2 * lane] = pe[0];
-          tE[2 * lane + 1] = pe[1];
-        }
-        cp_async_commit();
-        cp_async_wait<0>();
-        __syncwarp();
-        consume(tK, i0, nullptr, tE);
-        __syncwarp();
       }
     }
   }

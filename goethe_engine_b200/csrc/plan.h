@@ -26,7 +26,7 @@ struct Item {                       // one gc_work
   int pad;
 };
 
-struct QGroup {                     // up to 16/G consecutive chain tokens of one item, or one tree token
+struct QGroup {                     // up to 16/G consecutive chain tokens of one item, or one or two tree tokens
   int item;
   int j0;                           // first token (index within the item)
   int ntok;
@@ -35,6 +35,7 @@ struct QGroup {                     // up to 16/G consecutive chain tokens of on
   int part_base;                    // partial slot of (head 0, split 0); (head h, split s) = base + h * nsplit + s
   int path_off;                     // tree token: its path (token indices within the item, root .. self) in plan.paths
   int path_len;                     // tree token: depth + 1; chain: 0
+  int path_off1, path_len1;         // a second tree token j0 + 1 in the group (rows G .. 2G-1); path_len1 0: none
 };
 
 struct AttnWork {                   // one CTA of the attention kernel: nqg groups of one item, one kv head, one split

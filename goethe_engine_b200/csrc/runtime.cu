@@ -948,11 +948,20 @@ void build_plan(gc_handle *h, const std::vector<WorkIn> &ws, HostPlan &pl) {
     // query groups, then the attention work over kv heads and splits
     int qfirst = static_cast<int>(pl.qgroups.size());
     if (w.parents) {
-      for (uint32_t j = 0; j < w.n; j++) {
+      // f16 KV: two tree tokens per query group (their 2G rows fill the MMA's 8-row tile; each token's tail is walked
+      // with the other's rows left out, so a token's arithmetic is unchanged); fp8 KV keeps one (the exponent frame is
+      // per warp)
+      const int per = !h->kv_fp8 && 2 * G <= 8 ? 2 : 1;
+      for (uint32_t j = 0; j < w.n; j += per) {
         QGroup q{};
-        q.item = item; q.j0 = static_cast<int>(j); q.ntok = 1;
-        q.nvis = static_cast<int>(w.pos) + plen[j];
+        q.item = item; q.j0 = static_cast<int>(j); q.ntok = std::min<int>(per, static_cast<int>(w.n - j));
         q.path_off = poff[j]; q.path_len = plen[j];
+        q.nvis = static_cast<int>(w.pos) + plen[j];
+        if (q.ntok == 2) {
+          q.path_off1 = poff[j + 1];
+          q.path_len1 = plen[j + 1];
+          q.nvis = std::max(q.nvis, static_cast<int>(w.pos) + plen[j + 1]);
+        }
         pl.qgroups.push_back(q);
       }
       if (w.n > 1) multi = true;
@@ -983,7 +992,6 @@ void build_plan(gc_handle *h, const std::vector<WorkIn> &ws, HostPlan &pl) {
     q.part_base = pl.n_parts;
     pl.n_parts += h->KVH * q.nsplit;
   }
-  (void)G;
   pl.nw = multi ? 8 : 1;
   // work: per item, kv head, split: the item's query groups (chain token groups or tree nodes) packed nw to a CTA, from
   // the first that reaches the split (a tree node that does not idles in its CTA)
