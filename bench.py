@@ -318,6 +318,8 @@ class CpuSample:
     step's time does not depend on their values)."""
 
     VS = 8192
+    MAX_STEPS = 40          # decode steps timed at most (positions advance); at least TARGET_S seconds of CPU work
+    TARGET_S = 10.0
 
     def __init__(self, seqs=8, layers=2):
         from oracle import quants as Q
@@ -343,14 +345,14 @@ class CpuSample:
         self.head = mat("output.weight", self.VS)
         w = Weights(self.head.copy(), self.head, lw, eps=1e-5, theta=5e5, heads=32, kv_heads=8)
         self.ctx = contexts()[:seqs]
-        nb = int(sum(-(-(c + 1) // 16) for c in self.ctx))
+        nb = int(sum(-(-(c + 2 + self.MAX_STEPS) // 16) for c in self.ctx))
         self.o = PagedOracle(w, num_blocks=nb, kv="fp8", kv_scale="page")
         rng = np.random.default_rng(2)
         self.o.kc[:] = rng.integers(0, 0x78, self.o.kc.shape, dtype=np.uint8)
         self.o.vc[:] = rng.integers(0, 0x78, self.o.vc.shape, dtype=np.uint8)
         tabs, k = [], 0
         for c in self.ctx:
-            n = -(-(int(c) + 1) // 16)
+            n = -(-(int(c) + 2 + self.MAX_STEPS) // 16)
             tabs.append(list(range(k, k + n)))
             k += n
         self.items = [dict(sid=i, tokens=[7], pos=int(c), blocks=tabs[i], want=1) for i, c in enumerate(self.ctx)]
@@ -358,9 +360,19 @@ class CpuSample:
         self.o.step(self.items)          # warm
 
     def run(self):
-        t0 = time.perf_counter()
-        self.o.step(self.items)
-        t_all = time.perf_counter() - t0
+        # repeated decode steps (each sequence one token further) until TARGET_S seconds of CPU work, from the C3
+        # contexts again on every call
+        for it, c in zip(self.items, self.ctx):
+            it["pos"] = int(c)
+        n, t_sum = 0, 0.0
+        while n < self.MAX_STEPS and t_sum < self.TARGET_S:
+            for it in self.items:
+                it["pos"] += 1
+            t0 = time.perf_counter()
+            self.o.step(self.items)
+            t_sum += time.perf_counter() - t0
+            n += 1
+        t_all = t_sum / n
         h = np.ones((self.seqs, 4096), np.float32)
         t0 = time.perf_counter()
         for _ in range(3):
@@ -369,8 +381,8 @@ class CpuSample:
         per_step = max(t_all - t_head, 1e-9) * 32 / self.layers + t_head * 128256 / self.VS
         return {"value": round(self.seqs / per_step, 3), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
                 "sample": f"oracle decode step of {self.seqs} C3 sequences (contexts {list(map(int, self.ctx))}), "
-                          f"{self.layers}/32 layers and {self.VS}/128256 head rows timed ({t_all:.2f}s), scaled to "
-                          f"the full model: {per_step:.2f}s per step"}
+                          f"{self.layers}/32 layers and {self.VS}/128256 head rows, {n} steps timed ({t_sum:.1f}s, "
+                          f"{t_all:.2f}s each), scaled to the full model: {per_step:.2f}s per step"}
 
 
 def cpu_baseline(args):
