@@ -360,6 +360,13 @@ class CpuSample:
         self.o.step(self.items)          # warm
 
     def run(self):
+        # all of this process's host cores for the oracle's BLAS calls (torchrun sets OMP_NUM_THREADS=1 per rank)
+        from threadpoolctl import threadpool_limits
+        cores = len(os.sched_getaffinity(0))
+        with threadpool_limits(limits=cores, user_api="blas"):
+            return self._run(cores)
+
+    def _run(self, cores):
         # repeated decode steps (each sequence one token further) until TARGET_S seconds of CPU work, from the C3
         # contexts again on every call
         for it, c in zip(self.items, self.ctx):
@@ -379,7 +386,7 @@ class CpuSample:
             h @ self.head.T
         t_head = (time.perf_counter() - t0) / 3
         per_step = max(t_all - t_head, 1e-9) * 32 / self.layers + t_head * 128256 / self.VS
-        return {"value": round(self.seqs / per_step, 3), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+        return {"value": round(self.seqs / per_step, 3), "unit": "tok/s", "cores": cores, "kind": "port",
                 "sample": f"oracle decode step of {self.seqs} C3 sequences (contexts {list(map(int, self.ctx))}), "
                           f"{self.layers}/32 layers and {self.VS}/128256 head rows, {n} steps timed ({t_sum:.1f}s, "
                           f"{t_all:.2f}s each), scaled to the full model: {per_step:.2f}s per step"}
