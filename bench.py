@@ -30,7 +30,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 SPEC8B = dict(vocab=128256, d=4096, layers=32, heads=32, kv_heads=8, ffn=14336, eps=1e-5, theta=5e5, wtype="q4_k",
-              std=0.02, seed=0, ctx=8192 + 64, name="llama3-8b-shape-q4k")
+              std=0.02, seed=0, ctx=8192 + 128, name="llama3-8b-shape-q4k")
 B, PREFIX = 64, 1024
 METRIC = "decode tok/s (8B Q4_K, batch 64, fp8 KV)"
 # DRAM bytes (read + write) of one attention launch of this workload, from the ncu capture summarised in
@@ -206,7 +206,8 @@ def run_mine(args, rank, world, barrier, maxreduce):
         barrier()
     spec, d, ws = ensure_model(rank, world, barrier)
     ctx = contexts()
-    steps_total = args.warmup + args.steps
+    GEMM_PASS = 5                       # steps after the timed region with events around every GEMM launch
+    steps_total = args.warmup + args.steps + GEMM_PASS
     dev = int(os.environ.get("LOCAL_RANK", 0))
     t0 = time.time()
     be = gck.Backend(d, ws, pool_blocks=int(np.sum(ctx)) // 16 + 2 * B + 64, device=dev)
@@ -256,6 +257,15 @@ def run_mine(args, rank, world, barrier, maxreduce):
     st = Stats(size=C.sizeof(Stats))
     L.gck_stats_read(be.h, C.byref(st))
     torch.cuda.synchronize()
+    # the GEMM classes (q/k/v, o, gate/up, down, head), timed by events around each launch in a few steps after the
+    # timed region (the events cut the programmatic overlap at those launches, so this is an upper bound on their time)
+    GEMMS = (2, 6, 7, 8, 9)
+    L.gck_stats_enable(be.h, sum(1 << c for c in GEMMS))
+    for _ in range(GEMM_PASS):
+        step()
+    sg = Stats(size=C.sizeof(Stats))
+    L.gck_stats_read(be.h, C.byref(sg))
+    L.gck_stats_enable(be.h, 0)
     if world > 1:
         barrier()
     dev_s = maxreduce(st.forward_ms / 1e3)
@@ -287,6 +297,8 @@ def run_mine(args, rank, world, barrier, maxreduce):
                      "(profiles/attn_kernel_c3_decode_L2.md)",
                      "algorithmic_bytes_per_launch": int(attn_bytes), "launch_ms": round(attn_ms, 4),
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in pk else "fallback 6650 GB/s"},
+        "roofline_gemm": gemm_roofline(sg, GEMM_PASS, hbm, "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in pk else
+                                       "fallback 6650 GB/s"),
         "step_roofline": {"algorithmic_bytes": int(step_bytes), "weights_bytes": int(wbytes), "kv_bytes": int(kv_bytes),
                           "achieved_gbs": round(step_bytes / (ms_step / 1e3) / 1e9, 1),
                           "frac_of_measured": round(step_bytes / (ms_step / 1e3) / 1e9 / hbm, 4),
@@ -309,6 +321,28 @@ def run_mine(args, rank, world, barrier, maxreduce):
         if world == 1 and not args.no_cpu:
             res["cpu_baseline"] = cpu_baseline(args)
         print(json.dumps(res), flush=True)
+
+
+GATEUP_TRAFFIC = 67_172_864   # ncu DRAM bytes of one C3 gate/up launch (profiles/gemm_tc_gateup_c3_decode_L2.md)
+
+
+def gemm_roofline(sg, steps, hbm, peak_source):
+    """HBM roofline of the tcgen05 GEMM launches of a C3 step (the largest kernel class by time): the Q4_K weight
+    bytes of the step (every projection and the head, read once) over the GEMM classes' device time; and the gate/up
+    launch alone (66.06 MB of weights + 0.5 MB activations + 1.8 MB f16 output per launch)."""
+    GEMMS, GU = (2, 6, 7, 8, 9), 7
+    ms = sum(sg.class_ms[c] for c in GEMMS) / steps
+    wb = weight_bytes(SPEC8B)
+    gu_ms = sg.class_ms[GU] / max(1, sg.class_launches[GU])
+    gu_bytes = 2 * 14336 * 4096 * 144 // 256 + 64 * 4096 * 2 + 64 * 14336 * 2
+    return {"bound": "hbm", "kernel": "gemm_tc_kernel<Q4_K, 64> (all projections and the head)",
+            "achieved": round(wb / (ms / 1e3) / 1e9, 1), "peak": hbm, "unit": "GB/s",
+            "frac": round(wb / (ms / 1e3) / 1e9 / hbm, 4), "ms_per_step": round(ms, 4),
+            "launches_per_step": int(sum(sg.class_launches[c] for c in GEMMS) // steps), "algorithmic_bytes_per_step": int(wb),
+            "gateup": {"launch_ms": round(gu_ms, 4), "algorithmic_bytes_per_launch": int(gu_bytes),
+                       "achieved": round(gu_bytes / (gu_ms / 1e3) / 1e9, 1),
+                       "frac": round(gu_bytes / (gu_ms / 1e3) / 1e9 / hbm, 4), "traffic": GATEUP_TRAFFIC},
+            "timing": f"CUDA events around each GEMM launch, {steps} steps after the timed region", "peak_source": peak_source}
 
 
 class CpuSample:
