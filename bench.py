@@ -684,13 +684,7 @@ def run_c5(args):
     dev_s = st.forward_ms / 1e3
     value, e2e = B70 * args.steps / dev_s, B70 * args.steps / wall
     if args.profile:
-        names = ["embed", "rmsnorm", "gemm_qkv", "rope_kv", "attention", "attn_combine", "gemm_o", "gemm_gateup",
-                 "gemm_down", "gemm_head", "argmax", "splitk_reduce", "allreduce"]
-        tot = sum(st.class_ms[i] for i in range(len(names)))
-        print("[bench] rank 0 per-class device time (events around each launch):\n" + "\n".join(
-            f"{n:14s} {st.class_ms[i] / args.steps:8.3f} ms/step  {st.class_launches[i] // max(1, args.steps):5d} launches/step"
-            for i, n in enumerate(names)) + f"\n  sum {tot / args.steps:.3f} ms/step, step {st.forward_ms / args.steps:.3f} ms",
-            file=sys.stderr, flush=True)
+        print_classes(st, args.steps, "rank 0 ")
     ms_step = dev_s / args.steps * 1e3
     wbytes = weight_bytes(SPEC70B)
     kv = (CTX70 + args.warmup + args.steps / 2) * B70 * 2 * 8 * 128 * SPEC70B["layers"]
@@ -703,7 +697,8 @@ def run_c5(args):
         "data": "synthetic (seeded N(0,0.02) weights, uniform tokens)",
         "config": {"workload": "C5: Llama-3-70B shape, Q4_K weights, fp8 paged KV (per-page scale), 128 sequences at "
                                "context 4096, greedy decode", "batch": B70, "context": CTX70, "layers": SPEC70B["layers"],
-                   "parallelism": f"tp{tp} (one handle, NCCL all-reduce after o_proj and down_proj)",
+                   "parallelism": f"tp{tp} (one handle; after o_proj and down_proj a deterministic all-reduce over "
+                                  "peer memory, NCCL where peer access is missing)",
                    "l2": "inputs larger than L2, no flush"},
         "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": int(sum(len(t) for t in tables) * 4 + B70 * 64),
                 "d2h_bytes_per_step": B70 * 4, "path": "gc_step through the C ABI (ctypes), host buffers"},
@@ -740,6 +735,8 @@ def run_reference(args, rank, world):
 
 
 def main():
+    # rank 0 prints one JSON line on stdout: keep NCCL's version banner off it unless the caller asks for NCCL logs
+    os.environ.setdefault("NCCL_DEBUG", "WARN")
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
