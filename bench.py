@@ -20,6 +20,7 @@ import json
 import math
 import os
 import subprocess
+import tempfile
 import sys
 import threading
 import time
@@ -735,8 +736,9 @@ def run_reference(args, rank, world):
 
 
 def main():
-    # rank 0 prints one JSON line on stdout: keep NCCL's version banner off it unless the caller asks for NCCL logs
+    # rank 0 prints one JSON line on stdout: NCCL's banner and logs (NCCL_DEBUG) go to a file instead
     os.environ.setdefault("NCCL_DEBUG", "WARN")
+    os.environ.setdefault("NCCL_DEBUG_FILE", os.path.join(tempfile.gettempdir(), "gck_nccl.%h.%p.log"))
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
