@@ -13,6 +13,10 @@ namespace gck {
 
 GCK_DEV uint32_t smem_u32(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
+// SwiGLU of one feature, silu(g) * u = g / (1 + e^-g) * u (ref.py's F.silu(g) * u), with the fast exponential and
+// division intrinsics (a few ulp in f32, far below the f16 rounding of the result); every kernel uses this one
+GCK_DEV float silu_mul(float g, float u) { return __fdividef(g, 1.f + __expf(-g)) * u; }
+
 // Programmatic dependent launch. A forward kernel started by launch_pdl may begin while the kernel before it in the
 // stream still runs: it calls dep_wait() before its first access of memory that an earlier kernel writes or reads
 // (dep_wait returns once the earlier kernels have completed and their writes are visible), and dep_launch() so that

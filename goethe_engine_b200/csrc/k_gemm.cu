@@ -98,7 +98,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     return;
   }
   if (epi.kind == kEpiSwiGLU) {
-    // gate rows 0..63 and up rows 64..127 of the tile meet in shared memory
+    // gate rows (even) and their up rows (the odd row after each) of the tile meet in shared memory
     float *sC = reinterpret_cast<float *>(smem);  // [128][kBN + 1]
 #pragma unroll
     for (int mt = 0; mt < 2; mt++)
@@ -115,8 +115,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int f = i % 64, c = i / 64;
       int t = t0 + c, feat = nt * 64 + f;
       if (t < T && feat < epi.n) {
-        float gg = sC[f * (kBN + 1) + c], uu = sC[(64 + f) * (kBN + 1) + c];
-        epi.out_h[static_cast<size_t>(t) * epi.ld + feat] = __float2half_rn(gg / (1.f + expf(-gg)) * uu);
+        float gg = sC[(2 * f) * (kBN + 1) + c], uu = sC[(2 * f + 1) * (kBN + 1) + c];
+        epi.out_h[static_cast<size_t>(t) * epi.ld + feat] = __float2half_rn(silu_mul(gg, uu));
       }
     }
     return;

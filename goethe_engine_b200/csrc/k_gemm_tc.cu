@@ -176,13 +176,12 @@ struct Shape {
   static_assert(SPT == 2 || RAW % 2 == 0, "raw ring slots must each belong to one dequant group");
 };
 
-constexpr int kXchg = 64 * 17 * 4;         // SwiGLU hand-off: 64 rows x 16 columns (+1 pad) of f32
 
 template <int TYPE, int NT>
 constexpr int smem_total() {
   using S = Shape<TYPE, NT>;
   // at least 120 KB: one CTA per SM, since each takes all 512 TMEM columns
-  constexpr int need = 1024 + S::R * S::STAGE_B + S::RAW * TileFmt<TYPE>::BYTES + kXchg + 512;
+  constexpr int need = 1024 + S::R * S::STAGE_B + S::RAW * TileFmt<TYPE>::BYTES + 512;
   return need > 120 * 1024 ? need : 120 * 1024;
 }
 
@@ -215,8 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t *sB = smem;
   uint8_t *sRaw = sB + SR * S::STAGE_B;
-  float *xchg = reinterpret_cast<float *>(sRaw + RS * F::BYTES);
-  uint64_t *bars = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(xchg) + kXchg);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sRaw + RS * F::BYTES);
   uint64_t *raw_full = bars, *raw_empty = raw_full + RS;
   uint64_t *a_full = raw_empty + RS, *st_empty = a_full + SR, *b_full = st_empty + SR;
   uint64_t *acc_full = b_full + SR, *acc_empty = acc_full + 2, *mma_done = acc_empty + 2;
@@ -422,27 +420,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else if (epi.kind == kEpiSwiGLU) {
-        // rows 64..127 (up) hand 16 columns at a time to rows 0..63 (gate); all four warps reach every barrier
-        const int f = un.nt * 64 + r;
+        // even rows are gate rows, the odd row after each its up row (feature un.nt * 64 + r / 2): the two lanes swap
+        // values and each takes half the token columns (the gate lane the even ones)
+        const int f = un.nt * 64 + (r >> 1);
+        const int odd = r & 1;
         for (int c0 = 0; c0 < NT; c0 += 16) {
           uint32_t v[16];
           if (good) tmem_ld16(tbase + c0, v);
-          if (good && r >= 64) {
 #pragma unroll
-            for (int c = 0; c < 16; c++) xchg[(r - 64) * 17 + c] = __uint_as_float(v[c]);
-          }
-          asm volatile("bar.sync 1, 128;\n" ::: "memory");
-          if (good && r < 64) {
-#pragma unroll
-            for (int c = 0; c < 16; c++) {
-              int t = t0 + c0 + c;
-              if (t < T && f < epi.n) {
-                float g = __uint_as_float(v[c]), uu = xchg[r * 17 + c];
-                epi.out_h[static_cast<size_t>(t) * epi.ld + f] = __float2half_rn(g / (1.f + expf(-g)) * uu);
-              }
+          for (int c = 0; c < 16; c++) {
+            const float mine = __uint_as_float(v[c]);
+            const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
+            const int t = t0 + c0 + c;
+            if (good && (c & 1) == odd && t < T && f < epi.n) {
+              const float g = odd ? other : mine, uu = odd ? mine : other;
+              epi.out_h[static_cast<size_t>(t) * epi.ld + f] = __float2half_rn(silu_mul(g, uu));
             }
           }
-          asm volatile("bar.sync 1, 128;\n" ::: "memory");
         }
       } else if (good) {
         for (int c0 = 0; c0 < NT; c0 += 16) {

@@ -180,21 +180,16 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const uint8_t *__res
     return;
   }
   if (epi.kind == kEpiSwiGLU) {
-    // rows 64..127 of the band are the up rows of the gate rows 0..63 (features nt * 64 + r)
-    __syncthreads();
-    if (hs == 0 && r >= 64) {
+    // even rows are gate rows, the odd row after each its up row (feature nt * 64 + r / 2): the up value comes from
+    // the neighbouring lane (warps 0-3 hold whole rows here)
+    if (hs == 0) {
+      const int f = nt * 64 + (r >> 1);
 #pragma unroll
-      for (int t = 0; t < T; t++) sred[t][r] = acc[t];
-    }
-    __syncthreads();
-    if (hs == 0 && r < 64) {
-      const int f = nt * 64 + r;
-#pragma unroll
-      for (int t = 0; t < T; t++)
-        if (t < Tn && f < epi.n) {
-          const float g = acc[t], uu = sred[t][r + 64];
-          epi.out_h[static_cast<size_t>(t) * epi.ld + f] = __float2half_rn(g / (1.f + expf(-g)) * uu);
-        }
+      for (int t = 0; t < T; t++) {
+        const float uu = __shfl_xor_sync(0xffffffffu, acc[t], 1);
+        if ((r & 1) == 0 && t < Tn && f < epi.n)
+          epi.out_h[static_cast<size_t>(t) * epi.ld + f] = __float2half_rn(silu_mul(acc[t], uu));
+      }
     }
     return;
   }

@@ -418,7 +418,6 @@ void launch_rope_kv(const PlanView &pv, const float *qkv, int S, int ld, int H, 
 
 // ----------------------------------------------------------------------------------------------------------------
 // Split-K reduction: v = sum_{s=0..S-1} part[s, t, n] in that order, then the epilogue.
-__device__ __forceinline__ float silu(float g) { return g / (1.f + expf(-g)); }
 
 __global__ void splitk_reduce_kernel(const float *part, int S, int T, int Npad, Epi epi) {
   dep_wait();
@@ -427,32 +426,33 @@ __global__ void splitk_reduce_kernel(const float *part, int S, int T, int Npad, 
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
     if (epi.kind == kEpiSwiGLU) {
-      // four consecutive features of one 64-row half per thread: float4 loads of the gate and up rows
+      // four consecutive features per thread: gate and up rows alternate (row 2i of a 128-row tile is gate feature
+      // tile * 64 + i, row 2i + 1 its up row), so two float4 loads hold the four (gate, up) pairs
       int q4 = Npad / 2 / 4;
       int t = static_cast<int>(i / q4), f = static_cast<int>(i % q4) * 4;
       int tile = f / 64, w = f % 64;
-      int ng = tile * 128 + w, nu = ng + 64;
+      int n0 = tile * 128 + 2 * w;
       float4 g = make_float4(0.f, 0.f, 0.f, 0.f), u = g;
       for (int s0 = 0; s0 < S; s0 += kSplitChunk) {
         float4 a[kSplitChunk], b[kSplitChunk];
 #pragma unroll
         for (int j = 0; j < kSplitChunk; j++) {
           const float *row = part + (static_cast<size_t>(s0 + j) * T + t) * Npad;
-          a[j] = s0 + j < S ? *reinterpret_cast<const float4 *>(row + ng) : make_float4(0.f, 0.f, 0.f, 0.f);
-          b[j] = s0 + j < S ? *reinterpret_cast<const float4 *>(row + nu) : make_float4(0.f, 0.f, 0.f, 0.f);
+          a[j] = s0 + j < S ? *reinterpret_cast<const float4 *>(row + n0) : make_float4(0.f, 0.f, 0.f, 0.f);
+          b[j] = s0 + j < S ? *reinterpret_cast<const float4 *>(row + n0 + 4) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
         for (int j = 0; j < kSplitChunk; j++) {
           if (s0 + j >= S) break;
-          g.x += a[j].x; g.y += a[j].y; g.z += a[j].z; g.w += a[j].w;
-          u.x += b[j].x; u.y += b[j].y; u.z += b[j].z; u.w += b[j].w;
+          g.x += a[j].x; u.x += a[j].y; g.y += a[j].z; u.y += a[j].w;
+          g.z += b[j].x; u.z += b[j].y; g.w += b[j].z; u.w += b[j].w;
         }
       }
       __half *o = epi.out_h + static_cast<size_t>(t) * epi.ld + f;
-      if (f < epi.n) o[0] = __float2half_rn(silu(g.x) * u.x);
-      if (f + 1 < epi.n) o[1] = __float2half_rn(silu(g.y) * u.y);
-      if (f + 2 < epi.n) o[2] = __float2half_rn(silu(g.z) * u.z);
-      if (f + 3 < epi.n) o[3] = __float2half_rn(silu(g.w) * u.w);
+      if (f < epi.n) o[0] = __float2half_rn(silu_mul(g.x, u.x));
+      if (f + 1 < epi.n) o[1] = __float2half_rn(silu_mul(g.y, u.y));
+      if (f + 2 < epi.n) o[2] = __float2half_rn(silu_mul(g.z, u.z));
+      if (f + 3 < epi.n) o[3] = __float2half_rn(silu_mul(g.w, u.w));
     } else {
       int t = static_cast<int>(i / Npad), n = static_cast<int>(i % Npad);
       if (n >= epi.n) continue;

@@ -424,12 +424,13 @@ void load_model(gc_handle *h, const std::vector<std::unique_ptr<GgufFile>> &file
     }, "attn_qkv");
     ly.o = relayout(h, static_cast<int>(to.type), h->d, dq, [&](int n, const GgufTensor *&t, int &r) { t = &to; r = n; },
                     "attn_output", rk * dq);
-    // gate/up interleaved in 64-row halves of each 128-row tile: the SwiGLU epilogue finds g and u in one tile
+    // gate/up rows interleaved: row 2i of a 128-row tile is gate feature tile * 64 + i, row 2i + 1 its up row, so a
+    // SwiGLU epilogue finds a feature's two values in neighbouring lanes of one warp
     int Fp = (Fr + 63) / 64 * 64;
     ly.gu = relayout(h, static_cast<int>(tg.type), 2 * Fp, h->d, [&](int n, const GgufTensor *&t, int &r) {
       int tile = n / 128, w = n % 128;
-      int f = tile * 64 + (w % 64);
-      t = w < 64 ? &tg : &tu;
+      int f = tile * 64 + w / 2;
+      t = (w & 1) == 0 ? &tg : &tu;
       r = rk * Fr + std::min(f, Fr - 1);
       if (f >= Fr) t = nullptr;
     }, "ffn_gate_up", 0, false);
