@@ -156,13 +156,15 @@ class Backend:
         """Tokens per item (every item greedy) or float32 logits [sum(want), vocab] (into `logits` if given)."""
         n = len(work)
         greedy = self.device_argmax and all(w.greedy for w in work)
-        # every item's tokens in one int32 array, the records in one structured array (filled a column at a time), their
-        # addresses in another
+        # every item's tokens in one int32 array, every block table in one uint32 array, the records in one structured
+        # array (filled a column at a time), their addresses in another: a handful of numpy calls per step
         ntok = np.fromiter((len(w.tokens) for w in work), np.int64, n)
         toks = np.fromiter((t for w in work for t in w.tokens), np.int32, int(ntok.sum()))
         blks = [_u32(w.blocks) for w in work]
+        nblk = np.fromiter((len(x) for x in blks), np.int64, n)
+        ball = np.concatenate(blks) if n else np.zeros(0, np.uint32)
         rec = np.zeros(n, WORK_DTYPE)
-        keep = [toks, rec, blks]
+        keep = [toks, rec, ball]
         rec["size"] = WORK_DTYPE.itemsize
         rec["flags"] = [(1 if greedy else 0) | (2 if w.spec else 0) | (4 if w.feats else 0) for w in work]
         rec["sid"] = [w.sid for w in work]
@@ -170,8 +172,8 @@ class Backend:
         rec["want"] = [w.want for w in work]
         rec["n_tokens"] = ntok
         rec["tokens"] = _addr(toks) + 4 * (np.cumsum(ntok) - ntok).astype(np.uint64)
-        rec["blocks"] = [_addr(x) for x in blks]
-        rec["n_blocks"] = [len(x) for x in blks]
+        rec["blocks"] = _addr(ball) + 4 * (np.cumsum(nblk) - nblk).astype(np.uint64)
+        rec["n_blocks"] = nblk
         for i, w in enumerate(work):
             if w.parents is not None:
                 par = np.ascontiguousarray(w.parents, np.int32)

@@ -1,10 +1,11 @@
-"""Tensor parallelism (one handle over 2, 4 or 8 GPUs): heads, kv heads and FFN columns split across the
-ranks, o_proj / down_proj by their input columns with an NCCL all-reduce after each, the head by vocabulary rows.
+"""Tensor parallelism (one handle over 2, 4 or 8 GPUs): heads, kv heads and FFN columns split across the ranks,
+o_proj / down_proj by their input columns with an all-reduce after each (over peer memory, in rank order; NCCL where
+peer access is missing), the head by vocabulary rows.
 
 * the scripted session (prefill chunks, batched decode, tree verify, commit, copy_blocks) at tp = 2, 4, 8 against the
   oracle and against the single-GPU library, to the a16 tolerance;
 * greedy tokens of a tp handle equal the single-GPU ones wherever the top-2 margin exceeds the tolerance;
-* at tp = 2 a row's logits are bit-identical alone and batched (a sum of two partials is exact in either order).
+* at tp = 2 a row's logits are bit-identical alone and batched (the all-reduce adds the ranks in a fixed order).
 Each test runs only where enough GPUs are visible.
 """
 import numpy as np
