@@ -597,6 +597,10 @@ def run_c4(args):
     flop = n_seq * (2 * lin * ctx + sp["layers"] * 4 * sp["d"] * ctx * (ctx + 1) / 2 + 2 * sp["d"] * sp["vocab"])
     tc = peaks().get("bf16_tflops_sustained", 1400.0)
     ver_ms = st_v.forward_ms / args.steps
+    # verify step: every weight byte once, every sequence's KV (ctx rows, f16, all layers) once; FLOPs of 512 token rows
+    # through the linear layers, the head for 16 wanted rows per sequence, attention over ctx + path rows
+    v_bytes = weight_bytes(sp) * 272 // 144 + n_seq * ctx * sp["layers"] * sp["kv_heads"] * (sp["d"] // sp["heads"]) * 2 * 2
+    v_flop = 2 * lin * n_seq * 16 + 2 * sp["d"] * sp["vocab"] * n_seq * 16 + sp["layers"] * 4 * sp["d"] * ctx * n_seq * 16
     print(json.dumps({
         "metric": "prefill tok/s (8B Q8_0, 32 x 2048, a16) and tree-verify step ms (32 x 16-node trees)",
         "value": round(n_seq * ctx / (pre_ms / 1e3), 1), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
@@ -609,7 +613,12 @@ def run_c4(args):
                      "frac": round(flop / (pre_ms / 1e3) / 1e12 / tc, 4),
                      "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained"},
         "verify": {"ms_per_step": round(ver_ms, 4), "tokens_per_step": n_seq * 16,
-                   "tok_per_s": round(n_seq * 16 / (ver_ms / 1e3), 1), "e2e_ms_per_step": round(wall_v / args.steps * 1e3, 4)},
+                   "tok_per_s": round(n_seq * 16 / (ver_ms / 1e3), 1), "e2e_ms_per_step": round(wall_v / args.steps * 1e3, 4),
+                   # mixed bound: the step's weights and KV bytes, and its linear + head + attention FLOPs
+                   "bytes": int(v_bytes), "achieved_gbs": round(v_bytes / (ver_ms / 1e3) / 1e9, 1),
+                   "frac_of_measured_hbm": round(v_bytes / (ver_ms / 1e3) / 1e9 / peaks().get("hbm_gbs", 6650.0), 4),
+                   "flop": v_flop, "achieved_tflops": round(v_flop / (ver_ms / 1e3) / 1e12, 1),
+                   "frac_of_sustained_bf16": round(v_flop / (ver_ms / 1e3) / 1e12 / tc, 4)},
         "e2e": {"value": round(n_seq * ctx / wall_p, 1), "unit": "tok/s", "h2d_bytes_per_step": int(ctx * 4 + per_seq * 4),
                 "d2h_bytes_per_step": 4, "path": "gc_step through the C ABI (ctypes), host buffers"},
         "gpu_launches": int(st_p.launches + st_v.launches), "clocks": clk.summary()}), flush=True)
