@@ -163,6 +163,29 @@ def test_tree_verify_shares_prefix_bitwise(small_model):
         assert np.array_equal(alone[0], tree[0]) and np.array_equal(mixed[1], tree[0])
 
 
+def test_shared_prefix_pairing_bitwise(small_model):
+    """Decode tokens of sequences that share whole splits of prefix pages (a radix-cache prefix): each token's logits
+    batched equal its decode alone, bit for bit."""
+    pack, ws = small_model
+    rng = np.random.default_rng(11)
+    pre = [int(x) for x in rng.integers(1, 500, 1100)]
+    with backend(pack, ws, pool_blocks=256) as be:
+        t1 = list(range(0, 70))
+        be.step([gck.Work(1, pre[:1000], 0, t1, 0)])
+        be.step([gck.Work(1, pre[1000:], 1000, t1, 0)])
+        tabs = {1: t1}
+        for sid, base in ((2, 100), (3, 170)):
+            tabs[sid] = list(range(0, 64)) + list(range(base, base + 6))     # rows 0..1023 from sid 1's pages
+            own = [int(x) for x in rng.integers(1, 500, 80)]
+            be.step([gck.Work(sid, own, 1024, tabs[sid], 0)])
+        pos = {1: 1100, 2: 1104, 3: 1104}
+        tok = {1: 7, 2: 9, 3: 11}
+        alone = {sid: be.step([gck.Work(sid, [tok[sid]], pos[sid], tabs[sid], 1)])[0] for sid in (1, 2, 3)}
+        batch = be.step([gck.Work(sid, [tok[sid]], pos[sid], tabs[sid], 1) for sid in (1, 2, 3)])
+        for i, sid in enumerate((1, 2, 3)):
+            assert np.array_equal(batch[i], alone[sid]), sid
+
+
 def test_batch_and_chunk_invariance_bitwise(small_model):
     pack, ws = small_model
     rng = np.random.default_rng(0)
