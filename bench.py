@@ -271,9 +271,7 @@ def run_mine(args, rank, world, barrier, maxreduce):
         barrier()
     dev_s = maxreduce(st.forward_ms / 1e3)
     wall = maxreduce(wall)
-    tokens = B * args.steps * world
-    value = tokens / dev_s
-    e2e = tokens / wall
+    value, e2e = aggregate(B * args.steps, world, dev_s, wall)
     pk = peaks()
     hbm = pk.get("hbm_gbs", 6650.0)
     attn_ms = st.class_ms[ATTN] / max(1, st.class_launches[ATTN])
@@ -723,6 +721,38 @@ def run_c5(args):
     print(json.dumps(res), flush=True)
 
 
+def collectives(world, backend="nccl", timeout_s=600):
+    """The benchmark's only cross-rank steps, for one process per GPU (torchrun's RANK / WORLD_SIZE / MASTER_*): a
+    barrier, and the max over ranks of a time (the job takes as long as its slowest rank). Replicas exchange no data.
+    The process group's timeout ends a rank that waits for one which never arrives with an error. nccl on the GPU
+    box; gloo (host tensors) for the CPU tests of this logic. Returns (barrier, maxreduce)."""
+    if world == 1:
+        return (lambda: None), (lambda x: x)
+    import datetime
+    import torch
+    import torch.distributed as dist
+    if backend == "nccl":
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+    dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s))
+    dev = "cuda" if backend == "nccl" else "cpu"
+
+    def barrier():
+        dist.barrier()
+
+    def maxreduce(x):
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+    return barrier, maxreduce
+
+
+def aggregate(units_per_rank, world, dev_s_max, wall_s_max):
+    """Whole-job throughput: the units all ranks processed over the slowest rank's time (device, and host clock around
+    the C-ABI calls for e2e)."""
+    units = units_per_rank * world
+    return units / dev_s_max, units / wall_s_max
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return
@@ -781,22 +811,7 @@ def main():
         return run_c5(args)
     if args.impl == "reference":
         return run_reference(args, rank, world)
-    barrier = lambda: None  # noqa: E731
-    maxreduce = lambda x: x  # noqa: E731
-    if world > 1:
-        import datetime
-        import torch
-        import torch.distributed as dist
-        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=1800))
-
-        def barrier():
-            dist.barrier()
-
-        def maxreduce(x):
-            t = torch.tensor([x], dtype=torch.float64, device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            return float(t.item())
+    barrier, maxreduce = collectives(world)
     try:
         run_mine(args, rank, world, barrier, maxreduce)
     finally:
