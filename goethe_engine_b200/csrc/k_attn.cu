@@ -22,6 +22,8 @@
 // fp8 pages: K and V codes are exact in f16; the per-page exponents (scale 2^e, see k_misc.cu) come back as a 2^-ek
 // factor on each score and as a running exponent E on the accumulator (O is kept scaled by 2^E, E = the V exponent of
 // the group's first entry; entries of other pages in the group carry 2^(E - ev) on their probability).
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -67,8 +69,28 @@ __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
   asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;\n" : "=r"(d) : "r"(x));
   return d;
 }
+// four e4m3 codes (bytes 0..3 of w) -> f16x2 of bytes (0, 1) and of bytes (2, 3), the word split into its 16-bit halves
+__device__ __forceinline__ void e4m3x4_to_h2x2(uint32_t w, uint32_t &lo, uint32_t &hi) {
+  asm("{\n .reg .b16 l, h;\n mov.b32 {l, h}, %2;\n cvt.rn.f16x2.e4m3x2 %0, l;\n cvt.rn.f16x2.e4m3x2 %1, h;\n}\n"
+      : "=r"(lo), "=r"(hi)
+      : "r"(w));
+}
+// the CTA's barrier; a one-warp CTA needs only the warp's (which orders the lanes' shared-memory accesses, the cp.async
+// rows each lane waited for included)
+template <int NW>
+__device__ __forceinline__ void cta_sync() {
+  if constexpr (NW == 1) __syncwarp();
+  else __syncthreads();
+}
 // 2^e as a float for an integer e in [-126, 127], built from its bits (exact)
 __device__ __forceinline__ float pow2i(int e) { return __int_as_float((127 + e) << 23); }
+// 2^x by the hardware approximation (PTX ex2.approx.ftz: exactly 1 at 0 and +0 at -inf; results below 2^-126 flush
+// to 0, far under what an f16 probability or the f32 row sum can hold)
+__device__ __forceinline__ float ex2(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(r) : "f"(x));
+  return r;
+}
 
 // One warp = up to 8 * NT query rows (row r: token r / G of the group, query head head * G + r % G) against one kv
 // head. Per 16-entry group, with the entries as the MMA's M and the query rows as its N (tiles of 8 rows):
@@ -123,7 +145,7 @@ __global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn
       sGE[2 * gi + 1] = pe[1];
     }
   }
-  __syncthreads();
+  cta_sync<NW>();
 
   // ---- Q^T fragments: tile nt, lane (g, t): row nt*8 + g, dims t*dh/4 + 4s + {0,1} (b0) and {2,3} (b1)
   uint32_t qb[NT][C::NKS][2];
@@ -240,10 +262,8 @@ __global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn
     for (int s = 0; s < C::NKS; s++) {
       uint32_t af[4];
       if (FP8) {
-        af[0] = e4m3x2_to_h2(static_cast<uint16_t>(k0[s] & 0xffff));
-        af[2] = e4m3x2_to_h2(static_cast<uint16_t>(k0[s] >> 16));
-        af[1] = e4m3x2_to_h2(static_cast<uint16_t>(k1[s] & 0xffff));
-        af[3] = e4m3x2_to_h2(static_cast<uint16_t>(k1[s] >> 16));
+        e4m3x4_to_h2x2(k0[s], af[0], af[2]);
+        e4m3x4_to_h2x2(k1[s], af[1], af[3]);
       } else {
         af[0] = k0[2 * s]; af[2] = k0[2 * s + 1];
         af[1] = k1[2 * s]; af[3] = k1[2 * s + 1];
@@ -283,7 +303,9 @@ __global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn
       pv0 = pow2i(E - ev0);
       pv1 = pow2i(E - ev1);
     }
-    // ---- online softmax per row (log2 domain); a row's 16 entries sit in the 8 lanes of one t
+    // ---- online softmax per row (log2 domain); a row's 16 entries sit in the 8 lanes of one t. The max is reduced
+    // across those lanes every group; the row sum stays per lane (every lane of a row applies the same rescalings)
+    // and is reduced once after the last group
     uint32_t pb[NT][2];
     float f[NT][2];
 #pragma unroll
@@ -305,15 +327,11 @@ __global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
         const float mn = fmaxf(mrow[nt][c], mx);
-        const float alpha = mn == -INFINITY ? 1.f : exp2f(mrow[nt][c] - mn);
+        const float alpha = mn == -INFINITY ? 1.f : ex2(mrow[nt][c] - mn);
         mrow[nt][c] = mn;
-        p[0][c] = mn == -INFINITY ? 0.f : exp2f(x[0][c] - mn);
-        p[1][c] = mn == -INFINITY ? 0.f : exp2f(x[1][c] - mn);
-        float ps = p[0][c] + p[1][c];
-        ps += __shfl_xor_sync(0xffffffffu, ps, 4);
-        ps += __shfl_xor_sync(0xffffffffu, ps, 8);
-        ps += __shfl_xor_sync(0xffffffffu, ps, 16);
-        lrow[nt][c] = lrow[nt][c] * alpha + ps;
+        p[0][c] = mn == -INFINITY ? 0.f : ex2(x[0][c] - mn);
+        p[1][c] = mn == -INFINITY ? 0.f : ex2(x[1][c] - mn);
+        lrow[nt][c] = lrow[nt][c] * alpha + (p[0][c] + p[1][c]);
         f[nt][c] = alpha * fe;
       }
       // P^T as the PV B operand: (entries 2t, 2t+1 | 2t+8, 2t+9) of row g
@@ -354,13 +372,12 @@ __global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn
     for (int mt = 0; mt < C::NMT; mt++) {
       uint32_t af[4];
       if (FP8) {
-        // dims 2mt (rows g) and 2mt + 1 (rows g + 8) of the slice: byte 2mt % 4 (+1) of word mt / 2
+        // dims 2mt (rows g) and 2mt + 1 (rows g + 8) of the slice: byte 2mt % 4 (+1) of word mt / 2; one permute
+        // gathers both dims' entry pairs (low half: dim 2mt, high half: dim 2mt + 1)
         const int wi = mt / 2, b0 = 2 * (mt % 2);
-        const uint32_t s0 = b0 | ((4 + b0) << 4), s1 = (b0 + 1) | ((5 + b0) << 4);
-        af[0] = e4m3x2_to_h2(static_cast<uint16_t>(prmt(vr[0][wi], vr[1][wi], s0)));
-        af[1] = e4m3x2_to_h2(static_cast<uint16_t>(prmt(vr[0][wi], vr[1][wi], s1)));
-        af[2] = e4m3x2_to_h2(static_cast<uint16_t>(prmt(vr[2][wi], vr[3][wi], s0)));
-        af[3] = e4m3x2_to_h2(static_cast<uint16_t>(prmt(vr[2][wi], vr[3][wi], s1)));
+        const uint32_t sel = b0 | ((4 + b0) << 4) | ((b0 + 1) << 8) | ((5 + b0) << 12);
+        e4m3x4_to_h2x2(prmt(vr[0][wi], vr[1][wi], sel), af[0], af[1]);
+        e4m3x4_to_h2x2(prmt(vr[2][wi], vr[3][wi], sel), af[2], af[3]);
       } else {
         af[0] = prmt(vr[0][mt], vr[1][mt], 0x5410u);
         af[1] = prmt(vr[0][mt], vr[1][mt], 0x7632u);
@@ -377,11 +394,11 @@ __global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn
     if (gi + C::NST - 1 < ngroups) issue(gi + C::NST - 1, (gi + C::NST - 1) % C::NST);
     cp_async_commit();
     cp_async_wait<C::NST - 1>();
-    __syncthreads();
+    cta_sync<NW>();
     const int i0 = lo + gi * kGroup;
     if (active && i0 < qg.nvis)
       consume(sm + buf * C::BUF, i0, sPg[gi] >= 0 ? sGE + 2 * gi : nullptr, sEE + buf * kGroup * 2, 0xFFFFFFFFu);
-    __syncthreads();
+    cta_sync<NW>();
   }
   cp_async_wait<0>();
 
@@ -421,6 +438,18 @@ __global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn
       }
     }
   }
+
+  // the row sums: the 8 lanes of a row (same t) hold their entries' shares, reduced in one fixed order
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+    for (int c = 0; c < 2; c++) {
+      float l = lrow[nt][c];
+      l += __shfl_xor_sync(0xffffffffu, l, 4);
+      l += __shfl_xor_sync(0xffffffffu, l, 8);
+      l += __shfl_xor_sync(0xffffffffu, l, 16);
+      lrow[nt][c] = l;
+    }
 
   if (!active || w.split >= qg.nsplit) return;
   const int rows = qg.ntok * G;
@@ -465,47 +494,80 @@ __global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn
   last = __shfl_sync(0xffffffffu, last, 0);
   if (!last) return;
   __threadfence();
-  // the splits' (m, l) a lane each and their O rows kMergeChunk splits at a time are loaded together; the sums run in
-  // split order as before, so the loads are parallel and the arithmetic is unchanged
-  constexpr int kMergeChunk = 8;
+  // kMergeRows rows at a time: their (m, l) per split a lane each, then their O rows of kMergeChunk splits loaded
+  // together (a lane's DPL consecutive dims of each, one vector load); every element still sums in split order, and
+  // which split finished last does not change the arithmetic
+  constexpr int kMergeChunk = 8, kMergeRows = 2, DPL = DH / 32;
+  using Vec = typename std::conditional<DPL == 4, float4, float2>::type;
   const int pb0 = qg.part_base + head * qg.nsplit, S = qg.nsplit;
-  for (int r = 0; r < rows; r++) {
-    float m = -INFINITY;
-    for (int s0 = 0; s0 < S; s0 += 32)
-      if (s0 + lane < S) m = fmaxf(m, __ldcg(&a.part_ml[static_cast<size_t>(pb0 + s0 + lane) * 16 + r]).x);
-    m = warp_max(m);
-    float num[DH / 32], den = 0.f;
+  for (int rb = 0; rb < rows; rb += kMergeRows) {
+    float m[kMergeRows];
 #pragma unroll
-    for (int k = 0; k < DH / 32; k++) num[k] = 0.f;
+    for (int r = 0; r < kMergeRows; r++) m[r] = -INFINITY;
+    for (int s0 = 0; s0 < S; s0 += 32)
+#pragma unroll
+      for (int r = 0; r < kMergeRows; r++)
+        if (rb + r < rows && s0 + lane < S)
+          m[r] = fmaxf(m[r], __ldcg(&a.part_ml[static_cast<size_t>(pb0 + s0 + lane) * 16 + rb + r]).x);
+#pragma unroll
+    for (int r = 0; r < kMergeRows; r++) m[r] = warp_max(m[r]);
+    float num[kMergeRows][DPL], den[kMergeRows];
+#pragma unroll
+    for (int r = 0; r < kMergeRows; r++) {
+      den[r] = 0.f;
+#pragma unroll
+      for (int k = 0; k < DPL; k++) num[r][k] = 0.f;
+    }
     for (int s0 = 0; s0 < S; s0 += 32) {
-      const float2 ml = s0 + lane < S ? __ldcg(&a.part_ml[static_cast<size_t>(pb0 + s0 + lane) * 16 + r])
-                                      : make_float2(-INFINITY, 0.f);
-      const float w = ml.x == -INFINITY ? 0.f : exp2f(ml.x - m);
+      float wr[kMergeRows], lr[kMergeRows];
+#pragma unroll
+      for (int r = 0; r < kMergeRows; r++) {
+        const float2 ml = rb + r < rows && s0 + lane < S
+                              ? __ldcg(&a.part_ml[static_cast<size_t>(pb0 + s0 + lane) * 16 + rb + r])
+                              : make_float2(-INFINITY, 0.f);
+        wr[r] = ml.x == -INFINITY ? 0.f : exp2f(ml.x - m[r]);
+        lr[r] = ml.y;
+      }
       const int n = min(32, S - s0);
       for (int j0 = 0; j0 < n; j0 += kMergeChunk) {
-        float po[kMergeChunk][DH / 32];
+        float po[kMergeChunk][kMergeRows][DPL];
 #pragma unroll
-        for (int j = 0; j < kMergeChunk; j++) {
-          const float *src = a.part_o + (static_cast<size_t>(pb0 + s0 + j0 + j) * 16 + r) * DH;
+        for (int j = 0; j < kMergeChunk; j++)
 #pragma unroll
-          for (int k = 0; k < DH / 32; k++) po[j][k] = j0 + j < n ? __ldcg(src + lane + 32 * k) : 0.f;
-        }
+          for (int r = 0; r < kMergeRows; r++) {
+            Vec v;
+            if (j0 + j < n && rb + r < rows) {
+              const float *src = a.part_o + (static_cast<size_t>(pb0 + s0 + j0 + j) * 16 + rb + r) * DH + lane * DPL;
+              v = __ldcg(reinterpret_cast<const Vec *>(src));
+            } else {
+              v = Vec{};
+            }
+            const float *vf = reinterpret_cast<const float *>(&v);
 #pragma unroll
-        for (int j = 0; j < kMergeChunk; j++) {
-          const float wj = __shfl_sync(0xffffffffu, w, (j0 + j) & 31);
-          const float lj = __shfl_sync(0xffffffffu, ml.y, (j0 + j) & 31);
-          if (j0 + j < n) {
-#pragma unroll
-            for (int k = 0; k < DH / 32; k++) num[k] += po[j][k] * wj;
-            den += lj * wj;
+            for (int k = 0; k < DPL; k++) po[j][r][k] = vf[k];
           }
-        }
+#pragma unroll
+        for (int j = 0; j < kMergeChunk; j++)
+#pragma unroll
+          for (int r = 0; r < kMergeRows; r++) {
+            const float wj = __shfl_sync(0xffffffffu, wr[r], (j0 + j) & 31);
+            const float lj = __shfl_sync(0xffffffffu, lr[r], (j0 + j) & 31);
+            if (j0 + j < n) {
+#pragma unroll
+              for (int k = 0; k < DPL; k++) num[r][k] += po[j][r][k] * wj;
+              den[r] += lj * wj;
+            }
+          }
       }
     }
-    const int tok = it.tok0 + qg.j0 + r / G, qo = head * G + r % G;
-    __half *dst = a.out + (static_cast<size_t>(tok) * a.H + qo) * DH;
 #pragma unroll
-    for (int k = 0; k < DH / 32; k++) dst[lane + 32 * k] = __float2half_rn(num[k] / den);
+    for (int r = 0; r < kMergeRows; r++) {
+      if (rb + r >= rows) break;
+      const int tok = it.tok0 + qg.j0 + (rb + r) / G, qo = head * G + (rb + r) % G;
+      __half *dst = a.out + (static_cast<size_t>(tok) * a.H + qo) * DH + lane * DPL;
+#pragma unroll
+      for (int k = 0; k < DPL; k++) dst[k] = __float2half_rn(num[r][k] / den[r]);
+    }
   }
   if (lane == 0) a.sem[qgi * a.KVH + head] = 0;   // ready for the next launch
 }
