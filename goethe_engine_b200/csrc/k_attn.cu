@@ -82,6 +82,9 @@ __device__ __forceinline__ void cta_sync() {
   if constexpr (NW == 1) __syncwarp();
   else __syncthreads();
 }
+// the running max's starting value: finite, and so far below any score (|score| < 2^100 in the log2 domain) that
+// 2^(kMaxFloor - score) is 0
+constexpr float kMaxFloor = -1e30f;
 // 2^e as a float for an integer e in [-126, 127], built from its bits (exact)
 __device__ __forceinline__ float pow2i(int e) { return __int_as_float((127 + e) << 23); }
 // 2^x by the hardware approximation (PTX ex2.approx.ftz: exactly 1 at 0 and +0 at -inf; results below 2^-126 flush
@@ -182,6 +185,14 @@ __global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn
       rvalid[nt][c] = r < nrows;
       nvis[nt][c] = qg.path_len ? it.pos + (r / G == 0 ? qg.path_len : qg.path_len1) : it.pos + qg.j0 + r / G + 1;
     }
+  // a group that ends at or below every row's visible count needs no position masks (warp-uniform test)
+  int nvis_lo = INT_MAX;
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+    for (int c = 0; c < 2; c++)
+      if (rvalid[nt][c]) nvis_lo = min(nvis_lo, nvis[nt][c]);
+  nvis_lo = __reduce_min_sync(0xffffffffu, nvis_lo);
 
   const uint8_t *kbase = static_cast<const uint8_t *>(a.kc);
   const uint8_t *vbase = static_cast<const uint8_t *>(a.vc);
@@ -226,7 +237,9 @@ __global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn
     for (int j = 0; j < C::NMT; j++) o[nt][j][0] = o[nt][j][1] = o[nt][j][2] = o[nt][j][3] = 0.f;
   float mrow[NT][2], lrow[NT][2];
 #pragma unroll
-  for (int nt = 0; nt < NT; nt++) mrow[nt][0] = mrow[nt][1] = -INFINITY, lrow[nt][0] = lrow[nt][1] = 0.f;
+  // the running max starts at a finite floor far below any score: 2^(floor - m) is 0 once a score is seen, and
+  // exactly 1 (with p = 2^-inf = 0) while a row has seen only masked entries, so no -inf special cases are needed
+  for (int nt = 0; nt < NT; nt++) mrow[nt][0] = mrow[nt][1] = kMaxFloor, lrow[nt][0] = lrow[nt][1] = 0.f;
   int E = 0;
   bool have_e = false;
 
@@ -303,6 +316,7 @@ __global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn
       pv0 = pow2i(E - ev0);
       pv1 = pow2i(E - ev1);
     }
+    const bool full = i0 + kGroup <= nvis_lo;
     // ---- online softmax per row (log2 domain); a row's 16 entries sit in the 8 lanes of one t. The max is reduced
     // across those lanes every group; the row sum stays per lane (every lane of a row applies the same rescalings)
     // and is reduced once after the last group
@@ -314,10 +328,16 @@ __global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn
 #pragma unroll
       for (int c = 0; c < 2; c++) {
         const bool in = rvalid[nt][c] && ((rmask >> (nt * 8 + 2 * t + c)) & 1u);
-        const bool ok0 = in && i0 + g < nvis[nt][c];
-        const bool ok1 = in && i0 + g + 8 < nvis[nt][c];
-        x[0][c] = ok0 ? sc[nt][c] * ks0 : -INFINITY;
-        x[1][c] = ok1 ? sc[nt][2 + c] * ks1 : -INFINITY;
+        if (full) {
+          const float bias = in ? 0.f : -INFINITY;
+          x[0][c] = fmaf(sc[nt][c], ks0, bias);
+          x[1][c] = fmaf(sc[nt][2 + c], ks1, bias);
+        } else {
+          const bool ok0 = in && i0 + g < nvis[nt][c];
+          const bool ok1 = in && i0 + g + 8 < nvis[nt][c];
+          x[0][c] = ok0 ? sc[nt][c] * ks0 : -INFINITY;
+          x[1][c] = ok1 ? sc[nt][2 + c] * ks1 : -INFINITY;
+        }
       }
       float p[2][2];
 #pragma unroll
@@ -327,10 +347,10 @@ __global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
         const float mn = fmaxf(mrow[nt][c], mx);
-        const float alpha = mn == -INFINITY ? 1.f : ex2(mrow[nt][c] - mn);
+        const float alpha = ex2(mrow[nt][c] - mn);
         mrow[nt][c] = mn;
-        p[0][c] = mn == -INFINITY ? 0.f : ex2(x[0][c] - mn);
-        p[1][c] = mn == -INFINITY ? 0.f : ex2(x[1][c] - mn);
+        p[0][c] = ex2(x[0][c] - mn);
+        p[1][c] = ex2(x[1][c] - mn);
         lrow[nt][c] = lrow[nt][c] * alpha + (p[0][c] + p[1][c]);
         f[nt][c] = alpha * fe;
       }
