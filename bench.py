@@ -36,7 +36,7 @@ B, PREFIX = 64, 1024
 METRIC = "decode tok/s (8B Q4_K, batch 64, fp8 KV)"
 # DRAM bytes (read + write) of one attention launch of this workload, from the ncu capture summarised in
 # profiles/attn_kernel_c3_decode_L2.md (a layer's launch there has the full-size KV of these 64 contexts)
-ATTN_TRAFFIC = 287_648_512
+ATTN_TRAFFIC = 288_064_256
 
 
 def contexts():
