@@ -69,6 +69,32 @@ def test_gemv_tolerance_bucket(tmp_path, wtype):
     assert any(not np.array_equal(a, b) for a, b in zip(outs["tol"], outs["bi"]))
 
 
+@pytest.mark.parametrize("kv", ["f16", "fp8"])
+def test_long_context_merge_of_many_splits(tmp_path, kv):
+    """One sequence decoding over a 2200-row context in a tolerance bucket: a step with this little attention work takes
+    64-entry splits, so each token's 35 splits are merged in two passes (32 splits, then 3) by the last split to
+    finish; the decode logits match the oracle's (ref.py:39-62 over the same pages)."""
+    spec = synth.Spec(**SMALL128, wtype="q8_0", seed=21, ctx=4096)
+    ws = synth.make(str(tmp_path / "w"), spec, ncol=2, maxctx=4096)[1]
+    kv_scale = "page" if kv == "fp8" else "unit"
+    pack = synth.pack_dir(str(tmp_path / "tol"), spec, [dict(id="b200.FAST.main", ncol=2, maxctx=4096, kv=kv,
+                                                             determinism="tolerance",
+                                                             tune=dict(max_cols=2048, kv_scale=kv_scale))],
+                          weights_file=ws[0])
+    rng = np.random.default_rng(17)
+    toks = [int(x) for x in rng.integers(1, 500, 2203)]
+    blocks = list(range(140))
+    script = [dict(sid=1, tokens=toks[:2000], pos=0, blocks=blocks, want=0),
+              dict(sid=1, tokens=toks[2000:2200], pos=2000, blocks=blocks, want=0)]
+    script += [dict(sid=1, tokens=[toks[2200 + j]], pos=2200 + j, blocks=blocks, want=1) for j in range(3)]
+    with backend(pack, ws, buckets=("b200.FAST.main",), pool_blocks=150) as be:
+        got = [be.step([work(d)]) for d in script]
+    orc = oracle_for(ws, num_blocks=150, kv=kv, kv_scale=kv_scale)
+    ref = [orc.step([d]) for d in script]
+    for g, r in zip(got[2:], ref[2:]):
+        assert_logits_close(g, r, TOL_FP8 if kv == "fp8" else TOL_F16)
+
+
 @pytest.mark.parametrize("kv_scale", ["page", "unit"])
 def test_session_matches_oracle_fp8_kv(tmp_path, kv_scale):
     spec = synth.Spec(**SMALL128, wtype="q4_k", seed=5)
