@@ -133,9 +133,11 @@ void launch_tp_reduce_scatter(const TpPeers &p, int b, unsigned long long epoch,
 
 constexpr int kNormThreads = 512;
 constexpr int kNormMaxVec = 4;    // float4 loads per thread: d <= 512 * 4 * 4 = 8192
-// split-K partials are read kSplitChunk slices at a time, all their loads in flight together, and summed in split order
+// split-K partials are read kSplitChunk slices at a time (RMSNorm: as many as keep 16 float4 loads per thread),
+// all their loads in flight together, and summed in split order
 constexpr int kSplitChunk = 4;
 
+template <int NV>
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float *x, const int *rows, const float *gain, float eps,
                                                                int d, int ld, __half *out, const float *part, int S,
                                                                int pld, int T, TpPeers tp, int tpb,
@@ -156,15 +158,15 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float *x, const i
   float4 *xr = reinterpret_cast<float4 *>(x + static_cast<size_t>(src) * d);
   const float4 *gr = reinterpret_cast<const float4 *>(gain);
   const int nv = d / 4;
-  float4 v[kNormMaxVec];
+  float4 v[NV];
 #pragma unroll
-  for (int i = 0; i < kNormMaxVec; i++) {
+  for (int i = 0; i < NV; i++) {
     int e = threadIdx.x + i * kNormThreads;
     v[i] = e < nv ? xr[e] : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   if (tpsum) {
 #pragma unroll
-    for (int i = 0; i < kNormMaxVec; i++) {
+    for (int i = 0; i < NV; i++) {
       int e = threadIdx.x + i * kNormThreads;
       if (e >= nv) continue;
       const float4 a = __ldcv(reinterpret_cast<const float4 *>(tpsum) + e);
@@ -174,31 +176,33 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float *x, const i
   }
   if (part) {
     // per element: ((0 + p_0) + p_1) + ... in split order, then added to x; a chunk's loads are all issued first
-    float4 a[kNormMaxVec];
+    float4 a[NV];
 #pragma unroll
-    for (int i = 0; i < kNormMaxVec; i++) a[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int sp0 = 0; sp0 < S; sp0 += kSplitChunk) {
-      float4 pp[kSplitChunk][kNormMaxVec];
+    for (int i = 0; i < NV; i++) a[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    // a chunk of CH splits keeps 16 float4 loads in flight per thread whatever the row length
+    constexpr int CH = 16 / NV;
+    for (int sp0 = 0; sp0 < S; sp0 += CH) {
+      float4 pp[CH][NV];
 #pragma unroll
-      for (int j = 0; j < kSplitChunk; j++) {
+      for (int j = 0; j < CH; j++) {
         const float4 *pr = reinterpret_cast<const float4 *>(part + (static_cast<size_t>(sp0 + j) * T + src) * pld);
 #pragma unroll
-        for (int i = 0; i < kNormMaxVec; i++) {
+        for (int i = 0; i < NV; i++) {
           int e = threadIdx.x + i * kNormThreads;
           pp[j][i] = sp0 + j < S && e < nv ? pr[e] : make_float4(0.f, 0.f, 0.f, 0.f);
         }
       }
 #pragma unroll
-      for (int j = 0; j < kSplitChunk; j++) {
+      for (int j = 0; j < CH; j++) {
         if (sp0 + j >= S) break;
 #pragma unroll
-        for (int i = 0; i < kNormMaxVec; i++) {
+        for (int i = 0; i < NV; i++) {
           a[i].x += pp[j][i].x; a[i].y += pp[j][i].y; a[i].z += pp[j][i].z; a[i].w += pp[j][i].w;
         }
       }
     }
 #pragma unroll
-    for (int i = 0; i < kNormMaxVec; i++) {
+    for (int i = 0; i < NV; i++) {
       int e = threadIdx.x + i * kNormThreads;
       if (e >= nv) continue;
       v[i].x += a[i].x; v[i].y += a[i].y; v[i].z += a[i].z; v[i].w += a[i].w;
@@ -207,7 +211,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float *x, const i
   }
   float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < kNormMaxVec; i++) {
+  for (int i = 0; i < NV; i++) {
     ss = fmaf(v[i].x, v[i].x, ss);
     ss = fmaf(v[i].y, v[i].y, ss);
     ss = fmaf(v[i].z, v[i].z, ss);
@@ -227,7 +231,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float *x, const i
   float inv = rsqrtf(wsum[0] / static_cast<float>(d) + eps);
   __half2 *o = reinterpret_cast<__half2 *>(out + static_cast<size_t>(r) * ld);
 #pragma unroll
-  for (int i = 0; i < kNormMaxVec; i++) {
+  for (int i = 0; i < NV; i++) {
     int e = threadIdx.x + i * kNormThreads;
     if (e < nv) {
       float4 g = gr[e];
@@ -243,9 +247,19 @@ void launch_rmsnorm(float *x, const int *rows, int n, const float *gain, float e
                     unsigned long long tp_epoch, cudaStream_t s) {
   TpPeers none{};
   none.n = 1;
-  if (n > 0)
-    launch_pdl(rmsnorm_kernel, n, kNormThreads, 0, s, x, rows, gain, eps, d, ld, out, part, S, pld, T, tp ? *tp : none,
-               tp_buf, tp_epoch);
+  if (n <= 0) return;
+  // float4s per thread for a row of d: 1 (d <= 2048), 2 (d <= 4096) or 4 (d <= 8192)
+  const int nvec = (d / 4 + kNormThreads - 1) / kNormThreads;
+  const TpPeers &tpp = tp ? *tp : none;
+  if (nvec <= 1)
+    launch_pdl(rmsnorm_kernel<1>, n, kNormThreads, 0, s, x, rows, gain, eps, d, ld, out, part, S, pld, T, tpp, tp_buf,
+               tp_epoch);
+  else if (nvec == 2)
+    launch_pdl(rmsnorm_kernel<2>, n, kNormThreads, 0, s, x, rows, gain, eps, d, ld, out, part, S, pld, T, tpp, tp_buf,
+               tp_epoch);
+  else
+    launch_pdl(rmsnorm_kernel<kNormMaxVec>, n, kNormThreads, 0, s, x, rows, gain, eps, d, ld, out, part, S, pld, T,
+               tpp, tp_buf, tp_epoch);
 }
 
 // ----------------------------------------------------------------------------------------------------------------
