@@ -312,6 +312,38 @@ struct QkvSrc {
     }
     return v;
   }
+  // columns c[i], c[i] + 1 (each even) for i < N: every column's 8-byte load of a chunk of splits issued together
+  // (32 / N splits: 32 float2 in flight per thread), each column summed in split order as pair() does
+  template <int N>
+  __device__ void pairs(int t, const int (&c)[N], float2 (&v)[N]) const {
+    if (S == 1) {
+#pragma unroll
+      for (int i = 0; i < N; i++) v[i] = *reinterpret_cast<const float2 *>(p + static_cast<size_t>(t) * ld + c[i]);
+      return;
+    }
+    constexpr int CH = 32 / N;
+#pragma unroll
+    for (int i = 0; i < N; i++) v[i] = make_float2(0.f, 0.f);
+    for (int s0 = 0; s0 < S; s0 += CH) {
+      float2 x[CH][N];
+#pragma unroll
+      for (int jj = 0; jj < CH; jj++) {
+        const float *row = p + (static_cast<size_t>(s0 + jj) * T + t) * ld;
+#pragma unroll
+        for (int i = 0; i < N; i++)
+          x[jj][i] = s0 + jj < S ? *reinterpret_cast<const float2 *>(row + c[i]) : make_float2(0.f, 0.f);
+      }
+#pragma unroll
+      for (int jj = 0; jj < CH; jj++)
+        if (s0 + jj < S) {
+#pragma unroll
+          for (int i = 0; i < N; i++) {
+            v[i].x += x[jj][i].x;
+            v[i].y += x[jj][i].y;
+          }
+        }
+    }
+  }
 };
 
 // RoPE of one (even, odd) pair, rounded step by step (no contraction), so that every kernel site that rotates a row
@@ -354,11 +386,26 @@ __global__ void rope_kv_kernel(PlanView pv, QkvSrc qs, int H, int KVH, const flo
   const int r = is_q ? 0 : pv.kv_row[t];
   const int ft = fp8_page ? pv.first_tok[t] : -1;
   float2 x[NP], xv[NP], c[NP];
+  if (is_q) {
+    int cols[NP];
 #pragma unroll
-  for (int p = 0; p < NP; p++) x[p] = qs.pair(t, c0 + 2 * (lane + 32 * p));
-  if (!is_q) {
+    for (int p = 0; p < NP; p++) cols[p] = c0 + 2 * (lane + 32 * p);
+    qs.pairs<NP>(t, cols, x);
+  } else {
+    // the k and v columns in one gather
+    int cols[2 * NP];
+    float2 kv[2 * NP];
 #pragma unroll
-    for (int p = 0; p < NP; p++) xv[p] = qs.pair(t, vcol + 2 * (lane + 32 * p));
+    for (int p = 0; p < NP; p++) {
+      cols[p] = c0 + 2 * (lane + 32 * p);
+      cols[NP + p] = vcol + 2 * (lane + 32 * p);
+    }
+    qs.pairs<2 * NP>(t, cols, kv);
+#pragma unroll
+    for (int p = 0; p < NP; p++) {
+      x[p] = kv[p];
+      xv[p] = kv[NP + p];
+    }
   }
   const float2 *cs = rope_tab + static_cast<size_t>(pos) * (DH / 2);
 #pragma unroll
