@@ -9,6 +9,7 @@ returns per-item token lists (device argmax, all items greedy) or float32 logits
 Nothing here computes: every step runs in libgck.so on the GPU. A missing library or a machine without the device
 fails loudly (``GcError``); there is no fallback.
 """
+import array
 import ctypes as C
 import os
 from dataclasses import dataclass
@@ -64,6 +65,15 @@ assert WORK_DTYPE.itemsize == C.sizeof(WorkS) and all(
 
 def _addr(a):
     return a.__array_interface__["data"][0]
+
+
+def _flat(work, field, code, dtype):
+    """Every item's `field` (a sequence of ints) in one contiguous array. array.array converts Python ints at C speed
+    (about half the time of numpy.fromiter, a third of a conversion per item); out-of-range values raise."""
+    a = array.array(code)
+    for w in work:
+        a.extend(getattr(w, field))
+    return np.frombuffer(a, dtype) if len(a) else np.zeros(0, dtype)
 
 
 def _u32(x):
@@ -159,10 +169,12 @@ class Backend:
         # every item's tokens in one int32 array, every block table in one uint32 array, the records in one structured
         # array (filled a column at a time), their addresses in another: a handful of numpy calls per step
         ntok = np.fromiter((len(w.tokens) for w in work), np.int64, n)
-        toks = np.fromiter((t for w in work for t in w.tokens), np.int32, int(ntok.sum()))
-        blks = [_u32(w.blocks) for w in work]
-        nblk = np.fromiter((len(x) for x in blks), np.int64, n)
-        ball = np.concatenate(blks) if n else np.zeros(0, np.uint32)
+        toks = _flat(work, "tokens", "i", np.int32)
+        nblk = np.fromiter((len(w.blocks) for w in work), np.int64, n)
+        if n and all(isinstance(w.blocks, np.ndarray) for w in work):
+            ball = np.concatenate([_u32(w.blocks) for w in work])
+        else:
+            ball = _flat(work, "blocks", "I", np.uint32)
         rec = np.zeros(n, WORK_DTYPE)
         keep = [toks, rec, ball]
         rec["size"] = WORK_DTYPE.itemsize
