@@ -1693,11 +1693,12 @@ GC_API int gc_probe(int device, void *constants, uint64_t cap, uint64_t *size) {
     b.clock_mhz = static_cast<uint32_t>(clk / 1000);
     const size_t bytes = static_cast<size_t>(512) << 20;   // 512 MiB each way: well past L2
     const size_t n = bytes / sizeof(float4);
-    if (cudaMalloc(&x, bytes) != cudaSuccess || cudaMalloc(&y, bytes) != cudaSuccess) { rc = GC_E_DEVICE; break; }
-    cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
-    cudaEventCreate(&e0);
-    cudaEventCreate(&e1);
-    cudaMemsetAsync(x, 0, bytes, st);
+    if (cudaMalloc(&x, bytes) != cudaSuccess || cudaMalloc(&y, bytes) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess || cudaEventCreate(&e0) != cudaSuccess ||
+        cudaEventCreate(&e1) != cudaSuccess || cudaMemsetAsync(x, 0, bytes, st) != cudaSuccess) {
+      rc = GC_E_DEVICE;
+      break;
+    }
     const int grid = static_cast<int>(b.sms) * 8;
     float best = 1e30f;
     for (int it = 0; it < 5; it++) {
@@ -1727,6 +1728,7 @@ GC_API int gc_probe(int device, void *constants, uint64_t cap, uint64_t *size) {
   if (x) cudaFree(x);
   if (y) cudaFree(y);
   cudaSetDevice(prev);
+  if (rc != GC_OK) cudaGetLastError();   // a failed probe leaves no pending error for the caller's next CUDA call
   if (rc == GC_OK) std::memcpy(constants, &b, sizeof b);
   return rc;
 }
