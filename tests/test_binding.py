@@ -54,3 +54,26 @@ def test_logits_request_without_device_argmax():
     b = backend(False)
     lg = b.step([gck.Work(1, [3], 0, [0], 1)])
     assert lg.shape == (1, 1000) and b.L.seen[0]["flags"] == 0
+
+
+def test_all_array_tables_and_all_list_tables_give_the_same_records():
+    # block tables given as uint32 arrays pass through as one concatenation; Python lists are converted in one pass
+    tabs = [[3, 9, 1], [40], list(range(100, 137))]
+    b1, b2 = backend(True), backend(True)
+    b1.step([gck.Work(i, [i + 1, 7], 16 * i, t, 1, greedy=True) for i, t in enumerate(tabs)])
+    b2.step([gck.Work(i, np.array([i + 1, 7], np.int32), 16 * i, np.asarray(t, np.uint32), 1, greedy=True)
+             for i, t in enumerate(tabs)])
+    assert b1.L.seen == b2.L.seen
+    assert [r["blocks"] for r in b1.L.seen] == tabs
+
+
+def test_values_outside_the_record_types_raise_on_the_host():
+    # a negative block id or a token beyond int32 cannot be written into the records: an error, not a wrapped value
+    b = backend(True)
+    for bad in (gck.Work(1, [3], 0, [0, -1], 1, greedy=True), gck.Work(1, [2 ** 31], 0, [0], 1, greedy=True),
+                gck.Work(1, [3], 0, [2 ** 32], 1, greedy=True)):
+        try:
+            b.step([bad])
+        except (OverflowError, ValueError):
+            continue
+        raise AssertionError(f"accepted {bad}")
