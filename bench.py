@@ -34,9 +34,11 @@ SPEC8B = dict(vocab=128256, d=4096, layers=32, heads=32, kv_heads=8, ffn=14336, 
               std=0.02, seed=0, ctx=8192 + 128, name="llama3-8b-shape-q4k")
 B, PREFIX = 64, 1024
 METRIC = "decode tok/s (8B Q4_K, batch 64, fp8 KV)"
-# DRAM bytes (read + write) of one attention launch of this workload, from the ncu capture summarised in
-# profiles/attn_kernel_c3_decode_L2.md (a layer's launch there has the full-size KV of these 64 contexts)
-ATTN_TRAFFIC = 288_064_256
+# DRAM bytes (read + write) per launch from single-kernel ncu captures of this workload (the 8B shape with 2 of its 32
+# layers: a layer's launches have the full-size weights and KV); each names the library build it was captured on, and
+# is reported beside the live timing, never in place of it
+ATTN_TRAFFIC = dict(bytes=288_064_256, build="c152e19", kernel="attn_kernel<128, fp8, 1 warp, 1 row tile>")
+GEMM_TRAFFIC = None     # per GEMM launch of a 32-layer step: set from a capture of the current GEMM build
 
 
 def contexts():
@@ -198,8 +200,33 @@ def weight_bytes(spec):
     return n * 144 // 256
 
 
+class Stats:
+    """gck_ext.h step statistics of a handle: enable(mask) starts them, read() stops and returns them."""
+
+    def __init__(self, be):
+        import ctypes as C
+
+        class S(C.Structure):
+            _fields_ = [("size", C.c_uint32), ("steps", C.c_uint32), ("launches", C.c_uint64),
+                        ("forward_ms", C.c_double), ("class_ms", C.c_double * 16), ("class_launches", C.c_uint64 * 16)]
+        self.S, self.be, self.C = S, be, C
+        be.L.gck_stats_enable.argtypes = [C.c_void_p, C.c_uint32]
+        be.L.gck_stats_read.argtypes = [C.c_void_p, C.c_void_p]
+
+    def enable(self, mask=0):
+        self.be.L.gck_stats_enable(self.be.h, mask)
+
+    def read(self):
+        st = self.S(size=self.C.sizeof(self.S))
+        self.be.L.gck_stats_read(self.be.h, self.C.byref(st))
+        return st
+
+
+GEMMS = (2, 6, 7, 8, 9)           # gck_ext.h classes of the tcgen05 GEMM launches: q/k/v, o, gate/up, down, head
+ATTN, GATEUP = 4, 7
+
+
 def run_mine(args, rank, world, barrier, maxreduce):
-    import ctypes as C
     from goethe_engine_b200 import build, gck
     if rank == 0:
         build.build()
@@ -207,23 +234,16 @@ def run_mine(args, rank, world, barrier, maxreduce):
         barrier()
     spec, d, ws = ensure_model(rank, world, barrier)
     ctx = contexts()
-    GEMM_PASS = 5                       # steps after the timed region with events around every GEMM launch
-    steps_total = args.warmup + args.steps + GEMM_PASS
+    PASS = args.steps                   # steps of each per-kernel pass after the timed region
+    steps_total = args.warmup + args.steps + 2 * PASS
     dev = int(os.environ.get("LOCAL_RANK", 0))
     t0 = time.time()
     be = gck.Backend(d, ws, pool_blocks=int(np.sum(ctx)) // 16 + 2 * B + 64, device=dev)
     t_open = time.time() - t0
-    L = be.L
-    L.gck_stats_enable.argtypes = [C.c_void_p, C.c_uint32]
-    L.gck_stats_read.argtypes = [C.c_void_p, C.c_void_p]
-
-    class Stats(C.Structure):
-        _fields_ = [("size", C.c_uint32), ("steps", C.c_uint32), ("launches", C.c_uint64), ("forward_ms", C.c_double),
-                    ("class_ms", C.c_double * 16), ("class_launches", C.c_uint64 * 16)]
-    L.gck_stats_enable(be.h, 0)
+    stats = Stats(be)
+    stats.enable(0)
     tables, toks, t_prefill = setup_sequences(be, ctx, steps_total)
-    st0 = Stats(size=C.sizeof(Stats))
-    L.gck_stats_read(be.h, C.byref(st0))
+    st0 = stats.read()
     last = [t[-1] for t in toks]
     pos = [int(c) - 1 for c in ctx]
 
@@ -232,18 +252,17 @@ def run_mine(args, rank, world, barrier, maxreduce):
         for i in range(B):
             last[i] = out[i][0]
             pos[i] += 1
-    L.gck_stats_enable(be.h, 0)
+    stats.enable(0)
     for _ in range(args.warmup):
         step()
-    stw = Stats(size=C.sizeof(Stats))
-    L.gck_stats_read(be.h, C.byref(stw))
+    stw = stats.read()
     kv_bytes = np.mean([kv_unique_bytes(np.array(pos) + k, be.layout) for k in range(args.steps)])
     import torch
     torch.cuda.synchronize()
     if world > 1:
         barrier()
-    ATTN = 4
-    L.gck_stats_enable(be.h, 0xFFFF if args.profile else 1 << ATTN)
+    # the timed region: whole-step events only (events around single launches would cut the programmatic overlap)
+    stats.enable(0xFFFF if args.profile else 0)
     # GCK_PROFILE_WINDOW=1: the CUDA profiler window covers the first timed step only (ncu --profile-from-start off)
     window = bool(os.environ.get("GCK_PROFILE_WINDOW"))
     with Clocks(dev) as clk:
@@ -255,18 +274,20 @@ def run_mine(args, rank, world, barrier, maxreduce):
             if window and k == 0:
                 torch.cuda.profiler.stop()
         wall = time.perf_counter() - t0
-    st = Stats(size=C.sizeof(Stats))
-    L.gck_stats_read(be.h, C.byref(st))
+    st = stats.read()
     torch.cuda.synchronize()
-    # the GEMM classes (q/k/v, o, gate/up, down, head), timed by events around each launch in a few steps after the
-    # timed region (the events cut the programmatic overlap at those launches, so this is an upper bound on their time)
-    GEMMS = (2, 6, 7, 8, 9)
-    L.gck_stats_enable(be.h, sum(1 << c for c in GEMMS))
-    for _ in range(GEMM_PASS):
+    # per-kernel device time: the same decode steps again (PASS each, the positions one further every step), events
+    # around every launch of the GEMM classes, then around every attention launch. Those events cut the programmatic
+    # overlap at the bracketed launches, so the per-launch times are upper bounds.
+    stats.enable(sum(1 << c for c in GEMMS))
+    for _ in range(PASS):
         step()
-    sg = Stats(size=C.sizeof(Stats))
-    L.gck_stats_read(be.h, C.byref(sg))
-    L.gck_stats_enable(be.h, 0)
+    sg = stats.read()
+    stats.enable(1 << ATTN)
+    for _ in range(PASS):
+        step()
+    sa = stats.read()
+    stats.enable(0)
     if world > 1:
         barrier()
     dev_s = maxreduce(st.forward_ms / 1e3)
@@ -274,11 +295,13 @@ def run_mine(args, rank, world, barrier, maxreduce):
     value, e2e = aggregate(B * args.steps, world, dev_s, wall)
     pk = peaks()
     hbm = pk.get("hbm_gbs", 6650.0)
-    attn_ms = st.class_ms[ATTN] / max(1, st.class_launches[ATTN])
+    psrc = "MEASURED_PEAKS.json hbm_gbs (burst copy)" if "hbm_gbs" in pk else "fallback 6650 GB/s"
+    attn_ms = sa.class_ms[ATTN] / max(1, sa.class_launches[ATTN])
     attn_bytes = kv_bytes / be.layout.layers
     wbytes = weight_bytes(SPEC8B)
     step_bytes = kv_bytes + wbytes
     ms_step = dev_s / args.steps * 1e3
+    gemm = gemm_roofline(sg, PASS, hbm, psrc)
     res = {
         "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
@@ -290,14 +313,16 @@ def run_mine(args, rank, world, barrier, maxreduce):
                    "l2": "inputs larger than L2 (13 GB per step), no flush"},
         "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": int(sum(len(t) for t in tables) * 4 + B * 4 * 3 + B * 48),
                 "d2h_bytes_per_step": B * 4, "path": "gc_step through the C ABI (ctypes), host buffers"},
-        "roofline": {"bound": "hbm", "kernel": "attn_kernel (paged fp8 KV attention)", "achieved": round(attn_bytes / (attn_ms / 1e3) / 1e9, 1),
-                     "peak": hbm, "unit": "GB/s", "frac": round(attn_bytes / (attn_ms / 1e3) / 1e9 / hbm, 4),
-                     "traffic": ATTN_TRAFFIC, "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch "
-                     "(profiles/attn_kernel_c3_decode_L2.md)",
-                     "algorithmic_bytes_per_launch": int(attn_bytes), "launch_ms": round(attn_ms, 4),
-                     "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in pk else "fallback 6650 GB/s"},
-        "roofline_gemm": gemm_roofline(sg, GEMM_PASS, hbm, "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in pk else
-                                       "fallback 6650 GB/s"),
+        "roofline": gemm,
+        "roofline_attention": {
+            "bound": "hbm", "kernel": "attn_kernel (paged fp8 KV attention), one launch per layer",
+            "achieved": round(attn_bytes / (attn_ms / 1e3) / 1e9, 1), "peak": hbm, "unit": "GB/s",
+            "frac": round(attn_bytes / (attn_ms / 1e3) / 1e9 / hbm, 4),
+            "traffic": ATTN_TRAFFIC["bytes"], "traffic_build": ATTN_TRAFFIC["build"],
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch (single-kernel capture)",
+            "algorithmic_bytes_per_launch": int(attn_bytes), "launch_ms": round(attn_ms, 4),
+            "timing": f"CUDA events around each attention launch, {PASS} decode steps after the timed region",
+            "peak_source": psrc},
         "step_roofline": {"algorithmic_bytes": int(step_bytes), "weights_bytes": int(wbytes), "kv_bytes": int(kv_bytes),
                           "achieved_gbs": round(step_bytes / (ms_step / 1e3) / 1e9, 1),
                           "frac_of_measured": round(step_bytes / (ms_step / 1e3) / 1e9 / hbm, 4),
@@ -308,79 +333,219 @@ def run_mine(args, rank, world, barrier, maxreduce):
                   "launches_before_timed": int(st0.launches + stw.launches)},
     }
     if args.profile:
-        names = ["embed", "rmsnorm", "gemm_qkv", "rope_kv", "attention", "attn_combine", "gemm_o", "gemm_gateup",
-                 "gemm_down", "gemm_head", "argmax", "splitk_reduce"]
-        tot = sum(st.class_ms[i] for i in range(len(names)))
-        lines = [f"{n:14s} {st.class_ms[i] / args.steps:8.3f} ms/step  {st.class_launches[i] // max(1, args.steps):5d} "
-                 f"launches/step  {100 * st.class_ms[i] / max(tot, 1e-9):5.1f}%" for i, n in enumerate(names)]
-        print("[bench] per-class device time (events around each launch):\n" + "\n".join(lines) +
-              f"\n  sum {tot / args.steps:.3f} ms/step, step {st.forward_ms / args.steps:.3f} ms", file=sys.stderr, flush=True)
+        print_classes(st, args.steps)
     be.close()
     if rank == 0:
         if world == 1 and not args.no_cpu:
-            res["cpu_baseline"] = cpu_baseline(args)
+            res["parity"] = c3_parity()
+            res["cpu_baseline"] = cpu_baseline()
         print(json.dumps(res), flush=True)
 
 
-GATEUP_TRAFFIC = 67_172_864   # ncu DRAM bytes of one C3 gate/up launch (profiles/gemm_tc_gateup_c3_decode_L2.md)
-
-
 def gemm_roofline(sg, steps, hbm, peak_source):
-    """HBM roofline of the tcgen05 GEMM launches of a C3 step (the largest kernel class by time): the Q4_K weight
-    bytes of the step (every projection and the head, read once) over the GEMM classes' device time; and the gate/up
-    launch alone (66.06 MB of weights + 0.5 MB activations + 1.8 MB f16 output per launch)."""
-    GEMMS, GU = (2, 6, 7, 8, 9), 7
+    """HBM roofline of the dominant kernel of a C3 step, the tcgen05 GEMM (every projection and the head): the Q4_K
+    weight bytes the step's GEMM launches read (each weight once) over their summed device time, i.e. the algorithmic
+    bytes of the average launch over its average duration; and the gate/up launch alone (66.06 MB of weights, 0.5 MB
+    of activations, 1.8 MB of f16 output)."""
     ms = sum(sg.class_ms[c] for c in GEMMS) / steps
+    launches = sum(sg.class_launches[c] for c in GEMMS) // steps
     wb = weight_bytes(SPEC8B)
-    gu_ms = sg.class_ms[GU] / max(1, sg.class_launches[GU])
+    gu_ms = sg.class_ms[GATEUP] / max(1, sg.class_launches[GATEUP])
     gu_bytes = 2 * 14336 * 4096 * 144 // 256 + 64 * 4096 * 2 + 64 * 14336 * 2
-    return {"bound": "hbm", "kernel": "gemm_tc_kernel<Q4_K, 64> (all projections and the head)",
-            "achieved": round(wb / (ms / 1e3) / 1e9, 1), "peak": hbm, "unit": "GB/s",
-            "frac": round(wb / (ms / 1e3) / 1e9 / hbm, 4), "ms_per_step": round(ms, 4),
-            "launches_per_step": int(sum(sg.class_launches[c] for c in GEMMS) // steps), "algorithmic_bytes_per_step": int(wb),
-            "gateup": {"launch_ms": round(gu_ms, 4), "algorithmic_bytes_per_launch": int(gu_bytes),
-                       "achieved": round(gu_bytes / (gu_ms / 1e3) / 1e9, 1),
-                       "frac": round(gu_bytes / (gu_ms / 1e3) / 1e9 / hbm, 4), "traffic": GATEUP_TRAFFIC},
-            "timing": f"CUDA events around each GEMM launch, {steps} steps after the timed region", "peak_source": peak_source}
+    out = {"bound": "hbm", "kernel": "gemm_tc_kernel<Q4_K, 64> (q/k/v, o, gate/up, down of every layer, and the head)",
+           "achieved": round(wb / (ms / 1e3) / 1e9, 1), "peak": hbm, "unit": "GB/s",
+           "frac": round(wb / (ms / 1e3) / 1e9 / hbm, 4), "ms_per_step": round(ms, 4), "launches_per_step": int(launches),
+           "algorithmic_bytes_per_launch": int(wb / max(1, launches)), "launch_ms": round(ms / max(1, launches), 5),
+           "algorithmic_bytes_per_step": int(wb),
+           "traffic": GEMM_TRAFFIC["bytes"] if GEMM_TRAFFIC else None,
+           "traffic_build": GEMM_TRAFFIC["build"] if GEMM_TRAFFIC else None,
+           "gateup": {"launch_ms": round(gu_ms, 4), "algorithmic_bytes_per_launch": int(gu_bytes),
+                      "achieved": round(gu_bytes / (gu_ms / 1e3) / 1e9, 1),
+                      "frac": round(gu_bytes / (gu_ms / 1e3) / 1e9 / hbm, 4),
+                      "traffic": GEMM_TRAFFIC["gateup"] if GEMM_TRAFFIC else None},
+           "timing": f"CUDA events around each GEMM launch, {steps} decode steps after the timed region (upper bound: "
+                     "the events cut the programmatic overlap)", "peak_source": peak_source}
+    return out
 
 
-class CpuSample:
-    """The oracle (numpy restatement of ref.py) on a bounded sample of the same decode step: `seqs` sequences with the
-    first C3 contexts, `layers` of the 32 layers (dequantized from the same GGUF), the head on 8192 of the 128256
-    vocabulary rows; the step time is scaled to 32 layers and the full head. KV pages hold random fp8 codes (a decode
-    step's time does not depend on their values)."""
+# ------------------------------------------------------------------------------------------- C3 parity sample
+def c3_sample():
+    """A C3-shaped decode step of 64 sequences that the oracle can check: eight with contexts from the benchmark's own
+    draw (7969, 838 and 856 tokens of their own; 2234 and four of 1040 on the shared 1024-token prefix pages), and 56
+    that share the prefix pages with 16-48 tokens of their own (the step's token tile is the benchmark's 64 rows).
+    Returns contexts, block tables, tokens, the pool size, the prefill chunks (sequence, start, end; the shared prefix
+    first) and the decode items."""
+    ctx = contexts()
+    pick = [47, 54, 40, 0, 9, 12, 30, 14]
+    rng = np.random.default_rng(3)
+    cs = [int(ctx[i]) for i in pick] + [PREFIX + int(x) for x in rng.integers(16, 49, 56)]
+    share = [i < 32 for i in pick] + [True] * 56
+    rng = np.random.default_rng(1)
+    prefix = [int(x) for x in rng.integers(1, 128000, PREFIX)]
+    nxt, tabs, toks = PREFIX // 16, [], []
+    for c, sh in zip(cs, share):
+        own = -(-(c + 1) // 16) - (PREFIX // 16 if sh else 0)
+        tabs.append((list(range(PREFIX // 16)) if sh else []) + list(range(nxt, nxt + own)))
+        toks.append((prefix if sh else []) + [int(x) for x in rng.integers(1, 128000, c - (PREFIX if sh else 0))])
+        nxt += own
+    first = share.index(True)
+    pre = [(first, 0, PREFIX)] + [(i, PREFIX if sh else 0, c - 1) for i, (c, sh) in enumerate(zip(cs, share))
+                                  if i != first] + [(first, PREFIX, cs[first] - 1)]
+    dec = [dict(sid=i, tokens=[t[-1]], pos=c - 1, blocks=tabs[i], want=1) for i, (c, t) in enumerate(zip(cs, toks))]
+    return dict(cs=cs, tabs=tabs, toks=toks, nblk=nxt + 8, pre=pre, dec=dec)
 
-    VS = 8192
-    MAX_STEPS = 40          # decode steps timed at most (positions advance); at least TARGET_S seconds of CPU work
-    TARGET_S = 10.0
+
+def c3_sample_run(be, smp):
+    """The library's half: the prefill (the shared prefix alone, then steps of at most 2048 tokens), then the decode
+    step twice: float32 host logits, and greedy tokens from the device argmax (the same KV rows rewritten with the
+    same values)."""
+    from goethe_engine_b200 import gck
+    toks, tabs = smp["toks"], smp["tabs"]
+    (i0, a0, b0), queue = smp["pre"][0], [list(x) for x in smp["pre"][1:]]
+    be.step([gck.Work(i0, toks[i0][a0:b0], a0, tabs[i0], 0)])
+    while queue:
+        budget, items = 2048, []
+        for q in queue:
+            if budget and q[1] < q[2]:
+                n = min(budget, q[2] - q[1])
+                items.append(gck.Work(q[0], toks[q[0]][q[1]:q[1] + n], q[1], tabs[q[0]], 0))
+                q[1] += n
+                budget -= n
+        queue = [q for q in queue if q[1] < q[2]]
+        be.step(items)
+    dec = smp["dec"]
+    got = be.step([gck.Work(d["sid"], d["tokens"], d["pos"], d["blocks"], 1) for d in dec])
+    greedy = be.step([gck.Work(d["sid"], d["tokens"], d["pos"], d["blocks"], 1, greedy=True) for d in dec])
+    return got, np.array([g[0] for g in greedy])
+
+
+def c3_sample_oracle(gguf_path, smp):
+    """The oracle's half over the same GGUF: the shared prefix, then every other prefill chunk in one step, then the
+    decode step (oracle/ is test infrastructure; the benchmark runs it only in its CPU leg, as the checker)."""
+    from oracle.load import weights_from_gguf
+    from oracle.model import PagedOracle
+    toks, tabs, pre = smp["toks"], smp["tabs"], smp["pre"]
+    o = PagedOracle(weights_from_gguf(gguf_path), num_blocks=smp["nblk"], kv="fp8", kv_scale="page")
+    o.step([dict(sid=i, tokens=toks[i][a:b], pos=a, blocks=tabs[i], want=0) for i, a, b in pre[:1]])
+    o.step([dict(sid=i, tokens=toks[i][a:b], pos=a, blocks=tabs[i], want=0) for i, a, b in pre[1:]])
+    return o.step(smp["dec"])
+
+
+def c3_parity(tol=3e-2):
+    """Outside the timed region, on rank 0 at N = 1: the C3 shape with 2 of its 32 layers (its own GGUF, the same
+    synthesis), the 64-sequence c3_sample decode step through the C ABI against the oracle. max_rel_err: the largest
+    per-row max |a - b| / max |b| (the fp8-KV tolerance is 3e-2); tokens: the device argmax against the oracle's."""
+    from goethe_engine_b200 import gck, synth
+    t0 = time.time()
+    spec = synth.Spec(**dict(SPEC8B, layers=2, name=SPEC8B["name"] + "-L2"))
+    d = os.path.join(os.environ.get("GCK_BENCH_DIR", "/tmp/gck_bench"), f"{spec.name}-s{spec.seed}")
+    pack, ws = synth.make(d, spec, ncol=B, maxctx=spec.ctx, kv="fp8", tune=dict(max_cols=2048, kv_scale="page"))
+    smp = c3_sample()
+    with gck.Backend(pack, ws, pool_blocks=smp["nblk"]) as be:
+        got, greedy = c3_sample_run(be, smp)
+    ref = c3_sample_oracle(ws[0], smp)
+    a, r = got.astype(np.float64), ref.astype(np.float64)
+    err = np.abs(a - r).max(-1) / np.abs(r).max(-1)
+    top2 = np.sort(r, -1)[:, -2:]
+    sure = (top2[:, 1] - top2[:, 0]) / np.abs(r).max(-1) > 2 * tol
+    return {"workload": "C3 shape with 2 of 32 layers: one 64-sequence decode step (contexts 838-7969, 61 on the shared "
+                        "prefix pages), Q4_K, fp8 page-scaled KV, vocabulary 128256",
+            "rows": int(len(err)), "max_rel_err": round(float(err.max()), 6), "tolerance": tol,
+            "within_tolerance": bool((err <= tol).all()),
+            "tokens_equal": int((greedy == r.argmax(-1)).sum()),
+            "tokens_equal_where_margin_exceeds_2tol": f"{int((greedy == r.argmax(-1))[sure].sum())}/{int(sure.sum())}",
+            "device_argmax_equals_host_argmax": bool(np.array_equal(greedy, got.argmax(-1))),
+            "seconds": round(time.time() - t0, 1)}
+
+
+# ------------------------------------------------------------------------------------------- CPU baselines
+def reference_module():
+    """goethe_engine.ref and .backend from the reference installed offline in baseline/_ref, or None."""
+    p = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(p, "goethe_engine")):
+        return None
+    if p not in sys.path:
+        sys.path.insert(0, p)
+    import goethe_engine.backend as Bk
+    import goethe_engine.ref as R
+    return R, Bk
+
+
+class RefSample:
+    """The reference's own CPU implementation of the path, ref.py's RefModel + TorchBackend (ref.py:18-126), on a
+    bounded sample of the C3 decode step: the first `seqs` C3 sequences at their contexts, `layers` layers of the 8B
+    shape (d 4096, 32/8 heads of 128, FFN 14336) and a head of VS rows; the step time is scaled to 32 layers and the
+    full 128256-row head. RefModel draws its own seeded f32 weights (ref.py computes in f32 whatever the checkpoint's
+    storage); the fp8 KV pool holds random finite e4m3 codes (a decode step's time does not depend on the values)."""
+
+    VS, MAX_STEPS, TARGET_S = 8192, 40, 10.0
+
+    def __init__(self, R, Bk, seqs=8, layers=2):
+        import torch
+        self.torch, self.Bk = torch, Bk
+        self.m = R.RefModel(vocab=self.VS, d=4096, layers=layers, heads=32, kv_heads=8, ffn=14336, seed=0)
+        self.ctx = contexts()[:seqs]
+        tabs, k = [], 0
+        for c in self.ctx:
+            n = -(-(int(c) + 2 + self.MAX_STEPS) // 16)
+            tabs.append(list(range(k, k + n)))
+            k += n
+        self.be = R.TorchBackend(self.m, num_blocks=k, block_size=16, kv="fp8", max_seqs=seqs)
+        g = torch.Generator().manual_seed(2)
+        for c in (self.be.kc, self.be.vc):
+            c.view(torch.uint8).copy_(torch.randint(0, 0x78, c.shape, generator=g, dtype=torch.uint8))
+        self.tabs, self.seqs, self.layers = tabs, seqs, layers
+
+    def run(self):
+        torch = self.torch
+        cores = len(os.sched_getaffinity(0))
+        prev = torch.get_num_threads()
+        torch.set_num_threads(cores)          # torchrun sets one thread per rank; the sample uses every host core
+        try:
+            pos = [int(c) for c in self.ctx]
+            n, t_sum = 0, 0.0
+            with torch.no_grad():
+                while n < self.MAX_STEPS and t_sum < self.TARGET_S:
+                    work = [self.Bk.Work(i, [7], pos[i], self.tabs[i], 1) for i in range(self.seqs)]
+                    t0 = time.perf_counter()
+                    self.be.step(work)
+                    t_sum += time.perf_counter() - t0
+                    pos = [p + 1 for p in pos]
+                    n += 1
+                x = torch.ones(4096)
+                t0 = time.perf_counter()
+                for _ in range(3 * self.seqs):
+                    self.m.head @ x
+                t_head = (time.perf_counter() - t0) / 3
+        finally:
+            torch.set_num_threads(prev)
+        t_all = t_sum / n
+        per_step = max(t_all - t_head, 1e-9) * 32 / self.layers + t_head * 128256 / self.VS
+        return {"value": round(self.seqs / per_step, 3), "unit": "tok/s", "cores": cores, "kind": "reference",
+                "sample": f"ref.py RefModel + TorchBackend (torch {torch.__version__}, {cores} threads): decode step of "
+                          f"{self.seqs} C3 sequences (contexts {list(map(int, self.ctx))}), {self.layers}/32 layers and "
+                          f"{self.VS}/128256 head rows, {n} steps timed ({t_sum:.1f}s, {t_all:.2f}s each), scaled to "
+                          f"the full model: {per_step:.2f}s per step"}
+
+
+class PortSample:
+    """The oracle (numpy restatement of ref.py) on the same bounded sample: `seqs` C3 sequences, `layers` layers of
+    the 8B shape with seeded N(0, 0.02) f32 weights, a head of VS rows, random finite e4m3 KV codes; scaled the same
+    way."""
+
+    VS, MAX_STEPS, TARGET_S = 8192, 40, 10.0
 
     def __init__(self, seqs=8, layers=2):
-        from oracle import quants as Q
         from oracle.model import PagedOracle, Weights
-        import gguf
-        _, d = model_dir()
-        r = gguf.GGUFReader(os.path.join(d, "model.gguf"))
-        T = {t.name: t for t in r.tensors}
-
-        def mat(name, rows=None):
-            t = T[name]
-            ne = [int(x) for x in t.shape]
-            raw = np.asarray(t.data).view(np.uint8).reshape(ne[1], -1)
-            if rows:
-                raw = raw[:rows]
-            return Q.dequant(int(t.tensor_type), raw.tobytes(), (raw.shape[0], ne[0]))
-        lw = []
-        for i in range(layers):
-            b = f"blk.{i}."
-            lw.append(dict(q=mat(b + "attn_q.weight"), k=mat(b + "attn_k.weight"), v=mat(b + "attn_v.weight"),
-                           o=mat(b + "attn_output.weight"), g=mat(b + "ffn_gate.weight"), u=mat(b + "ffn_up.weight"),
-                           dn=mat(b + "ffn_down.weight")))
-        self.head = mat("output.weight", self.VS)
-        w = Weights(self.head.copy(), self.head, lw, eps=1e-5, theta=5e5, heads=32, kv_heads=8)
+        rng = np.random.default_rng(0)
+        mk = lambda *s: (rng.standard_normal(s, dtype=np.float32) * np.float32(0.02))
+        lw = [dict(q=mk(4096, 4096), k=mk(1024, 4096), v=mk(1024, 4096), o=mk(4096, 4096), g=mk(14336, 4096),
+                   u=mk(14336, 4096), dn=mk(4096, 14336)) for _ in range(layers)]
+        self.head = mk(self.VS, 4096)
+        w = Weights(self.head, self.head, lw, eps=1e-5, theta=5e5, heads=32, kv_heads=8)
         self.ctx = contexts()[:seqs]
         nb = int(sum(-(-(c + 2 + self.MAX_STEPS) // 16) for c in self.ctx))
         self.o = PagedOracle(w, num_blocks=nb, kv="fp8", kv_scale="page")
-        rng = np.random.default_rng(2)
         self.o.kc[:] = rng.integers(0, 0x78, self.o.kc.shape, dtype=np.uint8)
         self.o.vc[:] = rng.integers(0, 0x78, self.o.vc.shape, dtype=np.uint8)
         tabs, k = [], 0
@@ -390,43 +555,45 @@ class CpuSample:
             k += n
         self.items = [dict(sid=i, tokens=[7], pos=int(c), blocks=tabs[i], want=1) for i, c in enumerate(self.ctx)]
         self.seqs, self.layers = seqs, layers
-        self.o.step(self.items)          # warm
 
     def run(self):
-        # all of this process's host cores for the oracle's BLAS calls (torchrun sets OMP_NUM_THREADS=1 per rank)
         from threadpoolctl import threadpool_limits
         cores = len(os.sched_getaffinity(0))
         with threadpool_limits(limits=cores, user_api="blas"):
-            return self._run(cores)
-
-    def _run(self, cores):
-        # repeated decode steps (each sequence one token further) until TARGET_S seconds of CPU work, from the C3
-        # contexts again on every call
-        for it, c in zip(self.items, self.ctx):
-            it["pos"] = int(c)
-        n, t_sum = 0, 0.0
-        while n < self.MAX_STEPS and t_sum < self.TARGET_S:
-            for it in self.items:
-                it["pos"] += 1
+            for it, c in zip(self.items, self.ctx):
+                it["pos"] = int(c)
+            n, t_sum = 0, 0.0
+            while n < self.MAX_STEPS and t_sum < self.TARGET_S:
+                for it in self.items:
+                    it["pos"] += 1
+                t0 = time.perf_counter()
+                self.o.step(self.items)
+                t_sum += time.perf_counter() - t0
+                n += 1
+            h = np.ones((self.seqs, 4096), np.float32)
             t0 = time.perf_counter()
-            self.o.step(self.items)
-            t_sum += time.perf_counter() - t0
-            n += 1
+            for _ in range(3):
+                h @ self.head.T
+            t_head = (time.perf_counter() - t0) / 3
         t_all = t_sum / n
-        h = np.ones((self.seqs, 4096), np.float32)
-        t0 = time.perf_counter()
-        for _ in range(3):
-            h @ self.head.T
-        t_head = (time.perf_counter() - t0) / 3
         per_step = max(t_all - t_head, 1e-9) * 32 / self.layers + t_head * 128256 / self.VS
         return {"value": round(self.seqs / per_step, 3), "unit": "tok/s", "cores": cores, "kind": "port",
-                "sample": f"oracle decode step of {self.seqs} C3 sequences (contexts {list(map(int, self.ctx))}), "
-                          f"{self.layers}/32 layers and {self.VS}/128256 head rows, {n} steps timed ({t_sum:.1f}s, "
-                          f"{t_all:.2f}s each), scaled to the full model: {per_step:.2f}s per step"}
+                "sample": f"numpy oracle decode step of {self.seqs} C3 sequences, {self.layers}/32 layers and "
+                          f"{self.VS}/128256 head rows, {n} steps timed ({t_sum:.1f}s, {t_all:.2f}s each), scaled to the "
+                          f"full model: {per_step:.2f}s per step"}
 
 
-def cpu_baseline(args):
-    return CpuSample().run()
+def cpu_baseline():
+    """ref.py itself (kind "reference") when the reference is installed in baseline/_ref, with the numpy port as a
+    second figure; the port alone otherwise."""
+    port = PortSample().run()
+    ref = reference_module()
+    if ref is None:
+        port["note"] = "baseline/_ref absent: the reference's ref.py could not be imported"
+        return port
+    out = RefSample(*ref).run()
+    out["port"] = port
+    return out
 
 
 SPEC8B_Q8 = dict(SPEC8B, wtype="q8_0", ctx=4096, name="llama3-8b-shape-q80")
@@ -754,12 +921,13 @@ def aggregate(units_per_rank, world, dev_s_max, wall_s_max):
 
 
 def run_reference(args, rank, world):
+    """The reference arm: ref.py's RefModel + TorchBackend (the reference's CPU implementation of the path) on the
+    bounded C3 sample, all host cores, rank 0 only; the numpy port where baseline/_ref is absent. Nothing of this
+    repository's native code is loaded."""
     if rank != 0:
         return
-    from goethe_engine_b200 import build
-    build.build_synth()
-    ensure_model(0, 1, lambda: None)
-    smp = CpuSample()
+    ref = reference_module()
+    smp = RefSample(*ref) if ref is not None else PortSample()
     cb, vals = None, []
     for _ in range(max(1, min(args.steps, 3))):
         cb = smp.run()
@@ -768,8 +936,9 @@ def run_reference(args, rank, world):
     cb["value"] = v
     print(json.dumps({"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": world,
                       "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
-                      "dtype": "f32 (numpy oracle of ref.py; fp8 KV)", "data": "synthetic",
-                      "config": {"workload": "C3 decode step, bounded CPU sample (see cpu_baseline.sample)"},
+                      "dtype": "f32 weights and activations (ref.py), fp8 e4m3 KV" if ref else "f32 (numpy port), fp8 KV",
+                      "data": "synthetic",
+                      "config": {"workload": "C3 decode step, bounded CPU sample (cpu_baseline.sample)"},
                       "cpu_baseline": cb, "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0,
                                                    "d2h_bytes_per_step": 0}}), flush=True)
 

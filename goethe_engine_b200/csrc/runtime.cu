@@ -532,9 +532,11 @@ std::string read_file(const std::string &path) {
 
 // ============================================================================================== static commit scratch
 // gck_commit_static keeps its scratch (the move list and the staged rows) in this fixed device array instead of
-// memory the handle allocates, so that callers that may not allocate device memory can commit tree paths. Every GPU
-// that loads the library holds these 16 MiB until the process exits. In host code the name is only a stand-in: the
-// device address comes from cudaGetSymbolAddress, once per device, with that device current.
+// memory the handle allocates, so that callers that may not allocate device memory can commit tree paths. In host
+// code the name is only a stand-in: the device address comes from cudaGetSymbolAddress, once per device, with that
+// device current. gc_open looks it up for every device it opens (open_device): under CUDA's lazy module loading that
+// lookup is what loads this file's module and commits its 16 MiB on the device, so it happens at open, where the
+// handle allocates anyway, and never inside a commit. The device holds the array until the process exits.
 constexpr size_t kCommitStaticBytes = static_cast<size_t>(16) << 20;
 static __device__ __align__(256) unsigned char g_commit_static[kCommitStaticBytes];
 
@@ -580,6 +582,8 @@ void open_device(gc_handle *h, int dev, const std::vector<std::unique_ptr<GgufFi
   h->tp = c.tp;
   h->sms = prop.multiProcessorCount;
   ck(cudaStreamCreateWithFlags(&h->st, cudaStreamNonBlocking), "stream");
+  // the static commit array's address on this device (loads its module and commits the array now, not in a commit)
+  commit_static_address(dev);
   gemm_init();
   gemm_tc_init();
   load_model(h, files);
@@ -1554,6 +1558,7 @@ GC_API int gck_commit_static(gc_handle *h, uint64_t sid, uint32_t base, const ui
       fail(GC_E_ARG, "gck_commit_static: %d moved rows need %zu bytes of scratch; the static array holds %zu (at most %zu "
            "moved rows for this model)", nm, need, kCommitStaticBytes, (kCommitStaticBytes - 256) / (row_bytes + 8));
     ck(cudaSetDevice(h->dev), "cudaSetDevice");
+    // looked up at gc_open (open_device): this returns the cached address and allocates nothing
     uint8_t *base_ptr = static_cast<uint8_t *>(commit_static_address(h->dev));
     int *d_moves = reinterpret_cast<int *>(base_ptr);
     float *d_rows = reinterpret_cast<float *>(base_ptr + list_bytes);

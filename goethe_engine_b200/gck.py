@@ -109,7 +109,9 @@ class Work:
 
 
 def load(path=LIB_PATH):
-    """The library with its gc.h signatures; refuses a different ABI major or an older minor."""
+    """ctypes handle of libgck.so with argument and result types set for every gc.h entry point. Raises GcError when
+    the file is missing or when gc_abi_version reports a major other than 1 or a minor below the one this binding
+    was written for."""
     if not os.path.exists(path):
         raise GcError(E_DEVICE, f"{path} is not built (python -m goethe_engine_b200.build)")
     L = C.CDLL(path)

@@ -56,9 +56,10 @@ GC_API int gck_stats_read(gc_handle *h, gck_stats *out);
  *  - the scratch holds the move list and every moved row of every layer as float32: (path entries that move) times
  *    layers x 2 x kv_heads x head_dim x 4 bytes must fit 16 MiB less 256 bytes (an 8B-shaped model: about 63 rows;
  *    a 70B-shaped one: about 25); a longer path returns GC_E_ARG and a text giving the limit;
- *  - every GPU that loads the library holds the 16 MiB array until the process exits;
- *  - the first call on a device looks the array's address up (cudaGetSymbolAddress); make that first call before any
- *    stream capture on that device;
+ *  - gc_open looks the array's address up (cudaGetSymbolAddress) on every device it opens, with that device current;
+ *    under CUDA's lazy module loading that is when the array is committed on the device, so it counts toward the
+ *    handle's memory at open and a commit allocates nothing, its first one included. A device that opened a handle
+ *    holds the 16 MiB until the process exits;
  *  - all callers on one device share the array and it keeps the last call's contents; calls that overlap on the GPU
  *    (two handles of one device committing from different threads at once) race, so serialize them. The call itself
  *    returns only after its work on the handle's stream has finished. */

@@ -25,6 +25,21 @@ def _meta(r, key, default=None):
     return v.item() if hasattr(v, "item") and v.size == 1 else v
 
 
+class QuantRows:
+    """A quantized [rows, cols] matrix dequantized row by row on indexing (the embedding: a step reads only the rows of
+    its tokens, so the whole table is never expanded to float32)."""
+
+    def __init__(self, t):
+        ne = [int(x) for x in t.shape]
+        self.type, self.shape = int(t.tensor_type), (ne[1], ne[0])
+        self.raw = np.asarray(t.data).view(np.uint8).reshape(ne[1], -1)
+
+    def __getitem__(self, idx):
+        idx = np.asarray(idx, np.int64).reshape(-1)
+        rows = np.ascontiguousarray(self.raw[idx])
+        return Q.dequant(self.type, rows.tobytes(), (len(idx), self.shape[1]))
+
+
 def weights_from_gguf(path, layers=None):
     """oracle Weights of a llama GGUF file; layers: only the first n layers (a bounded CPU sample)."""
     r = _reader(path)
@@ -46,7 +61,7 @@ def weights_from_gguf(path, layers=None):
                        o=mat(b + "attn_output.weight"), g=mat(b + "ffn_gate.weight"), u=mat(b + "ffn_up.weight"),
                        dn=mat(b + "ffn_down.weight"), attn_norm=mat(b + "attn_norm.weight"),
                        ffn_norm=mat(b + "ffn_norm.weight")))
-    return Weights(mat("token_embd.weight"), mat("output.weight"), lw, out_norm=mat("output_norm.weight"),
+    return Weights(QuantRows(T["token_embd.weight"]), mat("output.weight"), lw, out_norm=mat("output_norm.weight"),
                    eps=float(_meta(r, "llama.attention.layer_norm_rms_epsilon", 1e-5)),
                    theta=float(_meta(r, "llama.rope.freq_base", 1e4)),
                    heads=int(_meta(r, "llama.attention.head_count")), kv_heads=int(_meta(r, "llama.attention.head_count_kv")))

@@ -20,7 +20,10 @@ What it follows, line by line:
 
 Tokens of one work item are run layer by layer for all its tokens at once. That is the same computation as the
 reference's token-at-a-time loop: a token's attention at layer l reads only rows of the cached prefix and of its
-own ancestors, and every such row is written (at layer l) before any attention of that layer runs.
+own ancestors, and every such row is written (at layer l) before any attention of that layer runs. A chain item (no
+parents) takes its attention in chunks of tokens with a causal mask (each chunk decodes its visible rows once), so
+that the oracle can prefill contexts of thousands of rows at the benchmark's model widths; tree items attend token
+by token over their paths. Either way every token sees exactly the rows ``TorchBackend.step`` gives it.
 
 fp8 KV: ``kv_scale="unit"`` is the reference's plain e4m3 cast; ``kv_scale="page"`` is the library's per-page
 power-of-two scale (``page_scale_exp``): a page's scale is fixed by its first row, later rows are clamped to it.
@@ -61,6 +64,15 @@ def rms(x, gain, eps):
     return (x * r * gain).astype(np.float32)
 
 
+def page_scale_exps(row_amax):
+    """page_scale_exp of every element of an array of amax values (float32), without a Python loop."""
+    a = np.asarray(row_amax, np.float32)
+    ok = (a > 0) & np.isfinite(a)
+    m, k = np.frexp(np.where(ok, a, np.float32(1.0)))
+    e = 6 - k + (m == 0.5).astype(np.int32)
+    return np.where(ok, np.clip(e, PAGE_EXP_MIN, PAGE_EXP_MAX), 0).astype(np.int32)
+
+
 def page_scale_exp(row_amax):
     """The exponent e of a page's scale 2^e, from the amax of the page's first row (over one layer, head, K or V):
     the largest e with amax * 2^e <= PAGE_TARGET, clamped to [-8, 15]. A stored value is code(x * 2^e)."""
@@ -94,6 +106,13 @@ class Weights:
         """x [..., dh] rotated at position p (interleaved pairs, ref.py:33-37)."""
         a = (self.inv * np.float32(p)).astype(np.float32)
         c, s = np.cos(a).astype(np.float32), np.sin(a).astype(np.float32)
+        x1, x2 = x[..., ::2], x[..., 1::2]
+        return np.stack([x1 * c - x2 * s, x1 * s + x2 * c], -1).reshape(x.shape).astype(np.float32)
+
+    def rope_rows(self, x, ps):
+        """x [n, heads, dh], row i rotated at position ps[i]: the same float32 operations as rope() row by row."""
+        a = (self.inv[None, :] * np.asarray(ps, np.float32)[:, None]).astype(np.float32)
+        c, s = np.cos(a).astype(np.float32)[:, None, :], np.sin(a).astype(np.float32)[:, None, :]
         x1, x2 = x[..., ::2], x[..., 1::2]
         return np.stack([x1 * c - x2 * s, x1 * s + x2 * c], -1).reshape(x.shape).astype(np.float32)
 
@@ -134,6 +153,53 @@ class PagedOracle:
         else:
             self.kc[l, slot], self.vc[l, slot] = Q.e4m3_encode(k), Q.e4m3_encode(v)
 
+    def _write_rows(self, l, slots, k, v):
+        """Rows slots[i] of layer l get k[i], v[i] ([n, KVH, dh] float32): the same result as _write row by row in this
+        order. A page's first row among them sets the page's exponents before any row is encoded, and it comes
+        before the page's other rows (a page's rows are consecutive positions), so every row sees the exponent the
+        sequential order would give it."""
+        slots = np.asarray(slots, np.int64)
+        if self.kv == "f16":
+            self.kc[l, slots], self.vc[l, slots] = k.astype(np.float16), v.astype(np.float16)
+            return
+        if self.kv_scale != "page":
+            self.kc[l, slots], self.vc[l, slots] = Q.e4m3_encode(k), Q.e4m3_encode(v)
+            return
+        b = slots // self.bs
+        first = slots % self.bs == 0
+        if first.any():
+            self.ke[l, b[first]] = page_scale_exps(np.abs(k[first]).max(-1))
+            self.ve[l, b[first]] = page_scale_exps(np.abs(v[first]).max(-1))
+        sk = np.float32(2.0) ** self.ke[l, b].astype(np.float32)
+        sv = np.float32(2.0) ** self.ve[l, b].astype(np.float32)
+        self.kc[l, slots] = Q.e4m3_encode(k * sk[:, :, None])
+        self.vc[l, slots] = Q.e4m3_encode(v * sv[:, :, None])
+
+    CHUNK = 512
+
+    def _attend_chain(self, l, q, sl, pos):
+        """Attention of a chain item's n tokens (q [n, H, dh], rotated): token j sees slots sl[:pos + j + 1]
+        (ref.py:101-104 with path(None, j) = 0..j), taken CHUNK tokens at a time with a causal mask."""
+        w, n = self.w, q.shape[0]
+        G = w.H // w.KVH
+        att = np.empty((n, w.H * w.dh), np.float32)
+        scale = np.float32(math.sqrt(w.dh))
+        for j0 in range(0, n, self.CHUNK):
+            j1 = min(n, j0 + self.CHUNK)
+            c, t = j1 - j0, pos + j1
+            K, V = self._read(l, sl[:t])
+            lim = np.repeat(pos + np.arange(j0, j1) + 1, G)            # visible rows of each (token, head in group)
+            masked = np.arange(t)[None, :] >= lim[:, None]
+            qc = q[j0:j1].reshape(c, w.KVH, G, w.dh)
+            for h in range(w.KVH):
+                sc = (qc[:, h].reshape(c * G, w.dh) @ K[:, h].T) / scale
+                sc[masked] = -np.inf
+                sc = sc - sc.max(-1, keepdims=True)
+                p = np.exp(sc)
+                p = p / p.sum(-1, keepdims=True)
+                att[j0:j1, h * G * w.dh:(h + 1) * G * w.dh] = (p @ V[:, h]).reshape(c, G * w.dh)
+        return att
+
     def _read(self, l, slots):
         """(K, V) float32 [n, KVH, dh] of the given rows of layer l."""
         if self.kv == "f16":
@@ -152,45 +218,62 @@ class PagedOracle:
     # -- the step ----------------------------------------------------------------------------------------------------
     def step(self, work):
         """work: dicts (sid, tokens, pos, blocks, want, parents=None). Returns float32 logits [sum(want), V] in work
-        order (TorchBackend.step, ref.py:94-112)."""
-        w, rows = self.w, []
+        order (TorchBackend.step, ref.py:94-112).
+
+        The step runs layer by layer over every token of every item at once (one product per weight per layer);
+        attention is per item. The reference runs items one after another, token by token: the results are the same
+        because a row's arithmetic involves only its own token and the KV rows it sees, and a valid step never lets
+        an item see rows another item of the same step writes (each item writes rows of its own pages; shared
+        prefix pages were written by earlier steps). Every row of layer l is written before any attention of
+        layer l runs, which the token-by-token order also guarantees for the rows a token sees."""
+        w = self.w
+        its, offs, T = [], [], 0
         for it in work:
-            toks, pos, want, par = list(it["tokens"]), int(it["pos"]), int(it["want"]), it.get("parents")
+            toks, par = list(it["tokens"]), it.get("parents")
             n = len(toks)
-            sl = self.slots(it["blocks"])
-            dep = depths(par, n)
-            x = w.emb[np.asarray(toks)].astype(np.float32)
-            for l, lw in enumerate(w.layers):
-                h = rms(x, lw["attn_norm"], w.eps)
-                q = (h @ lw["q"].T).reshape(n, w.H, w.dh)
-                k = (h @ lw["k"].T).reshape(n, w.KVH, w.dh)
-                v = (h @ lw["v"].T).reshape(n, w.KVH, w.dh)
-                for j in range(n):
-                    q[j] = w.rope(q[j], pos + dep[j])
-                    k[j] = w.rope(k[j], pos + dep[j])
-                for j in range(n):
-                    self._write(l, int(sl[pos + j]), k[j], v[j])
-                att = np.empty((n, w.H * w.dh), np.float32)
-                G = w.H // w.KVH
+            its.append(dict(toks=toks, pos=int(it["pos"]), want=int(it["want"]), par=par, n=n,
+                            sl=self.slots(it["blocks"]), dep=depths(par, n)))
+            offs.append(T)
+            T += n
+        if T == 0:
+            return np.zeros((0, w.V), np.float32)
+        x = w.emb[np.concatenate([np.asarray(i["toks"], np.int64) for i in its])].astype(np.float32)
+        ps = np.concatenate([i["pos"] + np.asarray(i["dep"]) for i in its])
+        G = w.H // w.KVH
+        for l, lw in enumerate(w.layers):
+            h = rms(x, lw["attn_norm"], w.eps)
+            q = w.rope_rows((h @ lw["q"].T).reshape(T, w.H, w.dh), ps)
+            k = w.rope_rows((h @ lw["k"].T).reshape(T, w.KVH, w.dh), ps)
+            v = (h @ lw["v"].T).reshape(T, w.KVH, w.dh)
+            for i, o in zip(its, offs):
+                self._write_rows(l, i["sl"][i["pos"]:i["pos"] + i["n"]], k[o:o + i["n"]], v[o:o + i["n"]])
+            att = np.empty((T, w.H * w.dh), np.float32)
+            for i, o in zip(its, offs):
+                n, pos, sl, par = i["n"], i["pos"], i["sl"], i["par"]
+                if par is None:
+                    att[o:o + n] = self._attend_chain(l, q[o:o + n], sl, pos)
+                    continue
                 for j in range(n):
                     vis = np.concatenate([sl[:pos], sl[pos + np.asarray(path(par, j))]])
                     K, V = self._read(l, vis)
-                    qj = q[j].reshape(w.KVH, G, w.dh)
+                    qj = q[o + j].reshape(w.KVH, G, w.dh)
                     sc = np.einsum("kgd,tkd->kgt", qj, K) / np.float32(math.sqrt(w.dh))
                     sc = sc - sc.max(-1, keepdims=True)
                     p = np.exp(sc)
                     p = p / p.sum(-1, keepdims=True)
-                    att[j] = np.einsum("kgt,tkd->kgd", p, V).reshape(-1)
-                x = x + att @ lw["o"].T
-                h = rms(x, lw["ffn_norm"], w.eps)
-                g = h @ lw["g"].T
-                u = h @ lw["u"].T
-                x = x + ((g / (1.0 + np.exp(-g))) * u).astype(np.float32) @ lw["dn"].T
-            if want:
-                hn = rms(x[n - want:], w.out_norm, w.eps)
-                rows.append((hn @ w.head.T).astype(np.float32))
+                    att[o + j] = np.einsum("kgt,tkd->kgd", p, V).reshape(-1)
+            x = x + att @ lw["o"].T
+            h = rms(x, lw["ffn_norm"], w.eps)
+            g = h @ lw["g"].T
+            u = h @ lw["u"].T
+            x = x + ((g / (1.0 + np.exp(-g))) * u).astype(np.float32) @ lw["dn"].T
+        want = np.concatenate([np.arange(o + i["n"] - i["want"], o + i["n"]) for i, o in zip(its, offs)])
+        for it in work:
             self.blk[it["sid"]] = list(it["blocks"])
-        return np.concatenate(rows) if rows else np.zeros((0, w.V), np.float32)
+        if not want.size:
+            return np.zeros((0, w.V), np.float32)
+        hn = rms(x[want], w.out_norm, w.eps)
+        return (hn @ w.head.T).astype(np.float32)
 
     def commit(self, sid, base, pth):
         """Row base + pth[j] becomes row base + j, all layers, K and V (ref.py:114-120)."""

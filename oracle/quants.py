@@ -65,8 +65,9 @@ def dequant_q4_k(raw, n):
     q = np.empty((b.shape[0], 8, 32), np.float32)
     q[:, 0::2] = qs & 0xF
     q[:, 1::2] = qs >> 4
-    w = (d * sc.astype(np.float32))[:, :, None] * q - (dmin * m.astype(np.float32))[:, :, None]
-    return w.reshape(-1)
+    q *= (d * sc.astype(np.float32))[:, :, None]          # d * sc[s] * q, then minus dmin * m[s]: float32, in place
+    q -= (dmin * m.astype(np.float32))[:, :, None]
+    return q.reshape(-1)
 
 
 def dequant(ggml_type, raw, shape):

@@ -99,3 +99,25 @@ def test_oracle_matches_ref_config1_shape(kv):
         np.testing.assert_allclose(lg[:, cols], ref, rtol=1e-3, atol=1e-3 * np.abs(ref).max())
         np.testing.assert_allclose(np.linalg.norm(lg, axis=1), g[f"{kv}.step{i}.norm"], rtol=1e-4)
         assert (lg.argmax(1) == g[f"{kv}.step{i}.argmax"]).all()
+
+
+@pytest.mark.parametrize("kv,kv_scale", [("f16", "unit"), ("fp8", "page")])
+def test_chunked_chain_attention_equals_token_by_token(kv, kv_scale, monkeypatch):
+    """A chain item's attention runs in chunks with a causal mask; the same tokens as a tree whose parents form a chain
+    take the token-by-token path over their paths. Both see the same rows, so the logits agree to float32 rounding,
+    across several chunks (CHUNK 8 here) and a cached prefix."""
+    rng = np.random.default_rng(0)
+    d, L, H, KVH, F, V = 64, 2, 4, 2, 96, 50
+    mk = lambda *s: (rng.standard_normal(s) / np.sqrt(s[-1])).astype(np.float32)
+    w = Weights(mk(V, d) * 2, mk(V, d) * 2, [dict(q=mk(d, d), k=mk(KVH * 16, d), v=mk(KVH * 16, d), o=mk(d, d),
+                                                  g=mk(F, d), u=mk(F, d), dn=mk(d, F)) for _ in range(L)],
+                eps=1e-6, heads=H, kv_heads=KVH)
+    monkeypatch.setattr(PagedOracle, "CHUNK", 8)
+    toks = [int(x) for x in rng.integers(0, V, 45)]
+    out = {}
+    for mode in ("chain", "tree"):
+        o = PagedOracle(w, num_blocks=8, block_size=16, kv=kv, kv_scale=kv_scale)
+        o.step([dict(sid=1, tokens=toks[:19], pos=0, blocks=list(range(8)), want=0)])
+        par = None if mode == "chain" else [-1] + list(range(25))
+        out[mode] = o.step([dict(sid=1, tokens=toks[19:], pos=19, blocks=list(range(8)), want=26, parents=par)])
+    np.testing.assert_allclose(out["chain"], out["tree"], rtol=0, atol=1e-4 * np.abs(out["tree"]).max())
