@@ -478,7 +478,7 @@ class RefSample:
     full 128256-row head. RefModel draws its own seeded f32 weights (ref.py computes in f32 whatever the checkpoint's
     storage); the fp8 KV pool holds random finite e4m3 codes (a decode step's time does not depend on the values)."""
 
-    VS, MAX_STEPS, TARGET_S = 8192, 40, 10.0
+    VS, MAX_STEPS, TARGET_S = 8192, 200, 10.0
 
     def __init__(self, R, Bk, seqs=8, layers=2):
         import torch

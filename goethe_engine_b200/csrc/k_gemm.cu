@@ -93,7 +93,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int e = 0; e < 4; e++) {
           int row = nt * kBM + wm * 32 + mt * 16 + g + (e / 2) * 8;
           int t = t0 + wn * 32 + j * 8 + 2 * tq + (e % 2);
-          if (t < T) p[static_cast<size_t>(t) * Npad + row] = acc[mt][j][e];
+          if (t < T) p[static_cast<size_t>(t) * Npad + row] = acc[mt][j][e] * epi_scale(epi, t);
         }
     return;
   }
@@ -108,7 +108,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int e = 0; e < 4; e++) {
           int row = wm * 32 + mt * 16 + g + (e / 2) * 8;
           int col = wn * 32 + j * 8 + 2 * tq + (e % 2);
-          sC[row * (kBN + 1) + col] = acc[mt][j][e];
+          sC[row * (kBN + 1) + col] = acc[mt][j][e] * (epi.scale && t0 + col < T ? epi.scale[t0 + col] : 1.f);
         }
     __syncthreads();
     for (int i = tid; i < 64 * kBN; i += kThreads) {
@@ -131,8 +131,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         int t = t0 + wn * 32 + j * 8 + 2 * tq + (e % 2);
         if (t < T && n < epi.n) {
           float *o = epi.out_f + static_cast<size_t>(t) * epi.ld + n;
-          if (epi.kind == kEpiAdd) *o += acc[mt][j][e];
-          else *o = acc[mt][j][e];
+          const float y = acc[mt][j][e] * epi_scale(epi, t);
+          if (epi.kind == kEpiAdd) *o += y;
+          else *o = y;
         }
       }
 }

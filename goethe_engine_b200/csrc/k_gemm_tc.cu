@@ -415,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int c = 0; c < 16; c++) {
               int t = t0 + c0 + c;
-              if (t < T) p[static_cast<size_t>(t) * Npad + row] = __uint_as_float(v[c]);
+              if (t < T) p[static_cast<size_t>(t) * Npad + row] = __uint_as_float(v[c]) * epi_scale(epi, t);
             }
           }
         }
@@ -429,9 +429,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (good) tmem_ld16(tbase + c0, v);
 #pragma unroll
           for (int c = 0; c < 16; c++) {
-            const float mine = __uint_as_float(v[c]);
-            const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
             const int t = t0 + c0 + c;
+            const float mine = __uint_as_float(v[c]) * (epi.scale && t < T ? epi.scale[t] : 1.f);
+            const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
             if (good && (c & 1) == odd && t < T && f < epi.n) {
               const float g = odd ? other : mine, uu = odd ? mine : other;
               epi.out_h[static_cast<size_t>(t) * epi.ld + f] = __float2half_rn(silu_mul(g, uu));
@@ -447,8 +447,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             int t = t0 + c0 + c;
             if (t < T && row < epi.n) {
               float *o = epi.out_f + static_cast<size_t>(t) * epi.ld + row;
-              if (epi.kind == kEpiAdd) *o += __uint_as_float(v[c]);
-              else *o = __uint_as_float(v[c]);
+              const float y = __uint_as_float(v[c]) * epi_scale(epi, t);
+              if (epi.kind == kEpiAdd) *o += y;
+              else *o = y;
             }
           }
         }

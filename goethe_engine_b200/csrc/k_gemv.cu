@@ -171,6 +171,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const uint8_t *__res
   if (hs == 0) {
 #pragma unroll
     for (int t = 0; t < T; t++) acc[t] += sred[t][r];
+    if (epi.scale)     // a8: every product of token row t times its activation scale
+#pragma unroll
+      for (int t = 0; t < T; t++)
+        if (t < Tn) acc[t] *= epi.scale[t];
   }
   if (gs > 1) {
     if (hs == 0)

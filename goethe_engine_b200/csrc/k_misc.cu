@@ -131,6 +131,10 @@ void launch_tp_reduce_scatter(const TpPeers &p, int b, unsigned long long epoch,
   tp_reduce_scatter_kernel<<<std::max(blocks, 1), 256, 0, s>>>(p, b, epoch, T, d, S, sig);
 }
 
+// a8: the per-token scale of a row whose largest magnitude is amax (symmetric int8: amax maps to 127); an all-zero row
+// keeps scale 1 (every code 0). IEEE division, as the oracle computes it.
+__device__ __forceinline__ float act_scale_of(float amax) { return amax > 0.f ? __fdiv_rn(amax, 127.f) : 1.f; }
+
 constexpr int kNormThreads = 512;
 constexpr int kNormMaxVec = 4;    // float4 loads per thread: d <= 512 * 4 * 4 = 8192
 // split-K partials are read kSplitChunk slices at a time (RMSNorm: as many as keep 16 float4 loads per thread),
@@ -141,7 +145,7 @@ template <int NV>
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float *x, const int *rows, const float *gain, float eps,
                                                                int d, int ld, __half *out, const float *part, int S,
                                                                int pld, int T, TpPeers tp, int tpb,
-                                                               unsigned long long tp_epoch) {
+                                                               unsigned long long tp_epoch, float *qscale) {
   dep_wait();
   dep_launch();
   int r = blockIdx.x;
@@ -230,21 +234,90 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(float *x, const i
   __syncthreads();
   float inv = rsqrtf(wsum[0] / static_cast<float>(d) + eps);
   __half2 *o = reinterpret_cast<__half2 *>(out + static_cast<size_t>(r) * ld);
+  if (qscale) {
+    // a8: the normalized row in float32, its amax over the block, then codes rint(y / s) with s = amax / 127
+    float am = 0.f;
 #pragma unroll
-  for (int i = 0; i < NV; i++) {
-    int e = threadIdx.x + i * kNormThreads;
-    if (e < nv) {
-      float4 g = gr[e];
-      o[2 * e] = __floats2half2_rn(v[i].x * inv * g.x, v[i].y * inv * g.y);
-      o[2 * e + 1] = __floats2half2_rn(v[i].z * inv * g.z, v[i].w * inv * g.w);
+    for (int i = 0; i < NV; i++) {
+      int e = threadIdx.x + i * kNormThreads;
+      if (e < nv) {
+        float4 g = gr[e];
+        v[i] = make_float4(v[i].x * inv * g.x, v[i].y * inv * g.y, v[i].z * inv * g.z, v[i].w * inv * g.w);
+        am = fmaxf(am, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+      }
+    }
+    am = warp_max(am);
+    __shared__ float wmax[32];
+    if (l == 0) wmax[w] = am;
+    __syncthreads();
+    if (w == 0) {
+      float m2 = l < kNormThreads / 32 ? wmax[l] : 0.f;
+      m2 = warp_max(m2);
+      if (l == 0) wmax[0] = m2;
+    }
+    __syncthreads();
+    const float sc = act_scale_of(wmax[0]);
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      int e = threadIdx.x + i * kNormThreads;
+      if (e < nv) {
+        o[2 * e] = __floats2half2_rn(rintf(__fdiv_rn(v[i].x, sc)), rintf(__fdiv_rn(v[i].y, sc)));
+        o[2 * e + 1] = __floats2half2_rn(rintf(__fdiv_rn(v[i].z, sc)), rintf(__fdiv_rn(v[i].w, sc)));
+      }
+    }
+    if (threadIdx.x == 0) qscale[r] = sc;
+  } else {
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      int e = threadIdx.x + i * kNormThreads;
+      if (e < nv) {
+        float4 g = gr[e];
+        o[2 * e] = __floats2half2_rn(v[i].x * inv * g.x, v[i].y * inv * g.y);
+        o[2 * e + 1] = __floats2half2_rn(v[i].z * inv * g.z, v[i].w * inv * g.w);
+      }
     }
   }
   for (int e = d / 2 + threadIdx.x; e < ld / 2; e += kNormThreads) o[e] = __floats2half2_rn(0.f, 0.f);
 }
 
+// ----------------------------------------------------------------------------------------------------------------
+// a8 activations of a GEMM input written by another kernel (attention output, SwiGLU output): one CTA per row, the
+// row's amax, then codes rint(x / s) in place (f16 integers, exact), s = amax / 127 into scale[row].
+constexpr int kQuantThreads = 256;
+
+__global__ void __launch_bounds__(kQuantThreads) act_quant_kernel(__half *buf, int n, int ld, float *scale) {
+  dep_wait();
+  dep_launch();
+  __half2 *row = reinterpret_cast<__half2 *>(buf + static_cast<size_t>(blockIdx.x) * ld);
+  const int n2 = n / 2;
+  float am = 0.f;
+  for (int e = threadIdx.x; e < n2; e += kQuantThreads) {
+    const float2 f = __half22float2(row[e]);
+    am = fmaxf(am, fmaxf(fabsf(f.x), fabsf(f.y)));
+  }
+  am = warp_max(am);
+  __shared__ float wmax[kQuantThreads / 32];
+  const int w = threadIdx.x / 32, l = threadIdx.x % 32;
+  if (l == 0) wmax[w] = am;
+  __syncthreads();
+  float m = l < kQuantThreads / 32 ? wmax[l] : 0.f;
+  m = warp_max(m);
+  const float sc = act_scale_of(m);
+  for (int e = threadIdx.x; e < n2; e += kQuantThreads) {
+    const float2 f = __half22float2(row[e]);
+    row[e] = __floats2half2_rn(rintf(__fdiv_rn(f.x, sc)), rintf(__fdiv_rn(f.y, sc)));
+  }
+  if (threadIdx.x == 0) scale[blockIdx.x] = sc;
+}
+
+void launch_act_quant(__half *buf, int T, int n, int ld, float *scale, cudaStream_t s) {
+  if (T <= 0) return;
+  launch_pdl(act_quant_kernel, T, kQuantThreads, 0, s, buf, n, ld, scale);
+}
+
 void launch_rmsnorm(float *x, const int *rows, int n, const float *gain, float eps, int d, int ld, __half *out,
                     const float *part, int S, int pld, int T, const TpPeers *tp, int tp_buf,
-                    unsigned long long tp_epoch, cudaStream_t s) {
+                    unsigned long long tp_epoch, float *qscale, cudaStream_t s) {
   TpPeers none{};
   none.n = 1;
   if (n <= 0) return;
@@ -253,13 +326,13 @@ void launch_rmsnorm(float *x, const int *rows, int n, const float *gain, float e
   const TpPeers &tpp = tp ? *tp : none;
   if (nvec <= 1)
     launch_pdl(rmsnorm_kernel<1>, n, kNormThreads, 0, s, x, rows, gain, eps, d, ld, out, part, S, pld, T, tpp, tp_buf,
-               tp_epoch);
+               tp_epoch, qscale);
   else if (nvec == 2)
     launch_pdl(rmsnorm_kernel<2>, n, kNormThreads, 0, s, x, rows, gain, eps, d, ld, out, part, S, pld, T, tpp, tp_buf,
-               tp_epoch);
+               tp_epoch, qscale);
   else
     launch_pdl(rmsnorm_kernel<kNormMaxVec>, n, kNormThreads, 0, s, x, rows, gain, eps, d, ld, out, part, S, pld, T,
-               tpp, tp_buf, tp_epoch);
+               tpp, tp_buf, tp_epoch, qscale);
 }
 
 // ----------------------------------------------------------------------------------------------------------------

@@ -37,7 +37,14 @@ struct Epi {
   int ld;         // leading dimension of the output
   float *out_f;   // Store / Add: f32 [T, ld]
   __half *out_h;  // SwiGLU: f16 [T, ld]
+  // a8 activations: the input rows hold integers (per-token int8 codes, exact in f16) and row t's products are
+  // multiplied by scale[t] before anything else (split-K partials included); null: a16, nothing is multiplied
+  const float *scale = nullptr;
 };
+#ifdef __CUDACC__
+// the a8 scale of token row t (1 for a16); multiplying by it is exact for a16
+__device__ __forceinline__ float epi_scale(const Epi &e, int t) { return e.scale ? e.scale[t] : 1.f; }
+#endif
 
 struct QWeight {            // a relaid-out weight on the device
   const uint8_t *data = nullptr;
@@ -92,9 +99,14 @@ void launch_tp_reduce_scatter(const TpPeers &p, int b, unsigned long long epoch,
 void launch_embed(const PlanView &pv, const uint8_t *emb, int type, size_t row_bytes, int d, float *x, cudaStream_t s);
 // part (nullable): S split-K partials [S, T, pld] of a residual-add GEMM, added into x before the norm.
 // tp (nullable): instead, the tensor-parallel sum of buffer tp_buf for this epoch, gathered from the rows' owners.
+// qscale (nullable): a8 activations. Each output row is quantized per token, symmetric int8: s = amax / 127 of the
+// row's normalized values (1 for an all-zero row), code = rint(value / s), written as f16 (exact); qscale[r] = s.
 void launch_rmsnorm(float *x, const int *rows, int n, const float *gain, float eps, int d, int ld, __half *out,
                     const float *part, int S, int pld, int T, const TpPeers *tp, int tp_buf,
-                    unsigned long long tp_epoch, cudaStream_t s);
+                    unsigned long long tp_epoch, float *qscale, cudaStream_t s);
+// a8 activations of a GEMM input computed elsewhere (attention output, SwiGLU output): rows [T, ld] f16, the first n
+// columns quantized in place the same way, scale[t] = s of row t
+void launch_act_quant(__half *buf, int T, int n, int ld, float *scale, cudaStream_t s);
 // qkv: [T, ld] rows (S == 1) or [S, T, ld] split-K partials
 void launch_rope_kv(const PlanView &pv, const float *qkv, int S, int ld, int H, int KVH, int dh,
                     const float2 *rope_tab, __half *q, void *kc, void *vc, int8_t *exps, int kv_fp8, int page_scale,

@@ -113,6 +113,10 @@ struct gc_handle {
   // limits
   int max_seqs = 0, max_cols = 0, max_ctx = 0, qg_tokens = 1;
   int gemv_max_t = 0;                       // tolerance buckets: steps of up to this many token rows run the GEMV
+  // a8 buckets: every GEMM input is quantized per token to int8 codes (held as f16 integers) with a float scale per
+  // row; the scales of the RMSNorm outputs, of the attention output and of the SwiGLU output [max_cols] each
+  bool a8 = false;
+  float *h_scale = nullptr, *att_scale = nullptr, *act_scale = nullptr;
   // scratch
   float *x = nullptr, *qkv = nullptr, *logits = nullptr, *part = nullptr, *attn_o = nullptr, *commit_tmp = nullptr;
   __half *h = nullptr, *q = nullptr, *att = nullptr, *act = nullptr;
@@ -567,7 +571,7 @@ struct OpenCfg {
   int ncol = 0, maxctx = 0, max_cols = 0, pool_tune = 0, tp = 1;
   bool tolerance = true;   // every opened bucket's determinism is "tolerance" (the GEMV for a few token rows)
   uint32_t pool_blocks = 0;
-  std::string kv, kv_scale;
+  std::string kv, kv_scale, act;   // act: "a16" (f16 activations) or "a8" (per-token int8 activations)
 };
 
 // One device's state: checks the device, loads (this rank's slices of) the weights, allocates scratch and the KV pool.
@@ -594,6 +598,7 @@ void open_device(gc_handle *h, int dev, const std::vector<std::unique_ptr<GgufFi
   h->page_scale = h->kv_fp8 && c.kv_scale != "unit";
   // batch-invariant buckets run the tcgen05 GEMM at every width (a row's arithmetic never depends on the batch)
   h->gemv_max_t = c.tolerance && c.tp == 1 ? kGemvMaxT : 0;
+  h->a8 = c.act == "a8";
   build_rope(h);
   // KV pool: [L][nblk][KVH][16][dh] for K and for V, plus fp8 page exponents [L][nblk][KVH][2]
   const size_t esz = h->kv_fp8 ? 1 : 2;
@@ -613,6 +618,11 @@ void open_device(gc_handle *h, int dev, const std::vector<std::unique_ptr<GgufFi
   ck(cudaMemset(h->act, 0, static_cast<size_t>(T) * Fpad * 2), "act");
   h->logits = static_cast<float *>(h->dalloc(static_cast<size_t>(T) * std::max(1, h->vocab_rows) * 4, "logits"));
   h->argmax = static_cast<int *>(h->dalloc(static_cast<size_t>(T) * 4, "argmax"));
+  if (h->a8) {
+    h->h_scale = static_cast<float *>(h->dalloc(static_cast<size_t>(T) * 4, "a8 scales"));
+    h->att_scale = static_cast<float *>(h->dalloc(static_cast<size_t>(T) * 4, "a8 scales"));
+    h->act_scale = static_cast<float *>(h->dalloc(static_cast<size_t>(T) * 4, "a8 scales"));
+  }
   h->arg_scratch = static_cast<int *>(h->dalloc(static_cast<size_t>(T) * 8 * 2 * 4, "argmax parts"));
   if (h->tp > 1) {
     h->tp_y = static_cast<float *>(h->dalloc(static_cast<size_t>(T) * d * 4, "tensor-parallel partial sums"));
@@ -772,6 +782,9 @@ GC_API int gc_open(const gc_open_params *p, gc_handle **out) {
       std::string bkv = b->str_or("kv", "f16");
       if (!c.kv.empty() && bkv != c.kv) fail(GC_E_MANIFEST, "buckets disagree on the KV dtype");
       c.kv = bkv;
+      std::string bact = b->str_or("act", "a16");
+      if (!c.act.empty() && bact != c.act) fail(GC_E_MANIFEST, "buckets disagree on the activation type (act)");
+      c.act = bact;
       c.tolerance = c.tolerance && b->str_or("determinism", "batch_invariant") == "tolerance";
       const int btp = static_cast<int>(b->num_or("tp", 1));
       if (i && btp != c.tp) fail(GC_E_MANIFEST, "buckets disagree on the tensor-parallel degree");
@@ -783,6 +796,10 @@ GC_API int gc_open(const gc_open_params *p, gc_handle **out) {
       }
     }
     if (c.kv != "f16" && c.kv != "fp8") fail(GC_E_MANIFEST, "kv dtype %s: f16 or fp8", c.kv.c_str());
+    if (c.act != "a16" && c.act != "a8") fail(GC_E_MANIFEST, "act %s: a16 or a8", c.act.c_str());
+    if (c.act == "a8" && c.tp > 1)
+      fail(GC_E_UNSUPPORTED, "a8 activations under tensor parallelism: a rank sees only its slice of a row, so the "
+           "per-token scale would differ from one GPU's");
     if (c.tp != 1 && c.tp != 2 && c.tp != 4 && c.tp != 8) fail(GC_E_MANIFEST, "tensor-parallel degree %d: 1, 2, 4 or 8", c.tp);
     // weights: the target's files (a NULL entry separates a drafter's, which a non-spec open has none of)
     std::vector<std::unique_ptr<GgufFile>> files;
@@ -1153,19 +1170,23 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
     const int ps = pend_s, pl = pend_ld;
     const TpPeers *tp = pend_tp ? &h->peers : nullptr;
     run(GCK_K_NORM, 1, [&] {
-      launch_rmsnorm(h->x, rows, n, gain, h->eps, h->d, h->d, h->h, pp, ps, pl, T, tp, pend_b, pend_ep, s);
+      launch_rmsnorm(h->x, rows, n, gain, h->eps, h->d, h->d, h->h, pp, ps, pl, T, tp, pend_b, pend_ep, h->h_scale, s);
     });
     pend = nullptr;
     pend_s = 0;
     pend_tp = false;
   };
-  auto residual = [&](int cls, const QWeight &w, const TmaSet &ts, const __half *act, int ldx) {
+  // a8: the input rows of the next GEMM quantized in place (attention output, SwiGLU output); a16: nothing
+  auto quant = [&](__half *buf, int n, int ld, float *scale) {
+    if (h->a8) run(GCK_K_QUANT, 1, [&] { launch_act_quant(buf, T, n, ld, scale, s); });
+  };
+  auto residual = [&](int cls, const QWeight &w, const TmaSet &ts, const __half *act, int ldx, const float *scale) {
     if (h->tp > 1 && h->tp_p2p) {
       // this rank's share of the projection into buffer b; then the ranks' deterministic sum over peer memory: flag,
       // reduce-scatter of the rows this rank owns, flag; the next RMSNorm gathers each row's sum from its owner
       const unsigned long long ep = ++h->tp_epoch;
       const int b = static_cast<int>(ep & 1);
-      const Epi e{kEpiStore, h->d, h->d, h->tp_bufs[b], nullptr};
+      const Epi e{kEpiStore, h->d, h->d, h->tp_bufs[b], nullptr, scale};
       Signal s1{h->tp_flags + b, ep * 4 + 1, h->sig_counter}, s2{h->tp_flags + b, ep * 4 + 2, h->sig_counter};
       if (w.type != kF16) {
         // the rank's split-K partials [splits][T][d] (or its output) straight into buffer b; publishes phase 1
@@ -1183,7 +1204,7 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
     }
     if (h->tp > 1) {
       // this rank's share of the projection (its input columns), summed over the ranks in place
-      gemm(cls, w, ts, act, ldx, T, Epi{kEpiStore, h->d, h->d, h->tp_y, nullptr}, false);
+      gemm(cls, w, ts, act, ldx, T, Epi{kEpiStore, h->d, h->d, h->tp_y, nullptr, scale}, false);
       run(GCK_K_ALLREDUCE, 1, [&] {
         nck(nccl().all_reduce(h->tp_y, h->tp_y, static_cast<size_t>(T) * h->d, ncclFloat, ncclSum,
                               static_cast<ncclComm_t>(h->comm), s), "all-reduce");
@@ -1193,7 +1214,7 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
       pend_ld = h->d;
       return;
     }
-    gemm(cls, w, ts, act, ldx, T, Epi{kEpiAdd, h->d, h->d, h->x, nullptr}, true);
+    gemm(cls, w, ts, act, ldx, T, Epi{kEpiAdd, h->d, h->d, h->x, nullptr, scale}, true);
     if (slices(w, T) > 1) {
       pend = h->part;
       pend_s = slices(w, T);
@@ -1217,7 +1238,7 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
   for (int l = 0; l < h->L; l++) {
     const Layer &ly = h->layers[l];
     norm(nullptr, T, ly.attn_norm);
-    gemm(GCK_K_QKV, ly.qkv, h->tma_h, h->h, h->d, T, Epi{kEpiStore, wq, wq, h->qkv, nullptr}, true);
+    gemm(GCK_K_QKV, ly.qkv, h->tma_h, h->h, h->d, T, Epi{kEpiStore, wq, wq, h->qkv, nullptr, h->h_scale}, true);
     uint8_t *kc = h->kc + l * h->layer_bytes, *vc = h->vc + l * h->layer_bytes;
     int8_t *ex = h->exps ? h->exps + l * h->exps_layer : nullptr;
     const int qs = slices(ly.qkv, T);
@@ -1230,15 +1251,18 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
     aa.vc = vc;
     aa.exps = h->page_scale ? ex : nullptr;
     run(GCK_K_ATTN, 1, [&] { launch_attention(pv, aa, nw, s); });
-    residual(GCK_K_O, ly.o, h->tma_att, h->att, h->H * h->dh);
+    quant(h->att, h->H * h->dh, h->H * h->dh, h->att_scale);
+    residual(GCK_K_O, ly.o, h->tma_att, h->att, h->H * h->dh, h->att_scale);
     norm(nullptr, T, ly.ffn_norm);
-    gemm(GCK_K_GATEUP, ly.gu, h->tma_h, h->h, h->d, T, Epi{kEpiSwiGLU, h->F, ly.dn.KT * kBK, nullptr, h->act}, false);
-    residual(GCK_K_DOWN, ly.dn, h->tma_act, h->act, ly.dn.KT * kBK);
+    gemm(GCK_K_GATEUP, ly.gu, h->tma_h, h->h, h->d, T,
+         Epi{kEpiSwiGLU, h->F, ly.dn.KT * kBK, nullptr, h->act, h->h_scale}, false);
+    quant(h->act, h->F, ly.dn.KT * kBK, h->act_scale);
+    residual(GCK_K_DOWN, ly.dn, h->tma_act, h->act, ly.dn.KT * kBK, h->act_scale);
   }
   if (pv.R > 0) {
     norm(pv.want_tok, pv.R, h->out_norm);
     gemm(GCK_K_HEAD, h->head, h->tma_h, h->h, h->d, pv.R,
-         Epi{kEpiStore, h->vocab_rows, h->vocab_rows, h->logits, nullptr}, false);
+         Epi{kEpiStore, h->vocab_rows, h->vocab_rows, h->logits, nullptr, h->h_scale}, false);
   }
 }
 

@@ -159,9 +159,10 @@ def write_gguf(spec, path):
 
 
 def pack_dir(d, spec, buckets, weights_file="model.gguf"):
-    """Write d/manifest.json for the given buckets: [{id, ncol, maxctx, kv, tune, tp, determinism}] (tune: the library's
-    knobs; tp: the tensor-parallel degree, 1 when absent; determinism: "batch_invariant" (default, contract "BI") or
-    "tolerance" (contract "FAST": the GEMV for steps of a few token rows, pack.py:639))."""
+    """Write d/manifest.json for the given buckets: [{id, ncol, maxctx, kv, act, tune, tp, determinism}] (tune: the
+    library's knobs; tp: the tensor-parallel degree, 1 when absent; act: "a16" (default) or "a8" (per-token int8
+    activations); determinism: "batch_invariant" (default, contract "BI") or "tolerance" (contract "FAST": the GEMV for
+    steps of a few token rows, pack.py:639))."""
     os.makedirs(d, exist_ok=True)
     bs = []
     for b in buckets:
@@ -169,7 +170,7 @@ def pack_dir(d, spec, buckets, weights_file="model.gguf"):
         bs.append(dict(id=b["id"], role="target", variant="v", sku="b200", contract="BI" if det != "tolerance" else "FAST",
                        ncol=b.get("ncol", 64), batch=b.get("batch", True), maxctx=b.get("maxctx", spec.ctx), weights=0,
                        files={}, lib="libgck.so", requires=dict(arch="sm_100a", cc="10.0", sms=148, name="NVIDIA B200"),
-                       determinism=det, act="a16", kv=b.get("kv", "f16"),
+                       determinism=det, act=b.get("act", "a16"), kv=b.get("kv", "f16"),
                        spec_caps=dict(verify=["linear", "tree"], tree_mask=True, verify_widths=[], taps=[],
                                       recurrent_commit=[], accept=[], drafter_roles=[]),
                        tune=dict(b.get("tune", {}))))

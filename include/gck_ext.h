@@ -25,6 +25,7 @@ enum {
   GCK_K_ARGMAX = 10,    /* device argmax */
   GCK_K_REDUCE = 11,    /* split-K reduction + epilogue of a GEMM with K splits */
   GCK_K_ALLREDUCE = 12, /* tensor parallelism: all-reduce of o_proj / down_proj, argmax gather */
+  GCK_K_QUANT = 13,     /* a8 buckets: per-token int8 quantization of the attention and SwiGLU outputs */
   GCK_K_CLASSES = 16
 };
 

@@ -27,6 +27,13 @@ by token over their paths. Either way every token sees exactly the rows ``TorchB
 
 fp8 KV: ``kv_scale="unit"`` is the reference's plain e4m3 cast; ``kv_scale="page"`` is the library's per-page
 power-of-two scale (``page_scale_exp``): a page's scale is fixed by its first row, later rows are clamped to it.
+
+a8 activations (``act="a8"``; the pack's bucket field ``act``, ``goethe_engine/pack.py:647-663`` ``wanted``): the
+reference states a8 as a numerics choice and carries no arithmetic for it (``ref.py`` computes in float32). Here it
+is the input of every linear product (q, k, v and gate, up from the RMSNorm output; o from the attention output; down
+from the SwiGLU output; the head from the final RMSNorm output) quantized per token row to symmetric int8: scale
+``s = amax / 127`` of the row (1 for an all-zero row), codes ``rint(x / s)`` (ties to even), and the product
+``(codes @ W.T) * s`` in float32 (``a8_quant``, ``PagedOracle._lin``).
 """
 import math
 
@@ -56,6 +63,14 @@ def path(parents, i):
     while parents[out[-1]] >= 0:
         out.append(parents[out[-1]])
     return out[::-1]
+
+
+def a8_quant(x):
+    """(codes, scales) of the rows of x [n, k] float32: per row s = amax / 127 (1 where the row is all zero) and codes
+    rint(x / s) as float32 integers in [-127, 127]."""
+    am = np.abs(x).max(-1).astype(np.float32)
+    s = np.where(am > 0, am / np.float32(127.0), np.float32(1.0)).astype(np.float32)
+    return np.rint(x / s[:, None]).astype(np.float32), s
 
 
 def rms(x, gain, eps):
@@ -120,8 +135,9 @@ class Weights:
 class PagedOracle:
     """The reference's TorchBackend semantics over numpy: a KV pool of num_blocks * block_size rows."""
 
-    def __init__(self, w, num_blocks, block_size=16, kv="f16", kv_scale="unit"):
-        self.w, self.bs, self.nb, self.kv, self.kv_scale = w, block_size, num_blocks, kv, kv_scale
+    def __init__(self, w, num_blocks, block_size=16, kv="f16", kv_scale="unit", act="a16"):
+        assert act in ("a16", "a8"), act
+        self.w, self.bs, self.nb, self.kv, self.kv_scale, self.act = w, block_size, num_blocks, kv, kv_scale, act
         rows = num_blocks * block_size
         shape = (w.L, rows, w.KVH, w.dh)
         if kv == "f16":
@@ -174,6 +190,13 @@ class PagedOracle:
         sv = np.float32(2.0) ** self.ve[l, b].astype(np.float32)
         self.kc[l, slots] = Q.e4m3_encode(k * sk[:, :, None])
         self.vc[l, slots] = Q.e4m3_encode(v * sv[:, :, None])
+
+    def _lin(self, x, W):
+        """x @ W.T, with x quantized per row first for a8 (a8_quant), the row's scale applied to its products."""
+        if self.act == "a16":
+            return x @ W.T
+        q, sc = a8_quant(x)
+        return ((q @ W.T) * sc[:, None]).astype(np.float32)
 
     CHUNK = 512
 
@@ -242,9 +265,9 @@ class PagedOracle:
         G = w.H // w.KVH
         for l, lw in enumerate(w.layers):
             h = rms(x, lw["attn_norm"], w.eps)
-            q = w.rope_rows((h @ lw["q"].T).reshape(T, w.H, w.dh), ps)
-            k = w.rope_rows((h @ lw["k"].T).reshape(T, w.KVH, w.dh), ps)
-            v = (h @ lw["v"].T).reshape(T, w.KVH, w.dh)
+            q = w.rope_rows(self._lin(h, lw["q"]).reshape(T, w.H, w.dh), ps)
+            k = w.rope_rows(self._lin(h, lw["k"]).reshape(T, w.KVH, w.dh), ps)
+            v = self._lin(h, lw["v"]).reshape(T, w.KVH, w.dh)
             for i, o in zip(its, offs):
                 self._write_rows(l, i["sl"][i["pos"]:i["pos"] + i["n"]], k[o:o + i["n"]], v[o:o + i["n"]])
             att = np.empty((T, w.H * w.dh), np.float32)
@@ -262,18 +285,18 @@ class PagedOracle:
                     p = np.exp(sc)
                     p = p / p.sum(-1, keepdims=True)
                     att[o + j] = np.einsum("kgt,tkd->kgd", p, V).reshape(-1)
-            x = x + att @ lw["o"].T
+            x = x + self._lin(att, lw["o"])
             h = rms(x, lw["ffn_norm"], w.eps)
-            g = h @ lw["g"].T
-            u = h @ lw["u"].T
-            x = x + ((g / (1.0 + np.exp(-g))) * u).astype(np.float32) @ lw["dn"].T
+            g = self._lin(h, lw["g"])
+            u = self._lin(h, lw["u"])
+            x = x + self._lin(((g / (1.0 + np.exp(-g))) * u).astype(np.float32), lw["dn"])
         want = np.concatenate([np.arange(o + i["n"] - i["want"], o + i["n"]) for i, o in zip(its, offs)])
         for it in work:
             self.blk[it["sid"]] = list(it["blocks"])
         if not want.size:
             return np.zeros((0, w.V), np.float32)
         hn = rms(x[want], w.out_norm, w.eps)
-        return (hn @ w.head.T).astype(np.float32)
+        return self._lin(hn, w.head).astype(np.float32)
 
     def commit(self, sid, base, pth):
         """Row base + pth[j] becomes row base + j, all layers, K and V (ref.py:114-120)."""

@@ -12,8 +12,8 @@ import numpy as np
 import pytest
 
 from goethe_engine_b200 import build, gck, synth
-from helpers import (SCENARIO, SMALL, SMALL128, TOL_F16, TOL_FP8, assert_logits_close, model, oracle_for, replay,
-                     work)
+from helpers import (SCENARIO, SMALL, SMALL128, TOL_A8, TOL_F16, TOL_FP8, assert_logits_close, model, oracle_for,
+                     rel_err, replay, work)
 
 pytestmark = pytest.mark.gpu
 GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
@@ -315,3 +315,44 @@ def test_probe_measures_the_device():
     assert 2000 < hbm < 10000 and 0 < launch < 50 and sms == 148
     us = C.c_double()
     assert L.gc_price(buf, n.value, b"b200.BI.main", C.byref(us)) == gck.OK and 300 < us.value < 5000
+
+
+@pytest.mark.parametrize("wtype,kv", [("q8_0", "f16"), ("q4_k", "fp8")])
+def test_a8_session_matches_oracle(tmp_path, wtype, kv):
+    """An a8 bucket (act "a8": every GEMM input quantized per token to int8, the scale applied in the GEMM epilogue;
+    BASELINE config 4 runs a8 x Q8_0): the scripted session against the oracle's a8 restatement, within TOL_A8 (f16
+    KV) or TOL_FP8 + TOL_A8 (fp8 KV). The a8 path is the one that ran: the logits are closer, on average, to the a8
+    oracle than to the a16 one over the same weights."""
+    spec = synth.Spec(**SMALL128, wtype=wtype, seed=23)
+    ws = synth.make(str(tmp_path / "w"), spec, ncol=8, maxctx=512)[1]
+    kv_scale = "page" if kv == "fp8" else "unit"
+    pack = synth.pack_dir(str(tmp_path / "a8"), spec, [dict(id="b200.BI.a8", ncol=8, maxctx=512, kv=kv, act="a8",
+                                                             tune=dict(kv_scale=kv_scale))], weights_file=ws[0])
+    with backend(pack, ws, pool_blocks=16) as be:
+        got = replay(be)
+    ref8 = replay(oracle_for(ws, kv=kv, kv_scale=kv_scale, act="a8"))
+    ref16 = replay(oracle_for(ws, kv=kv, kv_scale=kv_scale))
+    tol = TOL_A8 if kv == "f16" else TOL_FP8 + TOL_A8
+    e8, e16 = [], []
+    for g, r8, r16 in zip(got, ref8, ref16):
+        assert_logits_close(g, r8, tol)
+        if r8.size:
+            e8.append(rel_err(g, r8).mean())
+            e16.append(rel_err(g, r16).mean())
+    assert np.mean(e8) < np.mean(e16), (np.mean(e8), np.mean(e16))
+
+
+def test_a8_batch_invariance_bitwise(tmp_path):
+    """a8 quantizes each token row on its own (its own amax and scale), so a row's logits are bit-identical alone and
+    batched, as in a16 batch-invariant buckets."""
+    spec = synth.Spec(**SMALL128, wtype="q8_0", seed=29)
+    pack, ws = model(tmp_path, spec, ncol=8, maxctx=512, act="a8")
+    rng = np.random.default_rng(6)
+    prompts = [[int(x) for x in rng.integers(1, 500, 30 + 9 * i)] for i in range(3)]
+    tabs = [list(range(4 * i, 4 * i + 4)) for i in range(3)]
+    with backend(pack, ws, pool_blocks=16) as be:
+        be.step([gck.Work(i, p[:-1], 0, tabs[i], 0) for i, p in enumerate(prompts)])
+        last = [gck.Work(i, [p[-1]], len(p) - 1, tabs[i], 1) for i, p in enumerate(prompts)]
+        batched = be.step(last)
+        for i in range(3):
+            assert np.array_equal(be.step([last[i]]), batched[i:i + 1]), i

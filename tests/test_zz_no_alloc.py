@@ -64,12 +64,14 @@ def test_static_commit_matches_gc_commit_twice(tmp_path, kv):
             pos += 1
         # an unknown sequence is an error code, as with gc_commit
         assert commit(99, 0, [0, 1]) == gck.E_STATE
-        # this model stages 2 layers x K, V x 1 kv head x 128 dims x 4 bytes = 2 KiB per moved row (plus 8 bytes of
-        # move list): 16 MiB holds 8159 of them. A sequence whose table repeats one free block 520 times covers 8320
-        # rows; moving rows 1..8200 down by one needs 8200 moves, which the array cannot hold.
+        # this model stages 2 layers x K, V x 1 kv head x 128 dims x 4 bytes = 2 KiB per moved row, plus 8 bytes of
+        # move list (the list rounded up to 256 bytes): (16 MiB - 256) / 2056 = 8160 moves fit. A sequence whose table
+        # repeats one free block 520 times covers 8320 rows; moving rows 1..8200 down by one needs 8200 moves.
+        limit = ((16 << 20) - 256) // (2 * 2 * 1 * 128 * 4 + 8)
+        assert limit == 8160
         be.step([gck.Work(3, [1], 0, [31] * 520, 0)])
         assert commit(3, 0, [j + 1 for j in range(8200)]) == gck.E_ARG
         msg = (be.L.gc_last_error(be.h) or b"").decode()
-        assert "at most 8159 moved rows" in msg, msg
+        assert f"at most {limit} moved rows" in msg, msg
         # the refusal left the handle usable
         assert np.array_equal(be.step([gck.Work(1, [nxt], pos, ta, 1)]).shape, (1, be.vocab_size))
