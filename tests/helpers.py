@@ -16,7 +16,12 @@ SMALL = dict(vocab=512, d=256, layers=2, heads=4, kv_heads=2, ffn=512)      # dh
 SMALL128 = dict(vocab=512, d=512, layers=2, heads=4, kv_heads=1, ffn=768)   # dh 128, GQA 4
 # a16 with f16 KV: the north-star tolerance on logits, max |a - b| / max |b| per row
 TOL_F16 = 1e-2
-TOL_FP8 = 3e-2
+# fp8 e4m3 KV: 3 mantissa bits, so a stored code moves one step (6-12 % of the value) wherever the library's K or V and
+# the oracle's straddle a rounding boundary; the library's inputs carry f16 roundings the oracle's float32 ones do not.
+# Measured at the 8B shape (2 layers, 64 decode rows): the oracle itself moves by up to 0.028 (mean 0.018) when its
+# inputs are rounded to f16 the way the library stores them, and the library differs from it by up to 0.031 (mean
+# 0.021), while with f16 KV the library agrees to 0.0047. So fp8 KV is checked at 5e-2, f16 KV at 1e-2.
+TOL_FP8 = 5e-2
 # a8 (per-token int8 activations): the library and the oracle quantize nearly the same rows, but the library's inputs
 # were rounded to f16 (attention and SwiGLU outputs) where the oracle's are float32, so a code can differ by one step
 # (1/127 of the row's amax) wherever the two straddle a rounding boundary: looser than a16
