@@ -712,6 +712,19 @@ __global__ void argmax_part_kernel(const float *logits, int V, int *pick) {
   }
 }
 
+__global__ void spec_accept_kernel(const int *chain, const int *target, int K, int *out) {
+  dep_wait();
+  if (threadIdx.x != 0) return;
+  int j = 0;
+  while (j < K && chain[j + 1] == target[j]) j++;
+  for (int i = 0; i <= j; i++) out[i] = target[i];
+  out[K + 1] = j + 1;
+}
+
+void launch_spec_accept(const int *chain, const int *target, int K, int *out, cudaStream_t s) {
+  launch_pdl(spec_accept_kernel, 1, 32, 0, s, chain, target, K, out);
+}
+
 void launch_argmax_merge(const int *pick, int tp, int R, int *out, cudaStream_t s);
 void launch_argmax(const float *logits, int R, int V, int *out, int *scratch, cudaStream_t s) {
   if (R <= 0) return;

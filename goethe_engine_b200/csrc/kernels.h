@@ -114,6 +114,10 @@ void launch_rope_kv(const PlanView &pv, const float *qkv, int S, int ld, int H, 
 void launch_splitk_reduce(const float *part, int S, int T, int Npad, const Epi &epi, cudaStream_t s);
 // scratch: [8][R][2] ints (the parts' candidates)
 void launch_argmax(const float *logits, int R, int V, int *out, int *scratch, cudaStream_t s);
+// A speculative round's acceptance: chain[0] is the anchor and chain[1..K] the drafts; target[i] the target's argmax
+// after chain[0..i]. j = the longest prefix of drafts with chain[i + 1] == target[i]; out[0..j] = target[0..j] (the
+// accepted drafts, then the target's own next token) and out[K + 1] = j + 1.
+void launch_spec_accept(const int *chain, const int *target, int K, int *out, cudaStream_t s);
 // tensor parallelism: a rank's candidates (value bits, global index) of its vocabulary slice, and their merge
 void launch_argmax_pick(const float *logits, int R, int V, int offset, int *pick, cudaStream_t s);
 void launch_argmax_merge(const int *pick, int tp, int R, int *out, cudaStream_t s);

@@ -117,6 +117,15 @@ struct gc_handle {
   // row; the scales of the RMSNorm outputs, of the attention output and of the SwiGLU output [max_cols] each
   bool a8 = false;
   float *h_scale = nullptr, *att_scale = nullptr, *act_scale = nullptr;
+  // speculative pair (GC_OPEN_SPEC): this handle is the target of one linear stream; `drafter` a second handle on the
+  // same device that runs on this handle's stream; a round drafts spec_k tokens. The stream's tokens so far (row i of
+  // both KV caches holds hist[i]) and how many rows of the drafter's cache hold them (it lags after prefill steps).
+  gc_handle *drafter = nullptr;
+  int spec_k = 0;
+  std::vector<int> hist;
+  int draft_rows = 0;
+  std::vector<uint32_t> spec_table;          // the stream's block table: blocks 0 .. max_ctx / 16 of both pools
+  int *spec_out = nullptr, *spec_out_host = nullptr;   // [spec_k + 2]: a round's accepted tokens, then their count
   // scratch
   float *x = nullptr, *qkv = nullptr, *logits = nullptr, *part = nullptr, *attn_o = nullptr, *commit_tmp = nullptr;
   __half *h = nullptr, *q = nullptr, *att = nullptr, *act = nullptr;
@@ -166,10 +175,16 @@ struct gc_handle {
   }
   ~gc_handle() {
     if (st) cudaStreamSynchronize(st);
+    if (drafter) {
+      drafter->st = nullptr;                 // the target's stream, destroyed below
+      delete drafter;
+      cudaSetDevice(dev);
+    }
     for (void *p : allocs) cudaFree(p);
     if (plan_host) cudaFreeHost(plan_host);
     if (tok_host) cudaFreeHost(tok_host);
     if (kerr_host) cudaFreeHost(kerr_host);
+    if (spec_out_host) cudaFreeHost(spec_out_host);
     for (auto e : ev_pool) cudaEventDestroy(e);
     if (st) cudaStreamDestroy(st);
   }
@@ -572,7 +587,46 @@ struct OpenCfg {
   bool tolerance = true;   // every opened bucket's determinism is "tolerance" (the GEMV for a few token rows)
   uint32_t pool_blocks = 0;
   std::string kv, kv_scale, act;   // act: "a16" (f16 activations) or "a8" (per-token int8 activations)
+  int spec_k = 0;                  // a speculative pair's target: drafts per round
 };
+
+// The configuration of the buckets ids[0 .. n) of the manifest's bucket list: the widest columns and context, and the
+// KV dtype, activation type and tensor-parallel degree they must agree on.
+OpenCfg bucket_cfg(const Json &bl, const char *const *ids, uint32_t n, uint32_t pool_blocks) {
+  OpenCfg c;
+  c.pool_blocks = pool_blocks;
+  for (uint32_t i = 0; i < n; i++) {
+    if (!ids[i]) fail(GC_E_ARG, "gc_open: null bucket id");
+    const Json *b = nullptr;
+    for (auto &x : bl.arr)
+      if (x.str_or("id", "") == ids[i]) b = &x;
+    if (!b) fail(GC_E_MANIFEST, "bucket %s is not in the manifest", ids[i]);
+    c.ncol = std::max(c.ncol, static_cast<int>(b->num_or("ncol", 1)));
+    c.maxctx = std::max(c.maxctx, static_cast<int>(b->num_or("maxctx", 4096)));
+    std::string bkv = b->str_or("kv", "f16");
+    if (!c.kv.empty() && bkv != c.kv) fail(GC_E_MANIFEST, "buckets disagree on the KV dtype");
+    c.kv = bkv;
+    std::string bact = b->str_or("act", "a16");
+    if (!c.act.empty() && bact != c.act) fail(GC_E_MANIFEST, "buckets disagree on the activation type (act)");
+    c.act = bact;
+    c.tolerance = c.tolerance && b->str_or("determinism", "batch_invariant") == "tolerance";
+    const int btp = static_cast<int>(b->num_or("tp", 1));
+    if (i && btp != c.tp) fail(GC_E_MANIFEST, "buckets disagree on the tensor-parallel degree");
+    c.tp = btp;
+    if (const Json *t = b->get("tune")) {
+      c.max_cols = std::max(c.max_cols, static_cast<int>(t->num_or("max_cols", 0)));
+      c.pool_tune = std::max(c.pool_tune, static_cast<int>(t->num_or("pool_blocks", 0)));
+      c.kv_scale = t->str_or("kv_scale", c.kv_scale);
+    }
+  }
+  if (c.kv != "f16" && c.kv != "fp8") fail(GC_E_MANIFEST, "kv dtype %s: f16 or fp8", c.kv.c_str());
+  if (c.act != "a16" && c.act != "a8") fail(GC_E_MANIFEST, "act %s: a16 or a8", c.act.c_str());
+  if (c.act == "a8" && c.tp > 1)
+    fail(GC_E_UNSUPPORTED, "a8 activations under tensor parallelism: a rank sees only its slice of a row, so the "
+         "per-token scale would differ from one GPU's");
+  if (c.tp != 1 && c.tp != 2 && c.tp != 4 && c.tp != 8) fail(GC_E_MANIFEST, "tensor-parallel degree %d: 1, 2, 4 or 8", c.tp);
+  return c;
+}
 
 // One device's state: checks the device, loads (this rank's slices of) the weights, allocates scratch and the KV pool.
 void open_device(gc_handle *h, int dev, const std::vector<std::unique_ptr<GgufFile>> &files, const OpenCfg &c, int rank) {
@@ -755,10 +809,11 @@ GC_API int gc_open(const gc_open_params *p, gc_handle **out) {
     gc_open_params P{};
     std::memcpy(&P, p, std::min<size_t>(p->size, sizeof P));
     if (p->size < offsetof(gc_open_params, pool_blocks) + sizeof(uint32_t)) fail(GC_E_ARG, "gc_open: struct size %u", p->size);
-    if (P.flags & GC_OPEN_SPEC) fail(GC_E_UNSUPPORTED, "speculative pairs (GC_OPEN_SPEC) are not supported by this library");
+    const bool spec = (P.flags & GC_OPEN_SPEC) != 0;
     if (const char *e = std::getenv("GCK_PDL")) g_pdl = std::atoi(e) != 0;
     if (!P.pack_dir) fail(GC_E_ARG, "gc_open: no pack_dir");
     if (!P.n_buckets || !P.buckets) fail(GC_E_ARG, "gc_open: no bucket ids");
+    if (spec && P.n_buckets != 2) fail(GC_E_ARG, "gc_open: a speculative pair opens two buckets {target, drafter}");
     // manifest: the requested buckets
     Json m;
     try {
@@ -769,50 +824,53 @@ GC_API int gc_open(const gc_open_params *p, gc_handle **out) {
     }
     const Json *bl = m.get("buckets");
     if (!bl || bl->kind != Json::Arr) fail(GC_E_MANIFEST, "manifest.json has no buckets");
-    OpenCfg c;
-    c.pool_blocks = P.pool_blocks;
-    for (uint32_t i = 0; i < P.n_buckets; i++) {
-      if (!P.buckets[i]) fail(GC_E_ARG, "gc_open: null bucket id");
-      const Json *b = nullptr;
-      for (auto &x : bl->arr)
-        if (x.str_or("id", "") == P.buckets[i]) b = &x;
-      if (!b) fail(GC_E_MANIFEST, "bucket %s is not in the manifest", P.buckets[i]);
-      c.ncol = std::max(c.ncol, static_cast<int>(b->num_or("ncol", 1)));
-      c.maxctx = std::max(c.maxctx, static_cast<int>(b->num_or("maxctx", 4096)));
-      std::string bkv = b->str_or("kv", "f16");
-      if (!c.kv.empty() && bkv != c.kv) fail(GC_E_MANIFEST, "buckets disagree on the KV dtype");
-      c.kv = bkv;
-      std::string bact = b->str_or("act", "a16");
-      if (!c.act.empty() && bact != c.act) fail(GC_E_MANIFEST, "buckets disagree on the activation type (act)");
-      c.act = bact;
-      c.tolerance = c.tolerance && b->str_or("determinism", "batch_invariant") == "tolerance";
-      const int btp = static_cast<int>(b->num_or("tp", 1));
-      if (i && btp != c.tp) fail(GC_E_MANIFEST, "buckets disagree on the tensor-parallel degree");
-      c.tp = btp;
-      if (const Json *t = b->get("tune")) {
-        c.max_cols = std::max(c.max_cols, static_cast<int>(t->num_or("max_cols", 0)));
-        c.pool_tune = std::max(c.pool_tune, static_cast<int>(t->num_or("pool_blocks", 0)));
-        c.kv_scale = t->str_or("kv_scale", c.kv_scale);
+    // a speculative pair's target and drafter buckets each configure their own model; a ladder's buckets one
+    OpenCfg c = bucket_cfg(*bl, P.buckets, spec ? 1 : P.n_buckets, P.pool_blocks);
+    OpenCfg cd;
+    if (spec) {
+      cd = bucket_cfg(*bl, P.buckets + 1, 1, 0);
+      std::string pol = P.spec_policy ? P.spec_policy : "";
+      if (pol.empty()) {
+        // the pack's pair: manifest spec[] entry {target, drafter, policy {kind, K}}
+        if (const Json *sp = m.get("spec"))
+          for (auto &x : sp->arr)
+            if (x.str_or("target", "") == P.buckets[0] && x.str_or("drafter", "") == P.buckets[1])
+              if (const Json *po = x.get("policy")) {
+                const Json *K = po->get("K");
+                pol = po->str_or("kind", "") + ":" +
+                      (K ? (K->kind == Json::Str ? K->str : std::to_string(static_cast<int>(K->num))) : "");
+              }
       }
+      if (pol.rfind("ar:", 0) != 0)
+        fail(GC_E_UNSUPPORTED, "speculative policy '%s': this library runs ar:K (a draft model, K greedy drafts a round)",
+             pol.c_str());
+      c.spec_k = std::atoi(pol.c_str() + 3);
+      if (c.spec_k < 1 || c.spec_k > 15) fail(GC_E_ARG, "speculative policy '%s': K must be 1 .. 15", pol.c_str());
+      if (c.tp != 1 || cd.tp != 1) fail(GC_E_UNSUPPORTED, "a speculative pair runs on one GPU");
+      // one linear stream: each model gets a pool of one whole context (every position a round can reach)
+      c.ncol = cd.ncol = 1;
+      cd.maxctx = c.maxctx;
+      c.pool_blocks = cd.pool_blocks = static_cast<uint32_t>((c.maxctx + kBlock - 1) / kBlock + 1);
+      c.tolerance = cd.tolerance = false;     // rounds verify against chain rows: the batch-invariant path only
     }
-    if (c.kv != "f16" && c.kv != "fp8") fail(GC_E_MANIFEST, "kv dtype %s: f16 or fp8", c.kv.c_str());
-    if (c.act != "a16" && c.act != "a8") fail(GC_E_MANIFEST, "act %s: a16 or a8", c.act.c_str());
-    if (c.act == "a8" && c.tp > 1)
-      fail(GC_E_UNSUPPORTED, "a8 activations under tensor parallelism: a rank sees only its slice of a row, so the "
-           "per-token scale would differ from one GPU's");
-    if (c.tp != 1 && c.tp != 2 && c.tp != 4 && c.tp != 8) fail(GC_E_MANIFEST, "tensor-parallel degree %d: 1, 2, 4 or 8", c.tp);
-    // weights: the target's files (a NULL entry separates a drafter's, which a non-spec open has none of)
-    std::vector<std::unique_ptr<GgufFile>> files;
+    // weights: the target's files, then (a speculative pair) a NULL entry and the drafter's
+    std::vector<std::unique_ptr<GgufFile>> files, dfiles;
     if (!P.weights || !P.n_weights) fail(GC_E_WEIGHTS, "no weight files");
+    bool after_null = false;
     for (uint32_t i = 0; i < P.n_weights; i++) {
-      if (!P.weights[i]) break;
+      if (!P.weights[i]) {
+        after_null = true;
+        if (!spec) break;
+        continue;
+      }
       try {
-        files.emplace_back(new GgufFile(P.weights[i]));
+        (after_null ? dfiles : files).emplace_back(new GgufFile(P.weights[i]));
       } catch (const std::runtime_error &e) {
         fail(GC_E_WEIGHTS, "%s", e.what());
       }
     }
     if (files.empty()) fail(GC_E_WEIGHTS, "no weight files");
+    if (spec && dfiles.empty()) fail(GC_E_WEIGHTS, "a speculative pair needs the drafter's weight files after a NULL entry");
     // devices: `device` (or the current one) and, with tensor parallelism, the next tp - 1
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
@@ -826,6 +884,23 @@ GC_API int gc_open(const gc_open_params *p, gc_handle **out) {
     h = new gc_handle();
     if (c.tp == 1) {
       open_device(h, dev, files, c, 0);
+      if (spec) {
+        // the drafter: a second model on the same device, run on the target's stream (a round's launches are one
+        // ordered sequence); its own weights, KV pool and scratch
+        h->drafter = new gc_handle();
+        open_device(h->drafter, dev, dfiles, cd, 0);
+        ck(cudaSetDevice(dev), "cudaSetDevice");
+        ck(cudaStreamDestroy(h->drafter->st), "stream");
+        h->drafter->st = h->st;
+        if (h->drafter->vocab != h->vocab)
+          fail(GC_E_WEIGHTS, "drafter vocabulary %d differs from the target's %d", h->drafter->vocab, h->vocab);
+        h->spec_k = c.spec_k;
+        h->max_seqs = 1;
+        h->slots.assign(1, Slot{});
+        for (int b = 0; b < (h->max_ctx + kBlock - 1) / kBlock; b++) h->spec_table.push_back(static_cast<uint32_t>(b));
+        h->spec_out = static_cast<int *>(h->dalloc(static_cast<size_t>(h->spec_k + 2) * 4, "speculative round"));
+        ck(cudaMallocHost(&h->spec_out_host, static_cast<size_t>(h->spec_k + 2) * 4), "pinned speculative round");
+      }
     } else {
       h->tp = c.tp;
       h->dev = dev;
@@ -890,6 +965,29 @@ GC_API int gc_layout_get(gc_handle *h, gc_layout *o) {
   gc_layout l{};
   l.size = sizeof l;
   l.flags = GC_L_PAGED | GC_L_DEVICE_ARGMAX;
+  if (h->drafter) {
+    // a speculative pair: one linear stream whose single page is the whole context (gc.h:87-131); a round of a step
+    // verifies spec_k drafts and the anchor
+    l.flags = GC_L_SPEC | GC_L_DEVICE_ARGMAX;
+    l.vocab = h->vocab;
+    l.max_cols = h->max_cols;
+    l.max_seqs = 1;
+    l.max_ctx = h->max_ctx;
+    l.block_size = h->max_ctx;
+    l.num_blocks = 1;
+    l.layers = h->L;
+    l.kv_heads = h->KVH;
+    l.head_dim = h->dh;
+    l.kv_dtype = h->kv_fp8 ? GC_KV_FP8 : GC_KV_F16;
+    l.spec_width = h->spec_k + 1;
+    l.kv_bytes = 2 * h->layer_bytes * h->L + h->exps_layer * h->L + 2 * h->drafter->layer_bytes * h->drafter->L +
+                 h->drafter->exps_layer * h->drafter->L;
+    l.device_bytes = h->device_bytes + h->drafter->device_bytes;
+    uint32_t n = std::min<uint32_t>(o->size, sizeof l);
+    std::memcpy(o, &l, n);
+    o->size = n;
+    return GC_OK;
+  }
   l.vocab = h->vocab;
   l.max_cols = h->max_cols;
   l.max_seqs = h->max_seqs;
@@ -1041,36 +1139,35 @@ void build_plan(gc_handle *h, const std::vector<WorkIn> &ws, HostPlan &pl) {
   }
 }
 
-// pack the plan into the pinned buffer and upload it; returns the device view
-PlanView upload_plan(gc_handle *h, HostPlan &pl) {
-  std::vector<std::pair<const void *, size_t>> parts = {
+// A plan's parts in a buffer, each 256-byte aligned: their offsets, and the total bytes.
+size_t plan_layout(const HostPlan &pl, std::vector<size_t> &off) {
+  const size_t sizes[10] = {vbytes(pl.tok_id), vbytes(pl.rope_pos), vbytes(pl.kv_row), vbytes(pl.first_tok),
+                            vbytes(pl.items), vbytes(pl.qgroups), vbytes(pl.work), vbytes(pl.blocks),
+                            vbytes(pl.paths), vbytes(pl.want_tok)};
+  size_t total = 0;
+  off.clear();
+  for (size_t n : sizes) {
+    off.push_back(total);
+    total += (n + 255) / 256 * 256;
+  }
+  return total;
+}
+
+// the plan's parts copied to host memory at `host` (its layout `off`)
+void plan_copy(const HostPlan &pl, uint8_t *host, const std::vector<size_t> &off) {
+  const std::pair<const void *, size_t> parts[10] = {
       {pl.tok_id.data(), vbytes(pl.tok_id)},   {pl.rope_pos.data(), vbytes(pl.rope_pos)},
       {pl.kv_row.data(), vbytes(pl.kv_row)},   {pl.first_tok.data(), vbytes(pl.first_tok)},
       {pl.items.data(), vbytes(pl.items)},     {pl.qgroups.data(), vbytes(pl.qgroups)},
       {pl.work.data(), vbytes(pl.work)},       {pl.blocks.data(), vbytes(pl.blocks)},
       {pl.paths.data(), vbytes(pl.paths)},     {pl.want_tok.data(), vbytes(pl.want_tok)}};
-  size_t total = 0;
-  std::vector<size_t> off;
-  for (auto &p : parts) {
-    off.push_back(total);
-    total += (p.second + 255) / 256 * 256;
-  }
-  if (total > h->plan_cap) {
-    cudaStreamSynchronize(h->st);
-    if (h->plan_host) cudaFreeHost(h->plan_host);
-    h->plan_host = nullptr;
-    size_t cap = std::max<size_t>(total * 2, 1 << 20);
-    if (h->plan_dev) h->dfree(h->plan_dev, h->plan_cap);
-    h->plan_dev = static_cast<uint8_t *>(h->dalloc(cap, "plan"));
-    ck(cudaMallocHost(&h->plan_host, cap), "pinned plan");
-    h->plan_cap = cap;
-  }
-  // the previous step's upload has finished: every step ends with a stream synchronize
-  for (size_t i = 0; i < parts.size(); i++)
-    if (parts[i].second) std::memcpy(h->plan_host + off[i], parts[i].first, parts[i].second);
-  ck(cudaMemcpyAsync(h->plan_dev, h->plan_host, total, cudaMemcpyHostToDevice, h->st), "plan upload");
+  for (int i = 0; i < 10; i++)
+    if (parts[i].second) std::memcpy(host + off[i], parts[i].first, parts[i].second);
+}
+
+// the device view of a plan uploaded at `dev` (its layout `off`)
+PlanView plan_view(gc_handle *h, const HostPlan &pl, uint8_t *b, const std::vector<size_t> &off) {
   PlanView pv;
-  uint8_t *b = h->plan_dev;
   pv.tok_id = reinterpret_cast<const int *>(b + off[0]);
   pv.rope_pos = reinterpret_cast<const int *>(b + off[1]);
   pv.kv_row = reinterpret_cast<const int *>(b + off[2]);
@@ -1093,6 +1190,35 @@ PlanView upload_plan(gc_handle *h, HostPlan &pl) {
   for (const QGroup &q : pl.qgroups) pv.max_rows = std::max(pv.max_rows, q.ntok * (h->H / h->KVH));
   return pv;
 }
+
+// Several plans packed one after another into the handle's pinned buffer and uploaded with one copy on its stream;
+// returns their device views. The previous step's upload has finished: every step ends with a stream synchronize.
+std::vector<PlanView> upload_plans(gc_handle *h, const std::vector<const HostPlan *> &pls) {
+  std::vector<std::vector<size_t>> offs(pls.size());
+  std::vector<size_t> base(pls.size());
+  size_t total = 0;
+  for (size_t i = 0; i < pls.size(); i++) {
+    base[i] = total;
+    total += plan_layout(*pls[i], offs[i]);
+  }
+  if (total > h->plan_cap) {
+    cudaStreamSynchronize(h->st);
+    if (h->plan_host) cudaFreeHost(h->plan_host);
+    h->plan_host = nullptr;
+    size_t cap = std::max<size_t>(total * 2, 1 << 20);
+    if (h->plan_dev) h->dfree(h->plan_dev, h->plan_cap);
+    h->plan_dev = static_cast<uint8_t *>(h->dalloc(cap, "plan"));
+    ck(cudaMallocHost(&h->plan_host, cap), "pinned plan");
+    h->plan_cap = cap;
+  }
+  for (size_t i = 0; i < pls.size(); i++) plan_copy(*pls[i], h->plan_host + base[i], offs[i]);
+  ck(cudaMemcpyAsync(h->plan_dev, h->plan_host, total, cudaMemcpyHostToDevice, h->st), "plan upload");
+  std::vector<PlanView> out;
+  for (size_t i = 0; i < pls.size(); i++) out.push_back(plan_view(h, *pls[i], h->plan_dev + base[i], offs[i]));
+  return out;
+}
+
+PlanView upload_plan(gc_handle *h, HostPlan &pl) { return upload_plans(h, {&pl})[0]; }
 
 void forward(gc_handle *h, const PlanView &pv, int nw) {
   const int T = pv.T;
@@ -1368,6 +1494,134 @@ void step_device(gc_handle *h, const std::vector<WorkIn> &ws, bool greedy, uint6
   collect_stats(h, f0, f1);
 }
 
+// A speculative pair's step (GC_L_SPEC: one linear stream, gc.h:57,93,117,136,174-190). A prefill chunk or a plain
+// decode runs the target only; the drafter catches up at the next round. A decode with GC_W_SPEC runs a round: the
+// drafter drafts spec_k tokens greedily after the anchor (its first pass also takes the stream's tokens it has not
+// seen), the target verifies anchor and drafts as one chain, and the longest prefix of drafts equal to the target's
+// argmax is accepted and returned with the target's own next token (1 .. spec_k + 1 tokens). The drafts never leave
+// the device: each draft pass's argmax writes its token where the next pass and the verify read it, and one copy
+// brings the round back. In batch-invariant numerics a verify row equals a plain decode of the same token (chunk
+// invariance), so a round returns exactly the tokens the target alone would decode greedily.
+int spec_step(gc_handle *h, const gc_step_in *in, gc_step_out *o) {
+  if (in->n_work != 1) fail(GC_E_UNSUPPORTED, "a speculative pair runs one sequence a step (%u items)", in->n_work);
+  const gc_work *wp = in->work[0];
+  if (!wp) fail(GC_E_ARG, "work item 0 is null");
+  if (wp->size < offsetof(gc_work, want) + 4) fail(GC_E_ARG, "work item 0: struct size %u", wp->size);
+  gc_work W{};
+  std::memcpy(&W, wp, std::min<size_t>(wp->size, sizeof W));
+  if (!(W.flags & GC_W_GREEDY)) fail(GC_E_UNSUPPORTED, "a speculative pair runs greedy sequences (device argmax)");
+  if (W.parents) fail(GC_E_UNSUPPORTED, "a speculative pair verifies its own drafts: no tree items");
+  if (W.flags & GC_W_FEATS) fail(GC_E_UNSUPPORTED, "this pack has no tap features");
+  if (!W.n_tokens || !W.tokens || W.want > W.n_tokens) fail(GC_E_ARG, "work item 0: bad token count or want");
+  if (!W.blocks || W.n_blocks != 1 || W.blocks[0] != 0)
+    fail(GC_E_ARG, "work item 0: a speculative pair's sequence has the one page 0");
+  for (uint32_t j = 0; j < W.n_tokens; j++)
+    if (W.tokens[j] < 0 || W.tokens[j] >= h->vocab) fail(GC_E_ARG, "work item 0: token %d outside the vocabulary", W.tokens[j]);
+  const bool round = (W.flags & GC_W_SPEC) && W.want > 0;
+  if (round && W.n_tokens != 1) fail(GC_E_ARG, "a speculative round starts from one anchor token (%u given)", W.n_tokens);
+  const int K = h->spec_k;
+  const uint64_t end = static_cast<uint64_t>(W.pos) + W.n_tokens + (round ? K : 0);
+  if (end > static_cast<uint64_t>(h->max_ctx))
+    fail(GC_E_ARG, "work item 0: position %llu past the context %d", static_cast<unsigned long long>(end), h->max_ctx);
+  gc_step_out O{};
+  std::memcpy(&O, o, std::min<size_t>(o->size, sizeof O));
+  const uint32_t rows = round ? static_cast<uint32_t>(K + 1) : W.want;
+  o->n_rows = rows;
+  if (O.tokens_cap < rows || (rows && !O.tokens) || !O.counts) fail(GC_E_CAPACITY, "tokens buffer too small (%u rows)", rows);
+  const bool fresh = find_slot(h, W.sid, false) == nullptr;
+  if (!find_slot(h, W.sid, true)) fail(GC_E_STATE, "no free sequence slot (a speculative pair runs one)");
+  if (fresh) {
+    h->hist.clear();
+    h->draft_rows = 0;
+  }
+  if (W.pos > h->hist.size())
+    fail(GC_E_STATE, "position %u not contiguous: the stream holds %zu tokens", W.pos, h->hist.size());
+  h->hist.resize(W.pos);                                  // a rewind drops the rows past pos
+  h->draft_rows = std::min(h->draft_rows, static_cast<int>(W.pos));
+  h->hist.insert(h->hist.end(), W.tokens, W.tokens + W.n_tokens);
+  const uint32_t *table = h->spec_table.data();
+  const uint32_t ntab = static_cast<uint32_t>(h->spec_table.size());
+  if (!round) {
+    const WorkIn wi{W.flags, W.sid, W.pos, W.n_tokens, W.tokens, nullptr, table, ntab, W.want};
+    step_device(h, {wi}, true, W.want, in->flags, O, o);
+    O.counts[0] = W.want;
+    return GC_OK;
+  }
+  gc_handle *d = h->drafter;
+  const int pos = static_cast<int>(W.pos);
+  // the drafter's backlog beyond what one pass takes runs as plain prefill chunks first
+  while (pos - h->draft_rows + 1 > d->max_cols) {
+    const int n = std::min(d->max_cols, pos - h->draft_rows);
+    const WorkIn wi{0, W.sid, static_cast<uint32_t>(h->draft_rows), static_cast<uint32_t>(n),
+                    h->hist.data() + h->draft_rows, nullptr, table, ntab, 0};
+    step_device(d, {wi}, false, 0, 0, O, nullptr);
+    h->draft_rows += n;
+  }
+  // the plans: draft passes 1 .. K (the first over the backlog and the anchor), then the verify of anchor + drafts
+  std::vector<HostPlan> dp(K);
+  std::vector<int> first(h->hist.begin() + h->draft_rows, h->hist.begin() + pos + 1), zero(1, 0), chain(K + 1, 0);
+  build_plan(d, {WorkIn{GC_W_GREEDY, W.sid, static_cast<uint32_t>(h->draft_rows), static_cast<uint32_t>(first.size()),
+                        first.data(), nullptr, table, ntab, 1}}, dp[0]);
+  for (int k = 1; k < K; k++)
+    build_plan(d, {WorkIn{GC_W_GREEDY, W.sid, static_cast<uint32_t>(pos + k), 1, zero.data(), nullptr, table, ntab, 1}},
+               dp[k]);
+  chain[0] = W.tokens[0];
+  HostPlan vp;
+  build_plan(h, {WorkIn{GC_W_GREEDY, W.sid, W.pos, static_cast<uint32_t>(K + 1), chain.data(), nullptr, table, ntab,
+                        static_cast<uint32_t>(K + 1)}}, vp);
+  ck(cudaSetDevice(h->dev), "cudaSetDevice");
+  std::vector<const HostPlan *> dptr;
+  for (auto &x : dp) dptr.push_back(&x);
+  std::vector<PlanView> dv = upload_plans(d, dptr);
+  const PlanView vv = upload_plan(h, vp);
+  int *chain_dev = const_cast<int *>(vv.tok_id);          // the verify's tokens: the anchor, then each draft as made
+  cudaEvent_t f0 = nullptr, f1 = nullptr;
+  if (h->stats_on) {
+    f0 = h->event();
+    f1 = h->event();
+    cudaEventRecord(f0, h->st);
+  }
+  h->step_launches = 0;
+  uint64_t launches = 0;
+  for (int k = 0; k < K; k++) {
+    if (k > 0) dv[k].tok_id = chain_dev + k;                // pass k + 1 embeds draft k
+    forward(d, dv[k], dp[k].nw);
+    launches += d->step_launches + 1;
+    launch_argmax(d->logits, 1, d->vocab_rows, chain_dev + k + 1, d->arg_scratch, h->st);
+  }
+  forward(h, vv, vp.nw);
+  launches += h->step_launches + 2;
+  launch_argmax(h->logits, K + 1, h->vocab_rows, h->argmax, h->arg_scratch, h->st);
+  launch_spec_accept(chain_dev, h->argmax, K, h->spec_out, h->st);
+  h->step_launches = launches;
+  if (f1) cudaEventRecord(f1, h->st);
+  ck(cudaMemcpyAsync(h->spec_out_host, h->spec_out, static_cast<size_t>(K + 2) * 4, cudaMemcpyDeviceToHost, h->st),
+     "round");
+  ck(cudaMemcpyAsync(h->kerr_host, h->kerr, 4, cudaMemcpyDeviceToHost, h->st), "error word");
+  ck(cudaMemcpyAsync(d->kerr_host, d->kerr, 4, cudaMemcpyDeviceToHost, h->st), "error word");
+  ck(cudaStreamSynchronize(h->st), "round");
+  ck(cudaGetLastError(), "round");
+  for (gc_handle *x : {h, d})
+    if (*x->kerr_host) {
+      const int code = *x->kerr_host;
+      *x->kerr_host = 0;
+      ck(cudaMemset(x->kerr, 0, 16), "error word");
+      h->marks.clear();
+      h->ev_used = 0;
+      fail(GC_E_DEVICE, "a kernel's wait ran out of time (code %d); the round's results are invalid", code);
+    }
+  const int n = h->spec_out_host[K + 1];
+  if (n < 1 || n > K + 1) fail(GC_E_DEVICE, "speculative round: %d tokens accepted", n);
+  std::memcpy(O.tokens, h->spec_out_host, static_cast<size_t>(n) * 4);
+  O.counts[0] = static_cast<uint32_t>(n);
+  o->n_rows = static_cast<uint32_t>(n);
+  // rows pos + 1 .. pos + n - 1 hold the accepted drafts in both caches (the drafter's only up to pos + K - 1)
+  h->hist.insert(h->hist.end(), h->spec_out_host, h->spec_out_host + n - 1);
+  h->draft_rows = pos + std::min(n, K);
+  collect_stats(h, f0, f1);
+  return GC_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1377,6 +1631,10 @@ GC_API int gc_step(gc_handle *h, const gc_step_in *in, gc_step_out *o) {
   try {
     if (!in || !o || in->size < offsetof(gc_step_in, n_work) + 4 || o->size < offsetof(gc_step_out, counts) + 8)
       fail(GC_E_ARG, "gc_step: null argument or struct size");
+    if (h->drafter) {
+      if (!in->n_work || !in->work) fail(GC_E_ARG, "gc_step: no work items");
+      return spec_step(h, in, o);
+    }
     if (!in->n_work || !in->work) fail(GC_E_ARG, "gc_step: no work items");
     if (in->n_work > static_cast<uint32_t>(h->max_seqs))
       fail(GC_E_ARG, "gc_step: %u items, the bucket runs %d sequences", in->n_work, h->max_seqs);
@@ -1479,6 +1737,10 @@ extern "C" {
 
 GC_API int gc_commit(gc_handle *h, uint64_t sid, uint32_t base, const uint32_t *path, uint32_t n) {
   if (!h) return GC_E_ARG;
+  if (h->drafter) {
+    h->err = "gc_commit: a speculative pair keeps its own rounds' rows";
+    return GC_E_UNSUPPORTED;
+  }
   if (!h->ranks.empty()) return on_ranks(h, [&](gc_handle *r) { return gc_commit(r, sid, base, path, n); });
   try {
     Slot *sl = find_slot(h, sid, false);
@@ -1513,6 +1775,11 @@ GC_API int gc_commit(gc_handle *h, uint64_t sid, uint32_t base, const uint32_t *
 
 GC_API int gc_copy_blocks(gc_handle *h, const uint32_t *src, const uint32_t *dst, uint32_t n) {
   if (!h) return GC_E_ARG;
+  if (h->drafter) {
+    if (!n) return GC_OK;
+    h->err = "gc_copy_blocks: a speculative pair's stream has one page";
+    return GC_E_UNSUPPORTED;
+  }
   if (!h->ranks.empty()) return on_ranks(h, [&](gc_handle *r) { return gc_copy_blocks(r, src, dst, n); });
   try {
     if (n && (!src || !dst)) fail(GC_E_ARG, "gc_copy_blocks: null array");
@@ -1555,6 +1822,10 @@ GC_API int gc_copy_blocks(gc_handle *h, const uint32_t *src, const uint32_t *dst
 
 GC_API int gck_commit_static(gc_handle *h, uint64_t sid, uint32_t base, const uint32_t *path, uint32_t n) {
   if (!h) return GC_E_ARG;
+  if (h->drafter) {
+    h->err = "gck_commit_static: a speculative pair keeps its own rounds' rows";
+    return GC_E_UNSUPPORTED;
+  }
   if (!h->ranks.empty()) return on_ranks(h, [&](gc_handle *r) { return gck_commit_static(r, sid, base, path, n); });
   try {
     Slot *sl = find_slot(h, sid, false);
@@ -1613,6 +1884,10 @@ GC_API int gc_release(gc_handle *h, uint64_t sid) {
   if (!h) return GC_E_ARG;
   Slot *sl = find_slot(h, sid, false);
   if (sl) *sl = Slot{};
+  if (sl && h->drafter) {            // the stream's tokens go with its sequence
+    h->hist.clear();
+    h->draft_rows = 0;
+  }
   for (gc_handle *r : h->ranks) gc_release(r, sid);
   return GC_OK;
 }

@@ -20,7 +20,8 @@ ABI_MAJOR, ABI_MINOR = 1, 2
 OK, E_ARG, E_MANIFEST, E_WEIGHTS, E_DEVICE, E_UNSUPPORTED, E_STATE, E_CAPACITY = 0, -1, -2, -3, -4, -5, -6, -7
 W_GREEDY, W_SPEC, W_FEATS = 1, 2, 4
 S_HOST_LOGITS = 1
-L_PAGED, L_DEVICE_ARGMAX = 1, 2
+L_PAGED, L_DEVICE_ARGMAX, L_SPEC = 1, 2, 4
+OPEN_SPEC, OPEN_NO_CHECK = 1, 2
 KV_DTYPE = {0: "f16", 1: "fp8"}
 P_ = C.POINTER
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libgck.so")
@@ -140,13 +141,20 @@ def arr(ctype, xs):
 class Backend:
     """One gc_open handle: the engine-facing step / commit / copy_blocks / release of gc_c.GcBackend."""
 
-    def __init__(self, pack_dir, weights, buckets=("b200.BI.main",), pool_blocks=0, device=-1, lib=None):
+    def __init__(self, pack_dir, weights, buckets=("b200.BI.main",), pool_blocks=0, device=-1, lib=None,
+                 drafter_weights=None, policy=None):
+        """drafter_weights: a speculative pair (GC_OPEN_SPEC, gc_c.py:142-191): buckets are {target, drafter} and the
+        weight list is the target's files, a NULL, then the drafter's; policy "ar:K" or None for the pack's own."""
         self.L = lib or load()
         self.h = None
         ws = [weights] if isinstance(weights, str) else list(weights)
-        keep = [arr(C.c_char_p, [os.fsencode(w) for w in ws]), arr(C.c_char_p, [b.encode() for b in buckets])]
-        p = OpenParams(C.sizeof(OpenParams), 2, os.fsencode(pack_dir), keep[0], len(ws), device, keep[1], len(buckets),
-                       pool_blocks, None, None, 0)
+        spec = drafter_weights is not None
+        if spec:
+            ws += [None] + ([drafter_weights] if isinstance(drafter_weights, str) else list(drafter_weights))
+        keep = [arr(C.c_char_p, [None if w is None else os.fsencode(w) for w in ws]),
+                arr(C.c_char_p, [b.encode() for b in buckets])]
+        p = OpenParams(C.sizeof(OpenParams), OPEN_NO_CHECK | (OPEN_SPEC if spec else 0), os.fsencode(pack_dir), keep[0],
+                       len(ws), device, keep[1], len(buckets), pool_blocks, policy.encode() if policy else None, None, 0)
         h = C.c_void_p()
         rc = self.L.gc_open(C.byref(p), C.byref(h))
         if rc:
@@ -159,6 +167,7 @@ class Backend:
         self.block_size, self.num_blocks = lo.block_size, lo.num_blocks
         self.kv_dtype = KV_DTYPE.get(lo.kv_dtype, "f16")
         self.device_argmax = bool(lo.flags & L_DEVICE_ARGMAX)
+        self.spec_width = lo.spec_width if lo.flags & L_SPEC else 0
 
     def _ck(self, rc):
         if rc < 0:
@@ -199,8 +208,10 @@ class Backend:
         out = StepOut(size=C.sizeof(StepOut))
         counts = (C.c_uint32 * n)()
         if greedy:
-            tok = (C.c_int32 * max(rows, 1))()
-            out.tokens, out.tokens_cap, out.counts = tok, rows, counts
+            # a speculative round returns up to spec_width tokens for its one wanted row
+            cap = sum(max(w.want, self.spec_width if w.spec else 0) for w in work)
+            tok = (C.c_int32 * max(cap, 1))()
+            out.tokens, out.tokens_cap, out.counts = tok, cap, counts
         else:
             lg = logits if logits is not None else np.empty((rows, self.vocab_size), np.float32)
             out.logits, out.logits_cap = lg.ctypes.data, lg.size

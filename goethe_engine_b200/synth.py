@@ -158,27 +158,37 @@ def write_gguf(spec, path):
     return path
 
 
-def pack_dir(d, spec, buckets, weights_file="model.gguf"):
-    """Write d/manifest.json for the given buckets: [{id, ncol, maxctx, kv, act, tune, tp, determinism}] (tune: the
-    library's knobs; tp: the tensor-parallel degree, 1 when absent; act: "a16" (default) or "a8" (per-token int8
+def pack_dir(d, spec, buckets, weights_file="model.gguf", pairs=(), drafter_file=None):
+    """Write d/manifest.json for the given buckets: [{id, ncol, maxctx, kv, act, tune, tp, determinism, role}] (tune:
+    the library's knobs; tp: the tensor-parallel degree, 1 when absent; act: "a16" (default) or "a8" (per-token int8
     activations); determinism: "batch_invariant" (default, contract "BI") or "tolerance" (contract "FAST": the GEMV for
-    steps of a few token rows, pack.py:639))."""
+    steps of a few token rows, pack.py:639); role: "target" (default) or "drafter", whose weights are drafter_file).
+    pairs: speculative pairs (target id, drafter id, K), written as the manifest's spec list with policy
+    {kind: "ar", K} (pack.py:130-141); their targets list "ar" in spec_caps.accept."""
     os.makedirs(d, exist_ok=True)
     bs = []
+    targets = {t for t, _, _ in pairs}
     for b in buckets:
         det = b.get("determinism", "batch_invariant")
-        bs.append(dict(id=b["id"], role="target", variant="v", sku="b200", contract="BI" if det != "tolerance" else "FAST",
-                       ncol=b.get("ncol", 64), batch=b.get("batch", True), maxctx=b.get("maxctx", spec.ctx), weights=0,
+        role = b.get("role", "target")
+        bs.append(dict(id=b["id"], role=role, variant="v" if role == "target" else "dv", sku="b200",
+                       contract="BI" if det != "tolerance" else "FAST",
+                       ncol=b.get("ncol", 64), batch=b.get("batch", True), maxctx=b.get("maxctx", spec.ctx),
+                       weights=0 if role == "target" else 1,
                        files={}, lib="libgck.so", requires=dict(arch="sm_100a", cc="10.0", sms=148, name="NVIDIA B200"),
                        determinism=det, act=b.get("act", "a16"), kv=b.get("kv", "f16"),
                        spec_caps=dict(verify=["linear", "tree"], tree_mask=True, verify_widths=[], taps=[],
-                                      recurrent_commit=[], accept=[], drafter_roles=[]),
+                                      recurrent_commit=[], accept=["ar"] if b["id"] in targets else [],
+                                      drafter_roles=["ar"] if b["id"] in targets else []),
                        tune=dict(b.get("tune", {}))))
         if b.get("tp", 1) > 1:
             bs[-1]["tp"] = b["tp"]   # tensor-parallel degree: devices device .. device + tp - 1
+    files = [dict(file=weights_file)] + ([dict(file=drafter_file)] if drafter_file else [])
     m = dict(schema="gc-pack", abi="3.0.0", arch="sm_100a", cuda="12.9", runtime=dict(kind="gc-c", version=1),
-             contracts=sorted({x["contract"] for x in bs}), buckets=bs, model=dict(name=spec.name, weights=[dict(file=weights_file)]),
+             contracts=sorted({x["contract"] for x in bs}), buckets=bs, model=dict(name=spec.name, weights=files),
              synth=asdict(spec))
+    if pairs:
+        m["spec"] = [dict(target=t, drafter=dr, policy=dict(kind="ar", K=str(k))) for t, dr, k in pairs]
     with open(os.path.join(d, "manifest.json"), "w") as f:
         json.dump(m, f, indent=1, sort_keys=True)
     return d

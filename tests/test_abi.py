@@ -63,8 +63,11 @@ def test_open_errors_are_codes(lib, tiny, tmp_path):
     assert rc == gck.E_MANIFEST and "nope" in msg
     rc, h, msg = _open(lib, pack, [str(tmp_path / "missing.gguf")])
     assert rc == gck.E_WEIGHTS
+    # a speculative pair: two buckets {target, drafter}; a pair the manifest gives no ar:K policy is not run
     rc, h, msg = _open(lib, pack, ws, flags=3)
-    assert rc == gck.E_UNSUPPORTED
+    assert rc == gck.E_ARG and "two buckets" in msg
+    rc, h, msg = _open(lib, pack, ws, flags=3, buckets=("b200.BI.main", "b200.BI.main"))
+    assert rc == gck.E_UNSUPPORTED and "ar:K" in msg
     assert lib.gc_open(None, C.byref(C.c_void_p())) == gck.E_ARG
     bad = tmp_path / "bad.gguf"
     bad.write_bytes(b"not a gguf")
