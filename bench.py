@@ -208,7 +208,8 @@ class Stats:
 
         class S(C.Structure):
             _fields_ = [("size", C.c_uint32), ("steps", C.c_uint32), ("launches", C.c_uint64),
-                        ("forward_ms", C.c_double), ("class_ms", C.c_double * 16), ("class_launches", C.c_uint64 * 16)]
+                        ("forward_ms", C.c_double), ("class_ms", C.c_double * 16), ("class_launches", C.c_uint64 * 16),
+                        ("h2d_bytes", C.c_uint64), ("graph_steps", C.c_uint32), ("graph_captures", C.c_uint32)]
         self.S, self.be, self.C = S, be, C
         be.L.gck_stats_enable.argtypes = [C.c_void_p, C.c_uint32]
         be.L.gck_stats_read.argtypes = [C.c_void_p, C.c_void_p]
@@ -311,8 +312,10 @@ def run_mine(args, rank, world, barrier, maxreduce):
                    "batch": B, "context_sum": int(np.sum(ctx)), "block_size": be.block_size, "layers": SPEC8B["layers"],
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (13 GB per step), no flush"},
-        "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": int(sum(len(t) for t in tables) * 4 + B * 4 * 3 + B * 48),
-                "d2h_bytes_per_step": B * 4, "path": "gc_step through the C ABI (ctypes), host buffers"},
+        "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": int(st.h2d_bytes // max(1, st.steps)),
+                "d2h_bytes_per_step": B * 4 + 4, "path": "gc_step through the C ABI (ctypes), host buffers",
+                "h2d_source": "the library's own count of its plan and block-table patch uploads (gck_stats.h2d_bytes)",
+                "captured_steps": f"{st.graph_steps} of {st.steps} timed steps replayed a captured CUDA graph"},
         "roofline": gemm,
         "roofline_attention": {
             "bound": "hbm", "kernel": "attn_kernel (paged fp8 KV attention), one launch per layer",
@@ -620,7 +623,8 @@ def stats_api(be):
 
     class Stats(C.Structure):
         _fields_ = [("size", C.c_uint32), ("steps", C.c_uint32), ("launches", C.c_uint64), ("forward_ms", C.c_double),
-                    ("class_ms", C.c_double * 16), ("class_launches", C.c_uint64 * 16)]
+                    ("class_ms", C.c_double * 16), ("class_launches", C.c_uint64 * 16), ("h2d_bytes", C.c_uint64),
+                    ("graph_steps", C.c_uint32), ("graph_captures", C.c_uint32)]
     be.L.gck_stats_enable.argtypes = [C.c_void_p, C.c_uint32]
     be.L.gck_stats_read.argtypes = [C.c_void_p, C.c_void_p]
 
@@ -628,7 +632,7 @@ def stats_api(be):
         st = Stats(size=C.sizeof(Stats))
         be.L.gck_stats_read(be.h, C.byref(st))
         return st
-    return lambda prof=False: be.L.gck_stats_enable(be.h, 0xFFFF if prof else 1 << 4), read
+    return lambda prof=False: be.L.gck_stats_enable(be.h, 0xFFFF if prof else 0), read
 
 
 CLASS_NAMES = ["embed", "rmsnorm", "gemm_qkv", "rope_kv", "attention", "attn_combine", "gemm_o", "gemm_gateup",
@@ -693,8 +697,10 @@ def run_c2(args):
         "config": {"workload": "C2: Llama-3-8B shape, Q8_0 weights, a16, f16 paged KV, one sequence at context 2048",
                    "bucket": "single-stream, determinism tolerance (GEMV decode)",
                    "batch": 1, "context": ctx, "l2": "inputs larger than L2, no flush"},
-        "e2e": {"value": round(args.steps / wall, 2), "unit": "tok/s", "h2d_bytes_per_step": int(per_seq * 4 + 64),
-                "d2h_bytes_per_step": 4, "path": "gc_step through the C ABI (ctypes), host buffers"},
+        "e2e": {"value": round(args.steps / wall, 2), "unit": "tok/s", "h2d_bytes_per_step": int(st.h2d_bytes // max(1, st.steps)),
+                "d2h_bytes_per_step": 8, "path": "gc_step through the C ABI (ctypes), host buffers",
+                "h2d_source": "the library's own count of its plan and block-table patch uploads (gck_stats.h2d_bytes)",
+                "captured_steps": f"{st.graph_steps} of {st.steps} timed steps replayed a captured CUDA graph"},
         "step_roofline": {"algorithmic_bytes": int(wbytes + kv), "achieved_gbs": round(gbs, 1),
                           "frac_of_measured": round(gbs / hbm, 4), "frac_of_8tbs": round(gbs / 8000, 4)},
         "gpu_launches": int(st.launches), "clocks": clk.summary()}), flush=True)

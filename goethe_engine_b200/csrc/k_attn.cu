@@ -115,6 +115,7 @@ __global__ void __launch_bounds__(32 * NW, NT > 1 ? 1 : (NW == 1 ? 20 : 2)) attn
   int8_t *sEE = reinterpret_cast<int8_t *>(sm + C::EE_OFF);
 
   const AttnWork w = pv.work[blockIdx.x];
+  if (w.nqg == 0) return;   // an empty entry of a work list padded to a captured step's grid
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   const int g = lane / 4, t = lane % 4;
   const QGroup q0 = pv.qgroups[w.qg0];

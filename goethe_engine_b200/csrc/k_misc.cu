@@ -712,6 +712,16 @@ __global__ void argmax_part_kernel(const float *logits, int V, int *pick) {
   }
 }
 
+__global__ void table_patch_kernel(const uint2 *patches, int n, uint32_t *tables) {
+  dep_wait();
+  dep_launch();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) tables[patches[i].x] = patches[i].y;
+}
+
+void launch_table_patch(const uint2 *patches, int n, uint32_t *tables, cudaStream_t s) {
+  if (n > 0) launch_pdl(table_patch_kernel, std::min((n + 255) / 256, 148), 256, 0, s, patches, n, tables);
+}
+
 __global__ void spec_accept_kernel(const int *chain, const int *target, int K, int *out) {
   dep_wait();
   if (threadIdx.x != 0) return;

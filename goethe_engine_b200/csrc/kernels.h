@@ -117,6 +117,8 @@ void launch_argmax(const float *logits, int R, int V, int *out, int *scratch, cu
 // A speculative round's acceptance: chain[0] is the anchor and chain[1..K] the drafts; target[i] the target's argmax
 // after chain[0..i]. j = the longest prefix of drafts with chain[i + 1] == target[i]; out[0..j] = target[0..j] (the
 // accepted drafts, then the target's own next token) and out[K + 1] = j + 1.
+// The step's block-table patches: tables[p.x] = p.y for each of the n pairs.
+void launch_table_patch(const uint2 *patches, int n, uint32_t *tables, cudaStream_t s);
 void launch_spec_accept(const int *chain, const int *target, int K, int *out, cudaStream_t s);
 // tensor parallelism: a rank's candidates (value bits, global index) of its vocabulary slice, and their merge
 void launch_argmax_pick(const float *logits, int R, int V, int offset, int *pick, cudaStream_t s);

@@ -139,6 +139,17 @@ struct gc_handle {
   size_t plan_cap = 0;
   int *tok_host = nullptr;
   std::vector<Slot> slots;
+  // block tables resident on the device: row i (tab_stride entries) is slot i's table, mirrored by slots[i].blocks;
+  // a step uploads only the entries that differ from the mirror (patches)
+  uint32_t *tables = nullptr;
+  int tab_stride = 0;
+  // captured steps (CUDA graphs): a step whose shape (plan sizes, scratch generation) repeats replays its graph; a
+  // shape is captured the second time it is seen. Off under tensor parallelism, statistics and tree items.
+  struct Graph { std::vector<int64_t> key; cudaGraphExec_t exec; uint64_t launches; };
+  bool graphs_on = true;
+  std::vector<Graph> graphs;                 // most recent last
+  std::vector<std::vector<int64_t>> seen;   // shapes run once without a graph
+  uint64_t scratch_gen = 0;                  // bumped whenever a scratch buffer a kernel argument points to moves
   std::vector<void *> allocs;
   size_t device_bytes = 0;
   // step statistics (gck_ext.h)
@@ -185,6 +196,7 @@ struct gc_handle {
     if (tok_host) cudaFreeHost(tok_host);
     if (kerr_host) cudaFreeHost(kerr_host);
     if (spec_out_host) cudaFreeHost(spec_out_host);
+    for (auto &g : graphs) cudaGraphExecDestroy(g.exec);
     for (auto e : ev_pool) cudaEventDestroy(e);
     if (st) cudaStreamDestroy(st);
   }
@@ -718,6 +730,10 @@ void open_device(gc_handle *h, int dev, const std::vector<std::unique_ptr<GgufFi
     ck(cudaMemset(h->exps, 0, h->exps_layer * h->L), "KV page exponents");
   }
   h->slots.resize(h->max_seqs);
+  h->tab_stride = (h->max_ctx + kBlock - 1) / kBlock;
+  h->tables = static_cast<uint32_t *>(h->dalloc(static_cast<size_t>(h->max_seqs) * h->tab_stride * 4, "block tables"));
+  ck(cudaMemset(h->tables, 0, static_cast<size_t>(h->max_seqs) * h->tab_stride * 4), "block tables");
+  if (const char *e = std::getenv("GCK_GRAPH")) h->graphs_on = std::atoi(e) != 0;
   ck(cudaStreamSynchronize(h->st), "open");
 }
 
@@ -1016,7 +1032,7 @@ struct HostPlan {
   std::vector<Item> items;
   std::vector<QGroup> qgroups;
   std::vector<AttnWork> work;
-  std::vector<unsigned> blocks;
+  std::vector<uint2> patches;      // (entry of the device block tables, block id): where a table differs from its mirror
   int n_parts = 0, nw = 1, tree_cta = 0, split = kSplit;
 };
 
@@ -1029,6 +1045,20 @@ struct WorkIn {
   uint32_t nblocks, want;
 };
 
+Slot *find_slot(gc_handle *h, uint64_t sid, bool make) {
+  Slot *fr = nullptr;
+  for (auto &s : h->slots) {
+    if (s.used && s.sid == sid) return &s;
+    if (!s.used && !fr) fr = &s;
+  }
+  if (make && fr) {
+    fr->used = true;
+    fr->sid = sid;
+    return fr;
+  }
+  return nullptr;
+}
+
 void build_plan(gc_handle *h, const std::vector<WorkIn> &ws, HostPlan &pl) {
   const int G = h->H / h->KVH, QG = h->qg_tokens;
   int T = 0;
@@ -1038,11 +1068,19 @@ void build_plan(gc_handle *h, const std::vector<WorkIn> &ws, HostPlan &pl) {
     it.pos = static_cast<int>(w.pos);
     it.ntok = static_cast<int>(w.n);
     it.tok0 = T;
-    it.blk_off = static_cast<int>(pl.blocks.size());
-    it.nblk = static_cast<int>(w.nblocks);
+    // the item's table: its slot's row of the device tables, patched where it differs from the slot's mirror
+    Slot *sl = find_slot(h, w.sid, true);
+    if (!sl) fail(GC_E_STATE, "no free sequence slot (%d in use)", h->max_seqs);
+    const int slot = static_cast<int>(sl - h->slots.data());
+    const uint32_t nb = std::min<uint32_t>(w.nblocks, static_cast<uint32_t>(h->tab_stride));
+    it.blk_off = slot * h->tab_stride;
+    it.nblk = static_cast<int>(nb);
+    for (uint32_t b = 0; b < nb; b++)
+      if (b >= sl->blocks.size() || sl->blocks[b] != w.blocks[b])
+        pl.patches.push_back(make_uint2(static_cast<unsigned>(it.blk_off) + b, w.blocks[b]));
+    sl->blocks.assign(w.blocks, w.blocks + w.nblocks);
     it.tree = w.parents != nullptr;
     it.path_off = static_cast<int>(pl.paths.size());
-    pl.blocks.insert(pl.blocks.end(), w.blocks, w.blocks + w.nblocks);
     std::vector<int> depth(w.n), poff(w.n), plen(w.n);
     for (uint32_t j = 0; j < w.n; j++) {
       int par = w.parents ? w.parents[j] : static_cast<int>(j) - 1;
@@ -1141,9 +1179,10 @@ void build_plan(gc_handle *h, const std::vector<WorkIn> &ws, HostPlan &pl) {
 
 // A plan's parts in a buffer, each 256-byte aligned: their offsets, and the total bytes.
 size_t plan_layout(const HostPlan &pl, std::vector<size_t> &off) {
+  // the table patches last: every part a kernel argument points to has an offset fixed by the step's shape alone
   const size_t sizes[10] = {vbytes(pl.tok_id), vbytes(pl.rope_pos), vbytes(pl.kv_row), vbytes(pl.first_tok),
-                            vbytes(pl.items), vbytes(pl.qgroups), vbytes(pl.work), vbytes(pl.blocks),
-                            vbytes(pl.paths), vbytes(pl.want_tok)};
+                            vbytes(pl.items), vbytes(pl.qgroups), vbytes(pl.work), vbytes(pl.paths),
+                            vbytes(pl.want_tok), vbytes(pl.patches)};
   size_t total = 0;
   off.clear();
   for (size_t n : sizes) {
@@ -1159,8 +1198,8 @@ void plan_copy(const HostPlan &pl, uint8_t *host, const std::vector<size_t> &off
       {pl.tok_id.data(), vbytes(pl.tok_id)},   {pl.rope_pos.data(), vbytes(pl.rope_pos)},
       {pl.kv_row.data(), vbytes(pl.kv_row)},   {pl.first_tok.data(), vbytes(pl.first_tok)},
       {pl.items.data(), vbytes(pl.items)},     {pl.qgroups.data(), vbytes(pl.qgroups)},
-      {pl.work.data(), vbytes(pl.work)},       {pl.blocks.data(), vbytes(pl.blocks)},
-      {pl.paths.data(), vbytes(pl.paths)},     {pl.want_tok.data(), vbytes(pl.want_tok)}};
+      {pl.work.data(), vbytes(pl.work)},       {pl.paths.data(), vbytes(pl.paths)},
+      {pl.want_tok.data(), vbytes(pl.want_tok)}, {pl.patches.data(), vbytes(pl.patches)}};
   for (int i = 0; i < 10; i++)
     if (parts[i].second) std::memcpy(host + off[i], parts[i].first, parts[i].second);
 }
@@ -1175,9 +1214,9 @@ PlanView plan_view(gc_handle *h, const HostPlan &pl, uint8_t *b, const std::vect
   pv.items = reinterpret_cast<const Item *>(b + off[4]);
   pv.qgroups = reinterpret_cast<const QGroup *>(b + off[5]);
   pv.work = reinterpret_cast<const AttnWork *>(b + off[6]);
-  pv.blocks = reinterpret_cast<const unsigned *>(b + off[7]);
-  pv.paths = reinterpret_cast<const int *>(b + off[8]);
-  pv.want_tok = reinterpret_cast<const int *>(b + off[9]);
+  pv.blocks = h->tables;
+  pv.paths = reinterpret_cast<const int *>(b + off[7]);
+  pv.want_tok = reinterpret_cast<const int *>(b + off[8]);
   pv.T = static_cast<int>(pl.tok_id.size());
   pv.n_items = static_cast<int>(pl.items.size());
   pv.n_qg = static_cast<int>(pl.qgroups.size());
@@ -1208,11 +1247,17 @@ std::vector<PlanView> upload_plans(gc_handle *h, const std::vector<const HostPla
     size_t cap = std::max<size_t>(total * 2, 1 << 20);
     if (h->plan_dev) h->dfree(h->plan_dev, h->plan_cap);
     h->plan_dev = static_cast<uint8_t *>(h->dalloc(cap, "plan"));
+    h->scratch_gen++;
     ck(cudaMallocHost(&h->plan_host, cap), "pinned plan");
     h->plan_cap = cap;
   }
   for (size_t i = 0; i < pls.size(); i++) plan_copy(*pls[i], h->plan_host + base[i], offs[i]);
   ck(cudaMemcpyAsync(h->plan_dev, h->plan_host, total, cudaMemcpyHostToDevice, h->st), "plan upload");
+  if (h->stats_on) h->stats.h2d_bytes += total;
+  for (size_t i = 0; i < pls.size(); i++)
+    if (!pls[i]->patches.empty())
+      launch_table_patch(reinterpret_cast<const uint2 *>(h->plan_dev + base[i] + offs[i][9]),
+                         static_cast<int>(pls[i]->patches.size()), h->tables, h->st);
   std::vector<PlanView> out;
   for (size_t i = 0; i < pls.size(); i++) out.push_back(plan_view(h, *pls[i], h->plan_dev + base[i], offs[i]));
   return out;
@@ -1220,13 +1265,19 @@ std::vector<PlanView> upload_plans(gc_handle *h, const std::vector<const HostPla
 
 PlanView upload_plan(gc_handle *h, HostPlan &pl) { return upload_plans(h, {&pl})[0]; }
 
-void forward(gc_handle *h, const PlanView &pv, int nw) {
+// a GEMM of `rows` token rows: the GEMV (tolerance buckets, a few rows, quantized weights) or the tensor-core GEMM;
+// its split-K slices (partials for the next kernel) either way
+bool gemv_rows(const gc_handle *h, const QWeight &w, int rows) {
+  return rows > 0 && rows <= h->gemv_max_t && w.type != kF16;
+}
+
+// Split-K and attention scratch for a step's sizes (grown, never shrunk): before the step's launches, and outside any
+// stream capture. Bumps scratch_gen when a buffer moves.
+void forward_scratch(gc_handle *h, const PlanView &pv) {
   const int T = pv.T;
   cudaStream_t s = h->st;
-  // split-K and attention scratch for this step's sizes
-  // a GEMM of `rows` token rows: the GEMV (tolerance buckets, a few rows, quantized weights) or the tensor-core GEMM;
-  // its split-K slices (partials for the next kernel) either way
-  auto use_gemv = [&](const QWeight &w, int rows) { return rows > 0 && rows <= h->gemv_max_t && w.type != kF16; };
+  float *part0 = h->part;
+  auto use_gemv = [&](const QWeight &w, int rows) { return gemv_rows(h, w, rows); };
   auto slices = [&](const QWeight &w, int rows) { return use_gemv(w, rows) ? w.gslices : w.splits; };
   size_t need = 0;
   for (auto &ly : h->layers)
@@ -1243,6 +1294,7 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
     h->attn_o = static_cast<float *>(h->dalloc(cap * 16 * h->dh * 4, "attention partials"));
     h->attn_ml = static_cast<float2 *>(h->dalloc(cap * 16 * 8, "attention partials"));
     h->attn_parts_cap = cap;
+    h->scratch_gen++;
   }
   // per (query group, kv head): splits finished so far; zero between launches (the merging split resets it)
   const size_t nsem = static_cast<size_t>(pv.n_qg) * h->KVH;
@@ -1253,7 +1305,17 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
     h->attn_sem = static_cast<int *>(h->dalloc(cap * 4, "attention split counters"));
     ck(cudaMemsetAsync(h->attn_sem, 0, cap * 4, s), "attention split counters");
     h->attn_sem_cap = cap;
+    h->scratch_gen++;
   }
+  if (h->part != part0) h->scratch_gen++;
+}
+
+// A step's launches on the handle's stream (no allocation, no synchronization: a stream capture may record them)
+void forward_launch(gc_handle *h, const PlanView &pv, int nw) {
+  const int T = pv.T;
+  cudaStream_t s = h->st;
+  auto use_gemv = [&](const QWeight &w, int rows) { return gemv_rows(h, w, rows); };
+  auto slices = [&](const QWeight &w, int rows) { return use_gemv(w, rows) ? w.gslices : w.splits; };
   h->step_launches = 0;
   // run(cls, kernels, fn): launch fn on the stream, bracketed by events when the class is being timed
   auto run = [&](int cls, int nk, auto fn) {
@@ -1392,6 +1454,11 @@ void forward(gc_handle *h, const PlanView &pv, int nw) {
   }
 }
 
+void forward(gc_handle *h, const PlanView &pv, int nw) {
+  forward_scratch(h, pv);
+  forward_launch(h, pv, nw);
+}
+
 // after the step's synchronize: fold the recorded events into the statistics
 void collect_stats(gc_handle *h, cudaEvent_t f0, cudaEvent_t f1) {
   if (!h->stats_on) return;
@@ -1408,34 +1475,79 @@ void collect_stats(gc_handle *h, cudaEvent_t f0, cudaEvent_t f1) {
   h->stats.launches += h->step_launches;
 }
 
-Slot *find_slot(gc_handle *h, uint64_t sid, bool make) {
-  Slot *fr = nullptr;
-  for (auto &s : h->slots) {
-    if (s.used && s.sid == sid) return &s;
-    if (!s.used && !fr) fr = &s;
-  }
-  if (make && fr) {
-    fr->used = true;
-    fr->sid = sid;
-    return fr;
-  }
-  return nullptr;
-}
 
 // The device part of a step on one handle (or one tensor-parallel rank): slots, plan, forward, argmax, outputs. o (may be
 // null for ranks other than 0) receives logits_dev; O holds the caller's host buffers.
+// A step's launches (and its device argmax over R rows, R > 0) from a captured graph: replayed when the step's shape has
+// a graph, captured when the shape is seen the second time, else left to the caller (false). Every kernel argument of
+// a step is a function of the key: plan sizes (the plan's part offsets and the launches' grids), the plan buffer and
+// the scratch generation (the buffers the arguments point to).
+bool run_graph(gc_handle *h, const PlanView &pv, int nw, int R) {
+  const std::vector<int64_t> key = {pv.T, pv.n_items, pv.n_qg, pv.n_work, pv.R, pv.split, pv.max_rows, pv.tree_cta, nw,
+                                    R, static_cast<int64_t>(reinterpret_cast<uintptr_t>(h->plan_dev)),
+                                    static_cast<int64_t>(h->scratch_gen)};
+  for (size_t i = 0; i < h->graphs.size(); i++)
+    if (h->graphs[i].key == key) {
+      ck(cudaGraphLaunch(h->graphs[i].exec, h->st), "graph launch");
+      h->step_launches = h->graphs[i].launches;
+      if (h->stats_on) h->stats.graph_steps++;
+      std::rotate(h->graphs.begin() + i, h->graphs.begin() + i + 1, h->graphs.end());
+      return true;
+    }
+  if (std::find(h->seen.begin(), h->seen.end(), key) == h->seen.end()) {
+    h->seen.push_back(key);
+    if (h->seen.size() > 32) h->seen.erase(h->seen.begin());
+    return false;
+  }
+  cudaGraph_t g = nullptr;
+  uint64_t launches = 0;
+  ck(cudaStreamBeginCapture(h->st, cudaStreamCaptureModeRelaxed), "graph capture");
+  try {
+    forward_launch(h, pv, nw);
+    launches = h->step_launches;
+    if (R) {
+      launch_argmax(h->logits, R, h->vocab_rows, h->argmax, h->arg_scratch, h->st);
+      launches += 2;
+    }
+  } catch (...) {
+    cudaStreamEndCapture(h->st, &g);
+    if (g) cudaGraphDestroy(g);
+    cudaGetLastError();
+    throw;
+  }
+  cudaError_t e = cudaStreamEndCapture(h->st, &g);
+  cudaGraphExec_t ex = nullptr;
+  if (e == cudaSuccess) e = cudaGraphInstantiate(&ex, g, 0);
+  if (g) cudaGraphDestroy(g);
+  if (e != cudaSuccess) fail(GC_E_DEVICE, "step capture: %s", cudaGetErrorString(e));
+  if (h->graphs.size() >= 8) {
+    cudaGraphExecDestroy(h->graphs.front().exec);
+    h->graphs.erase(h->graphs.begin());
+  }
+  h->graphs.push_back({key, ex, launches});
+  ck(cudaGraphLaunch(ex, h->st), "graph launch");
+  h->step_launches = launches;
+  if (h->stats_on) h->stats.graph_captures++;
+  return true;
+}
+
 void step_device(gc_handle *h, const std::vector<WorkIn> &ws, bool greedy, uint64_t R, uint32_t flags,
                  const gc_step_out &O, gc_step_out *o) {
   for (auto &w : ws) {
     Slot *sl = find_slot(h, w.sid, true);
     if (!sl) fail(GC_E_STATE, "no free sequence slot (%d in use)", h->max_seqs);
-    sl->blocks.assign(w.blocks, w.blocks + w.nblocks);
     sl->last_pos = w.pos;
     sl->last_n = w.n;
   }
   ck(cudaSetDevice(h->dev), "cudaSetDevice");
   HostPlan pl;
   build_plan(h, ws, pl);
+  // a step that may run as a graph (not under per-class statistics, whose events bracket single launches): its
+  // attention work list padded (with empty entries) to a multiple of 512, so that the attention grid, part of the
+  // step's shape, changes only every few hundred splits
+  const bool graphable = h->graphs_on && h->tp == 1 && !(h->stats_on && h->stats_mask) && pl.paths.empty() &&
+                         !pl.work.empty();
+  if (graphable) pl.work.resize((pl.work.size() + 511) / 512 * 512, AttnWork{0, 0, 0, 0});
   PlanView pv = upload_plan(h, pl);
   cudaEvent_t f0 = nullptr, f1 = nullptr;
   if (h->stats_on) {
@@ -1443,8 +1555,12 @@ void step_device(gc_handle *h, const std::vector<WorkIn> &ws, bool greedy, uint6
     f1 = h->event();
     cudaEventRecord(f0, h->st);
   }
-  forward(h, pv, pl.nw);
-  if (greedy && R) {
+  forward_scratch(h, pv);
+  if (graphable && run_graph(h, pv, pl.nw, greedy ? static_cast<int>(R) : 0)) {
+    // launched
+  } else {
+    forward_launch(h, pv, pl.nw);
+    if (greedy && R) {
     bool rec = h->stats_on && ((h->stats_mask >> GCK_K_ARGMAX) & 1u);
     cudaEvent_t a = rec ? h->event() : nullptr, b = rec ? h->event() : nullptr;
     if (rec) cudaEventRecord(a, h->st);
@@ -1464,6 +1580,7 @@ void step_device(gc_handle *h, const std::vector<WorkIn> &ws, bool greedy, uint6
       h->marks.push_back({GCK_K_ARGMAX, a, b});
     }
     h->step_launches += 1;
+    }
   }
   if (f1) cudaEventRecord(f1, h->st);
   ck(cudaMemcpyAsync(h->kerr_host, h->kerr, 4, cudaMemcpyDeviceToHost, h->st), "error word");

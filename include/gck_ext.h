@@ -36,6 +36,9 @@ typedef struct gck_stats {
   double forward_ms;                      /* device time from a step's first kernel to its last, summed over steps */
   double class_ms[GCK_K_CLASSES];         /* device time of the masked classes' launches, summed */
   uint64_t class_launches[GCK_K_CLASSES]; /* launches of each masked class */
+  uint64_t h2d_bytes;                     /* host-to-device bytes those steps copied (plans, block-table patches) */
+  uint32_t graph_steps;                   /* steps replayed from a captured CUDA graph (class_mask 0 only) */
+  uint32_t graph_captures;                /* steps captured into a new graph */
 } gck_stats;
 
 /* Starts (and resets) step statistics on h; class_mask picks the classes whose launches are each bracketed by a
