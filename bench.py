@@ -37,8 +37,10 @@ METRIC = "decode tok/s (8B Q4_K, batch 64, fp8 KV)"
 # DRAM bytes (read + write) per launch from single-kernel ncu captures of this workload (the 8B shape with 2 of its 32
 # layers: a layer's launches have the full-size weights and KV); each names the library build it was captured on, and
 # is reported beside the live timing, never in place of it
-ATTN_TRAFFIC = dict(bytes=288_064_256, build="c152e19", kernel="attn_kernel<128, fp8, 1 warp, 1 row tile>")
-GEMM_TRAFFIC = None     # per GEMM launch of a 32-layer step: set from a capture of the current GEMM build
+ATTN_TRAFFIC = dict(bytes=287_385_088, build="13d6345", kernel="attn_kernel<128, fp8, 1 warp, 1 row tile>")
+# one layer's four GEMM launches (q/k/v, o, gate/up, down): 127.1 MB of DRAM traffic against 122.7 MB of Q4_K weights
+# (1.036); "bytes" is their mean per launch, "gateup" the gate/up launch alone (the head launch was not captured)
+GEMM_TRAFFIC = dict(bytes=31_778_560, gateup=67_404_032, build="13d6345", ratio_to_weight_bytes=1.036)
 
 
 def contexts():
@@ -363,6 +365,8 @@ def gemm_roofline(sg, steps, hbm, peak_source):
            "algorithmic_bytes_per_step": int(wb),
            "traffic": GEMM_TRAFFIC["bytes"] if GEMM_TRAFFIC else None,
            "traffic_build": GEMM_TRAFFIC["build"] if GEMM_TRAFFIC else None,
+           "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean per launch over one layer's four GEMM "
+                             "launches (--layers 2 case, full-size weights); 1.036 x their weight bytes",
            "gateup": {"launch_ms": round(gu_ms, 4), "algorithmic_bytes_per_launch": int(gu_bytes),
                       "achieved": round(gu_bytes / (gu_ms / 1e3) / 1e9, 1),
                       "frac": round(gu_bytes / (gu_ms / 1e3) / 1e9 / hbm, 4),
