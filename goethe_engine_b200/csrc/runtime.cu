@@ -1650,6 +1650,9 @@ int spec_step(gc_handle *h, const gc_step_in *in, gc_step_out *o) {
   if (fresh) {
     h->hist.clear();
     h->draft_rows = 0;
+    // a pair runs one stream: a drafter slot an earlier sequence still holds (not released) is the new stream's
+    for (Slot &s : h->drafter->slots)
+      if (s.used && s.sid != W.sid) s = Slot{};
   }
   if (W.pos > h->hist.size())
     fail(GC_E_STATE, "position %u not contiguous: the stream holds %zu tokens", W.pos, h->hist.size());
@@ -2001,9 +2004,12 @@ GC_API int gc_release(gc_handle *h, uint64_t sid) {
   if (!h) return GC_E_ARG;
   Slot *sl = find_slot(h, sid, false);
   if (sl) *sl = Slot{};
-  if (sl && h->drafter) {            // the stream's tokens go with its sequence
-    h->hist.clear();
-    h->draft_rows = 0;
+  if (h->drafter) {
+    gc_release(h->drafter, sid);     // the drafter's slot for the sequence
+    if (sl) {                        // the stream's tokens go with its sequence
+      h->hist.clear();
+      h->draft_rows = 0;
+    }
   }
   for (gc_handle *r : h->ranks) gc_release(r, sid);
   return GC_OK;

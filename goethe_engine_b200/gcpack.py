@@ -25,10 +25,12 @@ LIB_NAME = "libgck.so"
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), LIB_NAME)
 
 
-def manifest(pack_dir, lib_sha256, structure, weights=None, commit="0" * 40):
+def manifest(pack_dir, lib_sha256, structure, weights=None, commit="0" * 40, drafter_structure=None):
     """The engine-facing manifest (a dict) of a pack directory's manifest.json: every bucket runs the library whose
-    sha256 is lib_sha256; variant "v" has the given structure record; weights: [{file, bytes, sha256}] records of the
-    model's files (default: the directory's list, names only)."""
+    sha256 is lib_sha256; variant "v" (the target buckets) has the given structure record and, for a pack with
+    drafter buckets (a speculative pair, pack.py:130-141), variant "dv" the drafter weights' structure; weights:
+    [{file, bytes, sha256}] records of the model's files, the target's first and the drafter's second (default: the
+    directory's list, names only)."""
     with open(os.path.join(pack_dir, "manifest.json")) as f:
         m = json.load(f)
     skus = sorted({b["sku"] for b in m["buckets"]})
@@ -37,12 +39,16 @@ def manifest(pack_dir, lib_sha256, structure, weights=None, commit="0" * 40):
     for b in m["buckets"]:
         b["files"] = {LIB_NAME: lib_sha256}
         b["lib"] = LIB_NAME
-        b["variant"] = "v"
+        b["variant"] = "v" if b.get("role", "target") == "target" else "dv"
         b.setdefault("variants", [])
         b.setdefault("variant_of", None)
     if weights is not None:
         m["model"]["weights"] = weights
     m["variants"] = {"v": dict(structure=structure, weights=[0])}
+    if any(b["variant"] == "dv" for b in m["buckets"]):
+        if drafter_structure is None:
+            raise ValueError("a pack with drafter buckets needs the drafter weights' structure")
+        m["variants"]["dv"] = dict(structure=drafter_structure, weights=[1])
     m.pop("synth", None)
     return m
 
@@ -64,11 +70,11 @@ def write(path, m, blobs):
     return path
 
 
-def build(out, pack_dir, structure, lib=LIB_PATH, weights=None):
+def build(out, pack_dir, structure, lib=LIB_PATH, weights=None, drafter_structure=None):
     """out: a .gcpack of the library at lib (default: this package's build) under the manifest of pack_dir; returns
     out. Sign it with the engine's pack.sign_pack before GcBackend opens it (or use the engine's development switch
     for unsigned packs)."""
     with open(lib, "rb") as f:
         data = f.read()
     h = hashlib.sha256(data).hexdigest()
-    return write(out, manifest(pack_dir, h, structure, weights), {h: data})
+    return write(out, manifest(pack_dir, h, structure, weights, drafter_structure=drafter_structure), {h: data})

@@ -44,14 +44,16 @@ class Key:
             self.kid = sign.key_id(f.read())
 
 
-def signed_pack(d, pack_dir, weights, key):
-    """d/model.gcpack: libgck.so under pack_dir's manifest, the variant's structure from the engine's own
-    structure.describe over the weights, signed with key by the engine's pack.sign_pack. Returns the pack path."""
+def signed_pack(d, pack_dir, weights, key, drafter_weights=None):
+    """d/model.gcpack: libgck.so under pack_dir's manifest, the variants' structures (the target's and, for a
+    speculative pair, the drafter's) from the engine's own structure.describe over the weights, signed with key by the
+    engine's pack.sign_pack. Returns the pack path."""
     from goethe_engine import pack as P, structure
     from goethe_engine_b200 import gcpack
     out = os.path.join(d, "model.gcpack")
     st = structure.describe(list(weights), ["general.architecture"])
-    ws = [dict(file=os.path.basename(w), bytes=os.path.getsize(w)) for w in weights]
-    gcpack.build(out, pack_dir, st, weights=ws)
+    dst = structure.describe(list(drafter_weights), ["general.architecture"]) if drafter_weights else None
+    ws = [dict(file=os.path.basename(w), bytes=os.path.getsize(w)) for w in list(weights) + list(drafter_weights or [])]
+    gcpack.build(out, pack_dir, st, weights=ws, drafter_structure=dst)
     P.sign_pack(out, key.priv)
     return out

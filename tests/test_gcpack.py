@@ -54,3 +54,33 @@ def test_gc_backend_reaches_gc_open(packed):
     path, ws, key = packed
     with pytest.raises(P.PackError, match=r"gc_open -4: no CUDA device"):
         GcBackend(path, ws, sku="b200", trusted=(key.kid,), B=4)
+
+
+def test_engine_accepts_a_speculative_pair_pack(tmp_path):
+    """A pack with a target and a drafter bucket and a spec entry (pack.py:130-141): the engine's loader validates it,
+    picks variant v for the target weights and dv for the drafter's, names the pair with its ar policy, and a
+    GcBackend with drafter_weights reaches the library's gc_open."""
+    from goethe_engine import pack as P
+    from goethe_engine.gc_c import GcBackend
+    build.build()
+    d = str(tmp_path)
+    shape = dict(vocab=512, d=256, layers=1, heads=4, kv_heads=2, ffn=512)
+    tgt = synth.make(d + "/t", synth.Spec(**shape, wtype="q4_k", seed=5))[1][0]
+    dft = synth.make(d + "/d", synth.Spec(**dict(shape, layers=2), wtype="q8_0", seed=6))[1][0]
+    pack_dir = synth.pack_dir(d + "/p", synth.Spec(**shape, wtype="q4_k", seed=5),
+                              [dict(id="b200.BI.t", ncol=8, maxctx=256),
+                               dict(id="b200.BI.d", ncol=8, maxctx=256, role="drafter")],
+                              weights_file=os.path.basename(tgt), pairs=[("b200.BI.t", "b200.BI.d", 3)],
+                              drafter_file=os.path.basename(dft))
+    key = Key(d)
+    path = signed_pack(d, pack_dir, [tgt], key, drafter_weights=[dft])
+    st = P.stage(path, trusted=(key.kid,))
+    try:
+        m = st.manifest
+        assert P.pick_variant(m, [tgt]) == "v" and P.pick_variant(m, [dft], "drafter") == "dv"
+        t, dr, pol = P.spec_pair(P.for_variant(m, "v", "dv"), sku="b200")
+        assert (t["id"], dr["id"], pol) == ("b200.BI.t", "b200.BI.d", {"kind": "ar", "K": "3"})
+    finally:
+        st.close()
+    with pytest.raises(P.PackError, match="gc_open -4"):
+        GcBackend(path, [tgt], drafter_weights=[dft], sku="b200", trusted=(key.kid,))

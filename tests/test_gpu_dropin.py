@@ -230,3 +230,39 @@ def test_abi_1_0_struct_sizes_open(pack):
         L.gc_close(h)
     finally:
         st.close()
+
+
+def test_engine_speculative_pair_equals_the_target_alone(tmp_path):
+    """A speculative pair through the engine (SPEC_CAPS "ar", gc.h:56-59,93,117,136): the pack pairs a Q4_K target
+    with a Q8_0 drafter of the same init (policy {kind "ar", K "3"}); GcBackend(..., drafter_weights=...) opens the
+    pair, the engine runs its stream in device rounds (backend.spec_width), and greedy generation equals the target
+    alone token for token, with drafts accepted."""
+    from goethe_engine import Config, Engine, SamplingParams
+    from goethe_engine.gc_c import GcBackend
+    d = str(tmp_path)
+    tgt = synth.make(d + "/t", synth.Spec(**SHAPE, wtype="q4_k", seed=17))[1][0]
+    dft = synth.make(d + "/d", synth.Spec(**SHAPE, wtype="q8_0", seed=17))[1][0]
+    pack_dir = synth.pack_dir(d + "/p", synth.Spec(**SHAPE, wtype="q4_k", seed=17),
+                              [dict(id="b200.BI.t", ncol=8, maxctx=256),
+                               dict(id="b200.BI.d", ncol=8, maxctx=256, role="drafter")],
+                              weights_file=os.path.basename(tgt), pairs=[("b200.BI.t", "b200.BI.d", 3)],
+                              drafter_file=os.path.basename(dft))
+    key = Key(d)
+    path = signed_pack(d, pack_dir, [tgt], key, drafter_weights=[dft])
+    ps = prompts(3, seed=8)
+    plain = GcBackend(path, [tgt], sku="b200", trusted=(key.kid,))
+    try:
+        want = gen(plain, ps, 24)
+    finally:
+        plain.close()
+    pair = GcBackend(path, [tgt], drafter_weights=[dft], sku="b200", trusted=(key.kid,))
+    try:
+        assert pair.spec_width == 4
+        eng = Engine(pair, Config(max_model_len=200))
+        got = [o[0] for o in eng.generate([(p, SamplingParams(max_tokens=24)) for p in ps])]
+        eng.check()
+        m = eng.metrics()
+    finally:
+        pair.close()
+    assert got == want
+    assert m["spec_accepted"] > 0, m

@@ -8,6 +8,7 @@ greedy stream decoded in rounds equals the target's plain greedy decode, token f
 * drafter = the same init with Q8_0 instead of Q4_K weights: most drafts agree, some rounds stop early;
 * drafter = an unrelated one-layer model: most rounds accept no draft;
 * a rewind (a round restarted from an earlier position) and prefill chunks between rounds;
+* sequences one after another on the one stream (released in between);
 * what a pair refuses: tree items, several anchors, other pages, commit and copy_blocks.
 """
 import os
@@ -107,6 +108,33 @@ def test_rewind_and_prefill_between_rounds(pair):
         cont = seq[len(base) + len(ext):len(base) + len(ext) + 16]
     assert again == first
     assert cont == plain_greedy(pack, [files["self"]], base + ext, 16)
+
+
+def test_sequences_one_after_another(pair):
+    """The pair's one stream serves sequence after sequence (the engine's use: max_num_seqs 1, gc_release between
+    requests), each equal to the target alone; a new sequence while another still holds the stream is a state error."""
+    files, packs = pair
+    pack = packs["q8"]
+    other = [300, 301, 5, 6, 7, 302, 303]
+    with open_pair(pack, files, "q8") as be:
+        a, _ = rounds(be, PROMPT, 16)
+        be.release(0)
+        b = rounds_sid(be, 1, other, 16)
+        with pytest.raises(gck.GcError) as e:        # sequence 1 is not released: the stream is busy
+            be.step([gck.Work(2, PROMPT, 0, [0], 1, greedy=True)])
+        assert e.value.code == gck.E_STATE
+        be.release(1)
+        c = rounds_sid(be, 2, PROMPT, 16)
+    assert a == plain_greedy(pack, [files["self"]], PROMPT, 16)
+    assert b == plain_greedy(pack, [files["self"]], other, 16)
+    assert c == a
+
+
+def rounds_sid(be, sid, prompt, n):
+    seq = list(prompt) + be.step([gck.Work(sid, list(prompt), 0, [0], 1, greedy=True)])[0]
+    while len(seq) < len(prompt) + n:
+        seq += be.step([gck.Work(sid, [seq[-1]], len(seq) - 1, [0], 1, greedy=True, spec=True)])[0]
+    return seq[len(prompt):len(prompt) + n]
 
 
 def test_pair_refusals(pair):
