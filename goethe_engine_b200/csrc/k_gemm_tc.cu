@@ -185,14 +185,18 @@ constexpr int smem_total() {
   return need > 120 * 1024 ? need : 120 * 1024;
 }
 
-// Work unit w (0 .. units-1) = (token tile, weight tile, K split); a CTA takes units blockIdx.x, + gridDim.x, ...
+// Work unit w (0 .. units-1) = (weight tile, K split, token tile), the token tile fastest; a CTA takes units
+// blockIdx.x, + gridDim.x, ... With several token tiles (prefill) the CTAs that run at the same time then share row
+// bands, so a band's weight tiles come from DRAM once and from L2 for the other token tiles (token tile slowest, every
+// tile pass streamed all the weights again: 6.7x the weight bytes at a 2048-token step). A unit's arithmetic does not
+// depend on the order.
 struct Unit {
   int nt, split, tt, kt0, per;
 };
-GCK_DEV Unit unit_of(int w, int NTW, int KT, int splits) {
+GCK_DEV Unit unit_of(int w, int NTW, int KT, int splits, int TT) {
   Unit u;
-  u.tt = w / (NTW * splits);
-  int rem = w % (NTW * splits);
+  u.tt = w % TT;
+  int rem = w / TT;
   u.nt = rem / splits;
   u.split = rem % splits;
   const int base = KT / splits, extra = KT % splits;   // the first KT % splits splits take one more raw tile
@@ -208,6 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   using F = TileFmt<TYPE>;
   using S = Shape<TYPE, NT>;
   constexpr int RS = S::RAW, SR = S::R, ACC = S::ACC, KS = S::KS, SPT = S::SPT;
+  const int TT = units / (NTW * splits);     // token tiles
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned (the 128-byte swizzle atom) by an offset into the __shared__ array, so that every pointer derived
   // from it stays a shared-memory pointer to the compiler (shared loads, not generic ones)
@@ -250,7 +255,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       long c = 0;
       bool ok = true;
       for (int w = blockIdx.x; w < units && ok; w += gridDim.x) {
-        const Unit un = unit_of(w, NTW, KT, splits);
+        const Unit un = unit_of(w, NTW, KT, splits, TT);
         for (int u = 0; u < un.per; u++, c++) {
           const int rs = static_cast<int>(c % RS);
           if (!(ok = mbar_wait(&raw_empty[rs], static_cast<uint32_t>((c / RS) & 1) ^ 1, err, kErrRawEmpty))) break;
@@ -269,7 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       long c = 0;
       bool ok = true;
       for (int w = blockIdx.x; w < units && ok; w += gridDim.x) {
-        const Unit un = unit_of(w, NTW, KT, splits);
+        const Unit un = unit_of(w, NTW, KT, splits, TT);
         for (int i = 0; i < un.per * SPT; i++, c++) {
           const int s = static_cast<int>(c % SR);
           if (!(ok = mbar_wait(&st_empty[s], static_cast<uint32_t>((c / SR) & 1) ^ 1, err, kErrStageEmpty))) break;
@@ -290,7 +295,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int lu = 0;
       bool ok = true;
       for (int w = blockIdx.x; w < units && ok; w += gridDim.x, lu++) {
-        const Unit un = unit_of(w, NTW, KT, splits);
+        const Unit un = unit_of(w, NTW, KT, splits, TT);
         const int ab = ACC == 2 ? (lu & 1) : 0;
         const uint32_t ph = ACC == 2 ? static_cast<uint32_t>((lu >> 1) & 1) : static_cast<uint32_t>(lu & 1);
         if (!(ok = mbar_wait(&acc_empty[ab], ph ^ 1, err, kErrAcc))) break;
@@ -329,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     long c = 0, cr = 0;
     bool ok = true;
     for (int w = blockIdx.x; w < units && ok; w += gridDim.x) {
-      const Unit un = unit_of(w, NTW, KT, splits);
+      const Unit un = unit_of(w, NTW, KT, splits, TT);
       for (int u = 0; u < un.per && ok; u++, cr++) {
         const int rs = static_cast<int>(cr % RS);
         for (int sub = 0; sub < SPT; sub++, c++) {
@@ -399,7 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = q * 32 + lane;
     int lu = 0;
     for (int w = blockIdx.x; w < units; w += gridDim.x, lu++) {
-      const Unit un = unit_of(w, NTW, KT, splits);
+      const Unit un = unit_of(w, NTW, KT, splits, TT);
       const int ab = ACC == 2 ? (lu & 1) : 0;
       const uint32_t ph = ACC == 2 ? static_cast<uint32_t>((lu >> 1) & 1) : static_cast<uint32_t>(lu & 1);
       const bool good = mbar_wait_sleep(&acc_full[ab], ph, err, kErrAcc);
