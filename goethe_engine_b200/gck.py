@@ -10,6 +10,7 @@ Nothing here computes: every step runs in libgck.so on the GPU. A missing librar
 fails loudly (``GcError``); there is no fallback.
 """
 import array
+import operator
 import ctypes as C
 import os
 from dataclasses import dataclass
@@ -65,7 +66,10 @@ assert WORK_DTYPE.itemsize == C.sizeof(WorkS) and all(
 
 
 def _addr(a):
-    return a.__array_interface__["data"][0]
+    return a.ctypes.data
+
+
+_FIELDS = operator.attrgetter("sid", "pos", "want", "greedy", "spec", "feats", "parents", "tokens", "blocks")
 
 
 def _flat(work, field, code, dtype):
@@ -176,42 +180,54 @@ class Backend:
     def step(self, work, logits=None):
         """Tokens per item (every item greedy) or float32 logits [sum(want), vocab] (into `logits` if given)."""
         n = len(work)
-        greedy = self.device_argmax and all(w.greedy for w in work)
-        # every item's tokens in one int32 array, every block table in one uint32 array, the records in one structured
-        # array (filled a column at a time), their addresses in another: a handful of numpy calls per step
-        ntok = np.fromiter((len(w.tokens) for w in work), np.int64, n)
+        # one pass over the items collects every per-item field; then every item's tokens go into one int32 array, the
+        # block tables into one uint32 array, the records into one structured array (a column at a time) and their
+        # addresses into another: a handful of numpy calls per step
+        sid, pos, want_, gr, sp, ft, par, tk, bl = zip(*map(_FIELDS, work)) if n else ((),) * 9
+        greedy = self.device_argmax and all(gr)
+        spec_any, tree_any = any(sp), any(p is not None for p in par)
+        tables_np = all(type(b) is np.ndarray and b.dtype == np.uint32 for b in bl)
+        c = np.empty((n, 6), np.int64)
+        c[:, 0], c[:, 1], c[:, 2] = sid, pos, want_
+        c[:, 3] = list(map(len, tk))
+        c[:, 4] = list(map(len, bl))
+        c[:, 5] = np.array(sp, np.int64) * 2 + np.array(ft, np.int64) * 4
+        ntok, nblk = c[:, 3], c[:, 4]
         toks = _flat(work, "tokens", "i", np.int32)
-        nblk = np.fromiter((len(w.blocks) for w in work), np.int64, n)
-        if n and all(isinstance(w.blocks, np.ndarray) for w in work):
-            ball = np.concatenate([_u32(w.blocks) for w in work])
+        if n and tables_np:
+            ball = np.concatenate(bl)
         else:
             ball = _flat(work, "blocks", "I", np.uint32)
         rec = np.zeros(n, WORK_DTYPE)
         keep = [toks, rec, ball]
         rec["size"] = WORK_DTYPE.itemsize
-        rec["flags"] = [(1 if greedy else 0) | (2 if w.spec else 0) | (4 if w.feats else 0) for w in work]
-        rec["sid"] = [w.sid for w in work]
-        rec["pos"] = [w.pos for w in work]
-        rec["want"] = [w.want for w in work]
+        rec["flags"] = c[:, 5] | (1 if greedy else 0)
+        rec["sid"] = c[:, 0]
+        rec["pos"] = c[:, 1]
+        rec["want"] = c[:, 2]
         rec["n_tokens"] = ntok
         rec["tokens"] = _addr(toks) + 4 * (np.cumsum(ntok) - ntok).astype(np.uint64)
         rec["blocks"] = _addr(ball) + 4 * (np.cumsum(nblk) - nblk).astype(np.uint64)
         rec["n_blocks"] = nblk
-        for i, w in enumerate(work):
-            if w.parents is not None:
-                par = np.ascontiguousarray(w.parents, np.int32)
-                keep.append(par)
-                rec["parents"][i] = _addr(par)
+        if tree_any:
+            for i, w in enumerate(work):
+                if w.parents is not None:
+                    par = np.ascontiguousarray(w.parents, np.int32)
+                    keep.append(par)
+                    rec["parents"][i] = _addr(par)
         ptrs = _addr(rec) + WORK_DTYPE.itemsize * np.arange(n, dtype=np.uint64)
         pw = C.cast(C.c_void_p(_addr(ptrs)), P_(P_(WorkS)))
-        rows = sum(w.want for w in work)
+        want = c[:, 2]
+        rows = int(want.sum())
         out = StepOut(size=C.sizeof(StepOut))
-        counts = (C.c_uint32 * n)()
+        counts = np.zeros(n, np.uint32)
         if greedy:
             # a speculative round returns up to spec_width tokens for its one wanted row
-            cap = sum(max(w.want, self.spec_width if w.spec else 0) for w in work)
-            tok = (C.c_int32 * max(cap, 1))()
-            out.tokens, out.tokens_cap, out.counts = tok, cap, counts
+            cap = int(np.maximum(want, np.where(c[:, 5] & 2, self.spec_width, 0)).sum()) if spec_any else rows
+            tok = np.empty(max(cap, 1), np.int32)
+            out.tokens = tok.ctypes.data_as(P_(C.c_int32))
+            out.tokens_cap = cap
+            out.counts = counts.ctypes.data_as(P_(C.c_uint32))
         else:
             lg = logits if logits is not None else np.empty((rows, self.vocab_size), np.float32)
             out.logits, out.logits_cap = lg.ctypes.data, lg.size
@@ -219,11 +235,11 @@ class Backend:
                                 C.byref(out)))
         del keep, ptrs
         if greedy:
-            res, o = [], 0
-            for c in counts:
-                res.append(list(tok[o:o + c]))
-                o += c
-            return res
+            if not spec_any and rows == n and bool((counts == 1).all()):
+                return tok[:n, None].tolist()          # one token per item: the common decode step
+            ends = np.cumsum(counts)
+            flat = tok.tolist()
+            return [flat[e - k:e] for e, k in zip(ends.tolist(), counts.tolist())]
         return lg[:out.n_rows]
 
     def commit(self, sid, base, path):
