@@ -247,14 +247,14 @@ def run_mine(args, rank, world, barrier, maxreduce):
     stats.enable(0)
     tables, toks, t_prefill = setup_sequences(be, ctx, steps_total)
     st0 = stats.read()
-    last = [t[-1] for t in toks]
-    pos = [int(c) - 1 for c in ctx]
+    last = np.array([t[-1] for t in toks], np.int32)
+    pos = np.array([int(c) - 1 for c in ctx], np.int64)
+    sids = np.arange(B)
 
     def step():
-        out = be.step([gck.Work(i, [last[i]], pos[i], tables[i], 1, greedy=True) for i in range(B)])
-        for i in range(B):
-            last[i] = out[i][0]
-            pos[i] += 1
+        # one token per sequence through gc_step (Backend.decode: the work records built from columns)
+        last[:] = be.decode(sids, last, pos, tables)
+        pos[:] += 1
     stats.enable(0)
     for _ in range(args.warmup):
         step()
@@ -669,7 +669,7 @@ def run_c2(args):
     be.step([gck.Work(0, toks[:-1], 0, tab, 0)])
     last, pos = toks[-1], ctx - 1
     for _ in range(args.warmup):
-        last = be.step([gck.Work(0, [last], pos, tab, 1, greedy=True)])[0][0]
+        last = int(be.decode([0], [last], [pos], [tab])[0])
         pos += 1
     torch.cuda.synchronize()
     on(args.profile)
@@ -679,7 +679,7 @@ def run_c2(args):
         for k in range(args.steps):
             if window and k == 0:
                 torch.cuda.profiler.start()
-            last = be.step([gck.Work(0, [last], pos, tab, 1, greedy=True)])[0][0]
+            last = int(be.decode([0], [last], [pos], [tab])[0])
             if window and k == 0:
                 torch.cuda.profiler.stop()
             pos += 1
@@ -851,14 +851,13 @@ def c5_measure(tp, steps, warmup, prefill=True, profile_steps=3):
                 budget -= n
             be.step(items)
     t_prefill = time.time() - t0
-    last = [t[-1] for t in toks]
-    pos = [CTX70 - 1] * B70
+    last = np.array([t[-1] for t in toks], np.int32)
+    pos = np.full(B70, CTX70 - 1, np.int64)
+    sids = np.arange(B70)
 
     def step():
-        out = be.step([gck.Work(i, [last[i]], pos[i], tables[i], 1, greedy=True) for i in range(B70)])
-        for i in range(B70):
-            last[i] = out[i][0]
-            pos[i] += 1
+        last[:] = be.decode(sids, last, pos, tables)
+        pos[:] += 1
     for _ in range(warmup):
         step()
     torch.cuda.synchronize()

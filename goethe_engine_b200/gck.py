@@ -242,6 +242,43 @@ class Backend:
             return [flat[e - k:e] for e, k in zip(ends.tolist(), counts.tolist())]
         return lg[:out.n_rows]
 
+    def decode(self, sids, tokens, pos, blocks, greedy=True, logits=None):
+        """One decode step of n sequences given as columns: sids [n] ids, tokens [n] (one token each), pos [n] (the
+        token's row), blocks: n uint32 block tables. The same gc_step call as step() with n one-token items, want 1,
+        built from the columns without a Python object per item. Returns the next token of each sequence (int32 [n],
+        every item greedy with the device argmax) or float32 logits [n, vocab]."""
+        n = len(sids)
+        greedy = greedy and self.device_argmax
+        toks = np.ascontiguousarray(tokens, np.int32)
+        nblk = np.fromiter(map(len, blocks), np.int64, n)
+        ball = np.concatenate([_u32(b) for b in blocks]) if n else np.zeros(0, np.uint32)
+        rec = np.zeros(n, WORK_DTYPE)
+        rec["size"] = WORK_DTYPE.itemsize
+        rec["flags"] = 1 if greedy else 0
+        rec["sid"] = sids
+        rec["pos"] = pos
+        rec["want"] = 1
+        rec["n_tokens"] = 1
+        rec["tokens"] = _addr(toks) + 4 * np.arange(n, dtype=np.uint64)
+        rec["blocks"] = _addr(ball) + 4 * (np.cumsum(nblk) - nblk).astype(np.uint64)
+        rec["n_blocks"] = nblk
+        ptrs = _addr(rec) + WORK_DTYPE.itemsize * np.arange(n, dtype=np.uint64)
+        pw = C.cast(C.c_void_p(_addr(ptrs)), P_(P_(WorkS)))
+        out = StepOut(size=C.sizeof(StepOut))
+        counts = np.zeros(n, np.uint32)
+        if greedy:
+            tok = np.empty(max(n, 1), np.int32)
+            out.tokens = tok.ctypes.data_as(P_(C.c_int32))
+            out.tokens_cap = n
+            out.counts = counts.ctypes.data_as(P_(C.c_uint32))
+        else:
+            lg = logits if logits is not None else np.empty((n, self.vocab_size), np.float32)
+            out.logits, out.logits_cap = lg.ctypes.data, lg.size
+        self._ck(self.L.gc_step(self.h, C.byref(StepIn(C.sizeof(StepIn), 0 if greedy else S_HOST_LOGITS, pw, n, 0)),
+                                C.byref(out)))
+        del toks, ball, rec, ptrs
+        return tok[:n] if greedy else lg[:out.n_rows]
+
     def commit(self, sid, base, path):
         self._ck(self.L.gc_commit(self.h, sid, base, arr(C.c_uint32, path), len(path)))
 

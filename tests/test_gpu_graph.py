@@ -89,3 +89,37 @@ def test_captured_steps_equal_direct_launches(tmp_path):
             assert np.array_equal(g, r)
         else:
             assert g == r
+
+
+def test_decode_columns_equal_step(tmp_path):
+    """Backend.decode (a decode step built from columns) is the same gc_step as Backend.step with one-token items:
+    the same tokens and the same logits, bit for bit."""
+    spec = synth.Spec(**SMALL128, wtype="q8_0", seed=9)
+    pack, ws = model(tmp_path, spec, ncol=16, maxctx=1024)
+    rng = np.random.default_rng(4)
+    lens = [12, 130, 300, 5, 77, 513]
+    toks = [[int(x) for x in rng.integers(1, 500, n)] for n in lens]
+    tabs = [np.arange(PER * i, PER * (i + 1), dtype=np.uint32) for i in range(len(lens))]
+    outs = {}
+    for mode in ("step", "decode"):
+        with gck.Backend(pack, ws, pool_blocks=PER * 8) as be:
+            seqs = [list(t) for t in toks]
+            be.step([gck.Work(i, seqs[i], 0, tabs[i], 0) for i in range(len(lens))])
+            got = []
+            for k in range(20):
+                greedy = k % 4 != 3
+                sids = np.arange(len(lens))
+                last = [s[-1] for s in seqs]
+                pos = [len(s) - 1 for s in seqs]
+                if mode == "step":
+                    r = be.step([gck.Work(i, [last[i]], pos[i], tabs[i], 1, greedy=greedy) for i in range(len(lens))])
+                    nxt = [x[0] for x in r] if greedy else [int(np.argmax(x)) for x in r]
+                else:
+                    r = be.decode(sids, last, pos, tabs, greedy=greedy)
+                    nxt = [int(x) for x in r] if greedy else [int(np.argmax(x)) for x in r]
+                got.append(np.array(r).copy())
+                for s, t in zip(seqs, nxt):
+                    s.append(t)
+            outs[mode] = got
+    for a, b in zip(outs["step"], outs["decode"]):
+        assert np.array_equal(np.asarray(a).reshape(b.shape), b)
