@@ -77,3 +77,21 @@ def test_values_outside_the_record_types_raise_on_the_host():
         except (OverflowError, ValueError):
             continue
         raise AssertionError(f"accepted {bad}")
+
+
+def test_decode_columns_build_the_step_records():
+    """Backend.decode hands gc_step the same records as step() with one-token items (greedy and logits steps), and
+    returns the tokens in item order."""
+    rng = np.random.default_rng(3)
+    tabs = [np.arange(40 * i, 40 * i + int(rng.integers(3, 40)), dtype=np.uint32) for i in range(5)]
+    sids, toks, pos = [9, 2, 7, 4, 11], [5, 6, 7, 8, 9], [3, 50, 17, 600, 1]
+    for greedy in (True, False):
+        a, b = backend(greedy), backend(greedy)
+        a.spec_width = b.spec_width = 0
+        out_a = a.step([gck.Work(s, [t], p, tb, 1, greedy=greedy) for s, t, p, tb in zip(sids, toks, pos, tabs)])
+        out_b = b.decode(np.array(sids), toks, pos, tabs, greedy=greedy)
+        assert a.L.seen == b.L.seen
+        if greedy:
+            assert [x[0] for x in out_a] == list(out_b) == [100, 101, 102, 103, 104]
+        else:
+            assert out_a.shape == out_b.shape == (5, 1000)
