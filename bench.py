@@ -211,7 +211,8 @@ class Stats:
         class S(C.Structure):
             _fields_ = [("size", C.c_uint32), ("steps", C.c_uint32), ("launches", C.c_uint64),
                         ("forward_ms", C.c_double), ("class_ms", C.c_double * 16), ("class_launches", C.c_uint64 * 16),
-                        ("h2d_bytes", C.c_uint64), ("graph_steps", C.c_uint32), ("graph_captures", C.c_uint32)]
+                        ("h2d_bytes", C.c_uint64), ("graph_steps", C.c_uint32), ("graph_captures", C.c_uint32),
+                        ("gemm_pairs", C.c_uint32)]
         self.S, self.be, self.C = S, be, C
         be.L.gck_stats_enable.argtypes = [C.c_void_p, C.c_uint32]
         be.L.gck_stats_read.argtypes = [C.c_void_p, C.c_void_p]
@@ -628,7 +629,7 @@ def stats_api(be):
     class Stats(C.Structure):
         _fields_ = [("size", C.c_uint32), ("steps", C.c_uint32), ("launches", C.c_uint64), ("forward_ms", C.c_double),
                     ("class_ms", C.c_double * 16), ("class_launches", C.c_uint64 * 16), ("h2d_bytes", C.c_uint64),
-                    ("graph_steps", C.c_uint32), ("graph_captures", C.c_uint32)]
+                    ("graph_steps", C.c_uint32), ("graph_captures", C.c_uint32), ("gemm_pairs", C.c_uint32)]
     be.L.gck_stats_enable.argtypes = [C.c_void_p, C.c_uint32]
     be.L.gck_stats_read.argtypes = [C.c_void_p, C.c_void_p]
 
@@ -790,7 +791,8 @@ def run_c4(args):
         "data": "synthetic (seeded N(0,0.02) weights, uniform tokens, seeded draft trees)",
         "config": {"workload": f"C4: Llama-3-8B shape, {args.act} activations x Q8_0 weights, prefill 32 x 2048 then "
                                "verify 32 x 16-node trees",
-                   "batch": n_seq, "context": ctx, "tree_parents": parents, "l2": "inputs larger than L2, no flush"},
+                   "batch": n_seq, "context": ctx, "tree_parents": parents, "l2": "inputs larger than L2, no flush",
+                   "gemm_cta_pairs": int(st_p.gemm_pairs)},
         "roofline": {"bound": "tensor", "achieved": round(flop / (pre_ms / 1e3) / 1e12, 1), "peak": tc, "unit": "TFLOP/s",
                      "frac": round(flop / (pre_ms / 1e3) / 1e12 / tc, 4),
                      "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained"},

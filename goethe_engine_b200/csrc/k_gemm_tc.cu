@@ -18,6 +18,9 @@
 //                store, residual add, SwiGLU or split-K partial.
 // At a decode batch of 64 the M128 x N64 MMAs and the Q4_K weight stream need about the same time per tile, so the
 // MMA thread is kept fed by a stage ring of whole 256-K tiles.
+// For 128-row token tiles (prefill, verify) and an even band count, CTAs run in pairs (clusters of two): each streams
+// and dequantizes its own band, holds half of the token tile, and the pair's first CTA issues one M = 256 MMA
+// (tcgen05.mma.cta_group::2) for both, half as many MMA instructions per weight tile.
 // Every output element accumulates its K range in one order whatever NT is, so a row's result does not depend on the
 // rest of the batch. Every copy here reads this GPU's global memory into this CTA's own shared memory.
 //
@@ -153,14 +156,55 @@ GCK_DEV void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint3
       : "memory");
 }
 
+// ---- CTA pairs (cta_group::2): one M256 MMA over two CTAs' tensor memory and shared memory
+GCK_DEV uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+  return r;
+}
+GCK_DEV void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+// the cluster-window address of the variable at p's offset in the shared memory of CTA `rank` of this cluster
+GCK_DEV uint32_t cluster_addr(const void *p, uint32_t rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
+  return a;
+}
+// Arrive on the other CTA's barrier (a cluster-window address). Default semantics (release at CTA scope), the form
+// cluster pipelines use: the data the MMA reads after this signal are tensor memory, ordered by tcgen05.wait::st and
+// the tcgen05 fences around the barrier, and activations the tensor-map copy wrote (its completion seen on b_full
+// first). A release at cluster scope here cost about 1600 cycles per warp and stage, the arrive stalled until then.
+GCK_DEV void mbar_arrive_cluster(uint32_t addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];\n" ::"r"(addr) : "memory");
+}
+// A from both CTAs' tensor memory (128 rows each, same columns), B from both CTAs' shared memory (N / 2 rows each,
+// same offset), D into both CTAs' tensor memory (each its own 128 rows x N)
+GCK_DEV void umma_f16_ts_pair(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(
+          tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// arrives on the barrier at bar's offset in both CTAs of the pair once the issuing thread's MMAs have completed
+GCK_DEV void umma_commit_pair(uint64_t *bar) {
+  asm volatile(
+      "{\n .reg .b16 m;\n mov.b16 m, 3;\n"
+      " tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n}\n" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
 // Stage geometry. A stage is KS of K: KS / 2 TMEM columns of dequantized weights (128 rows, two f16 per column)
-// after the ACC accumulator buffers, and KS / 64 shared-memory activation boxes of NT rows x 64 K (128-byte swizzle).
-// KS is a whole raw tile (256) up to NT = 128 and half of one at NT = 256 (so that two activation stages fit).
-template <int TYPE, int NT>
+// after the ACC accumulator buffers, and KS / 64 shared-memory activation boxes of NT / P rows x 64 K (128-byte
+// swizzle; P = 2 for a CTA pair, each CTA holding half of the token tile). KS is a whole raw tile (256) up to NT = 128
+// and half of one at NT = 256 (so that two activation stages fit).
+template <int TYPE, int NT, int P = 1>
 struct Shape {
   static constexpr int KS = NT >= 256 ? 128 : 256;
   static constexpr int SPT = kBK / KS;                  // stages per raw tile
-  static constexpr int BOX_B = NT * 128;                // one 64-K activation box
+  static constexpr int BOX_B = NT / P * 128;            // one 64-K activation box
   static constexpr int STAGE_B = (KS / 64) * BOX_B;
   static constexpr int NCOLS = NT <= 32 ? 32 : NT <= 64 ? 64 : NT <= 128 ? 128 : 256;
   static constexpr int ACC = NT <= 128 ? 2 : 1;
@@ -177,9 +221,9 @@ struct Shape {
 };
 
 
-template <int TYPE, int NT>
+template <int TYPE, int NT, int P = 1>
 constexpr int smem_total() {
-  using S = Shape<TYPE, NT>;
+  using S = Shape<TYPE, NT, P>;
   // at least 120 KB: one CTA per SM, since each takes all 512 TMEM columns
   constexpr int need = 1024 + S::R * S::STAGE_B + S::RAW * TileFmt<TYPE>::BYTES + 512;
   return need > 120 * 1024 ? need : 120 * 1024;
@@ -205,17 +249,26 @@ GCK_DEV Unit unit_of(int w, int NTW, int KT, int splits, int TT) {
   return u;
 }
 
-template <int TYPE, int NT>
+// P = 1: one CTA per MMA (M = 128). P = 2: a cluster of two CTAs (a pair) takes two adjacent 128-row bands, band
+// 2 * pair band + CTA rank, against one token tile; each CTA streams and dequantizes its own band into its own tensor
+// memory and loads half of the token rows, and the pair's first CTA issues one M = 256 MMA for both
+// (tcgen05.mma.cta_group::2), which costs about what an M = 128 one does. The second CTA's dequant and epilogue warps
+// arrive on the first CTA's barriers (a_full, acc_empty); the MMA thread's commits arrive on both CTAs' barriers
+// (st_empty, acc_full, mma_done). Every copy still reads this GPU's global memory into this CTA's own shared memory.
+template <int TYPE, int NT, int P>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const uint8_t *__restrict__ W, int NTW, int KT, int splits, int units,
                    const __grid_constant__ CUtensorMap tmap, int T, Epi epi, float *part, int Npad, int *err, Signal sig) {
   using F = TileFmt<TYPE>;
-  using S = Shape<TYPE, NT>;
+  using S = Shape<TYPE, NT, P>;
   constexpr int RS = S::RAW, SR = S::R, ACC = S::ACC, KS = S::KS, SPT = S::SPT;
-  const int TT = units / (NTW * splits);     // token tiles
+  const uint32_t rank = P == 2 ? cluster_rank() : 0;
+  const int first = blockIdx.x / P, stride = gridDim.x / P;   // this CTA's pair (or CTA), the number of them
+  const int TT = units / (NTW / P * splits);           // token tiles
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned (the 128-byte swizzle atom) by an offset into the __shared__ array, so that every pointer derived
-  // from it stays a shared-memory pointer to the compiler (shared loads, not generic ones)
+  // from it stays a shared-memory pointer to the compiler (shared loads, not generic ones); the offset is the same in
+  // both CTAs of a pair, so the MMA's shared-memory descriptors address both
   uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t *sB = smem;
   uint8_t *sRaw = sB + SR * S::STAGE_B;
@@ -230,21 +283,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   dep_launch();
 
   if (threadIdx.x == 0) {
-    // a raw tile is read by one dequant group (KS = 256) or by both (KS = 128)
+    // a raw tile is read by one dequant group (KS = 256) or by both (KS = 128); a pair's a_full and acc_empty (used in
+    // its first CTA) count both CTAs' warps
     for (int i = 0; i < RS; i++) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], kGroupWarps * SPT); }
-    for (int i = 0; i < SR; i++) { mbar_init(&a_full[i], kGroupWarps); mbar_init(&st_empty[i], 1); mbar_init(&b_full[i], 1); }
-    for (int i = 0; i < 2; i++) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
+    for (int i = 0; i < SR; i++) { mbar_init(&a_full[i], P * kGroupWarps); mbar_init(&st_empty[i], 1); mbar_init(&b_full[i], 1); }
+    for (int i = 0; i < 2; i++) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4 * P); }
     mbar_init(mma_done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     fence_async_smem();
   }
   if (warp == 1) {   // all 512 columns: ACC accumulator buffers, then the weight stages (one CTA per SM)
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
-                 "r"(512));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
+    if constexpr (P == 2) {    // both CTAs' warps 1 together: the same columns in each
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
+                   "r"(512));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;\n" ::);
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
+                   "r"(512));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (P == 2) cluster_sync();   // both CTAs' barriers initialised before any remote arrive or multicast commit
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tmem_a = tmem + ACC * S::NCOLS;   // weight stage s at columns tmem_a + (KS / 2) * s
@@ -254,13 +315,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- raw weight tiles: one bulk copy each, up to RS tiles ahead, across unit boundaries
       long c = 0;
       bool ok = true;
-      for (int w = blockIdx.x; w < units && ok; w += gridDim.x) {
-        const Unit un = unit_of(w, NTW, KT, splits, TT);
+      for (int w = first; w < units && ok; w += stride) {
+        const Unit un = unit_of(w, NTW / P, KT, splits, TT);
+        const int band = P * un.nt + static_cast<int>(rank);
         for (int u = 0; u < un.per; u++, c++) {
           const int rs = static_cast<int>(c % RS);
           if (!(ok = mbar_wait(&raw_empty[rs], static_cast<uint32_t>((c / RS) & 1) ^ 1, err, kErrRawEmpty))) break;
           mbar_expect_tx(&raw_full[rs], F::BYTES);
-          bulk_g2s(sRaw + rs * F::BYTES, W + (static_cast<size_t>(un.nt) * KT + un.kt0 + u) * F::BYTES, F::BYTES,
+          bulk_g2s(sRaw + rs * F::BYTES, W + (static_cast<size_t>(band) * KT + un.kt0 + u) * F::BYTES, F::BYTES,
                    &raw_full[rs]);
         }
       }
@@ -269,33 +331,36 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 2) {
     if (lane == 0) {
-      // ---- activation stages: KS / 64 tensor-map copies (64 K each) per stage, up to SR stages ahead
+      // ---- activation stages: KS / 64 tensor-map copies (64 K each) per stage, up to SR stages ahead; a pair's CTA
+      // loads token rows rank * NT / 2 .. of the tile
       dep_wait();
       long c = 0;
       bool ok = true;
-      for (int w = blockIdx.x; w < units && ok; w += gridDim.x) {
-        const Unit un = unit_of(w, NTW, KT, splits, TT);
+      for (int w = first; w < units && ok; w += stride) {
+        const Unit un = unit_of(w, NTW / P, KT, splits, TT);
+        const int y = un.tt * NT + static_cast<int>(rank) * (NT / P);
         for (int i = 0; i < un.per * SPT; i++, c++) {
           const int s = static_cast<int>(c % SR);
           if (!(ok = mbar_wait(&st_empty[s], static_cast<uint32_t>((c / SR) & 1) ^ 1, err, kErrStageEmpty))) break;
           mbar_expect_tx(&b_full[s], S::STAGE_B);
           const int x = (un.kt0 + i / SPT) * kBK + (i % SPT) * KS;
 #pragma unroll
-          for (int b = 0; b < KS / 64; b++) tma_2d(sB + s * S::STAGE_B + b * S::BOX_B, &tmap, x + 64 * b, un.tt * NT, &b_full[s]);
+          for (int b = 0; b < KS / 64; b++) tma_2d(sB + s * S::STAGE_B + b * S::BOX_B, &tmap, x + 64 * b, y, &b_full[s]);
         }
       }
       for (long i = c > SR ? c - SR : 0; i < c; i++) mbar_wait(&b_full[i % SR], static_cast<uint32_t>((i / SR) & 1), err, kErrBFull);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---- MMA issuer: accumulator buffer (local unit index) % 2
-      const uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(NT >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
+    if (lane == 0 && rank == 0) {
+      // ---- MMA issuer (a pair's first CTA): accumulator buffer (local unit index) % 2
+      const uint32_t idesc =
+          (1u << 4) | (static_cast<uint32_t>(NT >> 3) << 17) | (static_cast<uint32_t>((P * kBM) >> 4) << 24);
       int s = 0;                 // stage slot and the parity of its current use
       uint32_t par = 0;
       int lu = 0;
       bool ok = true;
-      for (int w = blockIdx.x; w < units && ok; w += gridDim.x, lu++) {
-        const Unit un = unit_of(w, NTW, KT, splits, TT);
+      for (int w = first; w < units && ok; w += stride, lu++) {
+        const Unit un = unit_of(w, NTW / P, KT, splits, TT);
         const int ab = ACC == 2 ? (lu & 1) : 0;
         const uint32_t ph = ACC == 2 ? static_cast<uint32_t>((lu >> 1) & 1) : static_cast<uint32_t>(lu & 1);
         if (!(ok = mbar_wait(&acc_empty[ab], ph ^ 1, err, kErrAcc))) break;
@@ -308,19 +373,25 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t at = tmem_a + (KS / 2) * s;
           const uint64_t bd = umma_desc(sB + s * S::STAGE_B);
 #pragma unroll
-          for (int k = 0; k < KS / 16; k++)
-            umma_f16_ts(dt, at + 8 * k, bd + static_cast<uint64_t>((k >> 2) * (S::BOX_B >> 4) + 2 * (k & 3)), idesc,
-                        (i | k) != 0);
-          umma_commit(&st_empty[s]);
+          for (int k = 0; k < KS / 16; k++) {
+            const uint64_t bk = bd + static_cast<uint64_t>((k >> 2) * (S::BOX_B >> 4) + 2 * (k & 3));
+            if constexpr (P == 2) umma_f16_ts_pair(dt, at + 8 * k, bk, idesc, (i | k) != 0);
+            else umma_f16_ts(dt, at + 8 * k, bk, idesc, (i | k) != 0);
+          }
+          if constexpr (P == 2) umma_commit_pair(&st_empty[s]);
+          else umma_commit(&st_empty[s]);
           if (++s == SR) {
             s = 0;
             par ^= 1u;
           }
         }
-        umma_commit(&acc_full[ab]);   // arrives once every MMA of this unit has completed
+        // arrives once every MMA of this unit has completed
+        if constexpr (P == 2) umma_commit_pair(&acc_full[ab]);
+        else umma_commit(&acc_full[ab]);
       }
       // completes once every MMA issued above has: the exit below never frees tensor memory still being written
-      umma_commit(mma_done);
+      if constexpr (P == 2) umma_commit_pair(mma_done);
+      else umma_commit(mma_done);
     }
   } else if (warp >= kDeqWarp0) {
     // ---- dequant: two groups of 8 warps take alternate stages, so one group's waits overlap the other's arithmetic.
@@ -331,10 +402,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     const int r = q * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    const uint32_t a_full0 = P == 2 ? cluster_addr(a_full, 0) : 0u;   // the MMA-issuing CTA's a_full
     long c = 0, cr = 0;
     bool ok = true;
-    for (int w = blockIdx.x; w < units && ok; w += gridDim.x) {
-      const Unit un = unit_of(w, NTW, KT, splits, TT);
+    for (int w = first; w < units && ok; w += stride) {
+      const Unit un = unit_of(w, NTW / P, KT, splits, TT);
       for (int u = 0; u < un.per && ok; u++, cr++) {
         const int rs = static_cast<int>(cr % RS);
         for (int sub = 0; sub < SPT; sub++, c++) {
@@ -393,24 +465,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           // the stage's activation tiles must have landed too: then a_full alone tells the MMA thread both are ready
           ok = mbar_wait(&b_full[s], static_cast<uint32_t>((c / SR) & 1), err, kErrBFull);
           if (!(ok = __all_sync(0xffffffffu, ok))) break;
-          if (lane == 0) mbar_arrive(&a_full[s]);
+          if (lane == 0) {
+            if (P == 2 && rank != 0) mbar_arrive_cluster(a_full0 + 8u * s);
+            else mbar_arrive(&a_full[s]);
+          }
         }
       }
     }
   } else if (warp >= kEpiWarp0) {
-    // ---- epilogue: TMEM lane quarter q = weight rows 32q .. 32q+31 of the tile
+    // ---- epilogue: TMEM lane quarter q = weight rows 32q .. 32q+31 of this CTA's band
     dep_wait();
     const int q = warp & 3;
     const int r = q * 32 + lane;
+    const uint32_t acc_empty0 = P == 2 ? cluster_addr(acc_empty, 0) : 0u;
     int lu = 0;
-    for (int w = blockIdx.x; w < units; w += gridDim.x, lu++) {
-      const Unit un = unit_of(w, NTW, KT, splits, TT);
+    for (int w = first; w < units; w += stride, lu++) {
+      const Unit un = unit_of(w, NTW / P, KT, splits, TT);
+      const int band = P * un.nt + static_cast<int>(rank);
       const int ab = ACC == 2 ? (lu & 1) : 0;
       const uint32_t ph = ACC == 2 ? static_cast<uint32_t>((lu >> 1) & 1) : static_cast<uint32_t>(lu & 1);
       const bool good = mbar_wait_sleep(&acc_full[ab], ph, err, kErrAcc);
       tc_fence_after();
       const uint32_t tbase = tmem + ab * S::NCOLS + (static_cast<uint32_t>(q * 32) << 16);
-      const int row = un.nt * kBM + r, t0 = un.tt * NT;
+      const int row = band * kBM + r, t0 = un.tt * NT;
       if (splits > 1) {
         if (good) {
           float *p = part + static_cast<size_t>(un.split) * T * Npad;
@@ -425,9 +502,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else if (epi.kind == kEpiSwiGLU) {
-        // even rows are gate rows, the odd row after each its up row (feature un.nt * 64 + r / 2): the two lanes swap
+        // even rows are gate rows, the odd row after each its up row (feature band * 64 + r / 2): the two lanes swap
         // values and each takes half the token columns (the gate lane the even ones)
-        const int f = un.nt * 64 + (r >> 1);
+        const int f = band * 64 + (r >> 1);
         const int odd = r & 1;
         for (int c0 = 0; c0 < NT; c0 += 16) {
           uint32_t v[16];
@@ -461,7 +538,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[ab]);
+      if (lane == 0) {
+        if (P == 2 && rank != 0) mbar_arrive_cluster(acc_empty0 + 8u * ab);
+        else mbar_arrive(&acc_empty[ab]);
+      }
       if (!good) break;
     }
   }
@@ -471,40 +551,107 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (sig.flag && threadIdx.x == 0) signal_if_last(sig);
   if (warp == 1) {
-    // no MMA may still write the accumulators when they are freed (bounded; returns at once after a normal run)
+    // no MMA may still write the accumulators when they are freed (bounded; returns at once after a normal run); a
+    // pair's commit of mma_done reaches both CTAs
     if (lane == 0) mbar_wait(mma_done, 0, err, kErrAcc);
     __syncwarp();
+  }
+  if constexpr (P == 2) {
+    // neither CTA frees its tensor memory or leaves (its shared memory) while the other's arrives or the pair's MMAs
+    // may still reach them: every thread of both CTAs is past its loop here, and both MMA-done waits have returned
+    tc_fence_before();
+    cluster_sync();
+  }
+  if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(512));
+    if constexpr (P == 2) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(512));
+    else asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(512));
   }
 }
 
-template <int TYPE, int NT>
+// the number of two-CTA clusters of the paired kernel that can be resident at once (0: none)
+int g_pair_clusters = 0;
+
+template <int TYPE, int NT, int P>
 void launch_nt(const QWeight &w, const CUtensorMap *map, int T, const Epi &epi, float *part, int *err, int sms,
-               const Signal &sig, cudaStream_t s) {
-  const int units = w.NT * w.splits * ((T + NT - 1) / NT);
-  const int grid = units < sms ? units : sms;
-  launch_pdl(gemm_tc_kernel<TYPE, NT>, grid, kThreads, smem_total<TYPE, NT>(), s, w.data, w.NT, w.KT, w.splits, units,
-             *map, T, epi, part, w.NT * kBM, err, sig);
+               int pairs, const Signal &sig, cudaStream_t s) {
+  const int units = w.NT / P * w.splits * ((T + NT - 1) / NT);
+  int groups = P == 2 ? pairs : sms;
+  if (units < groups) groups = units;
+  const int smem = smem_total<TYPE, NT, P>();
+  if constexpr (P == 1) {
+    launch_pdl(gemm_tc_kernel<TYPE, NT, 1>, groups, kThreads, smem, s, w.data, w.NT, w.KT, w.splits, units, *map, T,
+               epi, part, w.NT * kBM, err, sig);
+  } else {
+    // a cluster of two CTAs per pair, with programmatic serialization as launch_pdl gives the other kernels
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * groups);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = at;
+    cfg.numAttrs = g_pdl ? 2 : 1;
+    cudaLaunchKernelEx(&cfg, gemm_tc_kernel<TYPE, NT, 2>, w.data, w.NT, w.KT, w.splits, units, *map, T, epi, part,
+                       w.NT * kBM, err, sig);
+  }
 }
 
 template <int TYPE>
 void launch_type(const QWeight &w, const TmaSet &ts, int T, const Epi &epi, float *part, int *err, int sms,
-                 const Signal &sig, cudaStream_t s) {
-  int nt = tc_token_tile(T);
+                 int pairs, const Signal &sig, cudaStream_t s) {
+  const int nt = tc_token_tile(T);
+  // pairs for even band counts at 128-row token tiles (each CTA loads the tile's half, a 64-row box). At 32 and 64
+  // rows (decode) pairs measured slower: a pair stage took as long as one CTA's (2379 vs 2292 cycles, C3 step 5.25 vs
+  // 5.15 ms), the MMA issue was not the limit there once halved.
+  if (pairs > 0 && w.NT % 2 == 0 && nt == 128) {
+    launch_nt<TYPE, 128, 2>(w, ts.map(64), T, epi, part, err, sms, pairs, sig, s);
+    return;
+  }
   const CUtensorMap *m = ts.map(nt);
   switch (nt) {
-    case 16: launch_nt<TYPE, 16>(w, m, T, epi, part, err, sms, sig, s); break;
-    case 32: launch_nt<TYPE, 32>(w, m, T, epi, part, err, sms, sig, s); break;
-    case 64: launch_nt<TYPE, 64>(w, m, T, epi, part, err, sms, sig, s); break;
-    case 128: launch_nt<TYPE, 128>(w, m, T, epi, part, err, sms, sig, s); break;
-    default: launch_nt<TYPE, 256>(w, m, T, epi, part, err, sms, sig, s); break;
+    case 16: launch_nt<TYPE, 16, 1>(w, m, T, epi, part, err, sms, pairs, sig, s); break;
+    case 32: launch_nt<TYPE, 32, 1>(w, m, T, epi, part, err, sms, pairs, sig, s); break;
+    case 64: launch_nt<TYPE, 64, 1>(w, m, T, epi, part, err, sms, pairs, sig, s); break;
+    case 128: launch_nt<TYPE, 128, 1>(w, m, T, epi, part, err, sms, pairs, sig, s); break;
+    default: launch_nt<TYPE, 256, 1>(w, m, T, epi, part, err, sms, pairs, sig, s); break;
   }
 }
 
-template <int TYPE, int NT>
+template <int TYPE, int NT, int P = 1>
 void set_attr() {
-  cudaFuncSetAttribute(gemm_tc_kernel<TYPE, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_total<TYPE, NT>());
+  cudaFuncSetAttribute(gemm_tc_kernel<TYPE, NT, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       smem_total<TYPE, NT, P>());
+}
+
+// how many two-CTA clusters of the pair kernel fit on the device at once (one CTA per SM); 0 if none or on error
+int max_pair_clusters() {
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(sms / 2 * 2);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem_total<kQ4_K, 128, 2>();
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<kQ4_K, 128, 2>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
 }
 
 }  // namespace
@@ -522,15 +669,21 @@ int tc_token_tile(int T) {
 void gemm_tc_init() {
   set_attr<kQ4_K, 16>(); set_attr<kQ4_K, 32>(); set_attr<kQ4_K, 64>(); set_attr<kQ4_K, 128>(); set_attr<kQ4_K, 256>();
   set_attr<kQ8_0, 16>(); set_attr<kQ8_0, 32>(); set_attr<kQ8_0, 64>(); set_attr<kQ8_0, 128>(); set_attr<kQ8_0, 256>();
+  set_attr<kQ4_K, 128, 2>(); set_attr<kQ8_0, 128, 2>();
+  g_pair_clusters = max_pair_clusters();
 }
+
+int tc_pair_clusters() { return g_pair_clusters; }
 
 size_t tc_tile_bytes(int type) { return type == kQ4_K ? TileFmt<kQ4_K>::BYTES : TileFmt<kQ8_0>::BYTES; }
 
 void launch_gemm_tc(const QWeight &w, const TmaSet &ts, int T, const Epi &epi, float *part, int *err, int sms,
-                    cudaStream_t s, const Signal &sig) {
+                    int pairs, cudaStream_t s, const Signal &sig) {
   if (T <= 0) return;
-  if (w.type == kQ4_K) launch_type<kQ4_K>(w, ts, T, epi, part, err, sms, sig, s);
-  else launch_type<kQ8_0>(w, ts, T, epi, part, err, sms, sig, s);
+  if (pairs > g_pair_clusters) pairs = g_pair_clusters;
+  if (pairs > sms / 2) pairs = sms / 2;
+  if (w.type == kQ4_K) launch_type<kQ4_K>(w, ts, T, epi, part, err, sms, pairs, sig, s);
+  else launch_type<kQ8_0>(w, ts, T, epi, part, err, sms, pairs, sig, s);
 }
 
 }  // namespace gck

@@ -151,9 +151,11 @@ struct TmaSet {            // tensor maps over one activation buffer [rows, K] f
 int tc_token_tile(int T);
 size_t tc_tile_bytes(int type);
 void gemm_tc_init();      // once per device
+int tc_pair_clusters();   // two-CTA clusters of the paired GEMM that fit on the device at once (0: none)
+// pairs: two-CTA clusters for the paired kernel (0: one CTA per MMA throughout; capped at tc_pair_clusters())
 // sig (optional): the GEMM's completion published to other GPUs (tensor parallelism, phase 1 of the all-reduce)
 void launch_gemm_tc(const QWeight &w, const TmaSet &ts, int T, const Epi &epi, float *part, int *err, int sms,
-                    cudaStream_t s, const Signal &sig = Signal{});
+                    int pairs, cudaStream_t s, const Signal &sig = Signal{});
 
 
 // Paged attention over the plan's work list: q [T, H, dh] f16 -> out [T, H, dh] f16. part_o / part_ml: split partials,

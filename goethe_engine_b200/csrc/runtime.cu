@@ -147,6 +147,8 @@ struct gc_handle {
   // shape is captured the second time it is seen. Off under tensor parallelism, statistics and tree items.
   struct Graph { std::vector<int64_t> key; cudaGraphExec_t exec; uint64_t launches; };
   bool graphs_on = true;
+  // two-CTA clusters for the paired tcgen05 GEMM (GCK_PAIR=0 at open: none, one CTA per MMA throughout)
+  int tc_pairs = 0;
   std::vector<Graph> graphs;                 // most recent last
   std::vector<std::vector<int64_t>> seen;   // shapes run once without a graph
   uint64_t scratch_gen = 0;                  // bumped whenever a scratch buffer a kernel argument points to moves
@@ -734,6 +736,8 @@ void open_device(gc_handle *h, int dev, const std::vector<std::unique_ptr<GgufFi
   h->tables = static_cast<uint32_t *>(h->dalloc(static_cast<size_t>(h->max_seqs) * h->tab_stride * 4, "block tables"));
   ck(cudaMemset(h->tables, 0, static_cast<size_t>(h->max_seqs) * h->tab_stride * 4), "block tables");
   if (const char *e = std::getenv("GCK_GRAPH")) h->graphs_on = std::atoi(e) != 0;
+  h->tc_pairs = tc_pair_clusters();
+  if (const char *e = std::getenv("GCK_PAIR")) h->tc_pairs = std::atoi(e) != 0 ? h->tc_pairs : 0;
   ck(cudaStreamSynchronize(h->st), "open");
 }
 
@@ -1340,7 +1344,7 @@ void forward_launch(gc_handle *h, const PlanView &pv, int nw) {
     run(cls, 1, [&] {
       if (use_gemv(w, rows)) launch_gemv(w, w.gslices, act, ldx, rows, e, h->part, s);
       else if (w.type == kF16) launch_gemm(w, act, rows, e, h->part, s);
-      else launch_gemm_tc(w, ts, rows, e, h->part, h->kerr, h->sms, s);
+      else launch_gemm_tc(w, ts, rows, e, h->part, h->kerr, h->sms, h->tc_pairs, s);
     });
     const int sl = slices(w, rows);
     if (sl > 1 && rows > 0 && !reader_reduces)
@@ -1378,7 +1382,7 @@ void forward_launch(gc_handle *h, const PlanView &pv, int nw) {
       Signal s1{h->tp_flags + b, ep * 4 + 1, h->sig_counter}, s2{h->tp_flags + b, ep * 4 + 2, h->sig_counter};
       if (w.type != kF16) {
         // the rank's split-K partials [splits][T][d] (or its output) straight into buffer b; publishes phase 1
-        run(cls, 1, [&] { launch_gemm_tc(w, ts, T, e, h->tp_bufs[b], h->kerr, h->sms, s, s1); });
+        run(cls, 1, [&] { launch_gemm_tc(w, ts, T, e, h->tp_bufs[b], h->kerr, h->sms, h->tc_pairs, s, s1); });
       } else {
         gemm(cls, w, ts, act, ldx, T, e, false);
         run(GCK_K_ALLREDUCE, 1, [&] { launch_tp_signal(s1.flag, s1.value, s); });
@@ -2034,6 +2038,7 @@ GC_API int gck_stats_read(gc_handle *h, gck_stats *out) {
   uint32_t n = std::min<uint32_t>(out->size, sizeof(gck_stats));
   gck_stats st = h->stats;
   st.size = n;
+  st.gemm_pairs = static_cast<uint32_t>(h->tc_pairs);
   std::memcpy(out, &st, n);
   return GC_OK;
 }

@@ -39,6 +39,7 @@ typedef struct gck_stats {
   uint64_t h2d_bytes;                     /* host-to-device bytes those steps copied (plans, block-table patches) */
   uint32_t graph_steps;                   /* steps replayed from a captured CUDA graph (class_mask 0 only) */
   uint32_t graph_captures;                /* steps captured into a new graph */
+  uint32_t gemm_pairs;                    /* two-CTA clusters the tcgen05 GEMM runs on (0: one CTA per MMA) */
 } gck_stats;
 
 /* Starts (and resets) step statistics on h; class_mask picks the classes whose launches are each bracketed by a
