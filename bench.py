@@ -227,7 +227,7 @@ class Stats:
 
 
 GEMMS = (2, 6, 7, 8, 9)           # gck_ext.h classes of the tcgen05 GEMM launches: q/k/v, o, gate/up, down, head
-ATTN, GATEUP = 4, 7
+ATTN, GATEUP, DOWN = 4, 7, 8
 
 
 def run_mine(args, rank, world, barrier, maxreduce):
@@ -359,7 +359,13 @@ def gemm_roofline(sg, steps, hbm, peak_source):
     wb = weight_bytes(SPEC8B)
     gu_ms = sg.class_ms[GATEUP] / max(1, sg.class_launches[GATEUP])
     gu_bytes = 2 * 14336 * 4096 * 144 // 256 + 64 * 4096 * 2 + 64 * 14336 * 2
-    out = {"bound": "hbm", "kernel": "gemm_tc_kernel<Q4_K, 64> (q/k/v, o, gate/up, down of every layer, and the head)",
+    # chained: one launch per layer runs gate/up and down_proj (the down class launches nothing)
+    chained = sg.class_launches[DOWN] == 0 and sg.class_launches[GATEUP] > 0
+    if chained:
+        gu_bytes += 4096 * 14336 * 144 // 256 + 64 * 14336 * 2 + 64 * 4096 * 4
+    out = {"bound": "hbm", "kernel": "gemm_tc_kernel<Q4_K, 64> (q/k/v, o, gate/up "
+                                     + ("chained with down in one launch" if chained else "and down")
+                                     + " in every layer, and the head)",
            "achieved": round(wb / (ms / 1e3) / 1e9, 1), "peak": hbm, "unit": "GB/s",
            "frac": round(wb / (ms / 1e3) / 1e9 / hbm, 4), "ms_per_step": round(ms, 4), "launches_per_step": int(launches),
            "algorithmic_bytes_per_launch": int(wb / max(1, launches)), "launch_ms": round(ms / max(1, launches), 5),
@@ -368,10 +374,11 @@ def gemm_roofline(sg, steps, hbm, peak_source):
            "traffic_build": GEMM_TRAFFIC["build"] if GEMM_TRAFFIC else None,
            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean per launch over one layer's four GEMM "
                              "launches (--layers 2 case, full-size weights); 1.036 x their weight bytes",
-           "gateup": {"launch_ms": round(gu_ms, 4), "algorithmic_bytes_per_launch": int(gu_bytes),
-                      "achieved": round(gu_bytes / (gu_ms / 1e3) / 1e9, 1),
-                      "frac": round(gu_bytes / (gu_ms / 1e3) / 1e9 / hbm, 4),
-                      "traffic": GEMM_TRAFFIC["gateup"] if GEMM_TRAFFIC else None},
+           ("gateup_down" if chained else "gateup"): {
+               "launch_ms": round(gu_ms, 4), "algorithmic_bytes_per_launch": int(gu_bytes),
+               "achieved": round(gu_bytes / (gu_ms / 1e3) / 1e9, 1),
+               "frac": round(gu_bytes / (gu_ms / 1e3) / 1e9 / hbm, 4),
+               "traffic": GEMM_TRAFFIC.get("gateup_down" if chained else "gateup") if GEMM_TRAFFIC else None},
            "timing": f"CUDA events around each GEMM launch, {steps} decode steps after the timed region (upper bound: "
                      "the events cut the programmatic overlap)", "peak_source": peak_source}
     return out

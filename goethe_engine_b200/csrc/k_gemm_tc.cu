@@ -28,6 +28,9 @@
 // drains what it issued (again bounded), frees its tensor memory and returns; gc_step reports GC_E_DEVICE.
 #include <cuda.h>
 
+#include <algorithm>
+#include <vector>
+
 #include "common.cuh"
 #include "dequant.cuh"
 #include "kernels.h"
@@ -41,7 +44,7 @@ constexpr int kDeqWarp0 = 7;               // warps 7-22: dequant, two groups
 constexpr int kGroupWarps = 8;             // per group: two threads per weight row
 constexpr unsigned long long kTimeoutNs = 2000000000ull;
 
-enum ErrCode { kErrRawFull = 1, kErrRawEmpty, kErrStageEmpty, kErrAFull, kErrBFull, kErrAcc };
+enum ErrCode { kErrRawFull = 1, kErrRawEmpty, kErrStageEmpty, kErrAFull, kErrBFull, kErrAcc, kErrChain };
 
 template <int TYPE>
 struct TileFmt;
@@ -100,6 +103,23 @@ GCK_DEV bool mbar_wait_sleep(uint64_t *b, uint32_t parity, int *err, int code) {
   for (uint32_t n = 1;; n++) {
     __nanosleep(256);
     if (mbar_try(b, parity)) return true;
+    if ((n & 63u) == 0 && now_ns() - t0 > kTimeoutNs) {
+      atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+}
+
+// Bounded wait until the counter reaches need (acquire at GPU scope); false (error word set) on timeout
+GCK_DEV bool wait_count(const unsigned *cnt, unsigned need, int *err, int code) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(cnt) : "memory");
+  if (v >= need) return true;
+  const unsigned long long t0 = now_ns();
+  for (uint32_t n = 1;; n++) {
+    __nanosleep(128);
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(cnt) : "memory");
+    if (v >= need) return true;
     if ((n & 63u) == 0 && now_ns() - t0 > kTimeoutNs) {
       atomicCAS(err, 0, code);
       return false;
@@ -258,13 +278,29 @@ GCK_DEV Unit unit_of(int w, int NTW, int KT, int splits, int TT) {
 template <int TYPE, int NT, int P>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const uint8_t *__restrict__ W, int NTW, int KT, int splits, int units,
-                   const __grid_constant__ CUtensorMap tmap, int T, Epi epi, float *part, int Npad, int *err, Signal sig) {
+                   const __grid_constant__ CUtensorMap tmap, int T, Epi epi, float *part, int Npad, int *err, Signal sig,
+                   const __grid_constant__ CUtensorMap tmap1, Chain ch) {
   using F = TileFmt<TYPE>;
   using S = Shape<TYPE, NT, P>;
   constexpr int RS = S::RAW, SR = S::R, ACC = S::ACC, KS = S::KS, SPT = S::SPT;
   const uint32_t rank = P == 2 ? cluster_rank() : 0;
   const int first = blockIdx.x / P, stride = gridDim.x / P;   // this CTA's pair (or CTA), the number of them
   const int TT = units / (NTW / P * splits);           // token tiles
+  // this CTA's units: first, first + stride, ... of the one GEMM; or, chained (P = 1, one token tile), its list in the
+  // schedule, entries with bit 31 set being units of the second GEMM
+  const bool chained = P == 1 && ch.W != nullptr;
+  const int s0 = chained ? ch.sched_off[blockIdx.x] : 0;
+  const int n_units = chained ? ch.sched_off[blockIdx.x + 1] - s0 : (units > first ? (units - first + stride - 1) / stride : 0);
+  auto job = [&](int i, int &ph) -> Unit {
+    if (chained) {
+      const int e = ch.sched[s0 + i];
+      ph = (e >> 31) & 1;
+      const int w = e & 0x7fffffff;
+      return ph ? unit_of(w, ch.NTW, ch.KT, ch.splits, 1) : unit_of(w, NTW, KT, splits, 1);
+    }
+    ph = 0;
+    return unit_of(first + i * stride, NTW / P, KT, splits, TT);
+  };
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned (the 128-byte swizzle atom) by an offset into the __shared__ array, so that every pointer derived
   // from it stays a shared-memory pointer to the compiler (shared loads, not generic ones); the offset is the same in
@@ -315,14 +351,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- raw weight tiles: one bulk copy each, up to RS tiles ahead, across unit boundaries
       long c = 0;
       bool ok = true;
-      for (int w = first; w < units && ok; w += stride) {
-        const Unit un = unit_of(w, NTW / P, KT, splits, TT);
+      for (int i = 0; i < n_units && ok; i++) {
+        int g2;
+        const Unit un = job(i, g2);
         const int band = P * un.nt + static_cast<int>(rank);
+        const uint8_t *Wp = g2 ? ch.W : W;
+        const int KTp = g2 ? ch.KT : KT;
         for (int u = 0; u < un.per; u++, c++) {
           const int rs = static_cast<int>(c % RS);
           if (!(ok = mbar_wait(&raw_empty[rs], static_cast<uint32_t>((c / RS) & 1) ^ 1, err, kErrRawEmpty))) break;
           mbar_expect_tx(&raw_full[rs], F::BYTES);
-          bulk_g2s(sRaw + rs * F::BYTES, W + (static_cast<size_t>(band) * KT + un.kt0 + u) * F::BYTES, F::BYTES,
+          bulk_g2s(sRaw + rs * F::BYTES, Wp + (static_cast<size_t>(band) * KTp + un.kt0 + u) * F::BYTES, F::BYTES,
                    &raw_full[rs]);
         }
       }
@@ -336,16 +375,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       dep_wait();
       long c = 0;
       bool ok = true;
-      for (int w = first; w < units && ok; w += stride) {
-        const Unit un = unit_of(w, NTW / P, KT, splits, TT);
+      for (int j = 0; j < n_units && ok; j++) {
+        int g2;
+        const Unit un = job(j, g2);
         const int y = un.tt * NT + static_cast<int>(rank) * (NT / P);
+        const CUtensorMap *map = g2 ? &tmap1 : &tmap;
         for (int i = 0; i < un.per * SPT; i++, c++) {
           const int s = static_cast<int>(c % SR);
+          const int kt = un.kt0 + i / SPT;
+          if (g2 && i % SPT == 0) {
+            // a chained unit's input K tile: every first-GEMM band that writes it (4 bands of 64 features; 4 epilogue
+            // warps each) has stored its rows; then its tensor-map copies may read them
+            const int nb = min(4, NTW - 4 * kt);
+            if (!(ok = wait_count(&ch.ready[kt], 4u * static_cast<unsigned>(nb), err, kErrChain))) break;
+            asm volatile("fence.proxy.async.global;\n" ::: "memory");
+          }
           if (!(ok = mbar_wait(&st_empty[s], static_cast<uint32_t>((c / SR) & 1) ^ 1, err, kErrStageEmpty))) break;
           mbar_expect_tx(&b_full[s], S::STAGE_B);
-          const int x = (un.kt0 + i / SPT) * kBK + (i % SPT) * KS;
+          const int x = kt * kBK + (i % SPT) * KS;
 #pragma unroll
-          for (int b = 0; b < KS / 64; b++) tma_2d(sB + s * S::STAGE_B + b * S::BOX_B, &tmap, x + 64 * b, y, &b_full[s]);
+          for (int b = 0; b < KS / 64; b++) tma_2d(sB + s * S::STAGE_B + b * S::BOX_B, map, x + 64 * b, y, &b_full[s]);
         }
       }
       for (long i = c > SR ? c - SR : 0; i < c; i++) mbar_wait(&b_full[i % SR], static_cast<uint32_t>((i / SR) & 1), err, kErrBFull);
@@ -359,8 +408,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t par = 0;
       int lu = 0;
       bool ok = true;
-      for (int w = first; w < units && ok; w += stride, lu++) {
-        const Unit un = unit_of(w, NTW / P, KT, splits, TT);
+      for (int j = 0; j < n_units && ok; j++, lu++) {
+        int g2;
+        const Unit un = job(j, g2);
         const int ab = ACC == 2 ? (lu & 1) : 0;
         const uint32_t ph = ACC == 2 ? static_cast<uint32_t>((lu >> 1) & 1) : static_cast<uint32_t>(lu & 1);
         if (!(ok = mbar_wait(&acc_empty[ab], ph ^ 1, err, kErrAcc))) break;
@@ -405,8 +455,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t a_full0 = P == 2 ? cluster_addr(a_full, 0) : 0u;   // the MMA-issuing CTA's a_full
     long c = 0, cr = 0;
     bool ok = true;
-    for (int w = first; w < units && ok; w += stride) {
-      const Unit un = unit_of(w, NTW / P, KT, splits, TT);
+    for (int j = 0; j < n_units && ok; j++) {
+      int g2;
+      const Unit un = job(j, g2);
       for (int u = 0; u < un.per && ok; u++, cr++) {
         const int rs = static_cast<int>(cr % RS);
         for (int sub = 0; sub < SPT; sub++, c++) {
@@ -479,8 +530,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = q * 32 + lane;
     const uint32_t acc_empty0 = P == 2 ? cluster_addr(acc_empty, 0) : 0u;
     int lu = 0;
-    for (int w = first; w < units; w += stride, lu++) {
-      const Unit un = unit_of(w, NTW / P, KT, splits, TT);
+    for (int j = 0; j < n_units; j++, lu++) {
+      int g2;
+      const Unit un = job(j, g2);
       const int band = P * un.nt + static_cast<int>(rank);
       const int ab = ACC == 2 ? (lu & 1) : 0;
       const uint32_t ph = ACC == 2 ? static_cast<uint32_t>((lu >> 1) & 1) : static_cast<uint32_t>(lu & 1);
@@ -488,7 +540,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t tbase = tmem + ab * S::NCOLS + (static_cast<uint32_t>(q * 32) << 16);
       const int row = band * kBM + r, t0 = un.tt * NT;
-      if (splits > 1) {
+      if (g2) {
+        // a chained second-GEMM unit: its split-K partial, or (one slice) its residual add / store
+        if (good) {
+          const bool sliced = ch.splits > 1;
+          float *p = sliced ? ch.part + static_cast<size_t>(un.split) * T * ch.Npad : nullptr;
+          for (int c0 = 0; c0 < NT; c0 += 16) {
+            uint32_t v[16];
+            tmem_ld16(tbase + c0, v);
+#pragma unroll
+            for (int c = 0; c < 16; c++) {
+              const int t = t0 + c0 + c;
+              if (t >= T) continue;
+              const float y = __uint_as_float(v[c]) * epi_scale(ch.epi, t);
+              if (sliced) p[static_cast<size_t>(t) * ch.Npad + row] = y;
+              else if (row < ch.epi.n) {
+                float *o = ch.epi.out_f + static_cast<size_t>(t) * ch.epi.ld + row;
+                if (ch.epi.kind == kEpiAdd) *o += y;
+                else *o = y;
+              }
+            }
+          }
+        }
+      } else if (splits > 1) {
         if (good) {
           float *p = part + static_cast<size_t>(un.split) * T * Npad;
           for (int c0 = 0; c0 < NT; c0 += 16) {
@@ -536,6 +610,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      if (chained && !g2) {
+        // this band's features are stored: count the warp in for the second GEMM's K tile that reads them (every
+        // lane's stores made visible at GPU scope first)
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(&ch.ready[(band * 64) / kBK], 1u);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -550,6 +631,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (sig.flag && threadIdx.x == 0) signal_if_last(sig);
+  if (chained && threadIdx.x == 0) {
+    // every thread of this CTA is past its waits on the K-tile counters; the last CTA to get here resets them for the
+    // next chained launch (which reads them only after this launch has completed)
+    __threadfence();
+    if (atomicAdd(ch.done, 1u) == gridDim.x - 1) {
+      for (int k = 0; k < ch.KT; k++) atomicExch(&ch.ready[k], 0u);
+      atomicExch(ch.done, 0u);
+      __threadfence();
+    }
+  }
   if (warp == 1) {
     // no MMA may still write the accumulators when they are freed (bounded; returns at once after a normal run); a
     // pair's commit of mma_done reaches both CTAs
@@ -581,7 +672,7 @@ void launch_nt(const QWeight &w, const CUtensorMap *map, int T, const Epi &epi, 
   const int smem = smem_total<TYPE, NT, P>();
   if constexpr (P == 1) {
     launch_pdl(gemm_tc_kernel<TYPE, NT, 1>, groups, kThreads, smem, s, w.data, w.NT, w.KT, w.splits, units, *map, T,
-               epi, part, w.NT * kBM, err, sig);
+               epi, part, w.NT * kBM, err, sig, *map, Chain{});
   } else {
     // a cluster of two CTAs per pair, with programmatic serialization as launch_pdl gives the other kernels
     cudaLaunchAttribute at[2];
@@ -599,7 +690,7 @@ void launch_nt(const QWeight &w, const CUtensorMap *map, int T, const Epi &epi, 
     cfg.attrs = at;
     cfg.numAttrs = g_pdl ? 2 : 1;
     cudaLaunchKernelEx(&cfg, gemm_tc_kernel<TYPE, NT, 2>, w.data, w.NT, w.KT, w.splits, units, *map, T, epi, part,
-                       w.NT * kBM, err, sig);
+                       w.NT * kBM, err, sig, *map, Chain{});
   }
 }
 
@@ -621,6 +712,24 @@ void launch_type(const QWeight &w, const TmaSet &ts, int T, const Epi &epi, floa
     case 64: launch_nt<TYPE, 64, 1>(w, m, T, epi, part, err, sms, pairs, sig, s); break;
     case 128: launch_nt<TYPE, 128, 1>(w, m, T, epi, part, err, sms, pairs, sig, s); break;
     default: launch_nt<TYPE, 256, 1>(w, m, T, epi, part, err, sms, pairs, sig, s); break;
+  }
+}
+
+template <int TYPE, int NT>
+void launch_chain_nt(const QWeight &w0, const CUtensorMap *m0, const Epi &e0, const CUtensorMap *m1, const Chain &ch,
+                     int ctas, int T, int *err, cudaStream_t s) {
+  // one token tile: the first GEMM's units are its bands (no K split: its SwiGLU epilogue needs whole sums)
+  launch_pdl(gemm_tc_kernel<TYPE, NT, 1>, ctas, kThreads, smem_total<TYPE, NT, 1>(), s, w0.data, w0.NT, w0.KT, 1,
+             w0.NT, *m0, T, e0, static_cast<float *>(nullptr), w0.NT * kBM, err, Signal{}, *m1, ch);
+}
+
+template <int TYPE>
+void launch_chain_type(const QWeight &w0, const TmaSet &ts0, const Epi &e0, const TmaSet &ts1, const Chain &ch,
+                       int ctas, int T, int *err, cudaStream_t s) {
+  switch (tc_token_tile(T)) {
+    case 16: launch_chain_nt<TYPE, 16>(w0, ts0.map(16), e0, ts1.map(16), ch, ctas, T, err, s); break;
+    case 32: launch_chain_nt<TYPE, 32>(w0, ts0.map(32), e0, ts1.map(32), ch, ctas, T, err, s); break;
+    default: launch_chain_nt<TYPE, 64>(w0, ts0.map(64), e0, ts1.map(64), ch, ctas, T, err, s); break;
   }
 }
 
@@ -674,6 +783,55 @@ void gemm_tc_init() {
 }
 
 int tc_pair_clusters() { return g_pair_clusters; }
+
+double chain_schedule(int NTW0, int KT0, int NTW1, int KT1, int splits1, int sms, int *ctas, int *sched_out,
+                      int *off_out) {
+  const int total = NTW0 + NTW1 * splits1;
+  const int G = std::min(sms, total);
+  std::vector<std::vector<int>> lists(G);
+  std::vector<double> load(G, 0.0);
+  // a unit costs its raw tiles plus about half a tile of epilogue not hidden under the next unit
+  for (int u = 0; u < NTW0; u++) {
+    lists[u % G].push_back(u);
+    load[u % G] += KT0 + 0.5;
+  }
+  const int base = KT1 / splits1, extra = KT1 % splits1;
+  for (int sp = 0; sp < splits1; sp++)
+    for (int nt = 0; nt < NTW1; nt++) {
+      const int b = static_cast<int>(std::min_element(load.begin(), load.end()) - load.begin());
+      lists[b].push_back(static_cast<int>(0x80000000u | static_cast<unsigned>(nt * splits1 + sp)));
+      load[b] += base + (sp < extra ? 1 : 0) + 0.5;
+    }
+  if (sched_out && off_out) {
+    int n = 0;
+    for (int b = 0; b < G; b++) {
+      off_out[b] = n;
+      for (int e : lists[b]) sched_out[n++] = e;
+    }
+    off_out[G] = n;
+  }
+  if (ctas) *ctas = G;
+  return *std::max_element(load.begin(), load.end());
+}
+
+void launch_gemm_tc_chain(const QWeight &w0, const TmaSet &ts0, const Epi &e0, const QWeight &w1, const TmaSet &ts1,
+                          const Epi &e1, float *part1, const ChainPlan &cp, int T, int *err, cudaStream_t s) {
+  if (T <= 0) return;
+  Chain ch;
+  ch.W = w1.data;
+  ch.NTW = w1.NT;
+  ch.KT = w1.KT;
+  ch.splits = w1.splits;
+  ch.epi = e1;
+  ch.part = part1;
+  ch.Npad = w1.NT * kBM;
+  ch.sched = cp.sched;
+  ch.sched_off = cp.off;
+  ch.ready = cp.ready;
+  ch.done = cp.done;
+  if (w0.type == kQ4_K) launch_chain_type<kQ4_K>(w0, ts0, e0, ts1, ch, cp.ctas, T, err, s);
+  else launch_chain_type<kQ8_0>(w0, ts0, e0, ts1, ch, cp.ctas, T, err, s);
+}
 
 size_t tc_tile_bytes(int type) { return type == kQ4_K ? TileFmt<kQ4_K>::BYTES : TileFmt<kQ8_0>::BYTES; }
 

@@ -152,6 +152,33 @@ int tc_token_tile(int T);
 size_t tc_tile_bytes(int type);
 void gemm_tc_init();      // once per device
 int tc_pair_clusters();   // two-CTA clusters of the paired GEMM that fit on the device at once (0: none)
+// A chained launch: the gate/up GEMM (SwiGLU epilogue) and, in the same persistent launch, the down projection that
+// reads its output, for steps of one token tile (T <= 64). Each CTA runs its units in the order of a host schedule
+// (first-GEMM units first); a down unit's activation producer waits, per 256-K tile of its input, until the four
+// gate/up bands that write that tile have stored it (ready[kt] counts their epilogue warps); the launch's last CTA
+// resets the counters. The results are those of the two launches, bit for bit.
+struct Chain {
+  const uint8_t *W = nullptr;   // the second weight's tiles (null: a launch of one GEMM)
+  int NTW = 0, KT = 0, splits = 1;
+  Epi epi{};                    // the second GEMM's epilogue (split-K partials when splits > 1)
+  float *part = nullptr;
+  int Npad = 0;
+  const int *sched = nullptr;      // per CTA its units in order; bit 31: a unit of the second GEMM
+  const int *sched_off = nullptr;  // [grid + 1]
+  unsigned *ready = nullptr;       // [KT of the second weight]
+  unsigned *done = nullptr;        // CTAs finished (reset with ready)
+};
+struct ChainPlan {               // a chained launch's schedule on the device
+  const int *sched = nullptr, *off = nullptr;
+  int ctas = 0;
+  unsigned *ready = nullptr, *done = nullptr;
+};
+// the schedule (host): the first GEMM's NTW0 bands round-robin, then the second GEMM's units (split-major, so those
+// whose inputs complete first come first) each to the least-loaded CTA; returns the busiest CTA's load in tile times
+double chain_schedule(int NTW0, int KT0, int NTW1, int KT1, int splits1, int sms, int *ctas, int *sched_out,
+                      int *off_out);
+void launch_gemm_tc_chain(const QWeight &w0, const TmaSet &ts0, const Epi &e0, const QWeight &w1, const TmaSet &ts1,
+                          const Epi &e1, float *part1, const ChainPlan &cp, int T, int *err, cudaStream_t s);
 // pairs: two-CTA clusters for the paired kernel (0: one CTA per MMA throughout; capped at tc_pair_clusters())
 // sig (optional): the GEMM's completion published to other GPUs (tensor parallelism, phase 1 of the all-reduce)
 void launch_gemm_tc(const QWeight &w, const TmaSet &ts, int T, const Epi &epi, float *part, int *err, int sms,

@@ -149,6 +149,9 @@ struct gc_handle {
   bool graphs_on = true;
   // two-CTA clusters for the paired tcgen05 GEMM (GCK_PAIR=0 at open: none, one CTA per MMA throughout)
   int tc_pairs = 0;
+  // gate/up and down_proj as one chained launch at steps of one token tile (GCK_CHAIN=0 at open: two launches)
+  ChainPlan chain{};
+  bool chain_ok = false, chain_on = true;
   std::vector<Graph> graphs;                 // most recent last
   std::vector<std::vector<int64_t>> seen;   // shapes run once without a graph
   uint64_t scratch_gen = 0;                  // bumped whenever a scratch buffer a kernel argument points to moves
@@ -267,6 +270,44 @@ int tc_splits(int NTW, int KT, int N, int sms, bool reader_sums) {
     }
   }
   return best;
+}
+
+// Steps of one token tile (T <= 64) can run gate/up and down_proj as one chained launch (launch_gemm_tc_chain). Where
+// the model allows it (a16, one GPU, gate/up and down_proj of one tcgen05 type in every layer), down_proj's split-K is
+// chosen for the chained schedule: the busiest CTA's tiles in tile times, plus each slice's partials written and read
+// at 64 rows. It is fixed for every step size alike (batch invariance), whether chaining is on or not.
+void setup_chain(gc_handle *h) {
+  if (h->layers.empty() || h->a8 || h->tp > 1) return;
+  const Layer &l0 = h->layers[0];
+  if ((l0.gu.type != kQ4_K && l0.gu.type != kQ8_0) || l0.dn.type != l0.gu.type) return;
+  for (const Layer &ly : h->layers)
+    if (ly.gu.type != l0.gu.type || ly.dn.type != l0.gu.type || ly.gu.splits != 1 || ly.gu.NT != l0.gu.NT ||
+        ly.gu.KT != l0.gu.KT || ly.dn.NT != l0.dn.NT || ly.dn.KT != l0.dn.KT)
+      return;
+  int best = l0.dn.splits;
+  double best_cost = 1e30;
+  for (int sp = 1; sp <= std::min(16, l0.dn.KT); sp++) {
+    double c = chain_schedule(l0.gu.NT, l0.gu.KT, l0.dn.NT, l0.dn.KT, sp, h->sms, nullptr, nullptr, nullptr);
+    if (sp > 1) c += sp * (64.0 * l0.dn.N * 8.0 / 5e12 / 1.05e-6);
+    if (c < best_cost - 1e-9) {
+      best_cost = c;
+      best = sp;
+    }
+  }
+  for (Layer &ly : h->layers) ly.dn.splits = best;
+  const int total = l0.gu.NT + l0.dn.NT * best;
+  std::vector<int> sched(total), off(h->sms + 1);
+  int ctas = 0;
+  chain_schedule(l0.gu.NT, l0.gu.KT, l0.dn.NT, l0.dn.KT, best, h->sms, &ctas, sched.data(), off.data());
+  int *d = static_cast<int *>(h->dalloc(static_cast<size_t>(total + ctas + 1) * 4, "chained launch schedule"));
+  ck(cudaMemcpy(d, sched.data(), static_cast<size_t>(total) * 4, cudaMemcpyHostToDevice), "chained launch schedule");
+  ck(cudaMemcpy(d + total, off.data(), static_cast<size_t>(ctas + 1) * 4, cudaMemcpyHostToDevice),
+     "chained launch schedule");
+  auto *cnt = static_cast<unsigned *>(h->dalloc(static_cast<size_t>(l0.dn.KT + 1) * 4, "chained launch counters"));
+  ck(cudaMemset(cnt, 0, static_cast<size_t>(l0.dn.KT + 1) * 4), "chained launch counters");
+  h->chain = ChainPlan{d, d + total, ctas, cnt, cnt + l0.dn.KT};
+  h->chain_ok = true;
+  if (const char *e = std::getenv("GCK_CHAIN")) h->chain_on = std::atoi(e) != 0;
 }
 
 // Build the tiled layout of a weight whose logical row n maps to (source, source row) by `rowmap`, on the host, and
@@ -667,6 +708,7 @@ void open_device(gc_handle *h, int dev, const std::vector<std::unique_ptr<GgufFi
   // batch-invariant buckets run the tcgen05 GEMM at every width (a row's arithmetic never depends on the batch)
   h->gemv_max_t = c.tolerance && c.tp == 1 ? kGemvMaxT : 0;
   h->a8 = c.act == "a8";
+  setup_chain(h);
   build_rope(h);
   // KV pool: [L][nblk][KVH][16][dh] for K and for V, plus fp8 page exponents [L][nblk][KVH][2]
   const size_t esz = h->kv_fp8 ? 1 : 2;
@@ -1427,6 +1469,9 @@ void forward_launch(gc_handle *h, const PlanView &pv, int nw) {
   aa.dh = h->dh;
   aa.kv_fp8 = h->kv_fp8;
   aa.scale_log2 = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(h->dh)));
+  // one token tile on the tcgen05 GEMM (not the GEMV of tolerance buckets): gate/up and down_proj chained
+  const bool chain = h->chain_ok && h->chain_on && T > 0 && T <= 64 && !h->layers.empty() &&
+                     !use_gemv(h->layers[0].gu, T) && !use_gemv(h->layers[0].dn, T);
   for (int l = 0; l < h->L; l++) {
     const Layer &ly = h->layers[l];
     norm(nullptr, T, ly.attn_norm);
@@ -1446,6 +1491,20 @@ void forward_launch(gc_handle *h, const PlanView &pv, int nw) {
     quant(h->att, h->H * h->dh, h->H * h->dh, h->att_scale);
     residual(GCK_K_O, ly.o, h->tma_att, h->att, h->H * h->dh, h->att_scale);
     norm(nullptr, T, ly.ffn_norm);
+    if (chain) {
+      // gate/up (SwiGLU) and down_proj (its split-K partials for the next RMSNorm) in one launch
+      const Epi e0{kEpiSwiGLU, h->F, ly.dn.KT * kBK, nullptr, h->act, h->h_scale};
+      const Epi e1{kEpiAdd, h->d, h->d, h->x, nullptr, h->act_scale};
+      run(GCK_K_GATEUP, 1, [&] {
+        launch_gemm_tc_chain(ly.gu, h->tma_h, e0, ly.dn, h->tma_act, e1, h->part, h->chain, T, h->kerr, s);
+      });
+      if (ly.dn.splits > 1) {
+        pend = h->part;
+        pend_s = ly.dn.splits;
+        pend_ld = ly.dn.NT * kBM;
+      }
+      continue;
+    }
     gemm(GCK_K_GATEUP, ly.gu, h->tma_h, h->h, h->d, T,
          Epi{kEpiSwiGLU, h->F, ly.dn.KT * kBK, nullptr, h->act, h->h_scale}, false);
     quant(h->act, h->F, ly.dn.KT * kBK, h->act_scale);

@@ -54,3 +54,12 @@ def test_gemm_roofline_math():
     assert abs(r["frac"] - 4_221_370_368 / 1e-3 / 1e9 / 6454.6) < 1e-3
     # the gate/up launch: 1 ms over 160 launches
     assert abs(r["gateup"]["launch_ms"] - 1.0 / 160) < 1e-4   # reported to 4 decimals
+    # chained steps: the gate/up class holds the one launch per layer that also runs down_proj
+    sg.class_launches[8], sg.class_ms[8] = 0, 0.0
+    sg.class_ms[7] = 2.0
+    r = bench.gemm_roofline(sg, 5, 6454.6, "test")
+    assert r["launches_per_step"] == 97 and "gateup" not in r and "chained" in r["kernel"]
+    mlp = r["gateup_down"]
+    assert mlp["algorithmic_bytes_per_launch"] == 2 * 14336 * 4096 * 144 // 256 + 4096 * 14336 * 144 // 256 + \
+        64 * 4096 * 2 + 2 * 64 * 14336 * 2 + 64 * 4096 * 4
+    assert abs(mlp["launch_ms"] - 2.0 / 160) < 1e-4

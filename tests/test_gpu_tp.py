@@ -79,3 +79,32 @@ def test_tp2_greedy_and_batch_invariance(tp_model):
         top2 = np.sort(ref, -1)[:, -2:]
         sure = (top2[:, 1] - top2[:, 0]) / np.abs(ref).max(-1) > 2 * TOL_F16
         assert (np.array([t[0] for t in g_tp])[sure] == ref.argmax(-1)[sure]).all()
+
+
+def test_tp2_paired_gemms_equal_single_cta(tmp_path):
+    """At tp = 2, steps of more than 64 rows run the per-rank GEMMs on CTA pairs (cta_group::2) with the completion
+    signal the all-reduce waits for; a handle opened with GCK_PAIR=0 runs them on one CTA per MMA. The logits agree bit
+    for bit (the pair's sums equal the single CTA's, and the ranks are added in a fixed order)."""
+    if gpus() < 2:
+        pytest.skip("2 GPUs needed")
+    import os
+    spec = synth.Spec(**TPSHAPE, wtype="q4_k", seed=13)
+    ws = synth.make(str(tmp_path / "w"), spec, ncol=256, maxctx=512)[1]
+    pack = synth.pack_dir(str(tmp_path / "tp2"), spec, [dict(id="b200.BI.main", ncol=256, maxctx=512, tp=2)],
+                          weights_file=ws[0])
+    rng = np.random.default_rng(5)
+    prompts = [[int(x) for x in rng.integers(1, 1000, n)] for n in (100, 90, 60)]
+    tabs = [list(range(8 * i, 8 * i + 8)) for i in range(3)]
+    outs = []
+    for pair in ("1", "0"):
+        os.environ["GCK_PAIR"] = pair
+        try:
+            with gck.Backend(pack, ws, pool_blocks=32, device=0) as be:
+                got = [be.step([gck.Work(0, prompts[0], 0, tabs[0], len(prompts[0]))]),
+                       be.step([gck.Work(i, p, 0, tabs[i], len(p)) for i, p in enumerate(prompts[1:], 1)])]
+                got.append(be.step([gck.Work(i, [p[-1]], len(p), tabs[i], 1) for i, p in enumerate(prompts)]))
+        finally:
+            os.environ.pop("GCK_PAIR", None)
+        outs.append(got)
+    for a, b in zip(*outs):
+        assert np.array_equal(a, b)
