@@ -38,9 +38,10 @@ METRIC = "decode tok/s (8B Q4_K, batch 64, fp8 KV)"
 # layers: a layer's launches have the full-size weights and KV); each names the library build it was captured on, and
 # is reported beside the live timing, never in place of it
 ATTN_TRAFFIC = dict(bytes=287_385_088, build="13d6345", kernel="attn_kernel<128, fp8, 1 warp, 1 row tile>")
-# one layer's four GEMM launches (q/k/v, o, gate/up, down): 127.1 MB of DRAM traffic against 122.7 MB of Q4_K weights
-# (1.036); "bytes" is their mean per launch, "gateup" the gate/up launch alone (the head launch was not captured)
-GEMM_TRAFFIC = dict(bytes=31_778_560, gateup=67_404_032, build="13d6345", ratio_to_weight_bytes=1.036)
+# one layer's three GEMM launches (q/k/v, o, gate/up chained with down): 128.1 MB of DRAM traffic against 122.7 MB of
+# Q4_K weights (1.044); "bytes" is their mean per launch, "gateup_down" the chained launch alone (the head launch was
+# not captured)
+GEMM_TRAFFIC = dict(bytes=42_703_701, gateup_down=103_319_040, build="dbd0dbe", ratio_to_weight_bytes=1.044)
 
 
 def contexts():
@@ -372,8 +373,8 @@ def gemm_roofline(sg, steps, hbm, peak_source):
            "algorithmic_bytes_per_step": int(wb),
            "traffic": GEMM_TRAFFIC["bytes"] if GEMM_TRAFFIC else None,
            "traffic_build": GEMM_TRAFFIC["build"] if GEMM_TRAFFIC else None,
-           "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean per launch over one layer's four GEMM "
-                             "launches (--layers 2 case, full-size weights); 1.036 x their weight bytes",
+           "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean per launch over one layer's three GEMM "
+                             "launches (--layers 2 case, full-size weights); 1.044 x their weight bytes",
            ("gateup_down" if chained else "gateup"): {
                "launch_ms": round(gu_ms, 4), "algorithmic_bytes_per_launch": int(gu_bytes),
                "achieved": round(gu_bytes / (gu_ms / 1e3) / 1e9, 1),
