@@ -69,12 +69,14 @@ def test_gemv_tolerance_bucket(tmp_path, wtype):
     assert any(not np.array_equal(a, b) for a, b in zip(outs["tol"], outs["bi"]))
 
 
+@pytest.mark.parametrize("shape", ["small", "small128"])
 @pytest.mark.parametrize("kv", ["f16", "fp8"])
-def test_long_context_merge_of_many_splits(tmp_path, kv):
+def test_long_context_merge_of_many_splits(tmp_path, kv, shape):
     """One sequence decoding over a 2200-row context in a tolerance bucket: a step with this little attention work takes
     64-entry splits, so each token's 35 splits are merged in two passes (32 splits, then 3) by the last split to
-    finish; the decode logits match the oracle's (ref.py:39-62 over the same pages)."""
-    spec = synth.Spec(**SMALL128, wtype="q8_0", seed=21, ctx=4096)
+    finish; the decode logits match the oracle's (ref.py:39-62 over the same pages). Both head dims: 64 (two kv heads,
+    GQA 2) and 128 (one kv head, GQA 4)."""
+    spec = synth.Spec(**(SMALL if shape == "small" else SMALL128), wtype="q8_0", seed=21, ctx=4096)
     ws = synth.make(str(tmp_path / "w"), spec, ncol=2, maxctx=4096)[1]
     kv_scale = "page" if kv == "fp8" else "unit"
     pack = synth.pack_dir(str(tmp_path / "tol"), spec, [dict(id="b200.FAST.main", ncol=2, maxctx=4096, kv=kv,
