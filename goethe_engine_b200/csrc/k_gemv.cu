@@ -5,11 +5,15 @@
 // At one to four token rows a step's linear layers are a stream of the quantized weights (Q4_K 0.5625 B, Q8_0
 // 1.0625 B per weight) with a handful of multiply-adds per byte, so this runs on the CUDA cores at the HBM roofline
 // instead of feeding 16-token tiles to the tensor cores. A CTA takes one unit = a 128-row band of the relaid weight
-// (the tcgen05 GEMM's tiles: 256 K per tile, rows' 16-byte chunks adjacent, so every load below is a coalesced 16-byte
-// vector load) over a fixed slice of its K tiles. Two threads per row split each tile's eight 32-K sub-blocks; the
-// next tile's raw bytes are loaded before the current one is dequantized (the shared f16 helpers: every weight rounded
-// once, as in the GEMM) and multiplied with the step's activations, staged once per CTA in shared memory. Each 32-K
-// sub-block accumulates in packed f16, then in f32; the two halves of a row add in a fixed order.
+// (the tcgen05 GEMM's tiles: 256 K per tile, rows' 16-byte chunks adjacent) over a fixed slice of its K tiles. The
+// tiles stream through a ring in shared memory, one 1-D bulk copy per tile issued by one thread, the first ones before
+// the kernel waits for its activations (the weights depend on no earlier kernel): a CTA keeps the whole ring in flight
+// (about 70 KB, two CTAs per SM), where a register double buffer held one tile of its threads' bytes and left HBM
+// half idle at batch 1. Two threads per row split each tile's eight 32-K sub-blocks: a thread takes its row's 16-byte
+// pieces of the tile from shared memory (rows adjacent: conflict-free), dequantizes them (the shared f16 helpers:
+// every weight rounded once, as in the GEMM) and multiplies them with the step's activations, staged once per CTA in
+// shared memory. Each 32-K sub-block accumulates in packed f16, then in f32; the two halves of a row add in a fixed
+// order. Every wait on the ring is bounded (about 2 s): a timeout sets the error word and the CTA returns.
 //
 // Numerics: the f16 sub-block sums make this path differ from the tcgen05 one in the last bits, and the library uses
 // it only for a few rows, so a row's result depends on the batch width: the manifest's "tolerance" determinism (a
@@ -26,29 +30,74 @@ namespace {
 
 constexpr int kGemvThreads = 256;   // two threads per row of the 128-row band
 
+constexpr unsigned long long kRingWaitNs = 2000000000ull;
+constexpr int kErrGemvRing = 17;    // error word: a tile of the ring did not land within the limit
+
 template <int TYPE>
 struct Raw;
 template <>
 struct Raw<kQ4_K> {                 // a thread's bytes of one tile: the row's header, sub-blocks 4h .. 4h+3
   static constexpr int TILE = kBM * 144;
   static constexpr int N = 5;
+  static constexpr int RING = 4;    // tiles in flight per CTA (73.7 KB)
 };
 template <>
 struct Raw<kQ8_0> {                 // the row's scales, blocks 4h .. 4h+3 (two 16-byte halves each)
   static constexpr int TILE = kBM * 272;
   static constexpr int N = 9;
+  static constexpr int RING = 2;    // 69.6 KB
 };
+// dynamic shared memory: the ring's barriers (128 B), the ring, then the activations [T][nk] f16
+constexpr int kRingOff = 128;
 
+GCK_DEV void ring_init(uint64_t *b) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_u32(b)));
+}
+// one 1-D bulk copy of a tile into its ring slot; the slot's barrier completes when the bytes have landed
+GCK_DEV void ring_fill(uint8_t *dst, const uint8_t *src, uint32_t bytes, uint64_t *b) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(b))
+               : "memory");
+}
+GCK_DEV bool ring_try(uint64_t *b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 1000;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// bounded wait for the phase of the given parity; false (and the error word set) on timeout
+GCK_DEV bool ring_wait(uint64_t *b, uint32_t parity, int *err) {
+  if (ring_try(b, parity)) return true;
+  unsigned long long t0, t;
+  asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t0));
+  for (uint32_t n = 1;; n++) {
+    if (ring_try(b, parity)) return true;
+    if ((n & 63u) == 0) {
+      asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+      if (t - t0 > kRingWaitNs) {
+        atomicCAS(err, 0, kErrGemvRing);
+        return false;
+      }
+    }
+  }
+}
+
+// a thread's 16-byte pieces of the tile in shared memory (row r, half hs)
 template <int TYPE>
 GCK_DEV void load_raw(const uint8_t *tile, int r, int hs, uint4 (&v)[Raw<TYPE>::N]) {
   const uint4 *t = reinterpret_cast<const uint4 *>(tile);
-  v[0] = __ldg(t + r);
+  v[0] = t[r];
   if (TYPE == kQ4_K) {
 #pragma unroll
-    for (int i = 0; i < 4; i++) v[1 + i] = __ldg(t + kBM + (4 * hs + i) * kBM + r);
+    for (int i = 0; i < 4; i++) v[1 + i] = t[kBM + (4 * hs + i) * kBM + r];
   } else {
 #pragma unroll
-    for (int i = 0; i < 8; i++) v[1 + i] = __ldg(t + kBM + (8 * hs + i) * kBM + r);
+    for (int i = 0; i < 8; i++) v[1 + i] = t[kBM + (8 * hs + i) * kBM + r];
   }
 }
 
@@ -114,20 +163,26 @@ GCK_DEV void tile_dot(const uint4 (&v)[Raw<TYPE>::N], int hs, const __half2 *xs,
 template <int TYPE, int T>
 __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const uint8_t *__restrict__ W, int KT, int gs,
                                                             const __half *__restrict__ x, int ldx, int K, int Tn,
-                                                            Epi epi, float *part, int Npad) {
-  extern __shared__ __align__(16) uint8_t gsm[];
+                                                            Epi epi, float *part, int Npad, int *err) {
+  constexpr int TILE = Raw<TYPE>::TILE, RING = Raw<TYPE>::RING;
+  extern __shared__ __align__(128) uint8_t gsm[];
+  uint64_t *full = reinterpret_cast<uint64_t *>(gsm);
+  uint8_t *ring = gsm + kRingOff;
   const int nt = blockIdx.x / gs, sl = blockIdx.x % gs;
   const int base = KT / gs, extra = KT % gs;
   const int per = base + (sl < extra ? 1 : 0), kt0 = sl * base + min(sl, extra);
   const int nk = per * kBK;
   const int r = threadIdx.x & (kBM - 1), hs = threadIdx.x / kBM;
-  const uint8_t *tiles = W + (static_cast<size_t>(nt) * KT + kt0) * Raw<TYPE>::TILE;
-  // the weights depend on no earlier kernel: the first tile is requested before waiting for the activations
-  uint4 cur[Raw<TYPE>::N];
-  load_raw<TYPE>(tiles, r, hs, cur);
+  const uint8_t *tiles = W + (static_cast<size_t>(nt) * KT + kt0) * TILE;
+  // the weights depend on no earlier kernel: the ring's first tiles are requested before waiting for the activations
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < RING; i++) ring_init(&full[i]);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    for (int i = 0; i < RING && i < per; i++) ring_fill(ring + i * TILE, tiles + static_cast<size_t>(i) * TILE, TILE, &full[i]);
+  }
   dep_wait();
   dep_launch();
-  __half *sx = reinterpret_cast<__half *>(gsm);
+  __half *sx = reinterpret_cast<__half *>(gsm + kRingOff + RING * TILE);
   const int k0 = kt0 * kBK, chunks = nk / 8;
   for (int i = threadIdx.x; i < T * chunks; i += kGemvThreads) {
     const int t = i / chunks, c = i % chunks, k = k0 + 8 * c;
@@ -144,20 +199,33 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const uint8_t *__res
     }
     reinterpret_cast<uint4 *>(sx + static_cast<size_t>(t) * nk)[c] = v;
   }
-  __syncthreads();
+  __syncthreads();   // the activations staged, the ring's barriers initialised
 
   float acc[T];
 #pragma unroll
   for (int t = 0; t < T; t++) acc[t] = 0.f;
   const __half2 *xs = reinterpret_cast<const __half2 *>(sx);
-  for (int u = 0; u < per; u++) {
-    uint4 nxt[Raw<TYPE>::N];
-    if (u + 1 < per) load_raw<TYPE>(tiles + static_cast<size_t>(u + 1) * Raw<TYPE>::TILE, r, hs, nxt);
-    tile_dot<TYPE, T>(cur, hs, xs + u * (kBK / 2), nk / 2, acc);
-    if (u + 1 < per) {
-#pragma unroll
-      for (int i = 0; i < Raw<TYPE>::N; i++) cur[i] = nxt[i];
+  int u = 0;
+  for (; u < per; u++) {
+    // tile u sits in slot u % RING, phase (u / RING) & 1 of its barrier; every thread waits for it
+    const int slot = u % RING;
+    const bool ok = ring_wait(&full[slot], static_cast<uint32_t>((u / RING) & 1), err);
+    uint4 cur[Raw<TYPE>::N];
+    load_raw<TYPE>(ring + slot * TILE, r, hs, cur);
+    // every thread holds its bytes of the slot; a timeout anywhere ends the loop for the whole CTA
+    if (__syncthreads_or(ok ? 0 : 1)) break;
+    if (threadIdx.x == 0 && u + RING < per) {
+      // the generic-proxy reads of the slot above are ordered before the bulk copy's writes into it
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+      ring_fill(ring + slot * TILE, tiles + static_cast<size_t>(u + RING) * TILE, TILE, &full[slot]);
     }
+    tile_dot<TYPE, T>(cur, hs, xs + u * (kBK / 2), nk / 2, acc);
+  }
+  if (u < per) {
+    // a tile did not land in time: the copies this CTA issued land before it exits (bounded), then it returns
+    if (threadIdx.x == 0)
+      for (int i = u; i < per && i < u + RING; i++) ring_wait(&full[i % RING], static_cast<uint32_t>((i / RING) & 1), err);
+    return;
   }
 
   // the row's two halves, in order (sub-blocks 0-3, then 4-7)
@@ -209,21 +277,23 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const uint8_t *__res
 }
 
 template <int TYPE, int T>
-void launch_tt(const QWeight &w, int gs, const __half *x, int ldx, int Tn, const Epi &epi, float *part, cudaStream_t s) {
+void launch_tt(const QWeight &w, int gs, const __half *x, int ldx, int Tn, const Epi &epi, float *part, int *err,
+               cudaStream_t s) {
   const int per_max = (w.KT + gs - 1) / gs;
-  const size_t smem = static_cast<size_t>(T) * per_max * kBK * 2;
+  const size_t smem = kRingOff + static_cast<size_t>(Raw<TYPE>::RING) * Raw<TYPE>::TILE +
+                      static_cast<size_t>(T) * per_max * kBK * 2;
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(gemv_kernel<TYPE, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   launch_pdl(gemv_kernel<TYPE, T>, w.NT * gs, kGemvThreads, smem, s, w.data, w.KT, gs, x, ldx, w.K, Tn, epi, part,
-             w.NT * kBM);
+             w.NT * kBM, err);
 }
 
 template <int TYPE>
-void launch_type(const QWeight &w, int gs, const __half *x, int ldx, int Tn, const Epi &epi, float *part,
+void launch_type(const QWeight &w, int gs, const __half *x, int ldx, int Tn, const Epi &epi, float *part, int *err,
                  cudaStream_t s) {
-  if (Tn <= 1) launch_tt<TYPE, 1>(w, gs, x, ldx, Tn, epi, part, s);
-  else if (Tn == 2) launch_tt<TYPE, 2>(w, gs, x, ldx, Tn, epi, part, s);
-  else launch_tt<TYPE, 4>(w, gs, x, ldx, Tn, epi, part, s);
+  if (Tn <= 1) launch_tt<TYPE, 1>(w, gs, x, ldx, Tn, epi, part, err, s);
+  else if (Tn == 2) launch_tt<TYPE, 2>(w, gs, x, ldx, Tn, epi, part, err, s);
+  else launch_tt<TYPE, 4>(w, gs, x, ldx, Tn, epi, part, err, s);
 }
 
 }  // namespace
@@ -238,11 +308,11 @@ int gemv_slices(int NTW, int KT, int sms, bool reader_sums) {
   return std::max(gs, lo);
 }
 
-void launch_gemv(const QWeight &w, int gs, const __half *x, int ldx, int T, const Epi &epi, float *part,
+void launch_gemv(const QWeight &w, int gs, const __half *x, int ldx, int T, const Epi &epi, float *part, int *err,
                  cudaStream_t s) {
   if (T <= 0) return;
-  if (w.type == kQ4_K) launch_type<kQ4_K>(w, gs, x, ldx, T, epi, part, s);
-  else launch_type<kQ8_0>(w, gs, x, ldx, T, epi, part, s);
+  if (w.type == kQ4_K) launch_type<kQ4_K>(w, gs, x, ldx, T, epi, part, err, s);
+  else launch_type<kQ8_0>(w, gs, x, ldx, T, epi, part, err, s);
 }
 
 }  // namespace gck

@@ -141,7 +141,7 @@ void launch_gemm(const QWeight &w, const __half *act, int T, const Epi &epi, flo
 // gs > 1, else the epilogue)
 constexpr int kGemvMaxT = 4;
 int gemv_slices(int NTW, int KT, int sms, bool reader_sums);
-void launch_gemv(const QWeight &w, int gs, const __half *x, int ldx, int T, const Epi &epi, float *part,
+void launch_gemv(const QWeight &w, int gs, const __half *x, int ldx, int T, const Epi &epi, float *part, int *err,
                  cudaStream_t s);
 
 struct TmaSet {            // tensor maps over one activation buffer [rows, K] f16, boxes of 64 K x {16..256} rows

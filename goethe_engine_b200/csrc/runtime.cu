@@ -1384,7 +1384,7 @@ void forward_launch(gc_handle *h, const PlanView &pv, int nw) {
   auto gemm = [&](int cls, const QWeight &w, const TmaSet &ts, const __half *act, int ldx, int rows, const Epi &e,
                   bool reader_reduces) {
     run(cls, 1, [&] {
-      if (use_gemv(w, rows)) launch_gemv(w, w.gslices, act, ldx, rows, e, h->part, s);
+      if (use_gemv(w, rows)) launch_gemv(w, w.gslices, act, ldx, rows, e, h->part, h->kerr, s);
       else if (w.type == kF16) launch_gemm(w, act, rows, e, h->part, s);
       else launch_gemm_tc(w, ts, rows, e, h->part, h->kerr, h->sms, h->tc_pairs, s);
     });
