@@ -299,11 +299,12 @@ void launch_type(const QWeight &w, int gs, const __half *x, int ldx, int Tn, con
 }  // namespace
 
 int gemv_slices(int NTW, int KT, int sms, bool reader_sums) {
-  // enough units for three CTAs per SM, at most 16 tiles (4096 K) of activations per CTA, at most 16 slices; a weight
+  // one wave: as many units as fit two CTAs per SM (the ring's shared memory admits two), so every unit streams at
+  // once with the same share of tiles; at most 16 tiles (4096 K) of activations per CTA, at most 16 slices; a weight
   // whose partials would need a reduce launch keeps one slice when its bands alone fill the SMs
   const int lo = (KT + 15) / 16;
   if (!reader_sums && NTW >= sms) return lo;
-  int gs = (3 * sms + NTW - 1) / NTW;
+  int gs = std::max(1, 2 * sms / NTW);
   gs = std::min(gs, std::min(16, KT));
   return std::max(gs, lo);
 }
